@@ -1,0 +1,105 @@
+// kernels.h -- host-side declarations of the device buffers and kernel launchers.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace ab2 {
+
+// A Q8_0 weight in the packed device layout described in common.cuh.
+struct Q8Weight {
+    uint8_t* qs = nullptr;  // [M16][KB][32][16]
+    uint8_t* d = nullptr;   // [M16][KB][8] x (f16, f16)
+    int64_t M = 0;          // logical rows
+    int M16 = 0;            // ceil(M/16)
+    int KB = 0;             // K / 32
+    size_t qs_bytes() const { return (size_t)M16 * KB * 512; }
+    size_t d_bytes() const { return (size_t)M16 * KB * 32; }
+};
+
+enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+
+struct GemmEpi {
+    int mode = EPI_STORE;
+    float* y = nullptr;  // STORE / RESID: y[b*ldy + row]; SWIGLU: optional f32 copy of h
+    int ldy = 0;
+    int m_out = 0;       // valid output rows (M, or ffn for SWIGLU)
+    uint8_t* xf_out = nullptr;  // SWIGLU: the next GEMM's activation fragments
+    XfragShape xs_out{};
+};
+
+// q8.cu
+int gemm_nsplit(int M16, int KB, int num_sms);
+int gemm_grid_x(int M16);
+size_t gemm_ws_floats(int M16, int KB, int batch, int num_sms);
+void launch_q8_gemm(const Q8Weight& w, const uint8_t* xf, int batch, float* ws, unsigned* tickets,
+                    const GemmEpi& ep, int num_sms, cudaStream_t st);
+void launch_q8_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
+                      int64_t stride, cudaStream_t st);
+void launch_q8_dequant_raw(const uint8_t* src, int64_t n_blocks, float* out, cudaStream_t st);
+void launch_q8p_dequant(const Q8Weight& w, int64_t rows, float* out, cudaStream_t st);
+void launch_embed(const Q8Weight& w, int vocab, const int32_t* tokens, int batch, float* x, int ldx, cudaStream_t st);
+
+// misc.cu
+void launch_rmsnorm_xfrag(const float* x, int ldx, const float* w, int D, float eps, int batch, uint8_t* xf,
+                          cudaStream_t st);
+void launch_to_xfrag(const float* x, int ldx, int K, int batch, uint8_t* xf, cudaStream_t st);
+void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st);
+void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st);
+void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st);
+void launch_seed_kv(void* dst, bool bf16, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
+                    uint64_t stream, float std, cudaStream_t st);
+
+// deltanet.cu
+struct DnParams {
+    const float* proj;   // [B][ldp]: qkv (3D) | gate (D) | beta_raw (H) | alpha_raw (H)
+    int ldp;
+    float* conv;         // [B][3D][K] (per-slot stride conv_stride floats)
+    int64_t conv_stride;
+    const float* conv_w; // [3D][K]
+    int K;
+    float* S;            // [B][H][128][128] (per-slot stride s_stride floats)
+    int64_t s_stride;
+    const float* ssm_a;  // [H]
+    const float* dt_bias;
+    const float* ssm_norm;  // [128]
+    float eps;
+    int D, H;
+    uint8_t* xf_out;     // activation fragments of the ssm_out GEMM (K = D)
+    XfragShape xs;
+    float* o_out;        // optional f32 copy of the gated output [B][D]
+};
+void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
+// recurrence core only (op API): q,k,v bf16 [B][H][128], beta/decay f32 [B][H], o f32 [B][H][128]
+void launch_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,
+                        const float* decay, int B, int H, float* o, cudaStream_t st);
+
+// attention.cu
+struct AttnParams {
+    const float* proj;   // [B][ldp]: q_full (Hq*2*HD, per head [q | gate]) | k (Hkv*HD) | v (Hkv*HD)
+    int ldp;
+    const float* q_norm; // [HD] or null
+    const float* k_norm; // [HD] or null
+    const float2* rope;  // [rope_rows][rot/2] (cos, sin)
+    int rot;
+    void* kc;            // K cache [slots][Hkv][cap][HD] (float or bf16)
+    void* vc;
+    int64_t kv_slot_stride;  // elements between consecutive slots
+    int cap;
+    const int32_t* pos;  // [B] position of the new token per slot
+    int Hq, Hkv;
+    int chunk;           // tokens per split
+    float* ws;           // split partials
+    unsigned* tickets;   // [B*Hkv]
+    uint8_t* xf_out;     // activation fragments of the wo GEMM (K = Hq*HD)
+    XfragShape xs;
+    float* o_out;        // optional f32 copy [B][Hq*HD]
+};
+int attn_nsplit(int max_len, int chunk);
+int attn_chunk(int batch, int hkv, int max_len, int num_sms);
+int attn_nsplit_bound(int batch, int hkv, int cap, int num_sms);
+size_t attn_ws_floats(int batch, int hkv, int nsplit, int hd, int gq);
+int launch_attention(const AttnParams& p, int batch, int hd, bool kv_bf16, int max_len, cudaStream_t st);
+
+}  // namespace ab2

@@ -1,0 +1,149 @@
+// misc.cu -- RMSNorm into GEMM activation fragments, f32 -> fragments, greedy argmax.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ab2 {
+
+// out = x * (1 / sqrt(mean(x^2) + eps)) * w, written as activation fragments for the next
+// GEMM (rmsnorm_vec, crates/cli/src/main.rs:1106-1113). One CTA per batch row.
+__global__ void __launch_bounds__(256) rmsnorm_xfrag_kernel(const float* __restrict__ x, int ldx,
+                                                            const float* __restrict__ w, int D, float eps,
+                                                            uint8_t* __restrict__ xf, XfragShape xs) {
+    __shared__ float red[8];
+    const int b = blockIdx.x;
+    const float* xb = x + (size_t)b * ldx;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < D; i += 256) ss += xb[i] * xb[i];
+    ss = block_sum<256>(ss, red);
+    ss = ss / (float)D;
+    const float inv = 1.0f / sqrtf(ss + eps);
+    for (int i = threadIdx.x; i < D; i += 256) xfrag_store(xf, xs, b, i, xb[i] * inv * w[i]);
+}
+
+__global__ void to_xfrag_kernel(const float* __restrict__ x, int ldx, int K, uint8_t* __restrict__ xf,
+                                XfragShape xs) {
+    const int b = blockIdx.x;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xfrag_store(xf, xs, b, i, x[(size_t)b * ldx + i]);
+}
+
+// argmax under f32::total_cmp with ties going to the last index, as Iterator::max_by
+// (greedy_sample, crates/cli/src/main.rs:1767-1785). One CTA per batch row.
+__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int ld, int V,
+                                                      int32_t* __restrict__ out) {
+    __shared__ int32_t sk[32];
+    __shared__ int32_t si[32];
+    const int b = blockIdx.x;
+    const float* l = logits + (size_t)b * ld;
+    int32_t bk = INT32_MIN, bi = -1;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        int32_t k = total_key(l[i]);
+        if (k > bk || (k == bk && i > bi)) {
+            bk = k;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
+        if (ok > bk || (ok == bk && oi > bi)) {
+            bk = ok;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    if (ln == 0) {
+        sk[w] = bk;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        bk = ln < nw ? sk[ln] : INT32_MIN;
+        bi = ln < nw ? si[ln] : -1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
+            if (ok > bk || (ok == bk && oi > bi)) {
+                bk = ok;
+                bi = oi;
+            }
+        }
+        if (ln == 0) out[b] = bi < 0 ? 0 : bi;
+    }
+}
+
+void launch_rmsnorm_xfrag(const float* x, int ldx, const float* w, int D, float eps, int batch, uint8_t* xf,
+                          cudaStream_t st) {
+    rmsnorm_xfrag_kernel<<<batch, 256, 0, st>>>(x, ldx, w, D, eps, xf, xfrag_shape(D, batch));
+}
+
+void launch_to_xfrag(const float* x, int ldx, int K, int batch, uint8_t* xf, cudaStream_t st) {
+    to_xfrag_kernel<<<batch, 256, 0, st>>>(x, ldx, K, xf, xfrag_shape(K, batch));
+}
+
+void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st) {
+    argmax_kernel<<<batch, 1024, 0, st>>>(logits, ld, V, out);
+}
+
+__global__ void pos_advance_kernel(int32_t* pos, int batch) {
+    int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < batch) pos[b] += 1;
+}
+
+// counter-based normal samples: splitmix64 hash of (seed, stream, index) -> Box-Muller
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ float hash_normal(uint64_t seed, uint64_t stream, uint64_t i) {
+    uint64_t h = mix64(seed ^ mix64(stream * 0x632be59bd9b4e019ull + i));
+    float u1 = ((float)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);   // (0, 1]
+    float u2 = (float)((h >> 16) & 0xffffffu) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+__global__ void seed_f32_kernel(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i < n; i += (int64_t)gridDim.x * blockDim.x) dst[i] = std * hash_normal(seed, stream, (uint64_t)i);
+}
+
+// rows of hd values at [row][0, hd) for rows with (row % cap) < n_tokens, bf16-representable
+template <typename T>
+__global__ void seed_kv_kernel(T* dst, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
+                               uint64_t stream, float std) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n = rows * hd;
+    for (; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t row = i / hd;
+        if (row % cap >= n_tokens) continue;
+        float v = __bfloat162float(__float2bfloat16_rn(std * hash_normal(seed, stream, (uint64_t)i)));
+        if constexpr (sizeof(T) == 4) dst[i] = v;
+        else dst[i] = __float2bfloat16_rn(v);
+    }
+}
+
+void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st) {
+    pos_advance_kernel<<<(batch + 127) / 128, 128, 0, st>>>(pos, batch);
+}
+
+void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st) {
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    seed_f32_kernel<<<(unsigned)blocks, 256, 0, st>>>(dst, n, seed, stream, std);
+}
+
+void launch_seed_kv(void* dst, bool bf16, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
+                    uint64_t stream, float std, cudaStream_t st) {
+    int64_t blocks = (rows * hd + 255) / 256;
+    if (blocks > 148 * 64) blocks = 148 * 64;
+    if (bf16)
+        seed_kv_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>((__nv_bfloat16*)dst, rows, cap, n_tokens,
+                                                                       hd, seed, stream, std);
+    else
+        seed_kv_kernel<float><<<(unsigned)blocks, 256, 0, st>>>((float*)dst, rows, cap, n_tokens, hd, seed, stream,
+                                                               std);
+}
+
+}  // namespace ab2

@@ -1,0 +1,1297 @@
+// runtime.cu -- host runtime and C ABI (include/ab2.h) of the B200 decode backend.
+//
+// Owns the GGUF parse, the Qwen3.5 hybrid configuration, the packed device weights, the
+// per-slot recurrent / conv / KV state and the decode-step driver that launches the kernels
+// of q8.cu, deltanet.cu, attention.cu and misc.cu on a context-owned stream.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/ab2.h"
+#include "kernels.h"
+
+#define AB2_API extern "C" __attribute__((visibility("default")))
+
+using namespace ab2;
+
+namespace {
+
+thread_local std::string g_err;
+
+int seterr(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) {                                                                     \
+            return seterr(e_ == cudaErrorMemoryAllocation ? AB2_ERR_OOM : AB2_ERR_CUDA, "%s: %s (%s:%d)", \
+                          #call, cudaGetErrorString(e_), __FILE__, __LINE__);                        \
+        }                                                                                            \
+    } while (0)
+
+#define RET(expr)               \
+    do {                        \
+        int r_ = (expr);        \
+        if (r_ != 0) return r_; \
+    } while (0)
+
+// ------------------------------------------------------------------------------------- GGUF
+// Same byte format and accessor semantics as the reference parser
+// (crates/gguf/src/parser.rs:17-347, :354-486), written for this runtime.
+enum : uint32_t { G_U8 = 0, G_I8, G_U16, G_I16, G_U32, G_I32, G_F32, G_BOOL, G_STRING, G_ARRAY, G_U64, G_I64, G_F64 };
+
+struct GValue {
+    uint32_t type = 0;
+    uint64_t u = 0;
+    double f = 0.0;
+    std::string s;
+    uint64_t count = 0;  // arrays
+};
+
+struct GTensor {
+    std::string name;
+    std::vector<uint64_t> dims;
+    uint32_t type = 0;
+    uint64_t offset = 0;
+    uint64_t nbytes = 0;
+    const uint8_t* data = nullptr;  // inside the caller's buffer
+};
+
+struct Gguf {
+    std::unordered_map<std::string, GValue> kv;
+    std::unordered_map<std::string, GTensor> tensors;
+    std::string arch;
+
+    const GValue* get(const std::string& k) const {
+        auto it = kv.find(k);
+        return it == kv.end() ? nullptr : &it->second;
+    }
+    bool u32(const std::string& key, uint64_t* v) const {  // MetadataValue::as_u32: exact type only
+        const GValue* g = get(arch + "." + key);
+        if (!g || g->type != G_U32) return false;
+        *v = g->u;
+        return true;
+    }
+    bool f32(const std::string& key, float* v) const {
+        const GValue* g = get(arch + "." + key);
+        if (!g || g->type != G_F32) return false;
+        *v = (float)g->f;
+        return true;
+    }
+    const GTensor* tensor(const std::string& n) const {
+        auto it = tensors.find(n);
+        return it == tensors.end() ? nullptr : &it->second;
+    }
+};
+
+struct Reader {
+    const uint8_t* p;
+    uint64_t n, o = 0;
+    template <typename T>
+    bool rd(T* v) {
+        if (sizeof(T) > n - o) return false;
+        memcpy(v, p + o, sizeof(T));
+        o += sizeof(T);
+        return true;
+    }
+    bool str(std::string* s) {
+        uint64_t len;
+        if (!rd(&len) || len > n - o) return false;
+        if (s) s->assign((const char*)p + o, len);
+        o += len;
+        return true;
+    }
+    bool value(uint32_t t, GValue* v, int depth) {
+        v->type = t;
+        switch (t) {
+            case G_U8: case G_I8: case G_BOOL: { uint8_t x; if (!rd(&x)) return false; v->u = x; return true; }
+            case G_U16: case G_I16: { uint16_t x; if (!rd(&x)) return false; v->u = x; return true; }
+            case G_U32: case G_I32: { uint32_t x; if (!rd(&x)) return false; v->u = x; return true; }
+            case G_U64: case G_I64: { uint64_t x; if (!rd(&x)) return false; v->u = x; return true; }
+            case G_F32: { float x; if (!rd(&x)) return false; v->f = x; return true; }
+            case G_F64: { double x; if (!rd(&x)) return false; v->f = x; return true; }
+            case G_STRING: return str(&v->s);
+            case G_ARRAY: {
+                uint32_t et;
+                uint64_t cnt;
+                if (depth > 3 || !rd(&et) || !rd(&cnt) || et > G_F64) return false;
+                v->count = cnt;
+                GValue tmp;
+                for (uint64_t i = 0; i < cnt; i++) {
+                    if (et == G_STRING) {
+                        if (!str(nullptr)) return false;
+                    } else if (!value(et, &tmp, depth + 1)) {
+                        return false;
+                    }
+                }
+                return true;
+            }
+            default: return false;
+        }
+    }
+};
+
+// block size / bytes per block of the GGML types the reference parser accepts (parser.rs:93-137)
+bool ggml_sizes(uint32_t t, uint64_t* bs, uint64_t* bpb) {
+    switch (t) {
+        case 0: *bs = 1; *bpb = 4; return true;     // F32
+        case 1: *bs = 1; *bpb = 2; return true;     // F16
+        case 2: *bs = 32; *bpb = 18; return true;   // Q4_0
+        case 3: *bs = 32; *bpb = 20; return true;   // Q4_1
+        case 6: *bs = 32; *bpb = 22; return true;   // Q5_0
+        case 7: *bs = 32; *bpb = 24; return true;   // Q5_1
+        case 8: *bs = 32; *bpb = 34; return true;   // Q8_0
+        case 12: *bs = 256; *bpb = 144; return true;  // Q4_K
+        case 13: *bs = 256; *bpb = 176; return true;  // Q5_K
+        case 14: *bs = 256; *bpb = 210; return true;  // Q6_K
+        default: return false;
+    }
+}
+
+int parse_gguf(const uint8_t* data, uint64_t len, Gguf* g) {
+    if (!data) return seterr(AB2_ERR_ARG, "gguf: null buffer");
+    Reader r{data, len};
+    uint32_t magic, version;
+    uint64_t nt, nkv;
+    if (!r.rd(&magic)) return seterr(AB2_ERR_FORMAT, "gguf: truncated header");
+    if (magic != 0x46554747u) return seterr(AB2_ERR_FORMAT, "gguf: bad magic 0x%08x", magic);
+    if (!r.rd(&version) || !r.rd(&nt) || !r.rd(&nkv)) return seterr(AB2_ERR_FORMAT, "gguf: truncated header");
+    if (version < 2 || version > 3) return seterr(AB2_ERR_FORMAT, "gguf: unsupported version %u", version);
+    for (uint64_t i = 0; i < nkv; i++) {
+        std::string key;
+        uint32_t t;
+        GValue v;
+        if (!r.str(&key) || !r.rd(&t)) return seterr(AB2_ERR_FORMAT, "gguf: truncated metadata");
+        if (!r.value(t, &v, 0)) return seterr(AB2_ERR_FORMAT, "gguf: bad metadata value for '%s'", key.c_str());
+        g->kv[key] = std::move(v);
+    }
+    std::vector<GTensor> ts;
+    for (uint64_t i = 0; i < nt; i++) {
+        GTensor t;
+        uint32_t nd;
+        if (!r.str(&t.name) || !r.rd(&nd) || nd > 8) return seterr(AB2_ERR_FORMAT, "gguf: truncated tensor info");
+        t.dims.resize(nd);
+        for (auto& d : t.dims)
+            if (!r.rd(&d)) return seterr(AB2_ERR_FORMAT, "gguf: truncated tensor info");
+        if (!r.rd(&t.type) || !r.rd(&t.offset)) return seterr(AB2_ERR_FORMAT, "gguf: truncated tensor info");
+        uint64_t bs, bpb, ne = 1;
+        if (!ggml_sizes(t.type, &bs, &bpb)) return seterr(AB2_ERR_FORMAT, "gguf: unsupported GGML type %u (%s)", t.type, t.name.c_str());
+        for (auto d : t.dims) ne *= d;
+        t.nbytes = (ne + bs - 1) / bs * bpb;
+        ts.push_back(std::move(t));
+    }
+    uint64_t align = 32;
+    const GValue* a = g->get("general.alignment");
+    if (a && a->type == G_U32) align = a->u;
+    if (align == 0) return seterr(AB2_ERR_FORMAT, "gguf: zero alignment");
+    const uint64_t base = (r.o + align - 1) / align * align;
+    for (auto& t : ts) {
+        if (t.offset > len || base > len - t.offset || t.nbytes > len - base - t.offset)
+            return seterr(AB2_ERR_FORMAT, "gguf: tensor '%s' lies outside the file", t.name.c_str());
+        t.data = data + base + t.offset;
+        g->tensors[t.name] = t;
+    }
+    const GValue* ar = g->get("general.architecture");
+    g->arch = (ar && ar->type == G_STRING) ? ar->s : std::string();
+    return 0;
+}
+
+// ------------------------------------------------------------------------------------ config
+struct Cfg {
+    int64_t dim = 0, ffn = 0, n_layers = 0, vocab = 0, n_heads = 0, n_kv = 0, hd = 0;
+    int64_t dn_heads = 0, dn_state = 0, conv_k = 0, ctx_len = 0;
+    float rope_base = 1e4f, eps = 1e-6f;
+    std::vector<uint8_t> is_dn;
+    int64_t n_dn = 0, n_attn = 0;
+};
+
+// ModelConfig::from_gguf + Qwen35Config::from_gguf (crates/engine/src/model.rs:20-98) with
+// the same defaults. The reference's 4096 context cap (model.rs:50) is not applied: the
+// context capacity is the max_ctx given to ab2_create.
+int derive_config(const Gguf& g, Cfg* c) {
+    if (g.arch != "qwen35") return seterr(AB2_ERR_FORMAT, "architecture must be qwen35, got '%s'", g.arch.c_str());
+    uint64_t v;
+    if (!g.u32("embedding_length", &v)) return seterr(AB2_ERR_FORMAT, "missing embedding_length");
+    c->dim = (int64_t)v;
+    if (!g.u32("attention.head_count", &v)) return seterr(AB2_ERR_FORMAT, "missing head_count");
+    c->n_heads = (int64_t)v;
+    c->n_kv = g.u32("attention.head_count_kv", &v) ? (int64_t)v : c->n_heads;
+    if (!g.u32("block_count", &v)) return seterr(AB2_ERR_FORMAT, "missing block_count");
+    c->n_layers = (int64_t)v;
+    if (!g.u32("feed_forward_length", &v)) return seterr(AB2_ERR_FORMAT, "missing feed_forward_length");
+    c->ffn = (int64_t)v;
+    const GValue* tok = g.get("tokenizer.ggml.tokens");
+    c->vocab = (tok && tok->type == G_ARRAY) ? (int64_t)tok->count : 32000;
+    if (!g.f32("rope.freq_base", &c->rope_base)) c->rope_base = 10000.0f;
+    c->ctx_len = g.u32("context_length", &v) ? (int64_t)v : 0;
+    if (!g.f32("attention.layer_norm_rms_epsilon", &c->eps)) c->eps = 1e-6f;
+    if (c->n_heads <= 0 || c->dim <= 0 || c->n_layers <= 0) return seterr(AB2_ERR_SHAPE, "zero-sized model");
+    c->hd = g.u32("attention.key_length", &v) ? (int64_t)v : c->dim / c->n_heads;
+    c->dn_state = g.u32("ssm.state_size", &v) ? (int64_t)v : 128;
+    c->conv_k = g.u32("ssm.conv_kernel", &v) ? (int64_t)v : 4;
+    c->dn_heads = g.u32("ssm.group_count", &v) ? (int64_t)v : 16;
+    c->is_dn.resize(c->n_layers);
+    for (int64_t l = 0; l < c->n_layers; l++) {
+        c->is_dn[l] = g.tensor("blk." + std::to_string(l) + ".ssm_a") != nullptr;
+        (c->is_dn[l] ? c->n_dn : c->n_attn)++;
+    }
+    return 0;
+}
+
+void fill_config(const Cfg& c, ab2_config* o) {
+    memset(o, 0, sizeof *o);
+    o->dim = c.dim;
+    o->ffn = c.ffn;
+    o->n_layers = c.n_layers;
+    o->vocab = c.vocab;
+    o->n_heads = c.n_heads;
+    o->n_kv_heads = c.n_kv;
+    o->head_dim = c.hd;
+    o->dn_heads = c.dn_heads;
+    o->dn_state = c.dn_state;
+    o->conv_kernel = c.conv_k;
+    o->n_dn = c.n_dn;
+    o->n_attn = c.n_attn;
+    o->context_length = c.ctx_len;
+    o->rope_base = c.rope_base;
+    o->eps = c.eps;
+}
+
+// tensor lookups with shape checks (extract_tensor_raw / extract_tensor_f32, crates/gguf/src/to_ane.rs:12-44)
+int find_q8(const Gguf& g, const std::string& name, int64_t m, int64_t n, const GTensor** out) {
+    const GTensor* t = g.tensor(name);
+    if (!t) return seterr(AB2_ERR_FORMAT, "tensor not found: %s", name.c_str());
+    if (t->type != 8) return seterr(AB2_ERR_SHAPE, "%s: only Q8_0 projections are supported (type %u)", name.c_str(), t->type);
+    int64_t ne0 = t->dims.empty() ? 0 : (int64_t)t->dims[0], ne1 = t->dims.size() > 1 ? (int64_t)t->dims[1] : 1;
+    if (ne0 != n || ne1 != m)
+        return seterr(AB2_ERR_SHAPE, "%s: shape %lldx%lld, expected %lldx%lld", name.c_str(), (long long)ne1,
+                      (long long)ne0, (long long)m, (long long)n);
+    if (n % 32) return seterr(AB2_ERR_SHAPE, "%s: n must be divisible by 32", name.c_str());
+    *out = t;
+    return 0;
+}
+
+int read_f32(const Gguf& g, const std::string& name, int64_t n, std::vector<float>* out) {
+    const GTensor* t = g.tensor(name);
+    if (!t) return seterr(AB2_ERR_FORMAT, "tensor not found: %s", name.c_str());
+    int64_t ne = 1;
+    for (auto d : t->dims) ne *= (int64_t)d;
+    if (ne != n) return seterr(AB2_ERR_SHAPE, "%s: %lld elements, expected %lld", name.c_str(), (long long)ne, (long long)n);
+    out->resize(n);
+    if (t->type == 0) {
+        memcpy(out->data(), t->data, n * 4);
+    } else if (t->type == 1) {
+        for (int64_t i = 0; i < n; i++) {
+            uint16_t h;
+            memcpy(&h, t->data + 2 * i, 2);
+            uint32_t sign = (uint32_t)(h & 0x8000u) << 16, ex = (h >> 10) & 0x1f, man = h & 0x3ff, bits;
+            if (ex == 0) {
+                float f = (float)man * 5.9604644775390625e-08f;
+                memcpy(&bits, &f, 4);
+                bits |= sign;
+            } else if (ex == 31) {
+                bits = sign | 0x7f800000u | (man << 13);
+            } else {
+                bits = sign | ((ex + 112) << 23) | (man << 13);
+            }
+            memcpy(&(*out)[i], &bits, 4);
+        }
+    } else {
+        return seterr(AB2_ERR_SHAPE, "%s: expected an F32 or F16 tensor", name.c_str());
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------------------------------- context
+enum { PC_ATTN = 0, PC_DN = 1, PC_GEMM = 2, PC_OTHER = 3 };
+
+struct Layer {
+    bool dn = false;
+    Q8Weight w_in, w_out, gate_up, down;
+    float *attn_norm = nullptr, *post_norm = nullptr;
+    float *conv_w = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;  // DeltaNet
+    float *q_norm = nullptr, *k_norm = nullptr;                                          // GQA
+    int local = 0;  // index among layers of the same kind
+};
+
+struct Profile {
+    bool on = false;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev[4];
+    size_t used[4] = {0, 0, 0, 0};
+    double ms[4] = {0, 0, 0, 0};
+    int64_t n[4] = {0, 0, 0, 0};
+};
+
+}  // namespace
+
+struct ab2_ctx {
+    int device = 0;
+    int num_sms = 148;
+    Cfg c;
+    int max_batch = 0, cap = 0;
+    bool kv_bf16 = true;
+    int rot = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<void*> allocs;
+    std::vector<Layer> layers;
+    Q8Weight embed, lm_head;
+    float* final_norm = nullptr;
+    // state
+    float* dn_S = nullptr;      // [n_dn][max_batch][H][128][128]
+    float* dn_conv = nullptr;   // [n_dn][max_batch][3D][K]
+    void* kc = nullptr;         // [n_attn][max_batch][Hkv][cap][hd]
+    void* vc = nullptr;
+    int32_t* pos_d = nullptr;   // [max_batch]
+    std::vector<int64_t> pos_h;
+    int64_t s_stride = 0, conv_stride = 0, kv_slot = 0;
+    // scratch
+    float* x = nullptr;         // residual stream [max_batch][D]
+    float* proj = nullptr;      // [max_batch][ldp]
+    int ldp = 0;
+    uint8_t *xfa = nullptr, *xfb = nullptr;
+    float* logits = nullptr;    // [max_batch][vocab]
+    int32_t *tok_d = nullptr, *next_d = nullptr;
+    float* gws = nullptr;       // GEMM split-K partials
+    unsigned* gtk = nullptr;    // GEMM tickets
+    float* aws = nullptr;       // attention split partials
+    size_t aws_floats = 0;
+    unsigned* atk = nullptr;    // attention tickets
+    float2* rope = nullptr;     // [cap][rot/2]
+    float* tmp_out = nullptr;   // [D] for per-layer entry points
+    // pinned host staging
+    int32_t *tok_h = nullptr, *next_h = nullptr;
+    float* logits_h = nullptr;
+    Profile prof;
+
+    template <typename T>
+    int dalloc(T** p, size_t bytes, bool zero = true) {
+        void* q = nullptr;
+        CK(cudaMalloc(&q, bytes ? bytes : 16));
+        allocs.push_back(q);
+        if (zero) CK(cudaMemsetAsync(q, 0, bytes ? bytes : 16, stream));
+        *p = reinterpret_cast<T*>(q);
+        return 0;
+    }
+};
+
+namespace {
+
+int upload_f32(ab2_ctx* x, const std::vector<float>& v, float** out) {
+    RET(x->dalloc(out, v.size() * 4, false));
+    CK(cudaMemcpyAsync(*out, v.data(), v.size() * 4, cudaMemcpyHostToDevice, x->stream));
+    return 0;
+}
+
+struct RepackSrc {
+    const GTensor* t;
+    int64_t rows, base, grp, stride;
+};
+
+// upload Q8_0 tensors (same K) into one packed weight of M rows through a device staging buffer
+int upload_q8(ab2_ctx* x, int64_t M, int64_t K, const std::vector<RepackSrc>& srcs, uint8_t* staging,
+              Q8Weight* w) {
+    w->M = M;
+    w->M16 = (int)((M + 15) / 16);
+    w->KB = (int)(K / 32);
+    RET(x->dalloc(&w->qs, w->qs_bytes(), true));
+    RET(x->dalloc(&w->d, w->d_bytes(), true));
+    for (auto& s : srcs) {
+        CK(cudaMemcpyAsync(staging, s.t->data, s.t->nbytes, cudaMemcpyHostToDevice, x->stream));
+        launch_q8_repack(staging, s.rows, w->KB, *w, s.base, s.grp, s.stride, x->stream);
+        CK(cudaGetLastError());
+        // the staging buffer is reused by the next copy; keep the order on the stream
+    }
+    return 0;
+}
+
+constexpr int64_t kPlain = (int64_t)1 << 40;  // grp for plain concatenation
+
+int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
+    Gguf g;
+    RET(parse_gguf(data, len, &g));
+    RET(derive_config(g, &x->c));
+    Cfg& c = x->c;
+    const int64_t D = c.dim, F = c.ffn, H = c.dn_heads, hd = c.hd, Hq = c.n_heads, Hkv = c.n_kv;
+    // what the kernels of this build support
+    if (D % 128) return seterr(AB2_ERR_SHAPE, "embedding_length must be a multiple of 128");
+    if (F % 32 || F % 8) return seterr(AB2_ERR_SHAPE, "feed_forward_length must be a multiple of 32");
+    if (c.n_dn > 0) {
+        if (c.dn_state != 128 || H <= 0 || D % H || D / H != 128)
+            return seterr(AB2_ERR_SHAPE, "DeltaNet heads must have dk = dv = dim/heads = 128");
+        if (c.conv_k < 1 || c.conv_k > 8) return seterr(AB2_ERR_SHAPE, "ssm.conv_kernel must be in [1, 8]");
+    }
+    if (c.n_attn > 0) {
+        if (hd != 128 && hd != 256) return seterr(AB2_ERR_SHAPE, "attention head_dim must be 128 or 256");
+        if (Hkv <= 0 || Hq % Hkv || Hq / Hkv != 4) return seterr(AB2_ERR_SHAPE, "GQA group must be 4 query heads per KV head");
+        if ((Hq * hd) % 32) return seterr(AB2_ERR_SHAPE, "q dim must be a multiple of 32");
+    }
+    x->rot = x->rot > 0 ? x->rot : (int)hd;
+    if (c.n_attn > 0 && (x->rot % 2 || x->rot > hd)) return seterr(AB2_ERR_SHAPE, "rope_dims must be even and <= head_dim");
+
+    // staging buffer for the largest Q8 tensor
+    uint64_t maxb = 0;
+    for (auto& kv : g.tensors)
+        if (kv.second.type == 8) maxb = std::max(maxb, kv.second.nbytes);
+    uint8_t* staging = nullptr;
+    CK(cudaMalloc(&staging, maxb ? maxb : 16));
+
+    int rc = 0;
+    do {
+        const GTensor *te, *tl;
+        if ((rc = find_q8(g, "token_embd.weight", c.vocab, D, &te))) break;
+        if ((rc = upload_q8(x, c.vocab, D, {{te, c.vocab, 0, kPlain, 0}}, staging, &x->embed))) break;
+        if (g.tensor("output.weight")) {  // lm_head = output.weight or tied token_embd (main.rs:1903-1904)
+            if ((rc = find_q8(g, "output.weight", c.vocab, D, &tl))) break;
+            if ((rc = upload_q8(x, c.vocab, D, {{tl, c.vocab, 0, kPlain, 0}}, staging, &x->lm_head))) break;
+        } else {
+            x->lm_head = x->embed;
+        }
+        std::vector<float> fv;
+        if ((rc = read_f32(g, "output_norm.weight", D, &fv)) || (rc = upload_f32(x, fv, &x->final_norm))) break;
+        x->layers.resize(c.n_layers);
+        int ndn = 0, nat = 0;
+        for (int64_t l = 0; l < c.n_layers && !rc; l++) {
+            Layer& L = x->layers[l];
+            const std::string p = "blk." + std::to_string(l) + ".";
+            L.dn = c.is_dn[l];
+            L.local = L.dn ? ndn++ : nat++;
+            if ((rc = read_f32(g, p + "attn_norm.weight", D, &fv)) || (rc = upload_f32(x, fv, &L.attn_norm))) break;
+            if ((rc = read_f32(g, p + "post_attention_norm.weight", D, &fv)) || (rc = upload_f32(x, fv, &L.post_norm)))
+                break;
+            const GTensor *t0, *t1, *t2, *t3;
+            if (L.dn) {
+                // input projections concatenated: qkv (3D) | gate (D) | beta (H) | alpha (H)
+                if ((rc = find_q8(g, p + "attn_qkv.weight", 3 * D, D, &t0)) ||
+                    (rc = find_q8(g, p + "attn_gate.weight", D, D, &t1)) ||
+                    (rc = find_q8(g, p + "ssm_beta.weight", H, D, &t2)) ||
+                    (rc = find_q8(g, p + "ssm_alpha.weight", H, D, &t3)))
+                    break;
+                if ((rc = upload_q8(x, 4 * D + 2 * H, D,
+                                    {{t0, 3 * D, 0, kPlain, 0}, {t1, D, 3 * D, kPlain, 0}, {t2, H, 4 * D, kPlain, 0},
+                                     {t3, H, 4 * D + H, kPlain, 0}},
+                                    staging, &L.w_in)))
+                    break;
+                if ((rc = find_q8(g, p + "ssm_out.weight", D, D, &t0)) ||
+                    (rc = upload_q8(x, D, D, {{t0, D, 0, kPlain, 0}}, staging, &L.w_out)))
+                    break;
+                if ((rc = read_f32(g, p + "ssm_conv1d.weight", 3 * D * c.conv_k, &fv)) || (rc = upload_f32(x, fv, &L.conv_w)))
+                    break;
+                if ((rc = read_f32(g, p + "ssm_a", H, &fv)) || (rc = upload_f32(x, fv, &L.ssm_a))) break;
+                if ((rc = read_f32(g, p + "ssm_dt.bias", H, &fv)) || (rc = upload_f32(x, fv, &L.dt_bias))) break;
+                if ((rc = read_f32(g, p + "ssm_norm.weight", 128, &fv)) || (rc = upload_f32(x, fv, &L.ssm_norm))) break;
+            } else {
+                // q (per head [q | gate]) | k | v
+                if ((rc = find_q8(g, p + "attn_q.weight", 2 * Hq * hd, D, &t0)) ||
+                    (rc = find_q8(g, p + "attn_k.weight", Hkv * hd, D, &t1)) ||
+                    (rc = find_q8(g, p + "attn_v.weight", Hkv * hd, D, &t2)))
+                    break;
+                if ((rc = upload_q8(x, 2 * Hq * hd + 2 * Hkv * hd, D,
+                                    {{t0, 2 * Hq * hd, 0, kPlain, 0}, {t1, Hkv * hd, 2 * Hq * hd, kPlain, 0},
+                                     {t2, Hkv * hd, 2 * Hq * hd + Hkv * hd, kPlain, 0}},
+                                    staging, &L.w_in)))
+                    break;
+                if ((rc = find_q8(g, p + "attn_output.weight", D, Hq * hd, &t0)) ||
+                    (rc = upload_q8(x, D, Hq * hd, {{t0, D, 0, kPlain, 0}}, staging, &L.w_out)))
+                    break;
+                if ((rc = read_f32(g, p + "attn_q_norm.weight", hd, &fv)) || (rc = upload_f32(x, fv, &L.q_norm))) break;
+                if ((rc = read_f32(g, p + "attn_k_norm.weight", hd, &fv)) || (rc = upload_f32(x, fv, &L.k_norm))) break;
+            }
+            // FFN gate/up interleaved per 8 rows so one m16 tile holds gate and up of 8 outputs
+            if ((rc = find_q8(g, p + "ffn_gate.weight", F, D, &t0)) || (rc = find_q8(g, p + "ffn_up.weight", F, D, &t1)) ||
+                (rc = find_q8(g, p + "ffn_down.weight", D, F, &t2)))
+                break;
+            if ((rc = upload_q8(x, 2 * F, D, {{t0, F, 0, 8, 16}, {t1, F, 8, 8, 16}}, staging, &L.gate_up))) break;
+            if ((rc = upload_q8(x, D, F, {{t2, D, 0, kPlain, 0}}, staging, &L.down))) break;
+        }
+    } while (0);
+    cudaError_t se = cudaStreamSynchronize(x->stream);
+    cudaFree(staging);
+    if (rc) return rc;
+    if (se != cudaSuccess) return seterr(AB2_ERR_CUDA, "weight upload: %s", cudaGetErrorString(se));
+
+    // ---- per-slot state
+    const int B = x->max_batch;
+    x->s_stride = H * 128 * 128;
+    x->conv_stride = 3 * D * c.conv_k;
+    x->kv_slot = Hkv * (int64_t)x->cap * hd;
+    const size_t kvel = x->kv_bf16 ? 2 : 4;
+    RET(x->dalloc(&x->dn_S, (size_t)std::max<int64_t>(c.n_dn, 1) * B * x->s_stride * 4));
+    RET(x->dalloc(&x->dn_conv, (size_t)std::max<int64_t>(c.n_dn, 1) * B * x->conv_stride * 4));
+    RET(x->dalloc(&x->kc, (size_t)std::max<int64_t>(c.n_attn, 1) * B * x->kv_slot * kvel));
+    RET(x->dalloc(&x->vc, (size_t)std::max<int64_t>(c.n_attn, 1) * B * x->kv_slot * kvel));
+    RET(x->dalloc(&x->pos_d, (size_t)B * 4));
+    x->pos_h.assign(B, 0);
+
+    // ---- scratch
+    int64_t mproj = 0, maxk = D;
+    for (auto& L : x->layers) mproj = std::max<int64_t>(mproj, L.w_in.M);
+    maxk = std::max<int64_t>(maxk, F);
+    maxk = std::max<int64_t>(maxk, Hq * hd);
+    x->ldp = (int)((mproj + 3) / 4 * 4);
+    RET(x->dalloc(&x->x, (size_t)B * D * 4));
+    RET(x->dalloc(&x->proj, (size_t)B * x->ldp * 4));
+    RET(x->dalloc(&x->xfa, xfrag_bytes((int)maxk, B)));
+    RET(x->dalloc(&x->xfb, xfrag_bytes((int)maxk, B)));
+    RET(x->dalloc(&x->logits, (size_t)B * c.vocab * 4));
+    RET(x->dalloc(&x->tok_d, (size_t)B * 4));
+    RET(x->dalloc(&x->next_d, (size_t)B * 4));
+    RET(x->dalloc(&x->tmp_out, (size_t)std::max<int64_t>(D, F) * 4));
+    size_t gws = 0;
+    int gtk = 1;
+    auto acc_gemm = [&](const Q8Weight& w) {
+        gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, B, x->num_sms));
+        gtk = std::max(gtk, gemm_grid_x(w.M16));
+    };
+    for (auto& L : x->layers) {
+        acc_gemm(L.w_in);
+        acc_gemm(L.w_out);
+        acc_gemm(L.gate_up);
+        acc_gemm(L.down);
+    }
+    acc_gemm(x->lm_head);
+    RET(x->dalloc(&x->gws, gws * 4));
+    RET(x->dalloc(&x->gtk, (size_t)gtk * 4));
+    if (c.n_attn > 0) {
+        size_t aws = 0;
+        for (int b = 1; b <= B; b++)
+            aws = std::max(aws, attn_ws_floats(b, (int)Hkv, attn_nsplit_bound(b, (int)Hkv, x->cap, x->num_sms),
+                                               (int)hd, (int)(Hq / Hkv)));
+        x->aws_floats = aws;
+        RET(x->dalloc(&x->aws, aws * 4));
+        RET(x->dalloc(&x->atk, (size_t)B * Hkv * 4));
+        // RoPE (cos, sin) table built with the host libm exactly as the reference computes it:
+        // freq = 1 / base^(i / rot) for even i, angle = pos * freq (deltanet.rs:600-623)
+        const int hr = x->rot / 2;
+        std::vector<float2> tab((size_t)x->cap * hr);
+        for (int j = 0; j < hr; j++) {
+            const float freq = 1.0f / powf(c.rope_base, (float)(2 * j) / (float)x->rot);
+            for (int64_t p = 0; p < x->cap; p++) {
+                const float val = (float)p * freq;
+                tab[(size_t)p * hr + j] = make_float2(cosf(val), sinf(val));
+            }
+        }
+        RET(x->dalloc(&x->rope, tab.size() * sizeof(float2), false));
+        CK(cudaMemcpyAsync(x->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice, x->stream));
+    }
+    CK(cudaMallocHost(&x->tok_h, (size_t)B * 4));
+    CK(cudaMallocHost(&x->next_h, (size_t)B * 4));
+    CK(cudaStreamSynchronize(x->stream));
+    return 0;
+}
+
+// --------------------------------------------------------------------------------- profiling
+struct ProfScope {
+    ab2_ctx* x;
+    int cls;
+    cudaStream_t st;
+    cudaEvent_t stop = nullptr;
+    ProfScope(ab2_ctx* x_, int cls_, cudaStream_t st_) : x(x_), cls(cls_), st(st_) {
+        if (!x->prof.on) return;
+        auto& v = x->prof.ev[cls];
+        size_t i = x->prof.used[cls]++;
+        if (i >= v.size()) {
+            cudaEvent_t a, b;
+            cudaEventCreate(&a);
+            cudaEventCreate(&b);
+            v.push_back({a, b});
+        }
+        cudaEventRecord(v[i].first, st);
+        stop = v[i].second;
+    }
+    ~ProfScope() {
+        if (stop) cudaEventRecord(stop, st);
+    }
+};
+
+void prof_collect(ab2_ctx* x) {
+    if (!x->prof.on) return;
+    for (int c = 0; c < 4; c++) {
+        for (size_t i = 0; i < x->prof.used[c]; i++) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, x->prof.ev[c][i].first, x->prof.ev[c][i].second);
+            x->prof.ms[c] += ms;
+            x->prof.n[c]++;
+        }
+        x->prof.used[c] = 0;
+    }
+}
+
+// --------------------------------------------------------------------------------- the step
+void gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st) {
+    ProfScope ps(x, PC_GEMM, st);
+    launch_q8_gemm(w, xf, B, x->gws, x->gtk, ep, x->num_sms, st);
+}
+
+GemmEpi epi_store(float* y, int ldy, int64_t m) {
+    GemmEpi e;
+    e.mode = EPI_STORE;
+    e.y = y;
+    e.ldy = ldy;
+    e.m_out = (int)m;
+    return e;
+}
+GemmEpi epi_resid(float* y, int ldy, int64_t m) {
+    GemmEpi e = epi_store(y, ldy, m);
+    e.mode = EPI_RESID;
+    return e;
+}
+GemmEpi epi_swiglu(uint8_t* xf, int F, int B) {
+    GemmEpi e;
+    e.mode = EPI_SWIGLU;
+    e.m_out = F;
+    e.xf_out = xf;
+    e.xs_out = xfrag_shape(F, B);
+    return e;
+}
+
+// mixer of layer L on the activation fragments in xfa (batch B starting at slot s0);
+// the mixer output goes to `out` with epilogue `mode` (RESID into x, or STORE)
+int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out, int ldo, int mode,
+              cudaStream_t st) {
+    const Cfg& c = x->c;
+    const int D = (int)c.dim;
+    gemm(x, L.w_in, x->xfa, B, epi_store(x->proj, x->ldp, L.w_in.M), st);
+    if (L.dn) {
+        DnParams p;
+        p.proj = x->proj;
+        p.ldp = x->ldp;
+        p.conv = x->dn_conv + ((size_t)L.local * x->max_batch + s0) * x->conv_stride;
+        p.conv_stride = x->conv_stride;
+        p.conv_w = L.conv_w;
+        p.K = (int)c.conv_k;
+        p.S = x->dn_S + ((size_t)L.local * x->max_batch + s0) * x->s_stride;
+        p.s_stride = x->s_stride;
+        p.ssm_a = L.ssm_a;
+        p.dt_bias = L.dt_bias;
+        p.ssm_norm = L.ssm_norm;
+        p.eps = c.eps;
+        p.D = D;
+        p.H = (int)c.dn_heads;
+        p.xf_out = x->xfb;
+        p.xs = xfrag_shape(D, B);
+        p.o_out = nullptr;
+        ProfScope ps(x, PC_DN, st);
+        launch_deltanet(p, B, st);
+    } else {
+        const size_t kvel = x->kv_bf16 ? 2 : 4;
+        AttnParams p;
+        p.proj = x->proj;
+        p.ldp = x->ldp;
+        p.q_norm = L.q_norm;
+        p.k_norm = L.k_norm;
+        p.rope = x->rope;
+        p.rot = x->rot;
+        p.kc = (uint8_t*)x->kc + ((size_t)L.local * x->max_batch + s0) * x->kv_slot * kvel;
+        p.vc = (uint8_t*)x->vc + ((size_t)L.local * x->max_batch + s0) * x->kv_slot * kvel;
+        p.kv_slot_stride = x->kv_slot;
+        p.cap = x->cap;
+        p.pos = x->pos_d + s0;
+        p.Hq = (int)c.n_heads;
+        p.Hkv = (int)c.n_kv;
+        p.chunk = attn_chunk(B, p.Hkv, max_len, x->num_sms);
+        if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv) > x->aws_floats)
+            return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
+        p.ws = x->aws;
+        p.tickets = x->atk;
+        p.xf_out = x->xfb;
+        p.xs = xfrag_shape((int)(c.n_heads * c.hd), B);
+        p.o_out = nullptr;
+        ProfScope ps(x, PC_ATTN, st);
+        if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st))
+            return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
+    }
+    GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
+    gemm(x, L.w_out, x->xfb, B, e, st);
+    return 0;
+}
+
+int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st) {
+    const int D = (int)x->c.dim, F = (int)x->c.ffn;
+    gemm(x, L.gate_up, x->xfa, B, epi_swiglu(x->xfb, F, B), st);
+    GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
+    gemm(x, L.down, x->xfb, B, e, st);
+    return 0;
+}
+
+int check_capacity(ab2_ctx* x, int B, int* max_len) {
+    if (B < 1 || B > x->max_batch) return seterr(AB2_ERR_CAPACITY, "batch %d outside [1, %d]", B, x->max_batch);
+    int64_t m = 0;
+    for (int b = 0; b < B; b++) {
+        if (x->pos_h[b] >= x->cap)
+            return seterr(AB2_ERR_CAPACITY, "slot %d is full (pos %lld, max_ctx %d)", b, (long long)x->pos_h[b], x->cap);
+        m = std::max<int64_t>(m, x->pos_h[b] + 1);
+    }
+    *max_len = (int)m;
+    return 0;
+}
+
+int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
+                 cudaStream_t st) {
+    const Cfg& c = x->c;
+    const int D = (int)c.dim;
+    {
+        ProfScope ps(x, PC_OTHER, st);
+        launch_embed(x->embed, (int)c.vocab, tok_d, B, x->x, D, st);
+    }
+    for (auto& L : x->layers) {
+        {
+            ProfScope ps(x, PC_OTHER, st);
+            launch_rmsnorm_xfrag(x->x, D, L.attn_norm, D, c.eps, B, x->xfa, st);
+        }
+        RET(run_mixer(x, L, 0, B, max_len, x->x, D, EPI_RESID, st));
+        {
+            ProfScope ps(x, PC_OTHER, st);
+            launch_rmsnorm_xfrag(x->x, D, L.post_norm, D, c.eps, B, x->xfa, st);
+        }
+        RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st));
+    }
+    {
+        ProfScope ps(x, PC_OTHER, st);
+        launch_rmsnorm_xfrag(x->x, D, x->final_norm, D, c.eps, B, x->xfa, st);
+    }
+    gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st);
+    {
+        ProfScope ps(x, PC_OTHER, st);
+        if (next_d) launch_argmax(logits_d, (int)c.vocab, (int)c.vocab, B, next_d, st);
+        launch_pos_advance(x->pos_d, B, st);
+    }
+    CK(cudaGetLastError());
+    for (int b = 0; b < B; b++) x->pos_h[b] += 1;
+    return 0;
+}
+
+int64_t launches_per_step(const ab2_ctx* x, int B) {
+    (void)B;
+    return 1 + (int64_t)x->layers.size() * 7 + 1 + 1 + 2;
+}
+
+// ------------------------------------------------------------------------- op-level cache
+struct OpCache {
+    std::mutex mu;
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    unsigned* tk = nullptr;
+    size_t tk_n = 0;
+    uint8_t* xf = nullptr;
+    size_t xf_bytes = 0;
+    float2* rope = nullptr;
+    int64_t rope_rows = 0;
+    int rope_rot = 0;
+    float rope_base = 0;
+};
+OpCache g_ops[64];
+
+int ensure(void** p, size_t* have, size_t need) {
+    if (*have >= need) return 0;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *have = 0;
+    CK(cudaMalloc(p, need));
+    CK(cudaMemset(*p, 0, need));
+    *have = need;
+    return 0;
+}
+
+}  // namespace
+
+struct ab2_q8 {
+    int device = 0;
+    int num_sms = 148;
+    Q8Weight w;
+    int64_t n = 0;
+};
+
+// ================================================================================== C ABI
+AB2_API const char* ab2_last_error(void) { return g_err.c_str(); }
+
+AB2_API int ab2_gguf_inspect(const uint8_t* gguf, uint64_t len, ab2_config* out) {
+    if (!out) return seterr(AB2_ERR_ARG, "null config pointer");
+    Gguf g;
+    RET(parse_gguf(gguf, len, &g));
+    Cfg c;
+    RET(derive_config(g, &c));
+    fill_config(c, out);
+    return 0;
+}
+
+AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
+                       const ab2_options* opt, ab2_ctx** out) {
+    if (!out) return seterr(AB2_ERR_ARG, "null output pointer");
+    *out = nullptr;
+    if (max_batch < 1 || max_batch > 64) return seterr(AB2_ERR_ARG, "max_batch must be in [1, 64]");
+    if (max_ctx < 1) return seterr(AB2_ERR_ARG, "max_ctx must be positive");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return seterr(AB2_ERR_DEVICE, "no CUDA device available");
+    }
+    if (device < 0 || device >= ndev) return seterr(AB2_ERR_ARG, "device %d out of range", device);
+    CK(cudaSetDevice(device));
+    auto* x = new ab2_ctx();
+    x->device = device;
+    x->max_batch = max_batch;
+    x->cap = max_ctx;
+    x->kv_bf16 = opt ? opt->kv_bf16 != 0 : true;
+    x->rot = opt ? opt->rope_dims : 0;
+    cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device);
+    int rc = 0;
+    if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)
+        rc = seterr(AB2_ERR_CUDA, "cudaStreamCreate failed");
+    if (!rc) rc = build_context(x, gguf, len);
+    if (rc) {
+        std::string keep = g_err;
+        ab2_destroy(x);
+        g_err = keep;
+        return rc;
+    }
+    *out = x;
+    return 0;
+}
+
+AB2_API void ab2_destroy(ab2_ctx* x) {
+    if (!x) return;
+    cudaSetDevice(x->device);
+    if (x->stream) cudaStreamSynchronize(x->stream);
+    for (void* p : x->allocs) cudaFree(p);
+    if (x->tok_h) cudaFreeHost(x->tok_h);
+    if (x->next_h) cudaFreeHost(x->next_h);
+    if (x->logits_h) cudaFreeHost(x->logits_h);
+    for (auto& v : x->prof.ev)
+        for (auto& e : v) {
+            cudaEventDestroy(e.first);
+            cudaEventDestroy(e.second);
+        }
+    if (x->stream) cudaStreamDestroy(x->stream);
+    delete x;
+}
+
+AB2_API int ab2_get_config(ab2_ctx* x, ab2_config* out) {
+    if (!x || !out) return seterr(AB2_ERR_ARG, "null argument");
+    fill_config(x->c, out);
+    out->max_batch = x->max_batch;
+    out->max_ctx = x->cap;
+    out->kv_bf16 = x->kv_bf16 ? 1 : 0;
+    out->rope_dims = x->rot;
+    return 0;
+}
+
+AB2_API int ab2_layer_is_deltanet(ab2_ctx* x, int layer) {
+    if (!x || layer < 0 || layer >= (int)x->layers.size()) return seterr(AB2_ERR_ARG, "bad layer");
+    return x->layers[layer].dn ? 1 : 0;
+}
+
+static int check_slot(ab2_ctx* x, int slot) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    if (slot < 0 || slot >= x->max_batch) return seterr(AB2_ERR_ARG, "slot %d out of range", slot);
+    CK(cudaSetDevice(x->device));
+    return 0;
+}
+
+AB2_API int ab2_reset_slot(ab2_ctx* x, int slot) {
+    RET(check_slot(x, slot));
+    const Cfg& c = x->c;
+    const size_t kvel = x->kv_bf16 ? 2 : 4;
+    for (int64_t i = 0; i < c.n_dn; i++) {
+        CK(cudaMemsetAsync(x->dn_S + ((size_t)i * x->max_batch + slot) * x->s_stride, 0, x->s_stride * 4, x->stream));
+        CK(cudaMemsetAsync(x->dn_conv + ((size_t)i * x->max_batch + slot) * x->conv_stride, 0, x->conv_stride * 4,
+                           x->stream));
+    }
+    for (int64_t i = 0; i < c.n_attn; i++) {
+        size_t off = ((size_t)i * x->max_batch + slot) * x->kv_slot * kvel;
+        CK(cudaMemsetAsync((uint8_t*)x->kc + off, 0, x->kv_slot * kvel, x->stream));
+        CK(cudaMemsetAsync((uint8_t*)x->vc + off, 0, x->kv_slot * kvel, x->stream));
+    }
+    CK(cudaStreamSynchronize(x->stream));
+    return ab2_set_pos(x, slot, 0);
+}
+
+AB2_API int ab2_set_pos(ab2_ctx* x, int slot, int64_t pos) {
+    RET(check_slot(x, slot));
+    if (pos < 0 || pos > x->cap) return seterr(AB2_ERR_ARG, "pos %lld outside [0, %d]", (long long)pos, x->cap);
+    int32_t p = (int32_t)pos;
+    CK(cudaMemcpyAsync(x->pos_d + slot, &p, 4, cudaMemcpyHostToDevice, x->stream));
+    CK(cudaStreamSynchronize(x->stream));
+    x->pos_h[slot] = pos;
+    return 0;
+}
+
+AB2_API int ab2_get_pos(ab2_ctx* x, int slot, int64_t* pos) {
+    RET(check_slot(x, slot));
+    if (!pos) return seterr(AB2_ERR_ARG, "null pos");
+    *pos = x->pos_h[slot];
+    return 0;
+}
+
+static int dn_layer(ab2_ctx* x, int layer, const Layer** L) {
+    if (layer < 0 || layer >= (int)x->layers.size()) return seterr(AB2_ERR_ARG, "bad layer %d", layer);
+    *L = &x->layers[layer];
+    return 0;
+}
+
+static int dn_state_io(ab2_ctx* x, int layer, int slot, float* rec, float* conv, bool set) {
+    RET(check_slot(x, slot));
+    const Layer* L;
+    RET(dn_layer(x, layer, &L));
+    if (!L->dn) return seterr(AB2_ERR_ARG, "layer %d is not a DeltaNet layer", layer);
+    float* S = x->dn_S + ((size_t)L->local * x->max_batch + slot) * x->s_stride;
+    float* C = x->dn_conv + ((size_t)L->local * x->max_batch + slot) * x->conv_stride;
+    auto kind = set ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+    if (rec) CK(cudaMemcpyAsync(set ? (void*)S : rec, set ? (const void*)rec : S, x->s_stride * 4, kind, x->stream));
+    if (conv) CK(cudaMemcpyAsync(set ? (void*)C : conv, set ? (const void*)conv : C, x->conv_stride * 4, kind, x->stream));
+    CK(cudaStreamSynchronize(x->stream));
+    return 0;
+}
+
+AB2_API int ab2_set_dn_state(ab2_ctx* x, int layer, int slot, const float* rec, const float* conv) {
+    return dn_state_io(x, layer, slot, const_cast<float*>(rec), const_cast<float*>(conv), true);
+}
+AB2_API int ab2_get_dn_state(ab2_ctx* x, int layer, int slot, float* rec, float* conv) {
+    return dn_state_io(x, layer, slot, rec, conv, false);
+}
+
+static inline uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return (uint16_t)((u >> 16) | 0x40);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static int kv_io(ab2_ctx* x, int layer, int slot, float* k, float* v, int64_t n, bool set) {
+    RET(check_slot(x, slot));
+    const Layer* L;
+    RET(dn_layer(x, layer, &L));
+    if (L->dn) return seterr(AB2_ERR_ARG, "layer %d is not an attention layer", layer);
+    if (n < 0 || n > x->cap) return seterr(AB2_ERR_ARG, "n_tokens %lld outside [0, %d]", (long long)n, x->cap);
+    if (!k || !v) return seterr(AB2_ERR_ARG, "null k/v");
+    const int64_t Hkv = x->c.n_kv, hd = x->c.hd;
+    const size_t kvel = x->kv_bf16 ? 2 : 4;
+    const size_t rowb = (size_t)n * hd * kvel;
+    std::vector<uint8_t> tmp(rowb);
+    for (int which = 0; which < 2; which++) {
+        float* host = which ? v : k;
+        uint8_t* dev = (uint8_t*)(which ? x->vc : x->kc) + ((size_t)L->local * x->max_batch + slot) * x->kv_slot * kvel;
+        for (int64_t h = 0; h < Hkv; h++) {
+            uint8_t* d = dev + (size_t)h * x->cap * hd * kvel;
+            float* hp = host + (size_t)h * n * hd;
+            if (set) {
+                if (x->kv_bf16) {
+                    uint16_t* t = (uint16_t*)tmp.data();
+                    for (int64_t i = 0; i < n * hd; i++) t[i] = f32_to_bf16_rne(hp[i]);
+                } else {
+                    memcpy(tmp.data(), hp, rowb);
+                }
+                CK(cudaMemcpy(d, tmp.data(), rowb, cudaMemcpyHostToDevice));
+            } else {
+                CK(cudaMemcpy(tmp.data(), d, rowb, cudaMemcpyDeviceToHost));
+                if (x->kv_bf16) {
+                    const uint16_t* t = (const uint16_t*)tmp.data();
+                    for (int64_t i = 0; i < n * hd; i++) {
+                        uint32_t u = (uint32_t)t[i] << 16;
+                        memcpy(&hp[i], &u, 4);
+                    }
+                } else {
+                    memcpy(hp, tmp.data(), rowb);
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+AB2_API int ab2_set_kv(ab2_ctx* x, int layer, int slot, const float* k, const float* v, int64_t n) {
+    return kv_io(x, layer, slot, const_cast<float*>(k), const_cast<float*>(v), n, true);
+}
+AB2_API int ab2_get_kv(ab2_ctx* x, int layer, int slot, float* k, float* v, int64_t n) {
+    return kv_io(x, layer, slot, k, v, n, false);
+}
+
+AB2_API int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tokens, float dn_std, float conv_std,
+                           float kv_std) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    if (n_slots < 1 || n_slots > x->max_batch) return seterr(AB2_ERR_ARG, "n_slots outside [1, max_batch]");
+    if (n_tokens < 0 || n_tokens >= x->cap) return seterr(AB2_ERR_ARG, "n_tokens outside [0, max_ctx)");
+    CK(cudaSetDevice(x->device));
+    const Cfg& c = x->c;
+    for (int64_t i = 0; i < c.n_dn; i++) {
+        launch_seed_f32(x->dn_S + (size_t)i * x->max_batch * x->s_stride, (int64_t)n_slots * x->s_stride, seed,
+                        (uint64_t)(3 * i), dn_std, x->stream);
+        launch_seed_f32(x->dn_conv + (size_t)i * x->max_batch * x->conv_stride, (int64_t)n_slots * x->conv_stride,
+                        seed, (uint64_t)(3 * i + 1), conv_std, x->stream);
+    }
+    const size_t kvel = x->kv_bf16 ? 2 : 4;
+    const int64_t rows = (int64_t)n_slots * c.n_kv * x->cap;
+    for (int64_t i = 0; i < c.n_attn; i++) {
+        size_t off = (size_t)i * x->max_batch * x->kv_slot * kvel;
+        launch_seed_kv((uint8_t*)x->kc + off, x->kv_bf16, rows, x->cap, n_tokens, (int)c.hd, seed,
+                       (uint64_t)(1000 + 2 * i), kv_std, x->stream);
+        launch_seed_kv((uint8_t*)x->vc + off, x->kv_bf16, rows, x->cap, n_tokens, (int)c.hd, seed,
+                       (uint64_t)(1001 + 2 * i), kv_std, x->stream);
+    }
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(x->stream));
+    for (int s = 0; s < n_slots; s++) RET(ab2_set_pos(x, s, n_tokens));
+    return 0;
+}
+
+AB2_API int ab2_decode_step_device(ab2_ctx* x, const int32_t* tok_d, int B, float* logits_d, int32_t* next_d,
+                                   void* stream) {
+    if (!x || !tok_d) return seterr(AB2_ERR_ARG, "null argument");
+    CK(cudaSetDevice(x->device));
+    int max_len;
+    RET(check_capacity(x, B, &max_len));
+    cudaStream_t st = stream ? (cudaStream_t)stream : x->stream;
+    return enqueue_step(x, tok_d, B, max_len, logits_d ? logits_d : x->logits, next_d, st);
+}
+
+AB2_API int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int B, float* logits, int32_t* next_tokens) {
+    if (!x || !tokens) return seterr(AB2_ERR_ARG, "null argument");
+    CK(cudaSetDevice(x->device));
+    int max_len;
+    RET(check_capacity(x, B, &max_len));
+    memcpy(x->tok_h, tokens, (size_t)B * 4);
+    CK(cudaMemcpyAsync(x->tok_d, x->tok_h, (size_t)B * 4, cudaMemcpyHostToDevice, x->stream));
+    RET(enqueue_step(x, x->tok_d, B, max_len, x->logits, x->next_d, x->stream));
+    if (next_tokens) CK(cudaMemcpyAsync(x->next_h, x->next_d, (size_t)B * 4, cudaMemcpyDeviceToHost, x->stream));
+    if (logits) CK(cudaMemcpyAsync(logits, x->logits, (size_t)B * x->c.vocab * 4, cudaMemcpyDeviceToHost, x->stream));
+    CK(cudaStreamSynchronize(x->stream));
+    prof_collect(x);
+    if (next_tokens) memcpy(next_tokens, x->next_h, (size_t)B * 4);
+    return 0;
+}
+
+AB2_API int ab2_launches_per_step(ab2_ctx* x, int B, int64_t* out) {
+    if (!x || !out) return seterr(AB2_ERR_ARG, "null argument");
+    *out = launches_per_step(x, B);
+    return 0;
+}
+
+AB2_API int ab2_profile(ab2_ctx* x, int enable) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    CK(cudaSetDevice(x->device));
+    CK(cudaStreamSynchronize(x->stream));
+    prof_collect(x);
+    x->prof.on = enable != 0;
+    return 0;
+}
+
+AB2_API int ab2_profile_read(ab2_ctx* x, double ms[4], int64_t n[4]) {
+    if (!x || !ms || !n) return seterr(AB2_ERR_ARG, "null argument");
+    CK(cudaSetDevice(x->device));
+    CK(cudaDeviceSynchronize());
+    prof_collect(x);
+    for (int c = 0; c < 4; c++) {
+        ms[c] = x->prof.ms[c];
+        n[c] = x->prof.n[c];
+        x->prof.ms[c] = 0;
+        x->prof.n[c] = 0;
+    }
+    return 0;
+}
+
+AB2_API int ab2_mixer_layer(ab2_ctx* x, int layer, int slot, const float* xin, float* out) {
+    RET(check_slot(x, slot));
+    if (!xin || !out) return seterr(AB2_ERR_ARG, "null argument");
+    const Layer* L;
+    RET(dn_layer(x, layer, &L));
+    if (x->pos_h[slot] >= x->cap) return seterr(AB2_ERR_CAPACITY, "slot %d is full", slot);
+    const int D = (int)x->c.dim;
+    CK(cudaMemcpyAsync(x->x, xin, (size_t)D * 4, cudaMemcpyHostToDevice, x->stream));
+    launch_to_xfrag(x->x, D, D, 1, x->xfa, x->stream);
+    RET(run_mixer(x, *L, slot, 1, (int)x->pos_h[slot] + 1, x->tmp_out, D, EPI_STORE, x->stream));
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(out, x->tmp_out, (size_t)D * 4, cudaMemcpyDeviceToHost, x->stream));
+    CK(cudaStreamSynchronize(x->stream));
+    prof_collect(x);
+    return 0;
+}
+
+AB2_API int ab2_ffn_layer(ab2_ctx* x, int layer, const float* xin, float* out) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    CK(cudaSetDevice(x->device));
+    if (!xin || !out) return seterr(AB2_ERR_ARG, "null argument");
+    const Layer* L;
+    RET(dn_layer(x, layer, &L));
+    const int D = (int)x->c.dim;
+    CK(cudaMemcpyAsync(x->x, xin, (size_t)D * 4, cudaMemcpyHostToDevice, x->stream));
+    launch_to_xfrag(x->x, D, D, 1, x->xfa, x->stream);
+    RET(run_ffn(x, *L, 1, x->tmp_out, D, EPI_STORE, x->stream));
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(out, x->tmp_out, (size_t)D * 4, cudaMemcpyDeviceToHost, x->stream));
+    CK(cudaStreamSynchronize(x->stream));
+    prof_collect(x);
+    return 0;
+}
+
+// ------------------------------------------------------------------------------- op level
+AB2_API int ab2_q8_create(const uint8_t* blocks, int64_t m, int64_t n, int device, ab2_q8** out) {
+    if (!blocks || !out) return seterr(AB2_ERR_ARG, "null argument");
+    *out = nullptr;
+    if (m < 1 || n < 32 || n % 32) return seterr(AB2_ERR_SHAPE, "n must be a positive multiple of 32");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return seterr(AB2_ERR_DEVICE, "no CUDA device available");
+    }
+    CK(cudaSetDevice(device));
+    auto* w = new ab2_q8();
+    w->device = device;
+    w->n = n;
+    cudaDeviceGetAttribute(&w->num_sms, cudaDevAttrMultiProcessorCount, device);
+    w->w.M = m;
+    w->w.M16 = (int)((m + 15) / 16);
+    w->w.KB = (int)(n / 32);
+    const size_t raw = (size_t)m * (n / 32) * 34;
+    uint8_t* staging = nullptr;
+    cudaError_t e = cudaMalloc(&w->w.qs, w->w.qs_bytes());
+    if (e == cudaSuccess) e = cudaMalloc(&w->w.d, w->w.d_bytes());
+    if (e == cudaSuccess) e = cudaMalloc(&staging, raw);
+    if (e == cudaSuccess) e = cudaMemset(w->w.qs, 0, w->w.qs_bytes());
+    if (e == cudaSuccess) e = cudaMemset(w->w.d, 0, w->w.d_bytes());
+    if (e == cudaSuccess) e = cudaMemcpy(staging, blocks, raw, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        launch_q8_repack(staging, m, w->w.KB, w->w, 0, kPlain, 0, 0);
+        e = cudaDeviceSynchronize();
+    }
+    if (staging) cudaFree(staging);
+    if (e != cudaSuccess) {
+        ab2_q8_destroy(w);
+        return seterr(e == cudaErrorMemoryAllocation ? AB2_ERR_OOM : AB2_ERR_CUDA, "ab2_q8_create: %s",
+                      cudaGetErrorString(e));
+    }
+    *out = w;
+    return 0;
+}
+
+AB2_API void ab2_q8_destroy(ab2_q8* w) {
+    if (!w) return;
+    cudaSetDevice(w->device);
+    if (w->w.qs) cudaFree(w->w.qs);
+    if (w->w.d) cudaFree(w->w.d);
+    delete w;
+}
+
+AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* stream) {
+    if (!w || !xin || !y) return seterr(AB2_ERR_ARG, "null argument");
+    if (batch < 1 || batch > 64) return seterr(AB2_ERR_CAPACITY, "batch must be in [1, 64]");
+    CK(cudaSetDevice(w->device));
+    OpCache& oc = g_ops[w->device & 63];
+    std::lock_guard<std::mutex> lk(oc.mu);
+    cudaStream_t st = (cudaStream_t)stream;
+    RET(ensure((void**)&oc.xf, &oc.xf_bytes, xfrag_bytes((int)w->n, batch)));
+    RET(ensure(&oc.ws, &oc.ws_bytes, std::max<size_t>(16, gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms) * 4)));
+    size_t tkb = oc.tk_n * 4;
+    RET(ensure((void**)&oc.tk, &tkb, (size_t)gemm_grid_x(w->w.M16) * 4));
+    oc.tk_n = tkb / 4;
+    launch_to_xfrag(xin, (int)w->n, (int)w->n, batch, oc.xf, st);
+    launch_q8_gemm(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, epi_store(y, (int)w->w.M, w->w.M), w->num_sms, st);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+AB2_API int ab2_q8_unpack(ab2_q8* w, float* out, void* stream) {
+    if (!w || !out) return seterr(AB2_ERR_ARG, "null argument");
+    CK(cudaSetDevice(w->device));
+    launch_q8p_dequant(w->w, w->w.M, out, (cudaStream_t)stream);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+AB2_API int ab2_q8_dequant(const uint8_t* blocks, int64_t n_blocks, float* out, void* stream) {
+    if (!blocks || !out || n_blocks < 0) return seterr(AB2_ERR_ARG, "bad argument");
+    if (n_blocks == 0) return 0;
+    launch_q8_dequant_raw(blocks, n_blocks, out, (cudaStream_t)stream);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+AB2_API int ab2_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,
+                            const float* decay, int B, int H, int dk, int dv, float* o, void* stream) {
+    if (!S || !q || !k || !v || !beta || !decay || !o) return seterr(AB2_ERR_ARG, "null argument");
+    if (dk != 128 || dv != 128) return seterr(AB2_ERR_SHAPE, "dk = dv = 128 required");
+    if (B < 0 || H < 0) return seterr(AB2_ERR_ARG, "negative size");
+    if (B == 0 || H == 0) return 0;
+    launch_gated_delta(S, q, k, v, beta, decay, B, H, o, (cudaStream_t)stream);
+    CK(cudaGetLastError());
+    return 0;
+}
+
+AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int64_t cap, const int32_t* pos, int B,
+                            int Hq, int Hkv, int hd, int kv_bf16, const float* q_norm, const float* k_norm,
+                            float rope_base, int rope_dims, int max_pos, float* out, void* stream) {
+    if (!proj || !k_cache || !v_cache || !pos || !out) return seterr(AB2_ERR_ARG, "null argument");
+    if (B < 1) return seterr(AB2_ERR_ARG, "B must be positive");
+    if ((hd != 128 && hd != 256) || Hkv < 1 || Hq != 4 * Hkv) return seterr(AB2_ERR_SHAPE, "unsupported head configuration");
+    if (rope_dims < 0 || rope_dims > hd || rope_dims % 2) return seterr(AB2_ERR_SHAPE, "bad rope_dims");
+    if (max_pos < 0 || max_pos >= cap) return seterr(AB2_ERR_CAPACITY, "max_pos outside [0, cap)");
+    int dev;
+    CK(cudaGetDevice(&dev));
+    int nsm = 148;
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+    OpCache& oc = g_ops[dev & 63];
+    std::lock_guard<std::mutex> lk(oc.mu);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int rot = rope_dims ? rope_dims : hd;
+    if (oc.rope_rows < cap || oc.rope_rot != rot || oc.rope_base != rope_base) {
+        const int hr = rot / 2;
+        std::vector<float2> tab((size_t)cap * hr);
+        for (int j = 0; j < hr; j++) {
+            const float freq = 1.0f / powf(rope_base, (float)(2 * j) / (float)rot);
+            for (int64_t p = 0; p < cap; p++) {
+                const float val = (float)p * freq;
+                tab[(size_t)p * hr + j] = make_float2(cosf(val), sinf(val));
+            }
+        }
+        CK(cudaStreamSynchronize(st));
+        if (oc.rope) cudaFree(oc.rope);
+        oc.rope = nullptr;
+        CK(cudaMalloc(&oc.rope, tab.size() * sizeof(float2) + 16));
+        CK(cudaMemcpy(oc.rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        oc.rope_rows = cap;
+        oc.rope_rot = rot;
+        oc.rope_base = rope_base;
+    }
+    const int max_len = max_pos + 1;
+    const int chunk = attn_chunk(B, Hkv, max_len, nsm);
+    RET(ensure(&oc.ws, &oc.ws_bytes, attn_ws_floats(B, Hkv, attn_nsplit(max_len, chunk), hd, Hq / Hkv) * 4));
+    size_t tkb = oc.tk_n * 4;
+    RET(ensure((void**)&oc.tk, &tkb, (size_t)B * Hkv * 4));
+    oc.tk_n = tkb / 4;
+    RET(ensure((void**)&oc.xf, &oc.xf_bytes, xfrag_bytes(Hq * hd, B)));
+    AttnParams p;
+    p.proj = proj;
+    p.ldp = Hq * 2 * hd + 2 * Hkv * hd;
+    p.q_norm = q_norm;
+    p.k_norm = k_norm;
+    p.rope = oc.rope;
+    p.rot = rot;
+    p.kc = k_cache;
+    p.vc = v_cache;
+    p.kv_slot_stride = (int64_t)Hkv * cap * hd;
+    p.cap = (int)cap;
+    p.pos = pos;
+    p.Hq = Hq;
+    p.Hkv = Hkv;
+    p.chunk = chunk;
+    p.ws = (float*)oc.ws;
+    p.tickets = oc.tk;
+    p.xf_out = oc.xf;
+    p.xs = xfrag_shape(Hq * hd, B);
+    p.o_out = out;
+    if (launch_attention(p, B, hd, kv_bf16 != 0, max_len, st)) return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
+    CK(cudaGetLastError());
+    return 0;
+}

@@ -1,0 +1,351 @@
+"""Decode-throughput benchmark of the B200 backend on the 2B-shape Qwen3.5 hybrid (Q8_0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
+
+Workload: 24 layers (every 4th GQA), hidden 2048, vocab 151936, random
+Q8_0 weights; per GPU 64 sequences whose bf16 KV cache is prefilled to 8192 tokens and whose
+DeltaNet / conv states are seeded; a step is one greedy decode token for every sequence
+(sequence-sharded across GPUs, no collective on the data path: weak scaling).
+
+Printed (rank 0): one JSON line with the whole-job tok/s measured on device with CUDA events
+(inputs resident, tokens fed back on device), the end-to-end tok/s through the host-buffer
+API, the roofline of the dominant kernel, the CPU baseline and the SM clocks seen.
+`--impl reference` times the CPU restatement of the reference decode path (oracle/) on the
+host cores for the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "ane-infer_b200")
+
+METRIC = "decode tok/s, 2B-shape Q8_0 B=64 ctx8K at 1/2/4/8 B200; % HBM roofline"
+SHAPE_KEYS = dict(n_layers=24, dim=2048, vocab=151936, ffn=6144, dn_heads=16, dn_state=128, attn_heads=8,
+                  kv_heads=2, head_dim=256)
+# dram__bytes_read.sum + dram__bytes_write.sum per attention launch from the ncu capture
+# summarised in profiles/attention_decode_b64_ctx8k.md (None until captured)
+NCU_TRAFFIC_ATTN_PER_LAUNCH = None
+
+
+def load_pkg():
+    name = "ane_infer_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks sampler
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.samples = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def gpu_id_for(torch, dev: int) -> str:
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except Exception:
+        return str(dev)
+
+
+# --------------------------------------------------------------------------- byte accounting
+def weight_bytes(cfg) -> int:
+    """Algorithmic Q8_0 weight bytes read per step (every projection + lm_head, not the embedding)."""
+    D, F, V = cfg["dim"], cfg["ffn"], cfg["vocab"]
+    H, hd, Hq, Hkv = cfg["dn_heads"], cfg["head_dim"], cfg["n_heads"], cfg["n_kv_heads"]
+    per_dn = 3 * D * D + D * D + 2 * H * D + D * D
+    per_at = 2 * Hq * hd * D + 2 * Hkv * hd * D + D * Hq * hd
+    ffn = 3 * D * F
+    elems = cfg["n_dn"] * (per_dn + ffn) + cfg["n_attn"] * (per_at + ffn) + V * D
+    return elems * 34 // 32
+
+
+def seq_bytes(cfg, ctx_len: int, kv_bytes: int = 2) -> int:
+    """Per-sequence state bytes per step: DeltaNet state r+w, conv state r+w, K+V read."""
+    dn = cfg["n_dn"] * (2 * cfg["dn_heads"] * 128 * 128 * 4 + 2 * 3 * cfg["dim"] * cfg["conv_kernel"] * 4)
+    kv = cfg["n_attn"] * 2 * cfg["n_kv_heads"] * ctx_len * cfg["head_dim"] * kv_bytes
+    return dn + kv
+
+
+def attn_launch_bytes(cfg, B: int, ctx_len: int) -> int:
+    return B * cfg["n_kv_heads"] * ctx_len * cfg["head_dim"] * 2 * 2
+
+
+# --------------------------------------------------------------------------- CPU reference
+def cpu_reference_tokps(gguf, shape, ctx_len: int, n_tokens: int = 0, seconds: float = 15.0, seq: int = 0):
+    """Time the oracle (CPU restatement, all host threads) decoding one sequence at ctx_len."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from ane_infer_b200 import synth
+    om = oracle.Model(gguf, ctx_cap=ctx_len + 64)
+    s = om.new_seq(kv_bf16=True)
+    for l in range(shape.n_layers):
+        if shape.layer_is_attn(l):
+            k, v = synth.seeded_kv(shape, seq, l, ctx_len)
+            s.set_kv(l, k, v)
+        else:
+            s.set_dn(l, synth.seeded_dn_state(shape, seq, l), synth.seeded_conv_state(shape, seq, l))
+    s.pos = ctx_len
+    tok = 1
+    s.forward(tok)          # warm-up token
+    t0 = time.perf_counter()
+    done = 0
+    while (n_tokens and done < n_tokens) or (not n_tokens and time.perf_counter() - t0 < seconds):
+        tok = oracle.greedy(s.forward(tok))
+        done += 1
+    dt = time.perf_counter() - t0
+    return done / dt, done, dt, oracle.lib().oracle_max_threads()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from ane_infer_b200 import synth
+    shape = synth.shape_2b()
+    gguf = synth.build_model_gguf(shape, seed=0)
+    total_steps = args.warmup + args.steps
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    om = oracle.Model(gguf, ctx_cap=args.ctx + total_steps + 8)
+    s = om.new_seq(kv_bf16=True)
+    for l in range(shape.n_layers):
+        if shape.layer_is_attn(l):
+            s.set_kv(l, *synth.seeded_kv(shape, 0, l, args.ctx))
+        else:
+            s.set_dn(l, synth.seeded_dn_state(shape, 0, l), synth.seeded_conv_state(shape, 0, l))
+    s.pos = args.ctx
+    tok = 1
+    for _ in range(args.warmup):
+        tok = oracle.greedy(s.forward(tok))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = oracle.greedy(s.forward(tok))
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cores = oracle.lib().oracle_max_threads()
+    sample = (f"1 of the {args.batch} sequences, {args.steps} greedy tokens at ctx {args.ctx} "
+              f"(the reference decodes one sequence at a time; {args.batch} sequences = {args.batch} sequential runs)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"2B-shape Qwen3.5 hybrid decode, Q8_0, ctx {args.ctx} prefilled",
+                   "global_batch": 1, "seq_len": args.ctx, "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    pkg = load_pkg()
+    from ane_infer_b200 import synth
+    shape = synth.shape_2b()
+    gguf = synth.build_model_gguf(shape, seed=0)
+    B = args.batch if not args.strong else args.batch // world
+    n_e2e = max(2, args.steps // 2)
+    cap = args.ctx + args.warmup * 3 + args.steps * 3 + n_e2e + 16
+    ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap, kv_bf16=True)
+    cfg = ctx.config
+    ctx.seed_state(seed=1 + rank, n_slots=B, n_tokens=args.ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
+    stream = torch.cuda.current_stream()
+    tok = [torch.from_numpy(synth.seeded_tokens(B, cfg["vocab"], seed=2 + rank)).cuda(),
+           torch.empty(B, dtype=torch.int32, device="cuda")]
+    logits = torch.empty((B, cfg["vocab"]), dtype=torch.float32, device="cuda")
+
+    def dev_steps(n, i0=0):
+        for i in range(n):
+            a, b = tok[(i0 + i) % 2], tok[(i0 + i + 1) % 2]
+            ctx.decode_step_device(a, B, logits, b, stream)
+
+    # ---- device-resident timed region
+    dev_steps(args.warmup)
+    barrier()
+    clock = ClockSampler(gpu_id_for(torch, local))
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    pos0 = ctx.get_pos(0)
+    e0.record(stream)
+    dev_steps(args.steps, args.warmup)
+    e1.record(stream)
+    barrier()
+    clocks = clock.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms)
+    value = world * B * args.steps / (ms_max / 1e3)
+    mean_len = pos0 + (args.steps + 1) / 2.0
+    step_bytes = weight_bytes(cfg) + B * seq_bytes(cfg, int(mean_len))
+    peak, peak_kind = measured_peaks()
+
+    # ---- per-kernel device time (CUDA events around each launch on the same stream)
+    ctx.profile(True)
+    prof_pos0 = ctx.get_pos(0)
+    dev_steps(args.steps, args.warmup + args.steps)
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    a = prof["attention"]
+    attn_len = prof_pos0 + (args.steps + 1) / 2.0
+    attn_ms = a["ms"] / max(a["launches"], 1)
+    attn_bytes = attn_launch_bytes(cfg, B, int(attn_len))
+    attn_gbs = attn_bytes / (attn_ms / 1e3) / 1e9
+    traffic = None
+    if NCU_TRAFFIC_ATTN_PER_LAUNCH is not None:
+        traffic = NCU_TRAFFIC_ATTN_PER_LAUNCH
+
+    # ---- end to end through the host-buffer API
+    host_tok = synth.seeded_tokens(B, cfg["vocab"], seed=5 + rank)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        _, nxt = ctx.decode_step(host_tok, want_logits=False)
+        host_tok = nxt
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = world * B * n_e2e / e2e_s
+
+    # ---- CPU baseline (rank 0, N = 1): the oracle on one sequence of the same workload
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, n, dt, cores = cpu_reference_tokps(gguf, shape, args.ctx, seconds=args.cpu_seconds)
+        cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"1 sequence, {n} greedy tokens at ctx {args.ctx} in {dt:.1f} s "
+                         f"(the reference decodes one sequence at a time)"}
+
+    if rank == 0:
+        launches = ctx.launches_per_step(B) * args.steps
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random Q8_0 weights, seeded DeltaNet/conv state, N(0,1) bf16 KV)",
+            "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {B} seq/GPU, ctx {args.ctx} "
+                                   f"prefilled bf16 KV", "model": "qwen35-hybrid-2B-shape (random init)",
+                       "global_batch": B * world, "seq_len": args.ctx,
+                       "parallelism": f"sequence-sharded x{world}, no collective",
+                       "l2": "inputs larger than L2 (each step reads ~%.1f GB)" % (step_bytes / 1e9)},
+            "step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms_max / args.steps) / 1e6, 1),
+                         "frac": round(step_bytes / (ms_max / args.steps) / 1e6 / peak, 4)},
+            "roofline": {"kernel": "attn_decode_kernel (GQA split-KV flash-decode)", "bound": "hbm",
+                         "achieved": round(attn_gbs, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(attn_gbs / peak, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": round(attn_ms, 5)},
+            "kernel_ms_per_step": {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+                    "steps": n_e2e},
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU (weak scaling)")
+    ap.add_argument("--ctx", type=int, default=8192)
+    ap.add_argument("--strong", action="store_true", help="split --batch across the GPUs instead")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,72 @@
+"""Shared fixtures. GPU tests are marked `gpu`; everything else runs on a CPU-only host."""
+from __future__ import annotations
+
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG_DIR = os.path.join(ROOT, "ane-infer_b200")
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+
+def load_pkg():
+    """Import the ane-infer_b200 directory as the package `ane_infer_b200`."""
+    name = "ane_infer_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and the built libab2.so")
+
+
+@pytest.fixture(scope="session")
+def pkg():
+    return load_pkg()
+
+
+@pytest.fixture(scope="session")
+def synth(pkg):
+    from ane_infer_b200 import synth as s
+    return s
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    import oracle as o
+    o.lib()
+    return o
+
+
+@pytest.fixture(scope="session")
+def tiny_gguf(synth):
+    return synth.build_model_gguf(synth.tiny_shape(), seed=0)
+
+
+@pytest.fixture(scope="session")
+def tiny_model(oracle, tiny_gguf):
+    return oracle.Model(tiny_gguf, ctx_cap=4096)
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+def rel_err(a, b) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))

@@ -1,0 +1,154 @@
+"""GPU parity of the fused DeltaNet and attention kernels against the oracle: the
+recurrence op (config 2), the flash-decode op (config 3) and the per-layer mixers."""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4   # max|diff| <= TOL * max|ref|
+
+
+def bf16_bits(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(torch.bfloat16).cuda()
+
+
+# ---------------------------------------------------------------------------- recurrence op
+def config2_inputs(rng, B, H=16):
+    S = rng.normal(0, 0.1, size=(B, H, 128, 128)).astype(np.float32)
+    q = rng.normal(size=(B, H, 128)).astype(np.float32)
+    k = rng.normal(size=(B, H, 128)).astype(np.float32)
+    v = rng.normal(size=(B, H, 128)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    beta = (1 / (1 + np.exp(-rng.normal(size=(B, H))))).astype(np.float32)
+    decay = np.exp(-np.log1p(np.exp(rng.normal(size=(B, H)))) * np.exp(rng.normal(0, 0.5, size=(B, H))))
+    return S, q, k, v, beta, decay.astype(np.float32)
+
+
+@pytest.mark.parametrize("B", [1, 16, 64, 256])
+def test_gated_delta_op(pkg, oracle, synth, cuda, B):
+    torch = cuda
+    rng = np.random.default_rng(B)
+    S, q, k, v, beta, decay = config2_inputs(rng, B)
+    q, k, v = synth.bf16_round(q), synth.bf16_round(k), synth.bf16_round(v)
+    o_ref, S_ref = oracle.gated_delta(S, q, k, v, beta, decay)
+    Sd = torch.from_numpy(S).cuda()
+    o = torch.empty((B, 16, 128), dtype=torch.float32, device="cuda")
+    pkg.gated_delta(Sd, bf16_bits(torch, q), bf16_bits(torch, k), bf16_bits(torch, v),
+                    torch.from_numpy(beta).cuda(), torch.from_numpy(decay).cuda(), o, B, 16)
+    torch.cuda.synchronize()
+    assert rel_err(o.cpu().numpy(), o_ref) < 1e-5
+    assert rel_err(Sd.cpu().numpy(), S_ref) < 1e-5
+
+
+def test_gated_delta_empty_batch(pkg, cuda):
+    torch = cuda
+    z = torch.zeros(1, device="cuda")
+    pkg.gated_delta(z, z, z, z, z, z, z, 0, 16)   # B = 0 is a no-op
+
+
+# ---------------------------------------------------------------------------- attention op
+def attn_case(rng, synth, B, Hq, Hkv, hd, ctx, cap, kv_bf16):
+    proj = rng.normal(size=(B, Hq * 2 * hd + 2 * Hkv * hd)).astype(np.float32)
+    kc = rng.normal(size=(B, Hkv, cap, hd)).astype(np.float32)
+    vc = rng.normal(size=(B, Hkv, cap, hd)).astype(np.float32)
+    if kv_bf16:
+        kc, vc = synth.bf16_round(kc), synth.bf16_round(vc)
+    pos = np.array([ctx - 1 - (b % 3) for b in range(B)], dtype=np.int32).clip(0)
+    return proj, kc, vc, pos
+
+
+@pytest.mark.parametrize("B,ctx,hd,rot,kv_bf16,norms", [
+    (1, 1, 256, 64, True, False),
+    (1, 1024, 256, 64, True, False),
+    (64, 1024, 256, 64, True, False),
+    (1, 4096, 256, 64, True, True),
+    (3, 777, 256, 256, True, True),
+    (1, 16384, 256, 64, True, False),
+    (2, 300, 128, 128, False, True),
+    (5, 129, 256, 256, False, False),
+])
+def test_attn_decode_op(pkg, oracle, synth, cuda, B, ctx, hd, rot, kv_bf16, norms):
+    torch = cuda
+    Hq, Hkv = 8, 2
+    cap = ctx + 8
+    rng = np.random.default_rng(ctx + B + hd)
+    proj, kc, vc, pos = attn_case(rng, synth, B, Hq, Hkv, hd, ctx, cap, kv_bf16)
+    qn = (1 + rng.normal(0, 0.02, size=hd)).astype(np.float32) if norms else None
+    kn = (1 + rng.normal(0, 0.02, size=hd)).astype(np.float32) if norms else None
+    dt = torch.bfloat16 if kv_bf16 else torch.float32
+    kd = torch.from_numpy(kc).to(dt).cuda()
+    vd = torch.from_numpy(vc).to(dt).cuda()
+    out = torch.empty((B, Hq * hd), dtype=torch.float32, device="cuda")
+    pkg.attn_decode(torch.from_numpy(proj).cuda(), kd, vd, cap, torch.from_numpy(pos).cuda(), B, Hq, Hkv, hd, kv_bf16,
+                    None if qn is None else torch.from_numpy(qn).cuda(),
+                    None if kn is None else torch.from_numpy(kn).cuda(), 1e7, rot, int(pos.max()), out)
+    torch.cuda.synchronize()
+    og = out.cpu().numpy()
+    kg = kd.float().cpu().numpy()
+    for b in range(B):
+        qf = proj[b, :Hq * 2 * hd].reshape(Hq, 2 * hd)
+        kn_ = proj[b, Hq * 2 * hd: Hq * 2 * hd + Hkv * hd].reshape(Hkv, hd)
+        vn_ = proj[b, Hq * 2 * hd + Hkv * hd:].reshape(Hkv, hd)
+        ref, kc2, _ = oracle.attn_op(qf[:, :hd], qf[:, hd:], kn_, vn_, kc[b], vc[b], int(pos[b]), 1e7, rot, qn, kn,
+                                     kv_bf16=kv_bf16)
+        assert rel_err(og[b].reshape(Hq, hd), ref) < TOL, b
+        p = int(pos[b])
+        assert rel_err(kg[b][:, p], kc2[:, p]) < 1e-2 if kv_bf16 else rel_err(kg[b][:, p], kc2[:, p]) < 1e-5
+        assert np.array_equal(kg[b][:, :p], kc[b][:, :p])
+
+
+# ---------------------------------------------------------------------------- model layers
+@pytest.fixture(scope="module")
+def tiny_ctx(pkg, tiny_gguf, cuda):
+    ctx = pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=128, kv_bf16=False)
+    yield ctx
+    ctx.close()
+
+
+def test_deltanet_layer(tiny_ctx, tiny_model):
+    rng = np.random.default_rng(11)
+    layer = 1
+    rec = rng.normal(0, 0.1, size=(8, 128, 128)).astype(np.float32)
+    conv = rng.normal(0, 1, size=(3072, 4)).astype(np.float32)
+    seq = tiny_model.new_seq()
+    seq.set_dn(layer, rec, conv)
+    tiny_ctx.set_dn_state(layer, 1, rec, conv)
+    for step in range(3):
+        x = rng.normal(size=1024).astype(np.float32)
+        ref = seq.mixer(layer, x)
+        got = tiny_ctx.mixer_layer(layer, 1, x)
+        assert rel_err(got, ref) < TOL, step
+    r_ref, c_ref = seq.get_dn(layer)
+    r_got, c_got = tiny_ctx.get_dn_state(layer, 1)
+    assert rel_err(r_got, r_ref) < 1e-5
+    assert np.array_equal(c_got, c_ref)       # the conv state is a pure shift of the projection
+
+
+def test_attention_layer(tiny_ctx, tiny_model):
+    rng = np.random.default_rng(12)
+    layer = 3
+    n = 50
+    k = rng.normal(size=(2, n, 128)).astype(np.float32)
+    v = rng.normal(size=(2, n, 128)).astype(np.float32)
+    seq = tiny_model.new_seq()
+    seq.set_kv(layer, k, v)
+    seq.pos = n
+    tiny_ctx.set_kv(layer, 0, k, v)
+    tiny_ctx.set_pos(0, n)
+    x = rng.normal(size=1024).astype(np.float32)
+    ref = seq.mixer(layer, x)
+    got = tiny_ctx.mixer_layer(layer, 0, x)
+    assert rel_err(got, ref) < TOL
+    kr, vr = seq.get_kv(layer, n + 1)
+    kg, vg = tiny_ctx.get_kv(layer, 0, n + 1)
+    assert rel_err(kg, kr) < 1e-5 and rel_err(vg, vr) < 1e-5
+
+
+def test_ffn_layer(tiny_ctx, tiny_model):
+    rng = np.random.default_rng(13)
+    for layer in (0, 3):
+        x = rng.normal(size=1024).astype(np.float32)
+        assert rel_err(tiny_ctx.ffn_layer(layer, x), tiny_model.ffn(layer, x)) < TOL
