@@ -72,6 +72,8 @@ SIGNATURES = {
     "ab2_seed_state": (C.c_int, [_vp, _u64, C.c_int, _i64, C.c_float, C.c_float, C.c_float]),
     "ab2_decode_step": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "ab2_decode_step_device": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp, _vp]),
+    "ab2_sync": (C.c_int, [_vp]),
+    "ab2_op_error": (C.c_int, [C.POINTER(C.c_uint32)]),
     "ab2_launches_per_step": (C.c_int, [_vp, C.c_int, C.POINTER(_i64)]),
     "ab2_profile": (C.c_int, [_vp, C.c_int]),
     "ab2_profile_read": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(_i64)]),
@@ -231,6 +233,10 @@ class DecodeContext:
         _check(load_library().ab2_decode_step_device(self._h, _dp(tokens_dev), batch, _dp(logits_dev),
                                                      _dp(next_dev), _stream(stream)))
 
+    def sync(self):
+        """Wait for queued device work; raises if a tensor-core pipeline wait timed out."""
+        _check(load_library().ab2_sync(self._h))
+
     def launches_per_step(self, batch: int) -> int:
         v = C.c_int64()
         _check(load_library().ab2_launches_per_step(self._h, batch, C.byref(v)))
@@ -287,6 +293,13 @@ class Q8Tensor:
 def q8_gemv(w: Q8Tensor, x, y, batch: int = 1, stream=None):
     """y[b][:] = W x[b][:] on device buffers (f32 [batch][n] -> [batch][m])."""
     _check(load_library().ab2_q8_gemv(w._h, _dp(x), batch, _dp(y), _stream(stream)))
+
+
+def op_error() -> int:
+    """Synchronise the device; return and clear the op-level tensor-core error word (0 = ok)."""
+    v = C.c_uint32()
+    _check(load_library().ab2_op_error(C.byref(v)))
+    return v.value
 
 
 def q8_dequant(blocks, n_blocks: int, out, stream=None):

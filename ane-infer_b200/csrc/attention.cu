@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnParams
             const int h = kvh * GQ + hh;
             float o = A / Lsum;
             o *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
-            xfrag_store(p.xf_out, p.xs, b, h * HD + d, o);
+            act_store(p.out, b, h * HD + d, o);
             if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = o;
         } else {
             if (d == 0) {
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnParams
         }
         float o = A / Lsum;
         o *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
-        xfrag_store(p.xf_out, p.xs, b, h * HD + d, o);
+        act_store(p.out, b, h * HD + d, o);
         if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = o;
     }
     if (threadIdx.x == 0) p.tickets[b * p.Hkv + kvh] = 0u;

@@ -88,6 +88,45 @@ __device__ __forceinline__ void xfrag_store(uint8_t* xf, const XfragShape& s, in
 }
 
 // ----------------------------------------------------------------------------------------
+// Activation layout of the tcgen05 GEMM ("x16"): the B operand in f16, stored exactly as the
+// shared-memory image of K-major 128-byte-swizzled tiles, so one bulk copy per 64-wide K tile
+// lands it ready for tcgen05.mma: [K/64][npad rows][128 B], where the 16-byte chunk j of row n
+// is stored at chunk position j ^ (n % 8). npad = batch rounded up to 16, 32 or 64.
+__host__ __device__ inline int x16_npad(int batch) { return batch <= 16 ? 16 : (batch <= 32 ? 32 : 64); }
+__host__ __device__ inline size_t x16_bytes(int K, int batch) {
+    return (size_t)((K + 63) / 64) * x16_npad(batch) * 128;
+}
+__device__ __forceinline__ size_t x16_offset(int npad, int b, int k) {
+    const int kt = k >> 6, kk = k & 63, j = kk >> 3, e = kk & 7;
+    return ((size_t)kt * npad + b) * 128 + ((j ^ (b & 7)) << 4) + e * 2;
+}
+
+// Where a kernel writes the activations of the next GEMM: xfrag (mma.sync path, exact
+// weights, f16 hi/lo activations) for small batches, x16 (tcgen05 path) for large ones.
+struct ActOut {
+    uint8_t* buf = nullptr;
+    int x16 = 0;
+    int npad = 16;
+    XfragShape xs{};
+};
+
+__host__ __device__ inline ActOut act_out(uint8_t* buf, int K, int batch, bool x16) {
+    ActOut o;
+    o.buf = buf;
+    o.x16 = x16 ? 1 : 0;
+    o.npad = x16_npad(batch);
+    o.xs = xfrag_shape(K, batch);
+    return o;
+}
+
+__device__ __forceinline__ void act_store(const ActOut& o, int b, int k, float v) {
+    if (o.x16)
+        *reinterpret_cast<__half*>(o.buf + x16_offset(o.npad, b, k)) = __float2half_rn(v);
+    else
+        xfrag_store(o.buf, o.xs, b, k, v);
+}
+
+// ----------------------------------------------------------------------------------------
 // f16 / bf16 helpers
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }

@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_fused_kernel(DnParams p) 
         const float g = proj[3 * D + h * DK + c];
         float nv = o_s[c] * sc[0] * p.ssm_norm[c];
         nv *= g / (1.0f + expf(-g));
-        xfrag_store(p.xf_out, p.xs, b, h * DK + c, nv);
+        act_store(p.out, b, h * DK + c, nv);
         if (p.o_out) p.o_out[(size_t)b * D + h * DK + c] = nv;
     }
 }

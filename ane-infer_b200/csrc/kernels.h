@@ -8,14 +8,22 @@
 namespace ab2 {
 
 // A Q8_0 weight in the packed device layout described in common.cuh.
+// A Q8_0 weight on the device, in one or both packed layouts:
+//   q8p (qs, d): mma.sync fragment order, used for batches <= 8 (exact weights);
+//   q8t (qt):    128-row x 64-col tiles for the tcgen05 GEMM, used for larger batches:
+//                [MT][KT][4 chunks][128 rows][16 B] offset-binary int8 + [128 rows][2] f16 d.
 struct Q8Weight {
     uint8_t* qs = nullptr;  // [M16][KB][32][16]
     uint8_t* d = nullptr;   // [M16][KB][8] x (f16, f16)
+    uint8_t* qt = nullptr;  // [MT][KT][8704]
     int64_t M = 0;          // logical rows
     int M16 = 0;            // ceil(M/16)
     int KB = 0;             // K / 32
+    int MT = 0;             // ceil(M/128)
+    int KT = 0;             // ceil(K/64)
     size_t qs_bytes() const { return (size_t)M16 * KB * 512; }
     size_t d_bytes() const { return (size_t)M16 * KB * 32; }
+    size_t qt_bytes() const { return (size_t)MT * KT * 8704; }
 };
 
 enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
@@ -25,9 +33,11 @@ struct GemmEpi {
     float* y = nullptr;  // STORE / RESID: y[b*ldy + row]; SWIGLU: optional f32 copy of h
     int ldy = 0;
     int m_out = 0;       // valid output rows (M, or ffn for SWIGLU)
-    uint8_t* xf_out = nullptr;  // SWIGLU: the next GEMM's activation fragments
-    XfragShape xs_out{};
+    ActOut out{};        // SWIGLU: activations of the next GEMM
 };
+
+// the batch above which the tcgen05 path (q8t weights, x16 activations) is used
+constexpr int kUmmaMinBatch = 9;
 
 // q8.cu
 int gemm_nsplit(int M16, int KB, int num_sms);
@@ -41,10 +51,19 @@ void launch_q8_dequant_raw(const uint8_t* src, int64_t n_blocks, float* out, cud
 void launch_q8p_dequant(const Q8Weight& w, int64_t rows, float* out, cudaStream_t st);
 void launch_embed(const Q8Weight& w, int vocab, const int32_t* tokens, int batch, float* x, int ldx, cudaStream_t st);
 
+// q8_umma.cu
+int umma_npad(int batch);
+int umma_nsplit(int MT, int KT, int num_sms);
+size_t umma_ws_floats(int MT, int KT, int num_sms);
+void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
+                       int64_t stride, cudaStream_t st);
+int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, float* ws, unsigned* tickets, unsigned* err,
+                   const GemmEpi& ep, int num_sms, cudaStream_t st);
+
 // misc.cu
-void launch_rmsnorm_xfrag(const float* x, int ldx, const float* w, int D, float eps, int batch, uint8_t* xf,
-                          cudaStream_t st);
-void launch_to_xfrag(const float* x, int ldx, int K, int batch, uint8_t* xf, cudaStream_t st);
+void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
+                        cudaStream_t st);
+void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st);
 void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st);
 void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st);
 void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st);
@@ -66,8 +85,7 @@ struct DnParams {
     const float* ssm_norm;  // [128]
     float eps;
     int D, H;
-    uint8_t* xf_out;     // activation fragments of the ssm_out GEMM (K = D)
-    XfragShape xs;
+    ActOut out;          // activations of the ssm_out GEMM (K = D)
     float* o_out;        // optional f32 copy of the gated output [B][D]
 };
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
@@ -92,8 +110,7 @@ struct AttnParams {
     int chunk;           // tokens per split
     float* ws;           // split partials
     unsigned* tickets;   // [B*Hkv]
-    uint8_t* xf_out;     // activation fragments of the wo GEMM (K = Hq*HD)
-    XfragShape xs;
+    ActOut out;          // activations of the wo GEMM (K = Hq*HD)
     float* o_out;        // optional f32 copy [B][Hq*HD]
 };
 int attn_nsplit(int max_len, int chunk);

@@ -6,9 +6,8 @@ namespace ab2 {
 
 // out = x * (1 / sqrt(mean(x^2) + eps)) * w, written as activation fragments for the next
 // GEMM (rmsnorm_vec, crates/cli/src/main.rs:1106-1113). One CTA per batch row.
-__global__ void __launch_bounds__(256) rmsnorm_xfrag_kernel(const float* __restrict__ x, int ldx,
-                                                            const float* __restrict__ w, int D, float eps,
-                                                            uint8_t* __restrict__ xf, XfragShape xs) {
+__global__ void __launch_bounds__(256) rmsnorm_act_kernel(const float* __restrict__ x, int ldx,
+                                                          const float* __restrict__ w, int D, float eps, ActOut out) {
     __shared__ float red[8];
     const int b = blockIdx.x;
     const float* xb = x + (size_t)b * ldx;
@@ -17,13 +16,12 @@ __global__ void __launch_bounds__(256) rmsnorm_xfrag_kernel(const float* __restr
     ss = block_sum<256>(ss, red);
     ss = ss / (float)D;
     const float inv = 1.0f / sqrtf(ss + eps);
-    for (int i = threadIdx.x; i < D; i += 256) xfrag_store(xf, xs, b, i, xb[i] * inv * w[i]);
+    for (int i = threadIdx.x; i < D; i += 256) act_store(out, b, i, xb[i] * inv * w[i]);
 }
 
-__global__ void to_xfrag_kernel(const float* __restrict__ x, int ldx, int K, uint8_t* __restrict__ xf,
-                                XfragShape xs) {
+__global__ void to_act_kernel(const float* __restrict__ x, int ldx, int K, ActOut out) {
     const int b = blockIdx.x;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) xfrag_store(xf, xs, b, i, x[(size_t)b * ldx + i]);
+    for (int i = threadIdx.x; i < K; i += blockDim.x) act_store(out, b, i, x[(size_t)b * ldx + i]);
 }
 
 // argmax under f32::total_cmp with ties going to the last index, as Iterator::max_by
@@ -72,13 +70,13 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     }
 }
 
-void launch_rmsnorm_xfrag(const float* x, int ldx, const float* w, int D, float eps, int batch, uint8_t* xf,
-                          cudaStream_t st) {
-    rmsnorm_xfrag_kernel<<<batch, 256, 0, st>>>(x, ldx, w, D, eps, xf, xfrag_shape(D, batch));
+void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
+                        cudaStream_t st) {
+    rmsnorm_act_kernel<<<batch, 256, 0, st>>>(x, ldx, w, D, eps, out);
 }
 
-void launch_to_xfrag(const float* x, int ldx, int K, int batch, uint8_t* xf, cudaStream_t st) {
-    to_xfrag_kernel<<<batch, 256, 0, st>>>(x, ldx, K, xf, xfrag_shape(K, batch));
+void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st) {
+    to_act_kernel<<<batch, 256, 0, st>>>(x, ldx, K, out);
 }
 
 void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st) {

@@ -115,7 +115,7 @@ __device__ __forceinline__ void gemm_epilogue(float acc[NT][4], int mt, int lane
                 int o = mt * 8 + g;
                 if (o < ep.m_out) {
                     float h = (v0 / (1.0f + expf(-v0))) * v1;
-                    if (ep.xf_out) xfrag_store(ep.xf_out, ep.xs_out, b, o, h);
+                    if (ep.out.buf) act_store(ep.out, b, o, h);
                     if (ep.y) ep.y[(size_t)b * ep.ldy + o] = h;
                 }
             } else {

@@ -371,8 +371,11 @@ struct ab2_ctx {
     unsigned* atk = nullptr;    // attention tickets
     float2* rope = nullptr;     // [cap][rot/2]
     float* tmp_out = nullptr;   // [D] for per-layer entry points
+    unsigned* err_d = nullptr;  // tensor-core pipeline error word (0 = ok)
+    bool use_umma = false;      // max_batch >= kUmmaMinBatch: q8t weights are packed too
     // pinned host staging
     int32_t *tok_h = nullptr, *next_h = nullptr;
+    unsigned* err_h = nullptr;
     float* logits_h = nullptr;
     Profile prof;
 
@@ -395,9 +398,15 @@ int upload_f32(ab2_ctx* x, const std::vector<float>& v, float** out) {
     return 0;
 }
 
+constexpr int64_t kPlain = (int64_t)1 << 40;  // grp for plain concatenation
+
+// A source tensor of a packed weight: its rows land at dst = base + (row/grp)*stride + row%grp.
+// kind 0: plain concatenation at `base`; kind 1 / 2: gate / up rows of an interleaved SwiGLU
+// pair (8-row groups in the q8p layout, 64-row groups in the q8t layout).
 struct RepackSrc {
     const GTensor* t;
-    int64_t rows, base, grp, stride;
+    int64_t rows, base;
+    int kind = 0;
 };
 
 // upload Q8_0 tensors (same K) into one packed weight of M rows through a device staging buffer
@@ -406,18 +415,24 @@ int upload_q8(ab2_ctx* x, int64_t M, int64_t K, const std::vector<RepackSrc>& sr
     w->M = M;
     w->M16 = (int)((M + 15) / 16);
     w->KB = (int)(K / 32);
+    w->MT = (int)((M + 127) / 128);
+    w->KT = (int)((K + 63) / 64);
     RET(x->dalloc(&w->qs, w->qs_bytes(), true));
     RET(x->dalloc(&w->d, w->d_bytes(), true));
+    if (x->use_umma) RET(x->dalloc(&w->qt, w->qt_bytes(), true));
     for (auto& s : srcs) {
         CK(cudaMemcpyAsync(staging, s.t->data, s.t->nbytes, cudaMemcpyHostToDevice, x->stream));
-        launch_q8_repack(staging, s.rows, w->KB, *w, s.base, s.grp, s.stride, x->stream);
+        const int64_t pg = s.kind ? 8 : kPlain, ps = s.kind ? 16 : 0, pb = s.kind == 2 ? 8 : s.base;
+        launch_q8_repack(staging, s.rows, w->KB, *w, pb, pg, ps, x->stream);
+        if (x->use_umma) {
+            const int64_t tg = s.kind ? 64 : kPlain, ts = s.kind ? 128 : 0, tb = s.kind == 2 ? 64 : s.base;
+            launch_q8t_repack(staging, s.rows, w->KB, *w, tb, tg, ts, x->stream);
+        }
         CK(cudaGetLastError());
-        // the staging buffer is reused by the next copy; keep the order on the stream
+        // the staging buffer is reused by the next copy; the stream keeps the order
     }
     return 0;
 }
-
-constexpr int64_t kPlain = (int64_t)1 << 40;  // grp for plain concatenation
 
 int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     Gguf g;
@@ -452,10 +467,10 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     do {
         const GTensor *te, *tl;
         if ((rc = find_q8(g, "token_embd.weight", c.vocab, D, &te))) break;
-        if ((rc = upload_q8(x, c.vocab, D, {{te, c.vocab, 0, kPlain, 0}}, staging, &x->embed))) break;
+        if ((rc = upload_q8(x, c.vocab, D, {{te, c.vocab, 0}}, staging, &x->embed))) break;
         if (g.tensor("output.weight")) {  // lm_head = output.weight or tied token_embd (main.rs:1903-1904)
             if ((rc = find_q8(g, "output.weight", c.vocab, D, &tl))) break;
-            if ((rc = upload_q8(x, c.vocab, D, {{tl, c.vocab, 0, kPlain, 0}}, staging, &x->lm_head))) break;
+            if ((rc = upload_q8(x, c.vocab, D, {{tl, c.vocab, 0}}, staging, &x->lm_head))) break;
         } else {
             x->lm_head = x->embed;
         }
@@ -480,12 +495,12 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
                     (rc = find_q8(g, p + "ssm_alpha.weight", H, D, &t3)))
                     break;
                 if ((rc = upload_q8(x, 4 * D + 2 * H, D,
-                                    {{t0, 3 * D, 0, kPlain, 0}, {t1, D, 3 * D, kPlain, 0}, {t2, H, 4 * D, kPlain, 0},
-                                     {t3, H, 4 * D + H, kPlain, 0}},
+                                    {{t0, 3 * D, 0}, {t1, D, 3 * D}, {t2, H, 4 * D},
+                                     {t3, H, 4 * D + H}},
                                     staging, &L.w_in)))
                     break;
                 if ((rc = find_q8(g, p + "ssm_out.weight", D, D, &t0)) ||
-                    (rc = upload_q8(x, D, D, {{t0, D, 0, kPlain, 0}}, staging, &L.w_out)))
+                    (rc = upload_q8(x, D, D, {{t0, D, 0}}, staging, &L.w_out)))
                     break;
                 if ((rc = read_f32(g, p + "ssm_conv1d.weight", 3 * D * c.conv_k, &fv)) || (rc = upload_f32(x, fv, &L.conv_w)))
                     break;
@@ -499,22 +514,23 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
                     (rc = find_q8(g, p + "attn_v.weight", Hkv * hd, D, &t2)))
                     break;
                 if ((rc = upload_q8(x, 2 * Hq * hd + 2 * Hkv * hd, D,
-                                    {{t0, 2 * Hq * hd, 0, kPlain, 0}, {t1, Hkv * hd, 2 * Hq * hd, kPlain, 0},
-                                     {t2, Hkv * hd, 2 * Hq * hd + Hkv * hd, kPlain, 0}},
+                                    {{t0, 2 * Hq * hd, 0}, {t1, Hkv * hd, 2 * Hq * hd},
+                                     {t2, Hkv * hd, 2 * Hq * hd + Hkv * hd}},
                                     staging, &L.w_in)))
                     break;
                 if ((rc = find_q8(g, p + "attn_output.weight", D, Hq * hd, &t0)) ||
-                    (rc = upload_q8(x, D, Hq * hd, {{t0, D, 0, kPlain, 0}}, staging, &L.w_out)))
+                    (rc = upload_q8(x, D, Hq * hd, {{t0, D, 0}}, staging, &L.w_out)))
                     break;
                 if ((rc = read_f32(g, p + "attn_q_norm.weight", hd, &fv)) || (rc = upload_f32(x, fv, &L.q_norm))) break;
                 if ((rc = read_f32(g, p + "attn_k_norm.weight", hd, &fv)) || (rc = upload_f32(x, fv, &L.k_norm))) break;
             }
-            // FFN gate/up interleaved per 8 rows so one m16 tile holds gate and up of 8 outputs
+            // FFN gate/up interleaved so that one tile holds the gate and up rows of the same
+            // outputs (8 + 8 rows per m16 tile in q8p, 64 + 64 rows per 128-row tile in q8t)
             if ((rc = find_q8(g, p + "ffn_gate.weight", F, D, &t0)) || (rc = find_q8(g, p + "ffn_up.weight", F, D, &t1)) ||
                 (rc = find_q8(g, p + "ffn_down.weight", D, F, &t2)))
                 break;
-            if ((rc = upload_q8(x, 2 * F, D, {{t0, F, 0, 8, 16}, {t1, F, 8, 8, 16}}, staging, &L.gate_up))) break;
-            if ((rc = upload_q8(x, D, F, {{t2, D, 0, kPlain, 0}}, staging, &L.down))) break;
+            if ((rc = upload_q8(x, 2 * F, D, {{t0, F, 0, 1}, {t1, F, 0, 2}}, staging, &L.gate_up))) break;
+            if ((rc = upload_q8(x, D, F, {{t2, D, 0}}, staging, &L.down))) break;
         }
     } while (0);
     cudaError_t se = cudaStreamSynchronize(x->stream);
@@ -543,8 +559,10 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     x->ldp = (int)((mproj + 3) / 4 * 4);
     RET(x->dalloc(&x->x, (size_t)B * D * 4));
     RET(x->dalloc(&x->proj, (size_t)B * x->ldp * 4));
-    RET(x->dalloc(&x->xfa, xfrag_bytes((int)maxk, B)));
-    RET(x->dalloc(&x->xfb, xfrag_bytes((int)maxk, B)));
+    const size_t actb = std::max(xfrag_bytes((int)maxk, B), x16_bytes((int)maxk, B));
+    RET(x->dalloc(&x->xfa, actb));
+    RET(x->dalloc(&x->xfb, actb));
+    RET(x->dalloc(&x->err_d, 16));
     RET(x->dalloc(&x->logits, (size_t)B * c.vocab * 4));
     RET(x->dalloc(&x->tok_d, (size_t)B * 4));
     RET(x->dalloc(&x->next_d, (size_t)B * 4));
@@ -554,6 +572,10 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     auto acc_gemm = [&](const Q8Weight& w) {
         gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, B, x->num_sms));
         gtk = std::max(gtk, gemm_grid_x(w.M16));
+        if (x->use_umma) {
+            gws = std::max(gws, umma_ws_floats(w.MT, w.KT, x->num_sms));
+            gtk = std::max(gtk, w.MT);
+        }
     };
     for (auto& L : x->layers) {
         acc_gemm(L.w_in);
@@ -588,6 +610,8 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     }
     CK(cudaMallocHost(&x->tok_h, (size_t)B * 4));
     CK(cudaMallocHost(&x->next_h, (size_t)B * 4));
+    CK(cudaMallocHost(&x->err_h, 16));
+    *x->err_h = 0;
     CK(cudaStreamSynchronize(x->stream));
     return 0;
 }
@@ -630,9 +654,20 @@ void prof_collect(ab2_ctx* x) {
 }
 
 // --------------------------------------------------------------------------------- the step
-void gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st) {
+// batches of kUmmaMinBatch or more run on the tcgen05 path
+bool umma_for(const ab2_ctx* x, int B) { return x->use_umma && B >= kUmmaMinBatch; }
+
+ActOut act(const ab2_ctx* x, uint8_t* buf, int K, int B) { return act_out(buf, K, B, umma_for(x, B)); }
+
+int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st) {
     ProfScope ps(x, PC_GEMM, st);
-    launch_q8_gemm(w, xf, B, x->gws, x->gtk, ep, x->num_sms, st);
+    if (umma_for(x, B)) {
+        if (launch_q8_umma(w, xf, B, x->gws, x->gtk, x->err_d, ep, x->num_sms, st))
+            return seterr(AB2_ERR_CUDA, "tcgen05 GEMM: could not set its shared-memory size");
+    } else {
+        launch_q8_gemm(w, xf, B, x->gws, x->gtk, ep, x->num_sms, st);
+    }
+    return 0;
 }
 
 GemmEpi epi_store(float* y, int ldy, int64_t m) {
@@ -648,12 +683,11 @@ GemmEpi epi_resid(float* y, int ldy, int64_t m) {
     e.mode = EPI_RESID;
     return e;
 }
-GemmEpi epi_swiglu(uint8_t* xf, int F, int B) {
+GemmEpi epi_swiglu(const ActOut& out, int F) {
     GemmEpi e;
     e.mode = EPI_SWIGLU;
     e.m_out = F;
-    e.xf_out = xf;
-    e.xs_out = xfrag_shape(F, B);
+    e.out = out;
     return e;
 }
 
@@ -663,7 +697,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
               cudaStream_t st) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
-    gemm(x, L.w_in, x->xfa, B, epi_store(x->proj, x->ldp, L.w_in.M), st);
+    RET(gemm(x, L.w_in, x->xfa, B, epi_store(x->proj, x->ldp, L.w_in.M), st));
     if (L.dn) {
         DnParams p;
         p.proj = x->proj;
@@ -680,8 +714,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.eps = c.eps;
         p.D = D;
         p.H = (int)c.dn_heads;
-        p.xf_out = x->xfb;
-        p.xs = xfrag_shape(D, B);
+        p.out = act(x, x->xfb, D, B);
         p.o_out = nullptr;
         ProfScope ps(x, PC_DN, st);
         launch_deltanet(p, B, st);
@@ -706,24 +739,21 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
             return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
         p.ws = x->aws;
         p.tickets = x->atk;
-        p.xf_out = x->xfb;
-        p.xs = xfrag_shape((int)(c.n_heads * c.hd), B);
+        p.out = act(x, x->xfb, (int)(c.n_heads * c.hd), B);
         p.o_out = nullptr;
         ProfScope ps(x, PC_ATTN, st);
         if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st))
             return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
-    gemm(x, L.w_out, x->xfb, B, e, st);
-    return 0;
+    return gemm(x, L.w_out, x->xfb, B, e, st);
 }
 
 int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st) {
     const int D = (int)x->c.dim, F = (int)x->c.ffn;
-    gemm(x, L.gate_up, x->xfa, B, epi_swiglu(x->xfb, F, B), st);
+    RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
-    gemm(x, L.down, x->xfb, B, e, st);
-    return 0;
+    return gemm(x, L.down, x->xfb, B, e, st);
 }
 
 int check_capacity(ab2_ctx* x, int B, int* max_len) {
@@ -746,23 +776,24 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
         ProfScope ps(x, PC_OTHER, st);
         launch_embed(x->embed, (int)c.vocab, tok_d, B, x->x, D, st);
     }
+    const ActOut xa = act(x, x->xfa, D, B);
     for (auto& L : x->layers) {
         {
             ProfScope ps(x, PC_OTHER, st);
-            launch_rmsnorm_xfrag(x->x, D, L.attn_norm, D, c.eps, B, x->xfa, st);
+            launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st);
         }
         RET(run_mixer(x, L, 0, B, max_len, x->x, D, EPI_RESID, st));
         {
             ProfScope ps(x, PC_OTHER, st);
-            launch_rmsnorm_xfrag(x->x, D, L.post_norm, D, c.eps, B, x->xfa, st);
+            launch_rmsnorm_act(x->x, D, L.post_norm, D, c.eps, B, xa, st);
         }
         RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st));
     }
     {
         ProfScope ps(x, PC_OTHER, st);
-        launch_rmsnorm_xfrag(x->x, D, x->final_norm, D, c.eps, B, x->xfa, st);
+        launch_rmsnorm_act(x->x, D, x->final_norm, D, c.eps, B, xa, st);
     }
-    gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st);
+    RET(gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st));
     {
         ProfScope ps(x, PC_OTHER, st);
         if (next_d) launch_argmax(logits_d, (int)c.vocab, (int)c.vocab, B, next_d, st);
@@ -771,6 +802,16 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
     CK(cudaGetLastError());
     for (int b = 0; b < B; b++) x->pos_h[b] += 1;
     return 0;
+}
+
+// a nonzero device error word means a tensor-core pipeline wait timed out: report it and re-arm
+int take_device_error(ab2_ctx* x) {
+    const unsigned e = *x->err_h;
+    if (!e) return 0;
+    *x->err_h = 0;
+    cudaMemsetAsync(x->err_d, 0, 4, x->stream);
+    cudaStreamSynchronize(x->stream);
+    return seterr(AB2_ERR_CUDA, "tcgen05 GEMM pipeline wait timed out (code 0x%x); results of this step are invalid", e);
 }
 
 int64_t launches_per_step(const ab2_ctx* x, int B) {
@@ -791,6 +832,7 @@ struct OpCache {
     int64_t rope_rows = 0;
     int rope_rot = 0;
     float rope_base = 0;
+    unsigned* err = nullptr;
 };
 OpCache g_ops[64];
 
@@ -846,6 +888,7 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
     x->cap = max_ctx;
     x->kv_bf16 = opt ? opt->kv_bf16 != 0 : true;
     x->rot = opt ? opt->rope_dims : 0;
+    x->use_umma = max_batch >= kUmmaMinBatch;
     cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device);
     int rc = 0;
     if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)
@@ -868,6 +911,7 @@ AB2_API void ab2_destroy(ab2_ctx* x) {
     for (void* p : x->allocs) cudaFree(p);
     if (x->tok_h) cudaFreeHost(x->tok_h);
     if (x->next_h) cudaFreeHost(x->next_h);
+    if (x->err_h) cudaFreeHost(x->err_h);
     if (x->logits_h) cudaFreeHost(x->logits_h);
     for (auto& v : x->prof.ev)
         for (auto& e : v) {
@@ -1067,10 +1111,21 @@ AB2_API int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int B, float* log
     RET(enqueue_step(x, x->tok_d, B, max_len, x->logits, x->next_d, x->stream));
     if (next_tokens) CK(cudaMemcpyAsync(x->next_h, x->next_d, (size_t)B * 4, cudaMemcpyDeviceToHost, x->stream));
     if (logits) CK(cudaMemcpyAsync(logits, x->logits, (size_t)B * x->c.vocab * 4, cudaMemcpyDeviceToHost, x->stream));
+    CK(cudaMemcpyAsync(x->err_h, x->err_d, 4, cudaMemcpyDeviceToHost, x->stream));
     CK(cudaStreamSynchronize(x->stream));
     prof_collect(x);
+    RET(take_device_error(x));
     if (next_tokens) memcpy(next_tokens, x->next_h, (size_t)B * 4);
     return 0;
+}
+
+AB2_API int ab2_sync(ab2_ctx* x) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    CK(cudaSetDevice(x->device));
+    CK(cudaMemcpyAsync(x->err_h, x->err_d, 4, cudaMemcpyDeviceToHost, x->stream));
+    CK(cudaDeviceSynchronize());
+    prof_collect(x);
+    return take_device_error(x);
 }
 
 AB2_API int ab2_launches_per_step(ab2_ctx* x, int B, int64_t* out) {
@@ -1110,7 +1165,7 @@ AB2_API int ab2_mixer_layer(ab2_ctx* x, int layer, int slot, const float* xin, f
     if (x->pos_h[slot] >= x->cap) return seterr(AB2_ERR_CAPACITY, "slot %d is full", slot);
     const int D = (int)x->c.dim;
     CK(cudaMemcpyAsync(x->x, xin, (size_t)D * 4, cudaMemcpyHostToDevice, x->stream));
-    launch_to_xfrag(x->x, D, D, 1, x->xfa, x->stream);
+    launch_to_act(x->x, D, D, 1, act(x, x->xfa, D, 1), x->stream);
     RET(run_mixer(x, *L, slot, 1, (int)x->pos_h[slot] + 1, x->tmp_out, D, EPI_STORE, x->stream));
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(out, x->tmp_out, (size_t)D * 4, cudaMemcpyDeviceToHost, x->stream));
@@ -1127,7 +1182,7 @@ AB2_API int ab2_ffn_layer(ab2_ctx* x, int layer, const float* xin, float* out) {
     RET(dn_layer(x, layer, &L));
     const int D = (int)x->c.dim;
     CK(cudaMemcpyAsync(x->x, xin, (size_t)D * 4, cudaMemcpyHostToDevice, x->stream));
-    launch_to_xfrag(x->x, D, D, 1, x->xfa, x->stream);
+    launch_to_act(x->x, D, D, 1, act(x, x->xfa, D, 1), x->stream);
     RET(run_ffn(x, *L, 1, x->tmp_out, D, EPI_STORE, x->stream));
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(out, x->tmp_out, (size_t)D * 4, cudaMemcpyDeviceToHost, x->stream));
@@ -1154,16 +1209,21 @@ AB2_API int ab2_q8_create(const uint8_t* blocks, int64_t m, int64_t n, int devic
     w->w.M = m;
     w->w.M16 = (int)((m + 15) / 16);
     w->w.KB = (int)(n / 32);
+    w->w.MT = (int)((m + 127) / 128);
+    w->w.KT = (int)((n + 63) / 64);
     const size_t raw = (size_t)m * (n / 32) * 34;
     uint8_t* staging = nullptr;
     cudaError_t e = cudaMalloc(&w->w.qs, w->w.qs_bytes());
     if (e == cudaSuccess) e = cudaMalloc(&w->w.d, w->w.d_bytes());
+    if (e == cudaSuccess) e = cudaMalloc(&w->w.qt, w->w.qt_bytes());
     if (e == cudaSuccess) e = cudaMalloc(&staging, raw);
     if (e == cudaSuccess) e = cudaMemset(w->w.qs, 0, w->w.qs_bytes());
     if (e == cudaSuccess) e = cudaMemset(w->w.d, 0, w->w.d_bytes());
+    if (e == cudaSuccess) e = cudaMemset(w->w.qt, 0, w->w.qt_bytes());
     if (e == cudaSuccess) e = cudaMemcpy(staging, blocks, raw, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) {
         launch_q8_repack(staging, m, w->w.KB, w->w, 0, kPlain, 0, 0);
+        launch_q8t_repack(staging, m, w->w.KB, w->w, 0, kPlain, 0, 0);
         e = cudaDeviceSynchronize();
     }
     if (staging) cudaFree(staging);
@@ -1181,6 +1241,7 @@ AB2_API void ab2_q8_destroy(ab2_q8* w) {
     cudaSetDevice(w->device);
     if (w->w.qs) cudaFree(w->w.qs);
     if (w->w.d) cudaFree(w->w.d);
+    if (w->w.qt) cudaFree(w->w.qt);
     delete w;
 }
 
@@ -1191,14 +1252,40 @@ AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* 
     OpCache& oc = g_ops[w->device & 63];
     std::lock_guard<std::mutex> lk(oc.mu);
     cudaStream_t st = (cudaStream_t)stream;
-    RET(ensure((void**)&oc.xf, &oc.xf_bytes, xfrag_bytes((int)w->n, batch)));
-    RET(ensure(&oc.ws, &oc.ws_bytes, std::max<size_t>(16, gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms) * 4)));
+    const bool tc = batch >= kUmmaMinBatch;
+    RET(ensure((void**)&oc.xf, &oc.xf_bytes, std::max(xfrag_bytes((int)w->n, batch), x16_bytes((int)w->n, batch))));
+    size_t wsf = std::max(gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms), umma_ws_floats(w->w.MT, w->w.KT, w->num_sms));
+    RET(ensure(&oc.ws, &oc.ws_bytes, std::max<size_t>(16, wsf * 4)));
     size_t tkb = oc.tk_n * 4;
-    RET(ensure((void**)&oc.tk, &tkb, (size_t)gemm_grid_x(w->w.M16) * 4));
+    RET(ensure((void**)&oc.tk, &tkb, (size_t)std::max(gemm_grid_x(w->w.M16), w->w.MT) * 4));
     oc.tk_n = tkb / 4;
-    launch_to_xfrag(xin, (int)w->n, (int)w->n, batch, oc.xf, st);
-    launch_q8_gemm(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, epi_store(y, (int)w->w.M, w->w.M), w->num_sms, st);
+    size_t errb = oc.err ? 16 : 0;
+    RET(ensure((void**)&oc.err, &errb, 16));
+    const ActOut in = act_out(oc.xf, (int)w->n, batch, tc);
+    launch_to_act(xin, (int)w->n, (int)w->n, batch, in, st);
+    const GemmEpi ep = epi_store(y, (int)w->w.M, w->w.M);
+    if (tc) {
+        if (launch_q8_umma(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, oc.err, ep, w->num_sms, st))
+            return seterr(AB2_ERR_CUDA, "tcgen05 GEMM: could not set its shared-memory size");
+    } else {
+        launch_q8_gemm(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, ep, w->num_sms, st);
+    }
     CK(cudaGetLastError());
+    return 0;
+}
+
+// device error word of the op-level calls on the current device (tcgen05 wait timeouts)
+AB2_API int ab2_op_error(uint32_t* code) {
+    if (!code) return seterr(AB2_ERR_ARG, "null argument");
+    int dev;
+    CK(cudaGetDevice(&dev));
+    OpCache& oc = g_ops[dev & 63];
+    std::lock_guard<std::mutex> lk(oc.mu);
+    *code = 0;
+    if (!oc.err) return 0;
+    CK(cudaDeviceSynchronize());
+    CK(cudaMemcpy(code, oc.err, 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemset(oc.err, 0, 4));
     return 0;
 }
 
@@ -1288,8 +1375,7 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
     p.chunk = chunk;
     p.ws = (float*)oc.ws;
     p.tickets = oc.tk;
-    p.xf_out = oc.xf;
-    p.xs = xfrag_shape(Hq * hd, B);
+    p.out = act_out(oc.xf, Hq * hd, B, false);
     p.o_out = out;
     if (launch_attention(p, B, hd, kv_bf16 != 0, max_len, st)) return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
     CK(cudaGetLastError());

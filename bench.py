@@ -231,7 +231,9 @@ def run_ours(args):
     ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap, kv_bf16=True)
     cfg = ctx.config
     ctx.seed_state(seed=1 + rank, n_slots=B, n_tokens=args.ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
-    stream = torch.cuda.current_stream()
+    # an explicit stream: every kernel of the step and the timing events share it
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
     tok = [torch.from_numpy(synth.seeded_tokens(B, cfg["vocab"], seed=2 + rank)).cuda(),
            torch.empty(B, dtype=torch.int32, device="cuda")]
     logits = torch.empty((B, cfg["vocab"]), dtype=torch.float32, device="cuda")

@@ -103,6 +103,10 @@ int ab2_decode_step(ab2_ctx* ctx, const int32_t* tokens, int batch, float* logit
  * stream) without synchronising. tokens_dev may alias next_dev of the previous step. */
 int ab2_decode_step_device(ab2_ctx* ctx, const int32_t* tokens_dev, int batch, float* logits_dev,
                            int32_t* next_dev, void* stream);
+/* Wait for all work of the context (including ab2_decode_step_device calls) and report a
+ * tensor-core pipeline timeout recorded by the device, if any. No reference counterpart:
+ * the Metal path waits with wait_until_completed (crates/engine/src/gpu_full_decode.rs:1031). */
+int ab2_sync(ab2_ctx* ctx);
 /* Kernel launches per decode step of `batch` sequences (for launch accounting). */
 int ab2_launches_per_step(ab2_ctx* ctx, int batch, int64_t* out);
 /* Per-kernel-class device time: enable recording CUDA events around every launch
@@ -129,6 +133,11 @@ void ab2_q8_destroy(ab2_q8* w);
  * Replaces q8_gemv (crates/engine/src/q8_gemv.rs:130) and encode_gemv_prealloc
  * (crates/engine/src/gpu_full_decode.rs:1048). stream may be NULL (legacy default). */
 int ab2_q8_gemv(ab2_q8* w, const float* x, int batch, float* y, void* stream);
+/* Batches of 9 or more run on the tcgen05 path, whose f16 weights are q*d rounded once
+ * (relative error <= 2^-11 per weight); smaller batches keep the weights exact. */
+/* Synchronise the current device and return (then clear) the error word of the op-level
+ * tensor-core calls: 0, or the code of a pipeline wait that timed out. */
+int ab2_op_error(uint32_t* code);
 /* The packed tensor expanded back to f32 [m][n] (exact). */
 int ab2_q8_unpack(ab2_q8* w, float* out, void* stream);
 /* n_blocks raw Q8_0 blocks (device) -> f32 (device), bit-exact with dequant_q8_0_block

@@ -66,6 +66,17 @@ def cuda():
     return torch
 
 
+def argmax_consistent(got_idx: int, ref_logits, got_logits) -> bool:
+    """The device's greedy pick equals the reference's, or the two candidates are closer in
+    the reference logits than the observed logit error (a near-tie the tolerance allows)."""
+    ref = np.asarray(ref_logits, dtype=np.float64)
+    want = int(np.argmax(ref))
+    if got_idx == want or (ref[got_idx] == ref[want]):
+        return True
+    err = float(np.max(np.abs(np.asarray(got_logits, dtype=np.float64) - ref)))
+    return ref[want] - ref[got_idx] <= 2.0 * err
+
+
 def rel_err(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)

@@ -8,15 +8,22 @@ from test_oracle_golden import kat_blocks_par, kats
 
 pytestmark = pytest.mark.gpu
 
-# the GEMV/GEMM result tolerance: max|diff| <= TOL * max|y_ref| per batch row
+# the GEMV/GEMM result tolerance: max|diff| <= tol * max|y_ref| per batch row.
+# Batches <= 8 (mma.sync path) keep the weights exact and the activations as an f16 hi/lo
+# pair; batches >= 9 (tcgen05 path) round each weight q*d and each activation to f16 once.
 TOL = 1e-5
+TC_TOL = 3e-3
+
+
+def tol(batch):
+    return TOL if batch <= 8 else TC_TOL
 
 
 def random_blocks(rng, nb, with_specials=True):
     b = np.empty((nb, 34), dtype=np.uint8)
     b[:, 2:] = rng.integers(-128, 128, size=(nb, 32)).astype(np.int8).view(np.uint8)
     d = np.abs(rng.normal(0, 0.01, size=nb)).astype(np.float16)
-    if with_specials:
+    if with_specials and nb >= 4:
         d[0] = 0
         d[1] = np.float16(-0.5)
         d[2] = np.float16(6e-8)     # subnormal
@@ -50,7 +57,7 @@ def test_repack_round_trip_bit_exact(pkg, oracle, cuda, m, n):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("batch", [1, 3, 8])
+@pytest.mark.parametrize("batch", [1, 3, 8, 9, 16, 32, 64])
 def test_gemv_reference_kat_exact(pkg, cuda, batch):
     # q8_gemv.rs:283-314 inputs; every partial sum is an exact integer so the result is exact
     torch = cuda
@@ -62,7 +69,8 @@ def test_gemv_reference_kat_exact(pkg, cuda, batch):
     torch.cuda.synchronize()
     exp = np.array(kats()["q8_gemv_par"]["expected"], dtype=np.float32)
     for b in range(batch):
-        assert np.array_equal(y[b].cpu().numpy(), exp)
+        assert np.array_equal(y[b].cpu().numpy(), exp), b
+    assert pkg.op_error() == 0
 
 
 SHAPES = [(6144, 2048), (2048, 6144), (4096, 2048), (151936, 2048), (16, 2048), (8224, 2048)]
@@ -84,7 +92,8 @@ def test_gemv_matches_oracle(pkg, oracle, synth, cuda, m, n, batch):
     rows = range(batch) if batch <= 4 else (0, batch // 2, batch - 1)
     for b in rows:
         ref = oracle.q8_gemv(blocks, m, n, x[b])
-        assert rel_err(yg[b], ref) < TOL, (b, rel_err(yg[b], ref))
+        assert rel_err(yg[b], ref) < tol(batch), (b, rel_err(yg[b], ref))
+    assert pkg.op_error() == 0
 
 
 @pytest.mark.parametrize("batch", [2, 4, 5, 9, 16, 33, 64])
@@ -102,7 +111,8 @@ def test_gemm_all_batch_modes(pkg, oracle, synth, cuda, batch):
     W = synth.dequant_q8_0(blocks).reshape(m, n).astype(np.float64)
     ref = x.astype(np.float64) @ W.T
     for b in range(batch):
-        assert rel_err(yg[b], ref[b]) < TOL, b
+        assert rel_err(yg[b], ref[b]) < tol(batch), (b, rel_err(yg[b], ref[b]))
+    assert pkg.op_error() == 0
 
 
 def test_gemv_rejects_bad_batch(pkg, synth, cuda):
