@@ -7,7 +7,24 @@
 
 namespace ab2 {
 
-// A Q8_0 weight in the packed device layout described in common.cuh.
+// Launch with programmatic stream serialization so the kernel can start (and prefetch what
+// does not depend on its predecessor) while the previous kernel on the stream finishes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // A Q8_0 weight on the device, in one or both packed layouts:
 //   q8p (qs, d): mma.sync fragment order, used for batches <= 8 (exact weights);
 //   q8t (qt):    128-row x 64-col tiles for the tcgen05 GEMM, used for larger batches:
@@ -53,16 +70,18 @@ void launch_embed(const Q8Weight& w, int vocab, const int32_t* tokens, int batch
 
 // q8_umma.cu
 int umma_npad(int batch);
-int umma_nsplit(int MT, int KT, int num_sms);
-size_t umma_ws_floats(int MT, int KT, int num_sms);
+// K splits of the tcgen05 GEMM; with more than one split the epilogue adds into y, so a
+// STORE-mode output must be zeroed first
+int umma_nsplit(int MT, int KT, int mode, int num_sms);
 void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
                        int64_t stride, cudaStream_t st);
-int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, float* ws, unsigned* tickets, unsigned* err,
-                   const GemmEpi& ep, int num_sms, cudaStream_t st);
+int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
+                   cudaStream_t st);
 
 // misc.cu
+// zero (optional): rows [0, batch) x [0, zero_n) of zero_ptr (leading dim zero_ld) are cleared
 void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
-                        cudaStream_t st);
+                        cudaStream_t st, float* zero_ptr = nullptr, int zero_ld = 0, int zero_n = 0);
 void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st);
 void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st);
 void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st);
@@ -112,7 +131,15 @@ struct AttnParams {
     unsigned* tickets;   // [B*Hkv]
     ActOut out;          // activations of the wo GEMM (K = Hq*HD)
     float* o_out;        // optional f32 copy [B][Hq*HD]
+    unsigned* err = nullptr;  // pipeline error word (tensor-core kernel)
 };
+// attn_mma.cu: tensor-core flash-decode over a bf16 cache read through two TMA tensor maps
+// (K and V viewed as [rows][hd]); row_base = row of (first slot, kv head 0, token 0)
+int make_kv_tensor_map(void* map_out /*128 bytes, 64-aligned*/, void* base, int64_t rows, int hd);
+int attn_mma_chunk(int batch, int hkv, int max_len, int num_sms);
+int attn_mma_nsplit_bound(int batch, int hkv, int cap, int num_sms);
+int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,
+                         int max_len, cudaStream_t st);
 int attn_nsplit(int max_len, int chunk);
 int attn_chunk(int batch, int hkv, int max_len, int num_sms);
 int attn_nsplit_bound(int batch, int hkv, int cap, int num_sms);

@@ -7,9 +7,14 @@ namespace ab2 {
 // out = x * (1 / sqrt(mean(x^2) + eps)) * w, written as activation fragments for the next
 // GEMM (rmsnorm_vec, crates/cli/src/main.rs:1106-1113). One CTA per batch row.
 __global__ void __launch_bounds__(256) rmsnorm_act_kernel(const float* __restrict__ x, int ldx,
-                                                          const float* __restrict__ w, int D, float eps, ActOut out) {
+                                                          const float* __restrict__ w, int D, float eps, ActOut out,
+                                                          float* __restrict__ zero_ptr, int zero_ld, int zero_n) {
     __shared__ float red[8];
     const int b = blockIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (zero_ptr)
+        for (int i = threadIdx.x; i < zero_n; i += 256) zero_ptr[(size_t)b * zero_ld + i] = 0.0f;
     const float* xb = x + (size_t)b * ldx;
     float ss = 0.0f;
     for (int i = threadIdx.x; i < D; i += 256) ss += xb[i] * xb[i];
@@ -71,8 +76,8 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
 }
 
 void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
-                        cudaStream_t st) {
-    rmsnorm_act_kernel<<<batch, 256, 0, st>>>(x, ldx, w, D, eps, out);
+                        cudaStream_t st, float* zero_ptr, int zero_ld, int zero_n) {
+    launch_pdl(rmsnorm_act_kernel, dim3(batch), dim3(256), 0, st, x, ldx, w, D, eps, out, zero_ptr, zero_ld, zero_n);
 }
 
 void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st) {

@@ -1,17 +1,22 @@
 // q8_umma.cu -- batched Q8_0 dequant-GEMM on the 5th-generation tensor cores (tcgen05).
 //
-// D[128 rows][N] = W[128 rows][K] * X[N][K]^T per CTA (N = batch padded to 16/32/64):
-//   * warp 0 streams each 128x64 weight tile (int8 + f16 scales, 8.5 KB, contiguous in the
-//     "q8t" layout) and the matching 64-wide activation tile (already in the swizzled smem
-//     image, the "x16" layout) into a 3-stage ring with cp.async.bulk + mbarrier tx counts;
-//   * warps 2-5 turn each weight tile into the f16 A operand (w = q * d rounded once to f16;
-//     q is exact in f16 and the product is one correctly rounded f16 multiply) in the
-//     K-major 128B-swizzled layout, then fence the writes to the async proxy;
-//   * warp 1 allocates the TMEM accumulator and one lane issues tcgen05.mma (M=128, N, K=16)
-//     x4 per tile, committing each stage back to the producer;
-//   * after the K loop warps 2-5 read their 32-lane TMEM quarter and run the epilogue
-//     (store / residual add / SwiGLU into the next GEMM's activations), or write split-K
-//     partials that the last CTA of the m-tile sums in split order.
+// D[128 rows][N] = W[128 rows][K-range] * X[N][K-range]^T per CTA (N = batch padded to
+// 16/32/64), with the accumulator in TMEM:
+//   * warp 0 streams the 128x64 weight tiles (int8 + f16 scales, 8.5 KB each, contiguous in
+//     the "q8t" layout) into an 8-deep ring with cp.async.bulk. Weights never depend on the
+//     previous kernel, so under programmatic dependent launch this ring fills while the
+//     predecessor is still running;
+//   * warp 10 waits for the predecessor (griddepcontrol.wait) and streams the matching
+//     activation tiles (already the swizzled shared-memory image, the "x16" layout);
+//   * warps 2-9 turn each weight tile into the f16 A operand (w = q * d, one correctly
+//     rounded f16 multiply of exact f16 values) in the K-major 128B-swizzled layout, release
+//     the weight stage, fence the writes to the async proxy and hand the operand stage on
+//     (a 4-deep A/B ring, so MMA completion latency stays off the critical path);
+//   * warp 1 allocates TMEM and one lane issues tcgen05.mma (M=128, N, K=16) x4 per tile,
+//     committing each operand stage back to its producers;
+//   * warps 2-9 then read their TMEM lane quarter (half the columns each) and run the epilogue. With K split
+//     across CTAs the partial sums are added with red.global.add into the residual stream
+//     (or into an output the caller has zeroed); SwiGLU is never split.
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code, drains its
 // own copies and MMAs (again bounded), frees its TMEM and returns.
 #include "common.cuh"
@@ -23,8 +28,10 @@ namespace ab2 {
 constexpr int kTileRows = 128;
 constexpr int kTileK = 64;
 constexpr int kWTileBytes = 8192 + 512;  // [4 chunks][128 rows][16 B] int8 + [128 rows][2] f16
-constexpr int kStages = 3;        // ~99 KB smem: two CTAs per SM
-constexpr int kUmmaThreads = 192;        // warp 0 producer, warp 1 MMA, warps 2-5 convert + epilogue
+constexpr int kWStages = 8;              // raw weight ring (70 KB)
+constexpr int kAStages = 4;              // f16 operand ring, A and B tiles (96 KB at N = 64)
+constexpr int kWarpW = 0, kWarpMma = 1, kWarpConv0 = 2, kConvWarps = 8, kWarpB = 10;
+constexpr int kUmmaThreads = 11 * 32;    // weights, MMA, 8 x convert + epilogue, activations
 
 // ------------------------------------------------------------------------------ repack
 // one thread per source (row, Q8_0 block): row -> dst row R = base + (row/grp)*stride + row%grp,
@@ -58,83 +65,106 @@ void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, in
 }
 
 // ------------------------------------------------------------------------------ kernel
-struct UmmaSmem {
-    // offsets from the 1024-aligned dynamic smem base
+struct UmmaSmem {  // offsets from the 1024-aligned dynamic shared-memory base
     static constexpr int a_off(int s) { return s * 16384; }
-    static constexpr int b_off(int s, int N) { return kStages * 16384 + s * N * 128; }
-    static constexpr int w_off(int s, int N) { return kStages * 16384 + kStages * N * 128 + s * kWTileBytes; }
-    static constexpr int bar_off(int N) { return w_off(kStages, N); }
-    // full[S], conv[S], freed[S], acc, + tmem slot
-    static constexpr int bytes(int N) { return bar_off(N) + (3 * kStages + 1) * 8 + 16; }
+    static constexpr int b_off(int s, int N) { return kAStages * 16384 + s * N * 128; }
+    static constexpr int w_off(int s, int N) { return kAStages * (16384 + N * 128) + s * kWTileBytes; }
+    static constexpr int bar_off(int N) { return w_off(kWStages, N); }
+    // w_full[W], w_free[W], a_full[A], b_full[A], ab_free[A], acc, tmem slot
+    static constexpr int n_bars() { return 2 * kWStages + 3 * kAStages + 1; }
+    static constexpr int bytes(int N) { return bar_off(N) + n_bars() * 8 + 16; }
 };
 
 template <int N>
-__global__ void __launch_bounds__(kUmmaThreads, 2)
-    q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, int KT, int MT, const uint8_t* __restrict__ x16, int batch,
-                        int kt_per_split, float* __restrict__ ws, unsigned* __restrict__ tickets,
-                        unsigned* __restrict__ err, GemmEpi ep) {
+__global__ void __launch_bounds__(kUmmaThreads, 1)
+    q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, int KT, const uint8_t* __restrict__ x16, int batch,
+                        int kt_per_split, unsigned* __restrict__ err, GemmEpi ep) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + UmmaSmem::bar_off(N));
-    uint64_t* conv = full + kStages;
-    uint64_t* freed = conv + kStages;
-    uint64_t* accb = freed + kStages;
+    uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + UmmaSmem::bar_off(N));
+    uint64_t* w_free = w_full + kWStages;
+    uint64_t* a_full = w_free + kWStages;
+    uint64_t* b_full = a_full + kAStages;
+    uint64_t* ab_free = b_full + kAStages;
+    uint64_t* accb = ab_free + kAStages;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
     __shared__ int s_abort;
-    __shared__ unsigned s_last;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = blockIdx.x, split = blockIdx.y, nsplit = gridDim.y;
     const int kt0 = split * kt_per_split, kt1 = min(KT, kt0 + kt_per_split);
     const int ntiles = kt1 - kt0;
     constexpr uint32_t kCols = N < 32 ? 32 : N;
+    constexpr int kConvThreads = kConvWarps * 32;
 
     if (threadIdx.x == 0) {
         s_abort = 0;
-        for (int s = 0; s < kStages; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&conv[s], 128);
-            mbar_init(&freed[s], 1);
+        for (int s = 0; s < kWStages; s++) {
+            mbar_init(&w_full[s], 1);
+            mbar_init(&w_free[s], kConvThreads);
+        }
+        for (int s = 0; s < kAStages; s++) {
+            mbar_init(&a_full[s], kConvThreads);
+            mbar_init(&b_full[s], 1);
+            mbar_init(&ab_free[s], 1);
         }
         mbar_init(accb, 1);
         mbar_fence_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, kCols);
+    if (warp == kWarpMma) tmem_alloc(tmem_slot, kCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_trigger();
 
-    if (warp == 0) {
-        // ---------------- producer
+    if (warp == kWarpW) {
+        // ---------------- weight producer (independent of the predecessor kernel)
         if (lane == 0) {
-            const uint8_t* wsrc = wt + ((size_t)mt * KT) * kWTileBytes;
+            const uint8_t* wsrc = wt + ((size_t)mt * KT + kt0) * kWTileBytes;
             int i = 0;
             for (; i < ntiles; i++) {
-                const int s = i % kStages;
-                if (i >= kStages && !mbar_wait(&freed[s], ((i / kStages) - 1) & 1)) {
+                const int s = i % kWStages;
+                if (i >= kWStages && !mbar_wait(&w_free[s], ((i / kWStages) - 1) & 1)) {
                     atomicOr(err, 1u);
                     s_abort = 1;
                     break;
                 }
                 if (*(volatile int*)&s_abort) break;
-                mbar_arrive_expect_tx(&full[s], kWTileBytes + N * 128);
-                bulk_g2s(smem + UmmaSmem::w_off(s, N), wsrc + (size_t)(kt0 + i) * kWTileBytes, kWTileBytes, &full[s]);
-                bulk_g2s(smem + UmmaSmem::b_off(s, N), x16 + (size_t)(kt0 + i) * N * 128, N * 128, &full[s]);
+                mbar_arrive_expect_tx(&w_full[s], kWTileBytes);
+                bulk_g2s(smem + UmmaSmem::w_off(s, N), wsrc + (size_t)i * kWTileBytes, kWTileBytes, &w_full[s]);
             }
-            // drain: the last min(i, S) issued stages must have landed before the CTA exits
-            for (int j = max(0, i - kStages); j < i; j++)
-                if (!mbar_wait(&full[j % kStages], (j / kStages) & 1)) atomicOr(err, 2u);
+            for (int j = max(0, i - kWStages); j < i; j++)  // issued copies land before exit
+                if (!mbar_wait(&w_full[j % kWStages], (j / kWStages) & 1)) atomicOr(err, 2u);
         }
-    } else if (warp == 1) {
+    } else if (warp == kWarpB) {
+        // ---------------- activation producer (after the predecessor has completed)
+        if (lane == 0) {
+            pdl_wait();
+            int i = 0;
+            for (; i < ntiles; i++) {
+                const int s = i % kAStages;
+                if (i >= kAStages && !mbar_wait(&ab_free[s], ((i / kAStages) - 1) & 1)) {
+                    atomicOr(err, 4u);
+                    s_abort = 1;
+                    break;
+                }
+                if (*(volatile int*)&s_abort) break;
+                mbar_arrive_expect_tx(&b_full[s], N * 128);
+                bulk_g2s(smem + UmmaSmem::b_off(s, N), x16 + (size_t)(kt0 + i) * N * 128, N * 128, &b_full[s]);
+            }
+            for (int j = max(0, i - kAStages); j < i; j++)
+                if (!mbar_wait(&b_full[j % kAStages], (j / kAStages) & 1)) atomicOr(err, 8u);
+        }
+    } else if (warp == kWarpMma) {
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(kTileRows, N);
-            int i = 0;
-            for (; i < ntiles; i++) {
-                const int s = i % kStages;
-                if (!mbar_wait(&conv[s], (i / kStages) & 1)) {
-                    atomicOr(err, 4u);
+            for (int i = 0; i < ntiles; i++) {
+                const int s = i % kAStages;
+                const uint32_t ph = (i / kAStages) & 1;
+                if (!mbar_wait(&a_full[s], ph) || !mbar_wait(&b_full[s], ph)) {
+                    atomicOr(err, 16u);
                     s_abort = 1;
                     break;
                 }
@@ -146,136 +176,111 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
                 for (int k = 0; k < kTileK / 16; k++)
                     umma_f16(tmem, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), idesc,
                              (i > 0 || k > 0) ? 1u : 0u);
-                umma_commit(&freed[s]);
+                umma_commit(&ab_free[s]);
             }
             umma_commit(accb);  // arrives once every MMA issued above has completed
         }
     } else {
-        // ---------------- converters (warps 2-5): row r of the 128-row tile
-        const int q = warp & 3;
-        const int r = q * 32 + lane;
+        // ---------------- converters (warps 2..9): row r of the tile, 16-column chunks 2h, 2h+1
+        const int r = (warp & 3) * 32 + lane;
+        const int h = (warp - kWarpConv0) >> 2;
         for (int i = 0; i < ntiles; i++) {
-            const int s = i % kStages;
-            if (!mbar_wait(&full[s], (i / kStages) & 1)) {
-                atomicOr(err, 8u);
+            const int sw = i % kWStages, sa = i % kAStages;
+            if (!mbar_wait(&w_full[sw], (i / kWStages) & 1) ||
+                (i >= kAStages && !mbar_wait(&ab_free[sa], ((i / kAStages) - 1) & 1))) {
+                atomicOr(err, 32u);
                 s_abort = 1;
                 break;
             }
             if (*(volatile int*)&s_abort) break;
-            const uint8_t* wb = smem + UmmaSmem::w_off(s, N);
-            uint8_t* ab = smem + UmmaSmem::a_off(s);
-            const uint32_t dd = *reinterpret_cast<const uint32_t*>(wb + 8192 + r * 4);
-            const __half2 d0 = __halves2half2(__ushort_as_half((unsigned short)(dd & 0xffffu)),
-                                              __ushort_as_half((unsigned short)(dd & 0xffffu)));
-            const __half2 d1 = __halves2half2(__ushort_as_half((unsigned short)(dd >> 16)),
-                                              __ushort_as_half((unsigned short)(dd >> 16)));
-            uint8_t* arow = ab + (r >> 3) * 1024 + (r & 7) * 128;
+            const uint8_t* wb = smem + UmmaSmem::w_off(sw, N);
+            uint4 qv[2];
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const uint4 qv = *reinterpret_cast<const uint4*>(wb + ((size_t)c * kTileRows + r) * 16);
-                const __half2 dh = c < 2 ? d0 : d1;
-                uint32_t h[8];
-                h[0] = q8_pair_to_h2<0x4140>(qv.x);
-                h[1] = q8_pair_to_h2<0x4342>(qv.x);
-                h[2] = q8_pair_to_h2<0x4140>(qv.y);
-                h[3] = q8_pair_to_h2<0x4342>(qv.y);
-                h[4] = q8_pair_to_h2<0x4140>(qv.z);
-                h[5] = q8_pair_to_h2<0x4342>(qv.z);
-                h[6] = q8_pair_to_h2<0x4140>(qv.w);
-                h[7] = q8_pair_to_h2<0x4342>(qv.w);
+            for (int c = 0; c < 2; c++)
+                qv[c] = *reinterpret_cast<const uint4*>(wb + ((size_t)(2 * h + c) * kTileRows + r) * 16);
+            const uint32_t dd = *reinterpret_cast<const uint32_t*>(wb + 8192 + r * 4);
+            mbar_arrive(&w_free[sw]);  // the raw weight stage has been read
+            const unsigned short dbits = (unsigned short)(h ? (dd >> 16) : (dd & 0xffffu));
+            const __half2 dh = __halves2half2(__ushort_as_half(dbits), __ushort_as_half(dbits));
+            uint8_t* arow = smem + UmmaSmem::a_off(sa) + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                uint32_t hv[8];
+                hv[0] = q8_pair_to_h2<0x4140>(qv[c].x);
+                hv[1] = q8_pair_to_h2<0x4342>(qv[c].x);
+                hv[2] = q8_pair_to_h2<0x4140>(qv[c].y);
+                hv[3] = q8_pair_to_h2<0x4342>(qv[c].y);
+                hv[4] = q8_pair_to_h2<0x4140>(qv[c].z);
+                hv[5] = q8_pair_to_h2<0x4342>(qv[c].z);
+                hv[6] = q8_pair_to_h2<0x4140>(qv[c].w);
+                hv[7] = q8_pair_to_h2<0x4342>(qv[c].w);
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    __half2 x = *reinterpret_cast<__half2*>(&h[e]);
+                    __half2 x = *reinterpret_cast<__half2*>(&hv[e]);
                     x = __hmul2(x, dh);
-                    h[e] = *reinterpret_cast<uint32_t*>(&x);
+                    hv[e] = *reinterpret_cast<uint32_t*>(&x);
                 }
-                const int j0 = 2 * c, j1 = 2 * c + 1;
-                *reinterpret_cast<uint4*>(arow + ((j0 ^ (r & 7)) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
-                *reinterpret_cast<uint4*>(arow + ((j1 ^ (r & 7)) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+                const int j0 = 4 * h + 2 * c, j1 = j0 + 1;  // 8-column chunks of the 64-wide row
+                *reinterpret_cast<uint4*>(arow + ((j0 ^ (r & 7)) << 4)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+                *reinterpret_cast<uint4*>(arow + ((j1 ^ (r & 7)) << 4)) = make_uint4(hv[4], hv[5], hv[6], hv[7]);
             }
             fence_proxy_async_smem();
-            mbar_arrive(&conv[s]);
+            mbar_arrive(&a_full[sa]);
         }
     }
 
-    // ---------------- epilogue: warps 2-5 hold rows q*32 + lane
-    float v[N];
-    const bool epi = warp >= 2;
-    bool have = false;
+    // ---------------- epilogue: converter warps; row q*32 + lane, columns [h*N/2, (h+1)*N/2)
+    constexpr int CPH = N / 2;
+    float v[CPH];
+    const bool epi = warp >= kWarpConv0 && warp < kWarpConv0 + kConvWarps;
+    const int h = epi ? (warp - kWarpConv0) >> 2 : 0;
     if (epi) {
         const int q = warp & 3;
-        if (!*(volatile int*)&s_abort && ntiles > 0) {
+        if (!*(volatile int*)&s_abort) {
             if (mbar_wait(accb, 0)) {
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < N; c += 16) tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c, v + c);
-                have = true;
+                for (int c = 0; c < CPH; c += 8)
+                    tmem_ld8(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * CPH + c), v + c);
             } else {
-                atomicOr(err, 16u);
+                atomicOr(err, 64u);
                 s_abort = 1;
             }
-        } else if (ntiles <= 0) {
-#pragma unroll
-            for (int c = 0; c < N; c++) v[c] = 0.0f;
-            have = true;
         }
     }
-    // the MMA warp waits (bounded) for its own MMAs before TMEM is released
-    if (warp == 1 && lane == 0 && *(volatile int*)&s_abort && ntiles > 0) {
-        if (!mbar_wait(accb, 0)) atomicOr(err, 32u);
+    // the MMA lane waits (bounded) for its own MMAs before TMEM is released
+    if (warp == kWarpMma && lane == 0 && *(volatile int*)&s_abort) {
+        if (!mbar_wait(accb, 0)) atomicOr(err, 128u);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kWarpMma) {
         tc_fence_after();
         tmem_dealloc(tmem, kCols);
         tmem_relinquish();
     }
-    if (s_abort) return;
+    if (s_abort || !epi) return;
+    pdl_wait();  // outputs may be read or written by earlier kernels of the stream
 
     const int r = (warp & 3) * 32 + lane;
-    if (nsplit > 1) {
-        if (epi && have) {
-#pragma unroll
-            for (int c = 0; c < N; c++) __stcg(&ws[(((size_t)split * MT + mt) * N + c) * kTileRows + r], v[c]);
-        }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const unsigned prev = atomicAdd(&tickets[mt], 1u);
-            s_last = (prev == (unsigned)nsplit - 1u) ? 1u : 0u;
-        }
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-        if (epi) {
-#pragma unroll
-            for (int c = 0; c < N; c++) v[c] = 0.0f;
-            for (int sp = 0; sp < nsplit; sp++)
-#pragma unroll
-                for (int c = 0; c < N; c++) v[c] += __ldcg(&ws[(((size_t)sp * MT + mt) * N + c) * kTileRows + r]);
-        }
-        if (threadIdx.x == 0) tickets[mt] = 0u;
-    }
-    if (!epi) return;
-
+    const int c0 = h * CPH;
     if (ep.mode == EPI_SWIGLU) {
         // rows 0..63 of the tile are gate rows, 64..127 the matching up rows (q8t interleave)
-        float* xch = reinterpret_cast<float*>(smem);  // operand buffers are free now
+        float* xch = reinterpret_cast<float*>(smem);  // the operand ring is idle now
         if (r >= 64)
 #pragma unroll
-            for (int c = 0; c < N; c++) xch[c * 64 + (r - 64)] = v[c];
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+            for (int c = 0; c < CPH; c++) xch[(c0 + c) * 64 + (r - 64)] = v[c];
+        asm volatile("bar.sync 1, %0;" ::"n"(kConvThreads) : "memory");
         if (r < 64) {
             const int o = mt * 64 + r;
             if (o < ep.m_out) {
 #pragma unroll
-                for (int c = 0; c < N; c++) {
-                    if (c >= batch) break;
-                    const float g = v[c], u = xch[c * 64 + r];
-                    const float h = (g / (1.0f + expf(-g))) * u;
-                    act_store(ep.out, c, o, h);
-                    if (ep.y) ep.y[(size_t)c * ep.ldy + o] = h;
+                for (int c = 0; c < CPH; c++) {
+                    if (c0 + c >= batch) break;
+                    const float g = v[c], u = xch[(c0 + c) * 64 + r];
+                    const float hval = (g / (1.0f + expf(-g))) * u;
+                    act_store(ep.out, c0 + c, o, hval);
+                    if (ep.y) ep.y[(size_t)(c0 + c) * ep.ldy + o] = hval;
                 }
             }
         }
@@ -284,10 +289,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
     const int m = mt * kTileRows + r;
     if (m >= ep.m_out) return;
 #pragma unroll
-    for (int c = 0; c < N; c++) {
-        if (c >= batch) break;
-        float* yp = ep.y + (size_t)c * ep.ldy + m;
-        if (ep.mode == EPI_RESID)
+    for (int c = 0; c < CPH; c++) {
+        if (c0 + c >= batch) break;
+        float* yp = ep.y + (size_t)(c0 + c) * ep.ldy + m;
+        if (nsplit > 1)
+            atomicAdd(yp, v[c]);  // result unused: compiles to a fire-and-forget reduction
+        else if (ep.mode == EPI_RESID)
             *yp += v[c];
         else
             *yp = v[c];
@@ -297,25 +304,21 @@ __global__ void __launch_bounds__(kUmmaThreads, 2)
 // ------------------------------------------------------------------------------ launcher
 int umma_npad(int batch) { return batch <= 16 ? 16 : (batch <= 32 ? 32 : 64); }
 
-// K splits so that the grid fills the two CTA slots of every SM once, with at least two K
-// tiles per split and at most 8 splits (the last CTA of an m-tile sums the partials)
-int umma_nsplit(int MT, int KT, int num_sms) {
-    int s = (2 * num_sms) / MT;
-    if (s > 8) s = 8;
-    if (s > KT / 2) s = KT / 2;
+// K splits so the grid covers the SMs about once (one CTA per SM), at least 4 K tiles per
+// split and at most 16 splits. SwiGLU epilogues are never split.
+int umma_nsplit(int MT, int KT, int mode, int num_sms) {
+    if (mode == EPI_SWIGLU) return 1;
+    int s = num_sms / MT;
+    if (s > 16) s = 16;
+    if (s > KT / 4) s = KT / 4;
     if (s <= 1) return 1;
     int per = (KT + s - 1) / s;
     return (KT + per - 1) / per;
 }
 
-size_t umma_ws_floats(int MT, int KT, int num_sms) {
-    int ns = umma_nsplit(MT, KT, num_sms);
-    return ns > 1 ? (size_t)ns * MT * 64 * kTileRows : 0;
-}
-
 template <int N>
-static int launch_umma_t(const Q8Weight& w, const uint8_t* x16, int batch, float* ws, unsigned* tickets,
-                         unsigned* err, const GemmEpi& ep, int num_sms, cudaStream_t st) {
+static int launch_umma_t(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep,
+                         int num_sms, cudaStream_t st) {
     const int smem = UmmaSmem::bytes(N) + 1024;
     static bool attr_set[64] = {};  // per template instance and device, before the first launch
     int dev = 0;
@@ -326,19 +329,20 @@ static int launch_umma_t(const Q8Weight& w, const uint8_t* x16, int batch, float
             return -1;
         attr_set[dev & 63] = true;
     }
-    const int ns = umma_nsplit(w.MT, w.KT, num_sms);
+    const int ns = umma_nsplit(w.MT, w.KT, ep.mode, num_sms);
     const int per = (w.KT + ns - 1) / ns;
-    dim3 grid(w.MT, ns);
-    q8_umma_gemm_kernel<N><<<grid, kUmmaThreads, smem, st>>>(w.qt, w.KT, w.MT, x16, batch, per, ws, tickets, err, ep);
+    if (launch_pdl(q8_umma_gemm_kernel<N>, dim3(w.MT, ns), dim3(kUmmaThreads), smem, st, w.qt, w.KT, x16, batch,
+                   per, err, ep) != cudaSuccess)
+        return -2;
     return 0;
 }
 
-int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, float* ws, unsigned* tickets, unsigned* err,
-                   const GemmEpi& ep, int num_sms, cudaStream_t st) {
+int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
+                   cudaStream_t st) {
     switch (umma_npad(batch)) {
-        case 16: return launch_umma_t<16>(w, x16, batch, ws, tickets, err, ep, num_sms, st);
-        case 32: return launch_umma_t<32>(w, x16, batch, ws, tickets, err, ep, num_sms, st);
-        default: return launch_umma_t<64>(w, x16, batch, ws, tickets, err, ep, num_sms, st);
+        case 16: return launch_umma_t<16>(w, x16, batch, err, ep, num_sms, st);
+        case 32: return launch_umma_t<32>(w, x16, batch, err, ep, num_sms, st);
+        default: return launch_umma_t<64>(w, x16, batch, err, ep, num_sms, st);
     }
 }
 

@@ -372,6 +372,8 @@ struct ab2_ctx {
     float2* rope = nullptr;     // [cap][rot/2]
     float* tmp_out = nullptr;   // [D] for per-layer entry points
     unsigned* err_d = nullptr;  // tensor-core pipeline error word (0 = ok)
+    alignas(64) uint8_t tmap_k[128];  // TMA tensor maps over the bf16 K / V caches ([rows][hd])
+    alignas(64) uint8_t tmap_v[128];
     bool use_umma = false;      // max_batch >= kUmmaMinBatch: q8t weights are packed too
     // pinned host staging
     int32_t *tok_h = nullptr, *next_h = nullptr;
@@ -572,10 +574,6 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     auto acc_gemm = [&](const Q8Weight& w) {
         gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, B, x->num_sms));
         gtk = std::max(gtk, gemm_grid_x(w.M16));
-        if (x->use_umma) {
-            gws = std::max(gws, umma_ws_floats(w.MT, w.KT, x->num_sms));
-            gtk = std::max(gtk, w.MT);
-        }
     };
     for (auto& L : x->layers) {
         acc_gemm(L.w_in);
@@ -588,10 +586,17 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     RET(x->dalloc(&x->gtk, (size_t)gtk * 4));
     if (c.n_attn > 0) {
         size_t aws = 0;
-        for (int b = 1; b <= B; b++)
-            aws = std::max(aws, attn_ws_floats(b, (int)Hkv, attn_nsplit_bound(b, (int)Hkv, x->cap, x->num_sms),
-                                               (int)hd, (int)(Hq / Hkv)));
+        for (int b = 1; b <= B; b++) {
+            const int ns = x->kv_bf16 ? attn_mma_nsplit_bound(b, (int)Hkv, x->cap, x->num_sms)
+                                      : attn_nsplit_bound(b, (int)Hkv, x->cap, x->num_sms);
+            aws = std::max(aws, attn_ws_floats(b, (int)Hkv, ns, (int)hd, (int)(Hq / Hkv)));
+        }
         x->aws_floats = aws;
+        if (x->kv_bf16) {
+            const int64_t rows = c.n_attn * (int64_t)B * Hkv * x->cap;
+            if (make_kv_tensor_map(x->tmap_k, x->kc, rows, (int)hd) || make_kv_tensor_map(x->tmap_v, x->vc, rows, (int)hd))
+                return seterr(AB2_ERR_CUDA, "could not encode the TMA tensor maps of the KV cache");
+        }
         RET(x->dalloc(&x->aws, aws * 4));
         RET(x->dalloc(&x->atk, (size_t)B * Hkv * 4));
         // RoPE (cos, sin) table built with the host libm exactly as the reference computes it:
@@ -662,8 +667,8 @@ ActOut act(const ab2_ctx* x, uint8_t* buf, int K, int B) { return act_out(buf, K
 int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st) {
     ProfScope ps(x, PC_GEMM, st);
     if (umma_for(x, B)) {
-        if (launch_q8_umma(w, xf, B, x->gws, x->gtk, x->err_d, ep, x->num_sms, st))
-            return seterr(AB2_ERR_CUDA, "tcgen05 GEMM: could not set its shared-memory size");
+        if (launch_q8_umma(w, xf, B, x->err_d, ep, x->num_sms, st))
+            return seterr(AB2_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     } else {
         launch_q8_gemm(w, xf, B, x->gws, x->gtk, ep, x->num_sms, st);
     }
@@ -734,16 +739,23 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.pos = x->pos_d + s0;
         p.Hq = (int)c.n_heads;
         p.Hkv = (int)c.n_kv;
-        p.chunk = attn_chunk(B, p.Hkv, max_len, x->num_sms);
+        p.chunk = x->kv_bf16 ? attn_mma_chunk(B, p.Hkv, max_len, x->num_sms) : attn_chunk(B, p.Hkv, max_len, x->num_sms);
         if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv) > x->aws_floats)
             return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
         p.ws = x->aws;
         p.tickets = x->atk;
         p.out = act(x, x->xfb, (int)(c.n_heads * c.hd), B);
         p.o_out = nullptr;
+        p.err = x->err_d;
         ProfScope ps(x, PC_ATTN, st);
-        if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st))
+        if (x->kv_bf16) {
+            // bf16 cache: TMA + tensor-core flash-decode; rows of (layer, slot s0, head 0, token 0)
+            const int64_t row_base = ((int64_t)L.local * x->max_batch + s0) * c.n_kv * x->cap;
+            if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, st))
+                return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
+        } else if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st)) {
             return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
+        }
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
     return gemm(x, L.w_out, x->xfb, B, e, st);
@@ -779,8 +791,11 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
     const ActOut xa = act(x, x->xfa, D, B);
     for (auto& L : x->layers) {
         {
+            // a K-split tcgen05 GEMM adds into its STORE output: clear the projection rows
+            const bool zero = umma_for(x, B) && umma_nsplit(L.w_in.MT, L.w_in.KT, EPI_STORE, x->num_sms) > 1;
             ProfScope ps(x, PC_OTHER, st);
-            launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st);
+            launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st, zero ? x->proj : nullptr, x->ldp,
+                               (int)L.w_in.M);
         }
         RET(run_mixer(x, L, 0, B, max_len, x->x, D, EPI_RESID, st));
         {
@@ -1254,10 +1269,10 @@ AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* 
     cudaStream_t st = (cudaStream_t)stream;
     const bool tc = batch >= kUmmaMinBatch;
     RET(ensure((void**)&oc.xf, &oc.xf_bytes, std::max(xfrag_bytes((int)w->n, batch), x16_bytes((int)w->n, batch))));
-    size_t wsf = std::max(gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms), umma_ws_floats(w->w.MT, w->w.KT, w->num_sms));
+    size_t wsf = gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms);
     RET(ensure(&oc.ws, &oc.ws_bytes, std::max<size_t>(16, wsf * 4)));
     size_t tkb = oc.tk_n * 4;
-    RET(ensure((void**)&oc.tk, &tkb, (size_t)std::max(gemm_grid_x(w->w.M16), w->w.MT) * 4));
+    RET(ensure((void**)&oc.tk, &tkb, (size_t)gemm_grid_x(w->w.M16) * 4));
     oc.tk_n = tkb / 4;
     size_t errb = oc.err ? 16 : 0;
     RET(ensure((void**)&oc.err, &errb, 16));
@@ -1265,8 +1280,10 @@ AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* 
     launch_to_act(xin, (int)w->n, (int)w->n, batch, in, st);
     const GemmEpi ep = epi_store(y, (int)w->w.M, w->w.M);
     if (tc) {
-        if (launch_q8_umma(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, oc.err, ep, w->num_sms, st))
-            return seterr(AB2_ERR_CUDA, "tcgen05 GEMM: could not set its shared-memory size");
+        if (umma_nsplit(w->w.MT, w->w.KT, EPI_STORE, w->num_sms) > 1)
+            CK(cudaMemsetAsync(y, 0, (size_t)batch * w->w.M * 4, st));
+        if (launch_q8_umma(w->w, oc.xf, batch, oc.err, ep, w->num_sms, st))
+            return seterr(AB2_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     } else {
         launch_q8_gemm(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, ep, w->num_sms, st);
     }
@@ -1352,8 +1369,10 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
         oc.rope_base = rope_base;
     }
     const int max_len = max_pos + 1;
-    const int chunk = attn_chunk(B, Hkv, max_len, nsm);
+    const int chunk = kv_bf16 ? attn_mma_chunk(B, Hkv, max_len, nsm) : attn_chunk(B, Hkv, max_len, nsm);
     RET(ensure(&oc.ws, &oc.ws_bytes, attn_ws_floats(B, Hkv, attn_nsplit(max_len, chunk), hd, Hq / Hkv) * 4));
+    size_t errb = oc.err ? 16 : 0;
+    RET(ensure((void**)&oc.err, &errb, 16));
     size_t tkb = oc.tk_n * 4;
     RET(ensure((void**)&oc.tk, &tkb, (size_t)B * Hkv * 4));
     oc.tk_n = tkb / 4;
@@ -1377,7 +1396,17 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
     p.tickets = oc.tk;
     p.out = act_out(oc.xf, Hq * hd, B, false);
     p.o_out = out;
-    if (launch_attention(p, B, hd, kv_bf16 != 0, max_len, st)) return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
+    p.err = oc.err;
+    if (kv_bf16) {
+        alignas(64) uint8_t tmk[128], tmv[128];
+        const int64_t rows = (int64_t)B * Hkv * cap;
+        if (make_kv_tensor_map(tmk, k_cache, rows, hd) || make_kv_tensor_map(tmv, v_cache, rows, hd))
+            return seterr(AB2_ERR_ARG, "could not encode TMA tensor maps for the caches (alignment?)");
+        if (launch_attention_mma(tmk, tmv, p, 0, B, hd, max_len, st))
+            return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
+    } else if (launch_attention(p, B, hd, false, max_len, st)) {
+        return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
+    }
     CK(cudaGetLastError());
     return 0;
 }

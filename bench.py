@@ -329,6 +329,69 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- op benchmarks
+def run_op(args):
+    """One op of BASELINE configs 2-4 on cuda:0, timed with CUDA events; one JSON line."""
+    import numpy as np
+    import torch
+    pkg = load_pkg()
+    from ane_infer_b200 import synth
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(0)
+    st = torch.cuda.Stream()
+    torch.cuda.set_stream(st)
+    peak, peak_kind = measured_peaks()
+    B = args.batch
+    if args.op == "gemm":
+        M, K = args.m, args.k
+        w = pkg.Q8Tensor(synth.random_q8_0(rng, M, K, std=0.01), M, K)
+        x = torch.from_numpy(synth.bf16_round(rng.normal(size=(B, K)).astype(np.float32))).cuda()
+        y = torch.empty((B, M), dtype=torch.float32, device="cuda")
+        fn = lambda: pkg.q8_gemv(w, x, y, B, st)
+        nbytes = M * K * 34 // 32 + B * K * 2 + B * M * 4
+        label = f"q8 gemm {M}x{K} batch {B}"
+    elif args.op == "recurrence":
+        H = 16
+        S = torch.from_numpy(rng.normal(0, 0.1, size=(B, H, 128, 128)).astype(np.float32)).cuda()
+        q = torch.randn(B, H, 128, device="cuda").to(torch.bfloat16)
+        k = torch.randn(B, H, 128, device="cuda").to(torch.bfloat16)
+        v = torch.randn(B, H, 128, device="cuda").to(torch.bfloat16)
+        beta = torch.rand(B, H, device="cuda")
+        decay = torch.rand(B, H, device="cuda")
+        o = torch.empty(B, H, 128, device="cuda")
+        fn = lambda: pkg.gated_delta(S, q, k, v, beta, decay, o, B, H, st)
+        nbytes = B * H * (2 * 128 * 128 * 4 + 3 * 128 * 2 + 128 * 4)
+        label = f"gated delta rule B={B} H=16 dk=dv=128"
+    else:
+        Hq, Hkv, hd, ctx = 8, 2, 256, args.ctx
+        cap = ctx + args.iters + args.warmup + 8
+        proj = torch.randn(B, Hq * 2 * hd + 2 * Hkv * hd, device="cuda")
+        kc = torch.randn(B, Hkv, cap, hd, device="cuda").to(torch.bfloat16)
+        vc = torch.randn(B, Hkv, cap, hd, device="cuda").to(torch.bfloat16)
+        pos = torch.full((B,), ctx - 1, dtype=torch.int32, device="cuda")
+        out = torch.empty(B, Hq * hd, device="cuda")
+        fn = lambda: pkg.attn_decode(proj, kc, vc, cap, pos, B, Hq, Hkv, hd, True, None, None, 1e7, 64, ctx - 1,
+                                     out, st)
+        nbytes = B * Hkv * ctx * hd * 2 * 2
+        label = f"gqa flash-decode B={B} ctx={ctx} Hq=8 Hkv=2 hd=256"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(args.iters):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize()
+    if pkg.op_error():
+        raise RuntimeError("tensor-core pipeline timeout")
+    ms = e0.elapsed_time(e1) / args.iters
+    gbs = nbytes / (ms / 1e3) / 1e9
+    print(json.dumps({"op": label, "us_per_launch": round(ms * 1e3, 2), "algorithmic_bytes": nbytes,
+                      "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": peak_kind,
+                      "frac": round(gbs / peak, 4), "iters": args.iters}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -340,10 +403,17 @@ def main():
     ap.add_argument("--strong", action="store_true", help="split --batch across the GPUs instead")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--op", choices=["gemm", "recurrence", "attention"], default=None,
+                    help="time one op (BASELINE configs 2-4) instead of the decode step")
+    ap.add_argument("--m", type=int, default=6144)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--iters", type=int, default=20)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.op:
+        run_op(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
