@@ -381,19 +381,33 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // merge: per-(split, head) weights e = exp(m_s - M) once into shared memory (the K/V ring
+    // is idle now), then every output element sums its splits in split order
     const float* parts = p.ws + (((size_t)b * p.Hkv + kvh) * nsplit) * part_floats;
+    float* e_s = reinterpret_cast<float*>(smem);  // [nsplit][kGQ]
+    float* lsum_s = e_s + nsplit * kGQ;           // [kGQ]
+    if (warp < kGQ) {
+        float M = -INFINITY;
+        for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(parts + s * part_floats + warp));
+        M = warp_max(M);
+        for (int s = lane; s < nsplit; s += 32) {
+            const float ms = __ldcg(parts + s * part_floats + warp);
+            e_s[s * kGQ + warp] = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            float Lsum = 0.0f;
+            for (int s = 0; s < nsplit; s++) Lsum += __ldcg(parts + s * part_floats + kGQ + warp) * e_s[s * kGQ + warp];
+            lsum_s[warp] = Lsum;
+        }
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < kGQ * HD; i += kAttnMmaThreads) {
         const int hh = i / HD, d = i % HD, h = kvh * kGQ + hh;
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(parts + s * part_floats + hh));
-        float Lsum = 0.0f, A = 0.0f;
-        for (int s = 0; s < nsplit; s++) {
-            const float ms = __ldcg(parts + s * part_floats + hh);
-            const float e = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            Lsum += __ldcg(parts + s * part_floats + kGQ + hh) * e;
-            A += __ldcg(parts + s * part_floats + 2 * kGQ + i) * e;
-        }
-        float o = A / Lsum;
+        float A = 0.0f;
+#pragma unroll 8
+        for (int s = 0; s < nsplit; s++) A += __ldcg(parts + s * part_floats + 2 * kGQ + i) * e_s[s * kGQ + hh];
+        float o = A / lsum_s[hh];
         o *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
         act_store(p.out, b, h * HD + d, o);
         if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = o;
@@ -428,19 +442,22 @@ int make_kv_tensor_map(void* map_out, void* base, int64_t rows, int hd) {
     return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-// tokens per split for the tensor-core kernel: about seven CTA waves over the SMs
+// tokens per split for the tensor-core kernel: about seven CTA waves over the SMs, and at
+// least kMinSplitTiles tiles per split so the pipeline fill and the merge stay small
+constexpr int kMinSplitTiles = 4;
 int attn_mma_chunk(int batch, int hkv, int max_len, int num_sms) {
     int pairs = batch * hkv;
     int want = (7 * num_sms + pairs - 1) / pairs;
     if (want < 1) want = 1;
     int chunk = (max_len + want - 1) / want;
     chunk = (chunk + kT - 1) / kT * kT;
-    return chunk < kT ? kT : chunk;
+    return chunk < kMinSplitTiles * kT ? kMinSplitTiles * kT : chunk;
 }
 
+// the split count is at most min(want, ceil(max_len / (kMinSplitTiles * kT)))
 int attn_mma_nsplit_bound(int batch, int hkv, int cap, int num_sms) {
     int want = (7 * num_sms + batch * hkv - 1) / (batch * hkv);
-    int by_len = (cap + kT - 1) / kT;
+    int by_len = (cap + kMinSplitTiles * kT - 1) / (kMinSplitTiles * kT);
     return want < by_len ? want : by_len;
 }
 

@@ -18,14 +18,20 @@ constexpr int kDnThreads = 256;
 // Gated delta rule on one head with the state in registers (deltanet.rs:485-512):
 //   S *= decay; sk = S^T k; delta = beta (v - sk); S += k delta^T; o = S^T q
 // q_s/k_s/v_s are shared [128] vectors; o_s receives the output.
-__device__ __forceinline__ void delta_rule_head(float* __restrict__ S, const float* q_s, const float* k_s,
+// this thread's 16 rows x 4 columns of the head state (rows warp*16.., columns lane*4..)
+__device__ __forceinline__ void load_state(const float* __restrict__ S, float4 s[16]) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int i = 0; i < 16; i++)
+        s[i] = __ldcs(reinterpret_cast<const float4*>(S + (size_t)(warp * 16 + i) * DK + lane * 4));
+}
+
+// s[] holds the state loaded by load_state (issued early so HBM latency overlaps other work)
+__device__ __forceinline__ void delta_rule_head(float4 s[16], float* __restrict__ S, const float* q_s, const float* k_s,
                                                 const float* v_s, float beta, float decay, float* red /*[8][128]*/,
                                                 float* delta_s, float* o_s) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = warp * 16, c0 = lane * 4;
-    float4 s[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) s[i] = __ldcs(reinterpret_cast<const float4*>(S + (size_t)(r0 + i) * DK + c0));
     float4 sk = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < 16; i++) {
@@ -83,6 +89,9 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_fused_kernel(DnParams p) 
     const int h = blockIdx.x, b = blockIdx.y;
     const int D = p.D, H = p.H, K = p.K;
     const float* proj = p.proj + (size_t)b * p.ldp;
+    float* S = p.S + (size_t)b * p.s_stride + (size_t)h * DK * DK;
+    float4 st_regs[16];
+    load_state(S, st_regs);  // 64 KB per CTA in flight while the prologue below runs
 
     // conv_shift_and_append + conv_apply + SiLU (deltanet_cache.rs:34-54, deltanet.rs:444-450)
     for (int c = threadIdx.x; c < 3 * DK; c += kDnThreads) {
@@ -134,8 +143,7 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_fused_kernel(DnParams p) 
     }
     __syncthreads();
 
-    float* S = p.S + (size_t)b * p.s_stride + (size_t)h * DK * DK;
-    delta_rule_head(S, qkv_s[0], qkv_s[1], qkv_s[2], sc[2], sc[3], red, delta_s, o_s);
+    delta_rule_head(st_regs, S, qkv_s[0], qkv_s[1], qkv_s[2], sc[2], sc[3], red, delta_s, o_s);
 
     // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533)
     if (warp == 0) {
@@ -167,13 +175,16 @@ __global__ void __launch_bounds__(kDnThreads) gated_delta_kernel(float* S, const
     __shared__ __align__(16) float delta_s[DK];
     __shared__ __align__(16) float o_s[DK];
     const int bh = blockIdx.y * H + blockIdx.x;
+    float4 st_regs[16];
+    load_state(S + (size_t)bh * DK * DK, st_regs);
     for (int c = threadIdx.x; c < 3 * DK; c += kDnThreads) {
         const int which = c / DK, j = c % DK;
         const uint16_t* src = which == 0 ? q : (which == 1 ? k : v);
         qkv_s[which][j] = __uint_as_float((uint32_t)src[(size_t)bh * DK + j] << 16);
     }
     __syncthreads();
-    delta_rule_head(S + (size_t)bh * DK * DK, qkv_s[0], qkv_s[1], qkv_s[2], beta[bh], decay[bh], red, delta_s, o_s);
+    delta_rule_head(st_regs, S + (size_t)bh * DK * DK, qkv_s[0], qkv_s[1], qkv_s[2], beta[bh], decay[bh], red, delta_s,
+                    o_s);
     if (threadIdx.x < DK) o[(size_t)bh * DK + threadIdx.x] = o_s[threadIdx.x];
 }
 

@@ -84,6 +84,10 @@ void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float ep
                         cudaStream_t st, float* zero_ptr = nullptr, int zero_ld = 0, int zero_n = 0);
 void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st);
 void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st);
+// argmax split over nch chunks per row (part: [batch][nch] scratch), same tie rule
+constexpr int kArgmaxChunks = 32;
+void launch_argmax2(const float* logits, int ld, int V, int batch, int32_t* out, int2* part, int nch,
+                    cudaStream_t st);
 void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st);
 void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st);
 void launch_seed_kv(void* dst, bool bf16, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,

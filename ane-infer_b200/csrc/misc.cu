@@ -75,6 +75,80 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     }
 }
 
+// two-pass argmax: pass 1 reduces chunk c of row b to (key, index) in part[b][c]
+__global__ void __launch_bounds__(512) argmax_part_kernel(const float* __restrict__ logits, int ld, int V,
+                                                           int2* __restrict__ part) {
+    __shared__ int32_t sk[16], si[16];
+    const int b = blockIdx.y, c = blockIdx.x, nch = gridDim.x;
+    const int per = (V + nch - 1) / nch;
+    const int lo = c * per, hi = min(V, lo + per);
+    const float* l = logits + (size_t)b * ld;
+    int32_t bk = INT32_MIN, bi = -1;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const int32_t k = total_key(l[i]);
+        if (k > bk || (k == bk && i > bi)) {
+            bk = k;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
+        if (ok > bk || (ok == bk && oi > bi)) {
+            bk = ok;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+    if (ln == 0) {
+        sk[w] = bk;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        bk = ln < nw ? sk[ln] : INT32_MIN;
+        bi = ln < nw ? si[ln] : -1;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
+            if (ok > bk || (ok == bk && oi > bi)) {
+                bk = ok;
+                bi = oi;
+            }
+        }
+        if (ln == 0) part[(size_t)b * nch + c] = make_int2(bk, bi);
+    }
+}
+
+// pass 2: one warp per row over its nch partials
+__global__ void argmax_final_kernel(const int2* __restrict__ part, int nch, int32_t* __restrict__ out) {
+    const int b = blockIdx.x, ln = threadIdx.x;
+    int32_t bk = INT32_MIN, bi = -1;
+    for (int c = ln; c < nch; c += 32) {
+        const int2 v = part[(size_t)b * nch + c];
+        if (v.y >= 0 && (v.x > bk || (v.x == bk && v.y > bi))) {
+            bk = v.x;
+            bi = v.y;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
+        if (ok > bk || (ok == bk && oi > bi)) {
+            bk = ok;
+            bi = oi;
+        }
+    }
+    if (ln == 0) out[b] = bi < 0 ? 0 : bi;
+}
+
+void launch_argmax2(const float* logits, int ld, int V, int batch, int32_t* out, int2* part, int nch,
+                    cudaStream_t st) {
+    argmax_part_kernel<<<dim3(nch, batch), 512, 0, st>>>(logits, ld, V, part);
+    argmax_final_kernel<<<batch, 32, 0, st>>>(part, nch, out);
+}
+
 void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
                         cudaStream_t st, float* zero_ptr, int zero_ld, int zero_n) {
     launch_pdl(rmsnorm_act_kernel, dim3(batch), dim3(256), 0, st, x, ldx, w, D, eps, out, zero_ptr, zero_ld, zero_n);

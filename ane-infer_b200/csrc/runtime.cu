@@ -364,6 +364,7 @@ struct ab2_ctx {
     uint8_t *xfa = nullptr, *xfb = nullptr;
     float* logits = nullptr;    // [max_batch][vocab]
     int32_t *tok_d = nullptr, *next_d = nullptr;
+    int2* amax_part = nullptr;  // [max_batch][kArgmaxChunks] partial (key, index) of the argmax
     float* gws = nullptr;       // GEMM split-K partials
     unsigned* gtk = nullptr;    // GEMM tickets
     float* aws = nullptr;       // attention split partials
@@ -568,6 +569,7 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     RET(x->dalloc(&x->logits, (size_t)B * c.vocab * 4));
     RET(x->dalloc(&x->tok_d, (size_t)B * 4));
     RET(x->dalloc(&x->next_d, (size_t)B * 4));
+    RET(x->dalloc(&x->amax_part, (size_t)B * kArgmaxChunks * sizeof(int2)));
     RET(x->dalloc(&x->tmp_out, (size_t)std::max<int64_t>(D, F) * 4));
     size_t gws = 0;
     int gtk = 1;
@@ -811,7 +813,7 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
     RET(gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st));
     {
         ProfScope ps(x, PC_OTHER, st);
-        if (next_d) launch_argmax(logits_d, (int)c.vocab, (int)c.vocab, B, next_d, st);
+        if (next_d) launch_argmax2(logits_d, (int)c.vocab, (int)c.vocab, B, next_d, x->amax_part, kArgmaxChunks, st);
         launch_pos_advance(x->pos_d, B, st);
     }
     CK(cudaGetLastError());
@@ -831,7 +833,8 @@ int take_device_error(ab2_ctx* x) {
 
 int64_t launches_per_step(const ab2_ctx* x, int B) {
     (void)B;
-    return 1 + (int64_t)x->layers.size() * 7 + 1 + 1 + 2;
+    // embed + 7 per layer + final norm + lm_head + 2 argmax passes + position advance
+    return 1 + (int64_t)x->layers.size() * 7 + 1 + 1 + 2 + 1;
 }
 
 // ------------------------------------------------------------------------- op-level cache
