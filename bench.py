@@ -32,9 +32,11 @@ PKG_DIR = os.path.join(ROOT, "ane-infer_b200")
 METRIC = "decode tok/s, 2B-shape Q8_0 B=64 ctx8K at 1/2/4/8 B200; % HBM roofline"
 SHAPE_KEYS = dict(n_layers=24, dim=2048, vocab=151936, ffn=6144, dn_heads=16, dn_state=128, attn_heads=8,
                   kv_heads=2, head_dim=256)
-# dram__bytes_read.sum + dram__bytes_write.sum per attention launch from the ncu capture
-# summarised in profiles/attention_decode_b64_ctx8k.md (None until captured)
-NCU_TRAFFIC_ATTN_PER_LAUNCH = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch, from the ncu capture
+# summarised in profiles/attn_mma_b8_ctx8k.md (B=8, ctx 8192: 134.44 MB read + 3.94 MB
+# written), scaled by 8 to the benchmark's B=64 launch; traffic grows with B (each sequence's
+# K/V is read once), so the scaling is proportional.
+NCU_TRAFFIC_ATTN_PER_LAUNCH = 8 * (134_440_192 + 3_943_168)
 
 
 def load_pkg():
@@ -214,15 +216,9 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
     pkg = load_pkg()
     from ane_infer_b200 import synth
+    from ane_infer_b200.shard import ShardedDecoder, max_over_ranks
     shape = synth.shape_2b()
     gguf = synth.build_model_gguf(shape, seed=0)
     B = args.batch if not args.strong else args.batch // world
@@ -279,13 +275,19 @@ def run_ours(args):
     if NCU_TRAFFIC_ATTN_PER_LAUNCH is not None:
         traffic = NCU_TRAFFIC_ATTN_PER_LAUNCH
 
-    # ---- end to end through the host-buffer API
-    host_tok = synth.seeded_tokens(B, cfg["vocab"], seed=5 + rank)
+    # ---- end to end through the host-buffer API: rank 0 holds every sequence's token id;
+    # with N > 1 the ids are scattered to the ranks and the next ids gathered back each step
+    host_tok = synth.seeded_tokens(B * world, cfg["vocab"], seed=5)
+    dec = None
+    if world > 1:
+        dec = ShardedDecoder(lambda t: ctx.decode_step(t, want_logits=False)[1], B * world)
     barrier()
     t0 = time.perf_counter()
     for _ in range(n_e2e):
-        _, nxt = ctx.decode_step(host_tok, want_logits=False)
-        host_tok = nxt
+        if dec is None:
+            _, host_tok = ctx.decode_step(host_tok, want_logits=False)
+        else:
+            host_tok = dec.step(host_tok if rank == 0 else None)
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = world * B * n_e2e / e2e_s
@@ -312,13 +314,14 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (each step reads ~%.1f GB)" % (step_bytes / 1e9)},
             "step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms_max / args.steps) / 1e6, 1),
                          "frac": round(step_bytes / (ms_max / args.steps) / 1e6 / peak, 4)},
-            "roofline": {"kernel": "attn_decode_kernel (GQA split-KV flash-decode)", "bound": "hbm",
+            "roofline": {"kernel": "attn_mma_kernel (GQA split-KV flash-decode, bf16 KV via TMA)", "bound": "hbm",
                          "achieved": round(attn_gbs, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": round(attn_gbs / peak, 4), "traffic": traffic,
                          "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": round(attn_ms, 5)},
             "kernel_ms_per_step": {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
+            "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B * world,
+                    "d2h_bytes_per_step": 4 * B * world,
                     "steps": n_e2e},
             "gpu_launches": launches,
             "clocks": clocks,
@@ -374,22 +377,28 @@ def run_op(args):
                                      out, st)
         nbytes = B * Hkv * ctx * hd * 2 * 2
         label = f"gqa flash-decode B={B} ctx={ctx} Hq=8 Hkv=2 hd=256"
+    # L2 (126 MB) is flushed before every timed launch by writing a 256 MB buffer, so inputs
+    # that fit in L2 (small batches) are still read from HBM
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
     for _ in range(args.warmup):
+        flush.fill_(1.0)
         fn()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(args.iters):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.iters)]
+    for e0, e1 in ev:
+        flush.fill_(1.0)
+        e0.record(st)
         fn()
-    e1.record(st)
+        e1.record(st)
     torch.cuda.synchronize()
     if pkg.op_error():
         raise RuntimeError("tensor-core pipeline timeout")
-    ms = e0.elapsed_time(e1) / args.iters
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.iters
     gbs = nbytes / (ms / 1e3) / 1e9
     print(json.dumps({"op": label, "us_per_launch": round(ms * 1e3, 2), "algorithmic_bytes": nbytes,
                       "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": peak_kind,
-                      "frac": round(gbs / peak, 4), "iters": args.iters}), flush=True)
+                      "frac": round(gbs / peak, 4), "iters": args.iters, "l2": "flushed before each launch"}),
+          flush=True)
 
 
 def main():
