@@ -82,6 +82,7 @@ SIGNATURES = {
     "ab2_q8_create": (C.c_int, [_vp, _i64, _i64, C.c_int, C.POINTER(_vp)]),
     "ab2_q8_destroy": (None, [_vp]),
     "ab2_q8_gemv": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
+    "ab2_q8_gemv_noalloc": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "ab2_q8_unpack": (C.c_int, [_vp, _vp, _vp]),
     "ab2_q8_dequant": (C.c_int, [_vp, _i64, _vp, _vp]),
     "ab2_gated_delta": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp]),
@@ -293,6 +294,12 @@ class Q8Tensor:
 def q8_gemv(w: Q8Tensor, x, y, batch: int = 1, stream=None):
     """y[b][:] = W x[b][:] on device buffers (f32 [batch][n] -> [batch][m])."""
     _check(load_library().ab2_q8_gemv(w._h, _dp(x), batch, _dp(y), _stream(stream)))
+
+
+def q8_gemv_noalloc(w: Q8Tensor, x, y, batch: int = 1, stream=None):
+    """q8_gemv for batch 1..8 with scratch in the library's fixed device array (no device
+    allocation); calls that can overlap on the device share that array and race."""
+    _check(load_library().ab2_q8_gemv_noalloc(w._h, _dp(x), batch, _dp(y), _stream(stream)))
 
 
 def op_error() -> int:

@@ -1413,3 +1413,70 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
     CK(cudaGetLastError());
     return 0;
 }
+
+// ===================================================================== allocation-free GEMV
+// ab2_q8_gemv allocates its activation buffer, split-K workspace and tickets with
+// cudaMalloc the first time a size is seen. Some callers cannot allow that: a host whose
+// device memory is carved up by its own pool before it loads this library (cudaMalloc would
+// fail or fragment it), and a caller on a latency-critical thread where cudaMalloc's implicit
+// device synchronisation would stall the other streams. ab2_q8_gemv_noalloc runs the same
+// mma.sync Q8_0 GEMM (batches 1..8) with all of its scratch in one fixed device array of
+// this module, so it never allocates.
+namespace {
+
+// 4 MiB: tickets | activation fragments | split-K partials
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+constexpr size_t kNoAllocTicketBytes = 16u << 10;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// device address of g_noalloc_scratch on `dev` (the current device), looked up once
+int noalloc_scratch(int dev, unsigned char** out) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return seterr(AB2_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
+                          cudaGetErrorString(e));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = (unsigned char*)g_noalloc_ptr[dev];
+    return 0;
+}
+
+}  // namespace
+
+AB2_API int ab2_q8_gemv_noalloc(ab2_q8* w, const float* xin, int batch, float* y, void* stream) {
+    if (!w || !xin || !y) return seterr(AB2_ERR_ARG, "null argument");
+    if (batch < 1 || batch >= kUmmaMinBatch)
+        return seterr(AB2_ERR_CAPACITY, "ab2_q8_gemv_noalloc: batch %d outside [1, %d]", batch, kUmmaMinBatch - 1);
+    if (w->device < 0 || w->device >= 64) return seterr(AB2_ERR_ARG, "device index out of range");
+    const int gx = gemm_grid_x(w->w.M16);
+    const size_t tk_bytes = (size_t)gx * 4;
+    const size_t xf_bytes = (xfrag_bytes((int)w->n, batch) + 255) & ~(size_t)255;
+    const size_t ws_bytes = gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms) * 4;
+    if (tk_bytes > kNoAllocTicketBytes || kNoAllocTicketBytes + xf_bytes + ws_bytes > kNoAllocScratchBytes)
+        return seterr(AB2_ERR_CAPACITY,
+                      "ab2_q8_gemv_noalloc: %lld x %lld at batch %d needs %zu B of scratch (tickets %zu, "
+                      "activations %zu, split-K %zu); the fixed scratch holds %zu B (tickets at most %zu)",
+                      (long long)w->w.M, (long long)w->n, batch, kNoAllocTicketBytes + xf_bytes + ws_bytes,
+                      tk_bytes, xf_bytes, ws_bytes, kNoAllocScratchBytes, kNoAllocTicketBytes);
+    CK(cudaSetDevice(w->device));
+    unsigned char* base = nullptr;
+    RET(noalloc_scratch(w->device, &base));
+    unsigned* tickets = (unsigned*)base;
+    uint8_t* xf = base + kNoAllocTicketBytes;
+    float* ws = (float*)(base + kNoAllocTicketBytes + xf_bytes);
+    cudaStream_t st = (cudaStream_t)stream;
+    // the split-K tickets must start at zero (the last CTA of each row group re-arms its
+    // ticket, but a fresh device array or an earlier aborted call gives no such guarantee)
+    CK(cudaMemsetAsync(tickets, 0, tk_bytes, st));
+    const ActOut in = act_out(xf, (int)w->n, batch, false);
+    launch_to_act(xin, (int)w->n, (int)w->n, batch, in, st);
+    launch_q8_gemm(w->w, xf, batch, ws, tickets, epi_store(y, (int)w->w.M, w->w.M), w->num_sms, st);
+    CK(cudaGetLastError());
+    return 0;
+}

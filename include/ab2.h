@@ -135,6 +135,17 @@ void ab2_q8_destroy(ab2_q8* w);
 int ab2_q8_gemv(ab2_q8* w, const float* x, int batch, float* y, void* stream);
 /* Batches of 9 or more run on the tcgen05 path, whose f16 weights are q*d rounded once
  * (relative error <= 2^-11 per weight); smaller batches keep the weights exact. */
+/* ab2_q8_gemv for batch 1..8 that allocates nothing: no reference counterpart. For callers
+ * that cannot call cudaMalloc (device memory already carved up by their own pool, or a
+ * thread where cudaMalloc's implicit synchronisation would stall other streams). Its
+ * activation buffer, split-K workspace and tickets live in one fixed 4 MiB device array of
+ * the library (16 KiB of it for tickets); a shape whose scratch does not fit, or a batch
+ * above 8, returns AB2_ERR_CAPACITY with the sizes in the message. The first call on a
+ * device looks up that array's address (cudaGetSymbolAddress) and should come before any
+ * stream capture. All calls on a device share the one array: calls that can overlap on the
+ * device (different streams or host threads) race, so serialise them. Same results as
+ * ab2_q8_gemv at the same batch. */
+int ab2_q8_gemv_noalloc(ab2_q8* w, const float* x, int batch, float* y, void* stream);
 /* Synchronise the current device and return (then clear) the error word of the op-level
  * tensor-core calls: 0, or the code of a pipeline wait that timed out. */
 int ab2_op_error(uint32_t* code);
