@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             for (int j = max(0, issued - kAttnStages); j < issued; j++)
                 if (!mbar_wait(&full[j % kAttnStages], (j / kAttnStages) & 1)) s_abort = 1;
         }
+        __syncwarp();  // lanes 1-31 wait for the producer lane before the CTA barrier below
     } else {
         // ---------------- compute warps
         const int g = lane >> 2, t = lane & 3;

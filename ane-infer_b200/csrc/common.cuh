@@ -92,7 +92,8 @@ __device__ __forceinline__ void xfrag_store(uint8_t* xf, const XfragShape& s, in
 // shared-memory image of K-major 128-byte-swizzled tiles, so one bulk copy per 64-wide K tile
 // lands it ready for tcgen05.mma: [K/64][npad rows][128 B], where the 16-byte chunk j of row n
 // is stored at chunk position j ^ (n % 8). npad = batch rounded up to 16, 32 or 64.
-__host__ __device__ inline int x16_npad(int batch) { return batch <= 16 ? 16 : (batch <= 32 ? 32 : 64); }
+// the tcgen05 GEMM takes the activations as its M = 64 operand: always 64 rows (batch <= 64)
+__host__ __device__ inline int x16_npad(int batch) { return (void)batch, 64; }
 __host__ __device__ inline size_t x16_bytes(int K, int batch) {
     return (size_t)((K + 63) / 64) * x16_npad(batch) * 128;
 }

@@ -27,12 +27,16 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 // A Q8_0 weight on the device, in one or both packed layouts:
 //   q8p (qs, d): mma.sync fragment order, used for batches <= 8 (exact weights);
-//   q8t (qt):    128-row x 64-col tiles for the tcgen05 GEMM, used for larger batches:
-//                [MT][KT][4 chunks][128 rows][16 B] offset-binary int8 + [128 rows][2] f16 d.
+//   q8u (qt):    128-row x 64-column tiles for the tcgen05 GEMM, used for larger batches:
+//                [4 chunks][128 rows][16 B] offset-binary int8 + [128 rows][2] f16 d per tile,
+//                stored as [MT/2 row-tile pairs][KT][2 tiles] so that one K tile of a 256-row
+//                pair is one contiguous 17 KB block (MT rounded up to even, padding zero).
+constexpr int kUTileRows = 128;
+constexpr int kUTileBytes = 4 * kUTileRows * 16 + kUTileRows * 4;  // 8704
 struct Q8Weight {
     uint8_t* qs = nullptr;  // [M16][KB][32][16]
     uint8_t* d = nullptr;   // [M16][KB][8] x (f16, f16)
-    uint8_t* qt = nullptr;  // [MT][KT][8704]
+    uint8_t* qt = nullptr;  // [MT][KT][kUTileBytes]
     int64_t M = 0;          // logical rows
     int M16 = 0;            // ceil(M/16)
     int KB = 0;             // K / 32
@@ -40,10 +44,12 @@ struct Q8Weight {
     int KT = 0;             // ceil(K/64)
     size_t qs_bytes() const { return (size_t)M16 * KB * 512; }
     size_t d_bytes() const { return (size_t)M16 * KB * 32; }
-    size_t qt_bytes() const { return (size_t)MT * KT * 8704; }
+    size_t qt_bytes() const { return (size_t)(MT + 1) / 2 * 2 * KT * kUTileBytes; }
 };
 
-enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+// EPI_ADD: y += Wx with reductions; the caller keeps y zeroed between uses (the tcgen05 path
+// runs the SwiGLU gate/up projection this way, K-split, and applies silu(g)*u with launch_glu)
+enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ADD = 3 };
 
 struct GemmEpi {
     int mode = EPI_STORE;
@@ -69,9 +75,8 @@ void launch_q8p_dequant(const Q8Weight& w, int64_t rows, float* out, cudaStream_
 void launch_embed(const Q8Weight& w, int vocab, const int32_t* tokens, int batch, float* x, int ldx, cudaStream_t st);
 
 // q8_umma.cu
-int umma_npad(int batch);
-// K splits of the tcgen05 GEMM; with more than one split the epilogue adds into y, so a
-// STORE-mode output must be zeroed first
+// K splits of the tcgen05 GEMM; with more than one split the epilogue adds into y
+// (red.add), so a STORE-mode output must be zeroed first. SwiGLU is never split.
 int umma_nsplit(int MT, int KT, int mode, int num_sms);
 void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
                        int64_t stride, cudaStream_t st);
@@ -83,6 +88,10 @@ int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* e
 void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
                         cudaStream_t st, float* zero_ptr = nullptr, int zero_ld = 0, int zero_n = 0);
 void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st);
+// SwiGLU of a gate/up projection summed in h2 [batch][ld] (rows interleaved per 64: in each
+// 128-row block the first 64 are gate rows, the next 64 the matching up rows): silu(g)*u for
+// the F outputs goes to `out` (and to y [batch][ldy] if y is set), and h2 is zeroed again.
+void launch_glu(float* h2, int ld, int F, int batch, const ActOut& out, float* y, int ldy, cudaStream_t st);
 void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st);
 // argmax split over nch chunks per row (part: [batch][nch] scratch), same tie rule
 constexpr int kArgmaxChunks = 32;

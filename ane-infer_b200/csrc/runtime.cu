@@ -367,6 +367,7 @@ struct ab2_ctx {
     int2* amax_part = nullptr;  // [max_batch][kArgmaxChunks] partial (key, index) of the argmax
     float* gws = nullptr;       // GEMM split-K partials
     unsigned* gtk = nullptr;    // GEMM tickets
+    float* h2 = nullptr;        // tcgen05 path: f32 gate/up sums [max_batch][2*ffn], kept zeroed
     float* aws = nullptr;       // attention split partials
     size_t aws_floats = 0;
     unsigned* atk = nullptr;    // attention tickets
@@ -405,7 +406,7 @@ constexpr int64_t kPlain = (int64_t)1 << 40;  // grp for plain concatenation
 
 // A source tensor of a packed weight: its rows land at dst = base + (row/grp)*stride + row%grp.
 // kind 0: plain concatenation at `base`; kind 1 / 2: gate / up rows of an interleaved SwiGLU
-// pair (8-row groups in the q8p layout, 64-row groups in the q8t layout).
+// pair (8-row groups in the q8p layout, 64-row groups in the q8u layout).
 struct RepackSrc {
     const GTensor* t;
     int64_t rows, base;
@@ -418,7 +419,7 @@ int upload_q8(ab2_ctx* x, int64_t M, int64_t K, const std::vector<RepackSrc>& sr
     w->M = M;
     w->M16 = (int)((M + 15) / 16);
     w->KB = (int)(K / 32);
-    w->MT = (int)((M + 127) / 128);
+    w->MT = (int)((M + kUTileRows - 1) / kUTileRows);
     w->KT = (int)((K + 63) / 64);
     RET(x->dalloc(&w->qs, w->qs_bytes(), true));
     RET(x->dalloc(&w->d, w->d_bytes(), true));
@@ -586,6 +587,7 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     acc_gemm(x->lm_head);
     RET(x->dalloc(&x->gws, gws * 4));
     RET(x->dalloc(&x->gtk, (size_t)gtk * 4));
+    if (x->use_umma) RET(x->dalloc(&x->h2, (size_t)B * 2 * F * 4));
     if (c.n_attn > 0) {
         size_t aws = 0;
         for (int b = 1; b <= B; b++) {
@@ -765,7 +767,19 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
 
 int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st) {
     const int D = (int)x->c.dim, F = (int)x->c.ffn;
-    RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
+    if (umma_for(x, B)) {
+        // K-split gate/up sums into the zeroed f32 scratch, then silu(g)*u (which re-zeroes it)
+        GemmEpi e;
+        e.mode = EPI_ADD;
+        e.y = x->h2;
+        e.ldy = 2 * F;
+        e.m_out = 2 * F;
+        RET(gemm(x, L.gate_up, x->xfa, B, e, st));
+        ProfScope ps(x, PC_OTHER, st);
+        launch_glu(x->h2, 2 * F, F, B, act(x, x->xfb, F, B), nullptr, 0, st);
+    } else {
+        RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
+    }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
     return gemm(x, L.down, x->xfb, B, e, st);
 }
@@ -832,9 +846,10 @@ int take_device_error(ab2_ctx* x) {
 }
 
 int64_t launches_per_step(const ab2_ctx* x, int B) {
-    (void)B;
-    // embed + 7 per layer + final norm + lm_head + 2 argmax passes + position advance
-    return 1 + (int64_t)x->layers.size() * 7 + 1 + 1 + 2 + 1;
+    // embed + 7 per layer (8 on the tcgen05 path: the SwiGLU kernel) + final norm + lm_head +
+    // 2 argmax passes + position advance
+    const int64_t per_layer = umma_for(x, B) ? 8 : 7;
+    return 1 + (int64_t)x->layers.size() * per_layer + 1 + 1 + 2 + 1;
 }
 
 // ------------------------------------------------------------------------- op-level cache
@@ -1227,7 +1242,7 @@ AB2_API int ab2_q8_create(const uint8_t* blocks, int64_t m, int64_t n, int devic
     w->w.M = m;
     w->w.M16 = (int)((m + 15) / 16);
     w->w.KB = (int)(n / 32);
-    w->w.MT = (int)((m + 127) / 128);
+    w->w.MT = (int)((m + kUTileRows - 1) / kUTileRows);
     w->w.KT = (int)((n + 63) / 64);
     const size_t raw = (size_t)m * (n / 32) * 34;
     uint8_t* staging = nullptr;
