@@ -12,9 +12,14 @@
 //   * the online softmax runs per 64-token tile across the warps through shared memory;
 //   * the CTA holding the new position first writes the new (normed, rotated) key and value
 //     into the cache and fences them to the async proxy before TMA reads that tile;
-//   * split partials are merged by the last CTA of a (sequence, kv head) in split order.
+//   * the kernel is persistent: CTA c takes the work items (split, sequence, kv head) c,
+//     c + grid, ..., and the producer streams their tiles through one ring without draining
+//     between items; split partials are merged in split order by attn_merge_kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdint>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -66,6 +71,8 @@ __device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
     lo = x - hi;
 }
 
+constexpr int kMaxSplits = 64;  // splits per (sequence, kv head)
+
 template <int HD>
 struct AttnSmem {
     static constexpr int kNDB = HD / 64;                   // 64-dim TMA boxes per row
@@ -74,155 +81,208 @@ struct AttnSmem {
     static constexpr int v_off(int s) { return (kAttnStages + s) * kTileBytes; }
     static constexpr int s_off() { return 2 * kAttnStages * kTileBytes; }     // scores [4][kT] f32
     static constexpr int p_off() { return s_off() + kGQ * kT * 4; }           // P [16][kPStride] bf16
-    static constexpr int q_off() { return p_off() + 16 * kPStride * 2; }      // q [4][HD] f32
-    static constexpr int kn_off() { return q_off() + kGQ * HD * 4; }          // new k [HD], new v [HD]
-    static constexpr int misc_off() { return kn_off() + 2 * HD * 4; }         // corr[4], m[4], l[4], sc[8]
-    static constexpr int bar_off() { return misc_off() + 32 * 4; }            // full[S], empty[S]
-    static constexpr int bytes() { return bar_off() + 2 * kAttnStages * 8; }
+    static constexpr int q_off(int j) { return p_off() + 16 * kPStride * 2 + j * kGQ * HD * 4; }  // q [2][4][HD]
+    static constexpr int o_off() { return q_off(2); }                         // O of an item [4][HD] f32
+    static constexpr int misc_off() { return o_off() + kGQ * HD * 4; }        // corr[4], m[4], l[4]
+    static constexpr int bar_off() { return misc_off() + 16 * 4; }            // full[S], empty[S], q_full[2], q_free[2]
+    static constexpr int bytes() { return bar_off() + (2 * kAttnStages + 4) * 8; }
 };
 
+// Work item `item` = (split, sequence, kv head): item = split * pairs + (b * Hkv + kvh).
+struct AttnItem {
+    int b, kvh, split, t0, t1, ntiles, nsplit_b;
+    bool has_new;  // the split holding the new position (its last tile)
+};
+__device__ __forceinline__ bool attn_item(const AttnParams& p, int item, int pairs, AttnItem& it) {
+    const int pair = item % pairs;
+    it.split = item / pairs;
+    it.b = pair / p.Hkv;
+    it.kvh = pair % p.Hkv;
+    const int pos = p.pos[it.b], L = pos + 1;
+    it.t0 = it.split * p.chunk;
+    if (it.t0 >= L) return false;
+    it.t1 = min(L, it.t0 + p.chunk);
+    it.ntiles = (it.t1 - it.t0 + kT - 1) / kT;
+    it.has_new = pos < it.t0 + p.chunk;
+    it.nsplit_b = (L + p.chunk - 1) / p.chunk;
+    return true;
+}
+
+// the number of kernels launch_attention_mma enqueues: the query/K/V prologue, the attention
+// kernel, and the merge when any split is cut
+int attn_mma_launches(int max_len, int chunk) { return (max_len + chunk - 1) / chunk > 1 ? 3 : 2; }
+
+// Prologue of every (sequence, kv head), before the attention kernel (deltanet.rs:565-625):
+// the kGQ queries RMS-normed with q_norm and rotated into qprep; the new key normed with
+// k_norm and rotated, and the new key and value appended to the bf16 cache at `pos`.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_prep_kernel(AttnParams p) {
+    __shared__ float q_s[kGQ * HD], kn_s[HD], sc[kGQ + 1];
+    const int kvh = blockIdx.x, b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int pos = p.pos[b];
+    const float* proj = p.proj + (size_t)b * p.ldp;
+    const int koff = p.Hq * 2 * HD, voff = koff + p.Hkv * HD;
+    for (int e = threadIdx.x; e < kGQ * HD; e += 128) {
+        const int hh = e / HD, d = e % HD;
+        q_s[e] = proj[(size_t)(kvh * kGQ + hh) * 2 * HD + d];
+    }
+    for (int d = threadIdx.x; d < HD; d += 128) kn_s[d] = proj[koff + kvh * HD + d];
+    __syncthreads();
+    // warps 0..3: query heads; warp 0 also the key
+    {
+        float ss = 0.0f;
+        for (int d = lane; d < HD; d += 32) ss += q_s[warp * HD + d] * q_s[warp * HD + d];
+        ss = warp_sum(ss);
+        if (lane == 0) sc[warp] = p.q_norm ? 1.0f / sqrtf(ss / (float)HD + 1e-6f) : 1.0f;
+        if (warp == 0) {
+            float sk = 0.0f;
+            for (int d = lane; d < HD; d += 32) sk += kn_s[d] * kn_s[d];
+            sk = warp_sum(sk);
+            if (lane == 0) sc[kGQ] = p.k_norm ? 1.0f / sqrtf(sk / (float)HD + 1e-6f) : 1.0f;
+        }
+    }
+    __syncthreads();
+    if (p.q_norm)
+        for (int e = threadIdx.x; e < kGQ * HD; e += 128) q_s[e] = q_s[e] * sc[e / HD] * p.q_norm[e % HD];
+    if (p.k_norm)
+        for (int d = threadIdx.x; d < HD; d += 128) kn_s[d] = kn_s[d] * sc[kGQ] * p.k_norm[d];
+    __syncthreads();
+    const int half_rot = p.rot / 2;
+    const float2* rope = p.rope + (size_t)pos * half_rot;
+    for (int e = threadIdx.x; e < (kGQ + 1) * half_rot; e += 128) {
+        const int hh = e / half_rot, j = e % half_rot;
+        float* tv = hh < kGQ ? q_s + hh * HD : kn_s;
+        const float2 cs = rope[j];
+        const float a0 = tv[2 * j], a1 = tv[2 * j + 1];
+        tv[2 * j] = a0 * cs.x - a1 * cs.y;
+        tv[2 * j + 1] = a0 * cs.y + a1 * cs.x;
+    }
+    __syncthreads();
+    float* qo = p.qprep + ((size_t)b * p.Hkv + kvh) * kGQ * HD;
+    for (int e = threadIdx.x; e < kGQ * HD; e += 128) qo[e] = q_s[e];
+    __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(p.kc) + (size_t)b * p.kv_slot_stride +
+                        (size_t)kvh * p.cap * HD + (size_t)pos * HD;
+    __nv_bfloat16* vc = reinterpret_cast<__nv_bfloat16*>(p.vc) + (size_t)b * p.kv_slot_stride +
+                        (size_t)kvh * p.cap * HD + (size_t)pos * HD;
+    for (int d = threadIdx.x; d < HD; d += 128) {
+        kc[d] = __float2bfloat16_rn(kn_s[d]);
+        vc[d] = __float2bfloat16_rn(proj[voff + kvh * HD + d]);
+    }
+}
+
+__device__ __forceinline__ void comp_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCompWarps * 32) : "memory"); }
+
+// Persistent kernel: CTA c takes items c, c + gridDim.x, ...; the producer warp streams the
+// tiles of all of them through one ring, so the pipeline does not drain between items, and
+// with each item's first tile it copies the item's prepared queries (attn_prep_kernel) into
+// one of two query slots, so a new item starts without a prologue.
 template <int HD>
 __global__ void __launch_bounds__(kAttnMmaThreads, 1)
     attn_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, AttnParams p,
-                    int64_t row_base) {
+                    int64_t row_base, int pairs, int n_items) {
     using L = AttnSmem<HD>;
     constexpr int NDB = L::kNDB;
+    constexpr int kCT = kCompWarps * 32;
+    constexpr uint32_t kQBytes = kGQ * HD * 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     float* S_s = reinterpret_cast<float*>(smem + L::s_off());
     __nv_bfloat16* P_s = reinterpret_cast<__nv_bfloat16*>(smem + L::p_off());
-    float* q_s = reinterpret_cast<float*>(smem + L::q_off());
-    float* kn_s = reinterpret_cast<float*>(smem + L::kn_off());
-    float* vn_s = kn_s + HD;
+    float* o_s = reinterpret_cast<float*>(smem + L::o_off());
     float* corr_s = reinterpret_cast<float*>(smem + L::misc_off());
     float* m_s = corr_s + 4;
     float* l_s = corr_s + 8;
-    float* sc = corr_s + 12;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off());
     uint64_t* empty = full + kAttnStages;
-    __shared__ unsigned s_last;
-    __shared__ int s_abort;
+    uint64_t* q_full = empty + kAttnStages;
+    uint64_t* q_free = q_full + 2;
 
-    const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, nsplit = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = p.pos[b], Ltok = pos + 1;
-    const int t0 = split * p.chunk, t1 = min(Ltok, t0 + p.chunk);
-    const int ntiles = t1 > t0 ? (t1 - t0 + kT - 1) / kT : 0;
-    const bool has_new = t0 <= pos && pos < t0 + p.chunk;
-    const int rows0 = (int)(row_base + ((int64_t)b * p.Hkv + kvh) * p.cap + t0);
-    const float* proj = p.proj + (size_t)b * p.ldp;
-    const int half_rot = p.rot / 2;
-    const float2* rope = p.rope + (size_t)pos * half_rot;
     constexpr uint32_t kStageTx = 2u * L::kTileBytes;
 
     if (threadIdx.x == 0) {
-        s_abort = 0;
         for (int s = 0; s < kAttnStages; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kCompWarps * 32);
+            mbar_init(&empty[s], kCT);
+        }
+        for (int j = 0; j < 2; j++) {
+            mbar_init(&q_full[j], 1);
+            mbar_init(&q_free[j], kCT);
         }
         mbar_fence_init();
     }
-    __syncthreads();
-
-    // tiles that cannot hold the new position are independent of the prologue: start them now
-    const int n_pre = min(kAttnStages, has_new ? ntiles - 1 : ntiles);
-    const bool producer = warp == kCompWarps && lane == 0;
-    if (producer) {
-        for (int i = 0; i < n_pre; i++) {
-            mbar_arrive_expect_tx(&full[i], kStageTx);
-#pragma unroll
-            for (int d = 0; d < NDB; d++) {
-                tma_load_2d(smem + L::k_off(i) + d * 8192, &tmk, d * 64, rows0 + i * kT, &full[i]);
-                tma_load_2d(smem + L::v_off(i) + d * 8192, &tmv, d * 64, rows0 + i * kT, &full[i]);
-            }
-        }
-    }
-
-    // ---- prologue: queries of the kGQ heads, new key / value (deltanet.rs:565-625)
-    const int koff = p.Hq * 2 * HD, voff = koff + p.Hkv * HD;
-    for (int i = threadIdx.x; i < kGQ * HD; i += kAttnMmaThreads) {
-        const int hh = i / HD, d = i % HD, h = kvh * kGQ + hh;
-        q_s[i] = proj[(size_t)h * 2 * HD + d];
-    }
-    if (has_new)
-        for (int d = threadIdx.x; d < HD; d += kAttnMmaThreads) {
-            kn_s[d] = proj[koff + kvh * HD + d];
-            vn_s[d] = proj[voff + kvh * HD + d];
-        }
+    // rows 8-15 of the P operand stay zero; rows 0-7 are rewritten for every tile
     for (int i = threadIdx.x; i < 16 * kPStride; i += kAttnMmaThreads) P_s[i] = __float2bfloat16_rn(0.0f);
-    __syncthreads();
-    if (warp < kGQ && p.q_norm) {
-        float ss = 0.0f;
-        for (int d = lane; d < HD; d += 32) ss += q_s[warp * HD + d] * q_s[warp * HD + d];
-        ss = warp_sum(ss);
-        if (lane == 0) sc[warp] = 1.0f / sqrtf(ss / (float)HD + 1e-6f);
-    }
-    if (warp == kGQ && has_new && p.k_norm) {
-        float ss = 0.0f;
-        for (int d = lane; d < HD; d += 32) ss += kn_s[d] * kn_s[d];
-        ss = warp_sum(ss);
-        if (lane == 0) sc[kGQ] = 1.0f / sqrtf(ss / (float)HD + 1e-6f);
-    }
-    __syncthreads();
-    if (p.q_norm)
-        for (int i = threadIdx.x; i < kGQ * HD; i += kAttnMmaThreads) q_s[i] = q_s[i] * sc[i / HD] * p.q_norm[i % HD];
-    if (has_new && p.k_norm)
-        for (int d = threadIdx.x; d < HD; d += kAttnMmaThreads) kn_s[d] = kn_s[d] * sc[kGQ] * p.k_norm[d];
-    __syncthreads();
-    for (int i = threadIdx.x; i < (kGQ + 1) * half_rot; i += kAttnMmaThreads) {
-        const int hh = i / half_rot, j = i % half_rot;
-        if (hh == kGQ && !has_new) continue;
-        float* t = hh < kGQ ? q_s + hh * HD : kn_s;
-        const float2 cs = rope[j];
-        const float a0 = t[2 * j], a1 = t[2 * j + 1];
-        t[2 * j] = a0 * cs.x - a1 * cs.y;
-        t[2 * j + 1] = a0 * cs.y + a1 * cs.x;
-    }
-    __syncthreads();
-    if (has_new) {
-        __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(p.kc) + (size_t)b * p.kv_slot_stride +
-                            (size_t)kvh * p.cap * HD + (size_t)pos * HD;
-        __nv_bfloat16* vc = reinterpret_cast<__nv_bfloat16*>(p.vc) + (size_t)b * p.kv_slot_stride +
-                            (size_t)kvh * p.cap * HD + (size_t)pos * HD;
-        for (int d = threadIdx.x; d < HD; d += kAttnMmaThreads) {
-            kc[d] = __float2bfloat16_rn(kn_s[d]);
-            vc[d] = __float2bfloat16_rn(vn_s[d]);
-        }
-        asm volatile("fence.proxy.async.global;" ::: "memory");  // visible to the TMA reads below
-    }
     __syncthreads();
 
     if (warp == kCompWarps) {
-        // ---------------- producer: the remaining tiles
+        // ---------------- producer: queries and K/V tiles of every item of this CTA, in order
         if (lane == 0) {
-            int issued = n_pre;
-            for (int i = n_pre; i < ntiles; i++) {
-                const int s = i % kAttnStages;
-                if (i >= kAttnStages && !mbar_wait(&empty[s], ((i / kAttnStages) - 1) & 1)) {
-                    s_abort = 1;
+            asm volatile("griddepcontrol.wait;" ::: "memory");  // prepared queries and appended K/V
+            int i = 0, k = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+                AttnItem it;
+                if (!attn_item(p, item, pairs, it)) continue;
+                const int pair = it.b * p.Hkv + it.kvh;
+                const int qs = k & 1;
+                if (k >= 2 && !mbar_wait(&q_free[qs], ((k >> 1) - 1) & 1)) {
+                    ok = false;
                     break;
                 }
-                if (*(volatile int*)&s_abort) break;
-                mbar_arrive_expect_tx(&full[s], kStageTx);
+                mbar_arrive_expect_tx(&q_full[qs], kQBytes);
+                bulk_g2s(smem + L::q_off(qs), p.qprep + (size_t)pair * kGQ * HD, kQBytes, &q_full[qs]);
+                k++;
+                const int rows0 = (int)(row_base + (int64_t)pair * p.cap + it.t0);
+                for (int t = 0; t < it.ntiles; t++, i++) {
+                    const int s = i % kAttnStages;
+                    if (i >= kAttnStages && !mbar_wait(&empty[s], ((i / kAttnStages) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], kStageTx);
 #pragma unroll
-                for (int d = 0; d < NDB; d++) {
-                    tma_load_2d(smem + L::k_off(s) + d * 8192, &tmk, d * 64, rows0 + i * kT, &full[s]);
-                    tma_load_2d(smem + L::v_off(s) + d * 8192, &tmv, d * 64, rows0 + i * kT, &full[s]);
+                    for (int d = 0; d < NDB; d++) {
+                        tma_load_2d(smem + L::k_off(s) + d * 8192, &tmk, d * 64, rows0 + t * kT, &full[s]);
+                        tma_load_2d(smem + L::v_off(s) + d * 8192, &tmv, d * 64, rows0 + t * kT, &full[s]);
+                    }
                 }
-                issued = i + 1;
             }
-            // every issued tile lands before the CTA can exit
-            for (int j = max(0, issued - kAttnStages); j < issued; j++)
-                if (!mbar_wait(&full[j % kAttnStages], (j / kAttnStages) & 1)) s_abort = 1;
+            if (!ok && p.err) atomicOr(p.err, 256u);
+            // every issued copy lands before the CTA can exit
+            for (int j = max(0, i - kAttnStages); j < i; j++) mbar_wait(&full[j % kAttnStages], (j / kAttnStages) & 1);
+            for (int j = max(0, k - 2); j < k; j++) mbar_wait(&q_full[j & 1], (j >> 1) & 1);
         }
-        __syncwarp();  // lanes 1-31 wait for the producer lane before the CTA barrier below
-    } else {
-        // ---------------- compute warps
-        const int g = lane >> 2, t = lane & 3;
-        const int hq = g & 3;             // head of this lane's operand row (rows 0-3 hi, 4-7 lo)
-        const bool lo_row = g >= 4;
+        __syncwarp();
+        return;
+    }
+
+    // ---------------- compute warps
+    const int ct = threadIdx.x;
+    const int g = lane >> 2, t = lane & 3;
+    const int hq = g & 3;  // head of this lane's operand row (rows 0-3 hi, 4-7 lo)
+    const bool lo_row = g >= 4;
+    const float sq = sqrtf((float)HD);
+    const uint32_t pbase = smem_u32(P_s);
+    constexpr int NPV = HD / 32;  // 8-dim n-tiles of this warp's HD/4 output dims
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // outputs may be read by earlier kernels
+    int i = 0, k = 0;  // tile and item counters, in step with the producer
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        AttnItem it;
+        if (!attn_item(p, item, pairs, it)) continue;
+        const int b = it.b, kvh = it.kvh;
+        const float* proj = p.proj + (size_t)b * p.ldp;
+
         // Q A-fragments for every k16 step: a0 = (row g, k 2t..2t+1), a2 = (row g, k 2t+8..+9)
+        const int qs = k & 1;
+        if (!mbar_wait(&q_full[qs], (k >> 1) & 1)) {
+            if (ct == 0 && p.err) atomicOr(p.err, 256u);
+            break;
+        }
+        const float* q_s = reinterpret_cast<const float*>(smem + L::q_off(qs));
         uint32_t qa0[HD / 16], qa2[HD / 16];
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ks++) {
@@ -236,22 +296,22 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             qa0[ks] = lo_row ? pack_bf16(l0, l1) : pack_bf16(h0, h1);
             qa2[ks] = lo_row ? pack_bf16(l2, l3) : pack_bf16(h2, h3);
         }
-        constexpr int NPV = HD / 32;  // 8-dim n-tiles of this warp's HD/4 output dims
+        mbar_arrive(&q_free[qs]);
+        k++;
         float o[NPV][4];
 #pragma unroll
         for (int n = 0; n < NPV; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
         float m_run = -INFINITY, l_run = 0.0f;  // head `warp` (warps 0..3 own heads 0..3)
-        const float sq = sqrtf((float)HD);
-        const uint32_t pbase = smem_u32(P_s);
 
-        for (int i = 0; i < ntiles; i++) {
+        bool ok = true;
+        for (int tt0 = 0; tt0 < it.ntiles; tt0++, i++) {
             const int s = i % kAttnStages;
             if (!mbar_wait(&full[s], (i / kAttnStages) & 1)) {
-                s_abort = 1;
+                ok = false;
                 break;
             }
             const uint32_t kb = smem_u32(smem + L::k_off(s)), vb = smem_u32(smem + L::v_off(s));
-            const int tbase = t0 + i * kT;
+            const int tbase = it.t0 + tt0 * kT;
             // S = Q K^T for tokens [16w, 16w+16) of the tile
 #pragma unroll
             for (int j = 0; j < 2; j++) {
@@ -271,11 +331,11 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                 const float s1 = acc[1] + __shfl_xor_sync(kFull, acc[1], 16);
                 if (g < 4) {
                     const int tt = n0 + 2 * t;
-                    S_s[g * kT + tt] = (tbase + tt < t1) ? s0 / sq : -INFINITY;
-                    S_s[g * kT + tt + 1] = (tbase + tt + 1 < t1) ? s1 / sq : -INFINITY;
+                    S_s[g * kT + tt] = (tbase + tt < it.t1) ? s0 / sq : -INFINITY;
+                    S_s[g * kT + tt + 1] = (tbase + tt + 1 < it.t1) ? s1 / sq : -INFINITY;
                 }
             }
-            asm volatile("bar.sync 1, %0;" ::"n"(kCompWarps * 32) : "memory");
+            comp_bar();
             // online softmax for head `warp` over the tile's 64 tokens
             {
                 const float v0 = S_s[warp * kT + lane], v1 = S_s[warp * kT + lane + 32];
@@ -298,7 +358,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                 P_s[(warp + 4) * kPStride + lane + 32] = __float2bfloat16_rn(pl);
                 if (lane == 0) corr_s[warp] = corr;
             }
-            asm volatile("bar.sync 1, %0;" ::"n"(kCompWarps * 32) : "memory");
+            comp_bar();
             // O = O * corr + P V for dims [warp*HD/4, (warp+1)*HD/4)
             const float cr = corr_s[hq];
 #pragma unroll
@@ -329,6 +389,11 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             }
             mbar_arrive(&empty[s]);
         }
+        if (!ok) {
+            // a timed-out wait: report it and stop; the results of this launch are invalid
+            if (ct == 0 && p.err) atomicOr(p.err, 256u);
+            break;
+        }
         // merge hi/lo rows: lanes g < 4 hold head g for dims d0 + 8n + 2t, +1
 #pragma unroll
         for (int n = 0; n < NPV; n++) {
@@ -339,81 +404,79 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             m_s[warp] = m_run;
             l_s[warp] = l_run;
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(kCompWarps * 32) : "memory");
-        // unnormalised O of this CTA into q_s (reused as [4][HD])
+        // unnormalised O of this item into o_s [4][HD]
         if (g < 4) {
 #pragma unroll
             for (int n = 0; n < NPV; n++) {
                 const int d = warp * (HD / 4) + 8 * n + 2 * t;
-                q_s[g * HD + d] = o[n][0];
-                q_s[g * HD + d + 1] = o[n][1];
+                o_s[g * HD + d] = o[n][0];
+                o_s[g * HD + d + 1] = o[n][1];
             }
         }
-    }
-    __syncthreads();
-    // a timed-out wait leaves this CTA's numbers invalid: report it, but keep taking part in
-    // the split ticket below so the per-(sequence, head) counters stay consistent
-    if (s_abort && threadIdx.x == 0 && p.err) atomicOr(p.err, 256u);
-
-    // ---- finish: one split writes its partial; the last CTA merges in split order
-    const size_t part_floats = (size_t)kGQ * 2 + (size_t)kGQ * HD;
-    if (nsplit == 1) {
-        for (int i = threadIdx.x; i < kGQ * HD; i += kAttnMmaThreads) {
-            const int hh = i / HD, d = i % HD, h = kvh * kGQ + hh;
-            float o = q_s[i] / l_s[hh];
-            o *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
-            act_store(p.out, b, h * HD + d, o);
-            if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = o;
+        comp_bar();
+        if (it.nsplit_b == 1) {
+            // a lone split: the output itself
+            for (int e = ct; e < kGQ * HD; e += kCT) {
+                const int hh = e / HD, d = e % HD, h = kvh * kGQ + hh;
+                float ov = o_s[e] / l_s[hh];
+                ov *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
+                act_store(p.out, b, h * HD + d, ov);
+                if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = ov;
+            }
+        } else {
+            // a split of several: its partial (m, l, unnormalised O) for attn_merge_kernel
+            const size_t part_floats = (size_t)kGQ * 2 + (size_t)kGQ * HD;
+            float* mypart = p.ws + (((size_t)b * p.Hkv + kvh) * kMaxSplits + it.split) * part_floats;
+            for (int e = ct; e < kGQ * HD; e += kCT) __stcg(mypart + 2 * kGQ + e, o_s[e]);
+            if (ct < kGQ) {
+                __stcg(mypart + ct, m_s[ct]);
+                __stcg(mypart + kGQ + ct, l_s[ct]);
+            }
         }
-        return;
+        comp_bar();  // o_s, m_s, l_s are reused by the next item
     }
-    float* mypart = p.ws + (((size_t)b * p.Hkv + kvh) * nsplit + split) * part_floats;
-    for (int i = threadIdx.x; i < kGQ * HD; i += kAttnMmaThreads) __stcg(mypart + 2 * kGQ + i, q_s[i]);
-    if (threadIdx.x < kGQ) {
-        __stcg(mypart + threadIdx.x, m_s[threadIdx.x]);
-        __stcg(mypart + kGQ + threadIdx.x, l_s[threadIdx.x]);
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&p.tickets[b * p.Hkv + kvh], 1u);
-        s_last = (prev == (unsigned)nsplit - 1u) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // merge: per-(split, head) weights e = exp(m_s - M) once into shared memory (the K/V ring
-    // is idle now), then every output element sums its splits in split order
-    const float* parts = p.ws + (((size_t)b * p.Hkv + kvh) * nsplit) * part_floats;
-    float* e_s = reinterpret_cast<float*>(smem);  // [nsplit][kGQ]
-    float* lsum_s = e_s + nsplit * kGQ;           // [kGQ]
+}
+
+// Merge of the split partials of one (sequence, kv head) per CTA, in split order: weights
+// e_s = exp(m_s - M) per (split, head), O = sum_s e_s O_s / sum_s e_s l_s, times the sigmoid
+// output gate. Sequences handled by a single split were written by attn_mma_kernel.
+template <int HD>
+__global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
+    __shared__ float e_s[kMaxSplits * kGQ], lsum_s[kGQ];
+    const int kvh = blockIdx.x, b = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int L = p.pos[b] + 1;
+    const int nsplit = (L + p.chunk - 1) / p.chunk;
+    if (nsplit <= 1) return;
+    const size_t part_floats = (size_t)kGQ * 2 + (size_t)kGQ * HD;
+    const float* parts = p.ws + (((size_t)b * p.Hkv + kvh) * kMaxSplits) * part_floats;
+    const float* proj = p.proj + (size_t)b * p.ldp;
     if (warp < kGQ) {
         float M = -INFINITY;
         for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(parts + s * part_floats + warp));
         M = warp_max(M);
+        float Ls = 0.0f;
         for (int s = lane; s < nsplit; s += 32) {
             const float ms = __ldcg(parts + s * part_floats + warp);
-            e_s[s * kGQ + warp] = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+            const float e = (ms == -INFINITY) ? 0.0f : expf(ms - M);
+            e_s[s * kGQ + warp] = e;
+            Ls += __ldcg(parts + s * part_floats + kGQ + warp) * e;
         }
-        __syncwarp();
-        if (lane == 0) {
-            float Lsum = 0.0f;
-            for (int s = 0; s < nsplit; s++) Lsum += __ldcg(parts + s * part_floats + kGQ + warp) * e_s[s * kGQ + warp];
-            lsum_s[warp] = Lsum;
-        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) lsum_s[warp] = Ls;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < kGQ * HD; i += kAttnMmaThreads) {
-        const int hh = i / HD, d = i % HD, h = kvh * kGQ + hh;
+    for (int e = threadIdx.x; e < kGQ * HD; e += blockDim.x) {
+        const int hh = e / HD, d = e % HD, h = kvh * kGQ + hh;
         float A = 0.0f;
 #pragma unroll 8
-        for (int s = 0; s < nsplit; s++) A += __ldcg(parts + s * part_floats + 2 * kGQ + i) * e_s[s * kGQ + hh];
-        float o = A / lsum_s[hh];
-        o *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
-        act_store(p.out, b, h * HD + d, o);
-        if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = o;
+        for (int s = 0; s < nsplit; s++) A += __ldcg(parts + s * part_floats + 2 * kGQ + e) * e_s[s * kGQ + hh];
+        float ov = A / lsum_s[hh];
+        ov *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
+        act_store(p.out, b, h * HD + d, ov);
+        if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = ov;
     }
-    if (threadIdx.x == 0) p.tickets[b * p.Hkv + kvh] = 0u;
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -443,28 +506,40 @@ int make_kv_tensor_map(void* map_out, void* base, int64_t rows, int hd) {
     return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-// tokens per split for the tensor-core kernel: about seven CTA waves over the SMs, and at
-// least kMinSplitTiles tiles per split so the pipeline fill and the merge stay small
+// Tokens per split of the persistent kernel. Items (split, sequence, kv head) are dealt to
+// the SMs round-robin, so the item count should sit just below a multiple of the SM count;
+// each item also costs about one tile of fixed work (prologue, partial write, merge). The
+// chunk minimising ceil(items / SMs) * (tiles per item + 1) wins, with at least
+// kMinSplitTiles tiles per split and at most kMaxSplits splits.
 constexpr int kMinSplitTiles = 4;
 int attn_mma_chunk(int batch, int hkv, int max_len, int num_sms) {
-    int pairs = batch * hkv;
-    int want = (7 * num_sms + pairs - 1) / pairs;
-    if (want < 1) want = 1;
-    int chunk = (max_len + want - 1) / want;
-    chunk = (chunk + kT - 1) / kT * kT;
-    return chunk < kMinSplitTiles * kT ? kMinSplitTiles * kT : chunk;
+    const int64_t pairs = (int64_t)batch * hkv;
+    int best_chunk = 0;
+    int64_t best_cost = INT64_MAX;
+    const int min_chunk = std::max(kMinSplitTiles * kT, (max_len + kMaxSplits - 1) / kMaxSplits);
+    for (int chunk = (min_chunk + kT - 1) / kT * kT; ; chunk += kT) {
+        const int64_t splits = (max_len + chunk - 1) / chunk;
+        const int64_t items = pairs * splits;
+        const int64_t per_cta = (items + num_sms - 1) / num_sms;
+        const int64_t cost = per_cta * (chunk / kT + 1);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best_chunk = chunk;
+        }
+        if (splits == 1) break;
+    }
+    return best_chunk;
 }
 
-// the split count is at most min(want, ceil(max_len / (kMinSplitTiles * kT)))
+// splits per (sequence, kv head) never exceed kMaxSplits: the workspace is sized for that
 int attn_mma_nsplit_bound(int batch, int hkv, int cap, int num_sms) {
-    int want = (7 * num_sms + batch * hkv - 1) / (batch * hkv);
-    int by_len = (cap + kMinSplitTiles * kT - 1) / (kMinSplitTiles * kT);
-    return want < by_len ? want : by_len;
+    (void)batch, (void)hkv, (void)cap, (void)num_sms;
+    return kMaxSplits;
 }
 
 template <int HD>
 static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch,
-                        int max_len, cudaStream_t st) {
+                        int max_len, int num_sms, cudaStream_t st) {
     const int smem = AttnSmem<HD>::bytes() + 1024;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -474,17 +549,25 @@ static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, i
             return -1;
         attr_set[dev & 63] = true;
     }
-    dim3 grid(attn_nsplit(max_len, p.chunk), p.Hkv, batch);
-    attn_mma_kernel<HD><<<grid, kAttnMmaThreads, smem, st>>>(*reinterpret_cast<const CUtensorMap*>(tmk),
-                                                             *reinterpret_cast<const CUtensorMap*>(tmv), p, row_base);
+    const int pairs = batch * p.Hkv;
+    const int splits = attn_nsplit(max_len, p.chunk);
+    if (splits > kMaxSplits || !p.qprep) return -1;
+    const int n_items = pairs * splits;
+    const int grid = std::min(n_items, num_sms);
+    if (launch_pdl(attn_prep_kernel<HD>, dim3(p.Hkv, batch), dim3(128), 0, st, p) != cudaSuccess) return -2;
+    if (launch_pdl(attn_mma_kernel<HD>, dim3(grid), dim3(kAttnMmaThreads), smem, st,
+                   *reinterpret_cast<const CUtensorMap*>(tmk), *reinterpret_cast<const CUtensorMap*>(tmv), p, row_base,
+                   pairs, n_items) != cudaSuccess)
+        return -2;
+    if (splits > 1) launch_pdl(attn_merge_kernel<HD>, dim3(p.Hkv, batch), dim3(256), 0, st, p);
     return 0;
 }
 
 int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,
-                         int max_len, cudaStream_t st) {
+                         int max_len, int num_sms, cudaStream_t st) {
     if (p.Hq != kGQ * p.Hkv) return -1;
-    if (hd == 256) return launch_mma_t<256>(tmk, tmv, p, row_base, batch, max_len, st);
-    if (hd == 128) return launch_mma_t<128>(tmk, tmv, p, row_base, batch, max_len, st);
+    if (hd == 256) return launch_mma_t<256>(tmk, tmv, p, row_base, batch, max_len, num_sms, st);
+    if (hd == 128) return launch_mma_t<128>(tmk, tmv, p, row_base, batch, max_len, num_sms, st);
     return -1;
 }
 

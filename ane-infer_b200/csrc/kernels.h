@@ -141,6 +141,7 @@ struct AttnParams {
     int Hq, Hkv;
     int chunk;           // tokens per split
     float* ws;           // split partials
+    float* qprep = nullptr;  // tensor-core kernel: normed, rotated queries [B][Hkv][Hq/Hkv][HD]
     unsigned* tickets;   // [B*Hkv]
     ActOut out;          // activations of the wo GEMM (K = Hq*HD)
     float* o_out;        // optional f32 copy [B][Hq*HD]
@@ -151,8 +152,9 @@ struct AttnParams {
 int make_kv_tensor_map(void* map_out /*128 bytes, 64-aligned*/, void* base, int64_t rows, int hd);
 int attn_mma_chunk(int batch, int hkv, int max_len, int num_sms);
 int attn_mma_nsplit_bound(int batch, int hkv, int cap, int num_sms);
+int attn_mma_launches(int max_len, int chunk);
 int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,
-                         int max_len, cudaStream_t st);
+                         int max_len, int num_sms, cudaStream_t st);
 int attn_nsplit(int max_len, int chunk);
 int attn_chunk(int batch, int hkv, int max_len, int num_sms);
 int attn_nsplit_bound(int batch, int hkv, int cap, int num_sms);

@@ -369,6 +369,7 @@ struct ab2_ctx {
     unsigned* gtk = nullptr;    // GEMM tickets
     float* h2 = nullptr;        // tcgen05 path: f32 gate/up sums [max_batch][2*ffn], kept zeroed
     float* aws = nullptr;       // attention split partials
+    float* aqp = nullptr;       // tensor-core attention: prepared queries [max_batch][Hq][hd]
     size_t aws_floats = 0;
     unsigned* atk = nullptr;    // attention tickets
     float2* rope = nullptr;     // [cap][rot/2]
@@ -602,6 +603,7 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
                 return seterr(AB2_ERR_CUDA, "could not encode the TMA tensor maps of the KV cache");
         }
         RET(x->dalloc(&x->aws, aws * 4));
+        if (x->kv_bf16) RET(x->dalloc(&x->aqp, (size_t)B * Hq * hd * 4));
         RET(x->dalloc(&x->atk, (size_t)B * Hkv * 4));
         // RoPE (cos, sin) table built with the host libm exactly as the reference computes it:
         // freq = 1 / base^(i / rot) for even i, angle = pos * freq (deltanet.rs:600-623)
@@ -747,6 +749,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv) > x->aws_floats)
             return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
         p.ws = x->aws;
+        p.qprep = x->aqp;
         p.tickets = x->atk;
         p.out = act(x, x->xfb, (int)(c.n_heads * c.hd), B);
         p.o_out = nullptr;
@@ -755,7 +758,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         if (x->kv_bf16) {
             // bf16 cache: TMA + tensor-core flash-decode; rows of (layer, slot s0, head 0, token 0)
             const int64_t row_base = ((int64_t)L.local * x->max_batch + s0) * c.n_kv * x->cap;
-            if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, st))
+            if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, x->num_sms, st))
                 return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
         } else if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st)) {
             return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
@@ -849,7 +852,15 @@ int64_t launches_per_step(const ab2_ctx* x, int B) {
     // embed + 7 per layer (8 on the tcgen05 path: the SwiGLU kernel) + final norm + lm_head +
     // 2 argmax passes + position advance
     const int64_t per_layer = umma_for(x, B) ? 8 : 7;
-    return 1 + (int64_t)x->layers.size() * per_layer + 1 + 1 + 2 + 1;
+    int64_t n = 1 + (int64_t)x->layers.size() * per_layer + 1 + 1 + 2 + 1;
+    if (x->kv_bf16 && x->c.n_attn > 0) {
+        // the tensor-core attention adds a merge kernel when the current context is split
+        int max_len = 1;
+        for (int b = 0; b < B && b < (int)x->pos_h.size(); b++) max_len = std::max(max_len, (int)x->pos_h[b] + 1);
+        const int chunk = attn_mma_chunk(B, (int)x->c.n_kv, max_len, x->num_sms);
+        n += x->c.n_attn * (attn_mma_launches(max_len, chunk) - 1);
+    }
+    return n;
 }
 
 // ------------------------------------------------------------------------- op-level cache
@@ -862,6 +873,8 @@ struct OpCache {
     uint8_t* xf = nullptr;
     size_t xf_bytes = 0;
     float2* rope = nullptr;
+    float* qp = nullptr;  // prepared queries of the tensor-core attention
+    size_t qp_bytes = 0;
     int64_t rope_rows = 0;
     int rope_rot = 0;
     float rope_base = 0;
@@ -1388,13 +1401,16 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
     }
     const int max_len = max_pos + 1;
     const int chunk = kv_bf16 ? attn_mma_chunk(B, Hkv, max_len, nsm) : attn_chunk(B, Hkv, max_len, nsm);
-    RET(ensure(&oc.ws, &oc.ws_bytes, attn_ws_floats(B, Hkv, attn_nsplit(max_len, chunk), hd, Hq / Hkv) * 4));
+    // the tensor-core kernel lays partials out with a fixed split stride (its split bound)
+    const int ws_splits = kv_bf16 ? attn_mma_nsplit_bound(B, Hkv, max_len, nsm) : attn_nsplit(max_len, chunk);
+    RET(ensure(&oc.ws, &oc.ws_bytes, attn_ws_floats(B, Hkv, ws_splits, hd, Hq / Hkv) * 4));
     size_t errb = oc.err ? 16 : 0;
     RET(ensure((void**)&oc.err, &errb, 16));
     size_t tkb = oc.tk_n * 4;
     RET(ensure((void**)&oc.tk, &tkb, (size_t)B * Hkv * 4));
     oc.tk_n = tkb / 4;
     RET(ensure((void**)&oc.xf, &oc.xf_bytes, xfrag_bytes(Hq * hd, B)));
+    if (kv_bf16) RET(ensure((void**)&oc.qp, &oc.qp_bytes, (size_t)B * Hq * hd * 4));
     AttnParams p;
     p.proj = proj;
     p.ldp = Hq * 2 * hd + 2 * Hkv * hd;
@@ -1411,6 +1427,7 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
     p.Hkv = Hkv;
     p.chunk = chunk;
     p.ws = (float*)oc.ws;
+    p.qprep = oc.qp;
     p.tickets = oc.tk;
     p.out = act_out(oc.xf, Hq * hd, B, false);
     p.o_out = out;
@@ -1420,7 +1437,7 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
         const int64_t rows = (int64_t)B * Hkv * cap;
         if (make_kv_tensor_map(tmk, k_cache, rows, hd) || make_kv_tensor_map(tmv, v_cache, rows, hd))
             return seterr(AB2_ERR_ARG, "could not encode TMA tensor maps for the caches (alignment?)");
-        if (launch_attention_mma(tmk, tmv, p, 0, B, hd, max_len, st))
+        if (launch_attention_mma(tmk, tmv, p, 0, B, hd, max_len, nsm, st))
             return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
     } else if (launch_attention(p, B, hd, false, max_len, st)) {
         return seterr(AB2_ERR_SHAPE, "unsupported attention shape");
