@@ -446,6 +446,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
     const int kvh = blockIdx.x, b = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int L = p.pos[b] + 1;
     const int nsplit = (L + p.chunk - 1) / p.chunk;
     if (nsplit <= 1) return;

@@ -90,6 +90,10 @@ __global__ void __launch_bounds__(kDnThreads) deltanet_fused_kernel(DnParams p) 
     const int D = p.D, H = p.H, K = p.K;
     const float* proj = p.proj + (size_t)b * p.ldp;
     float* S = p.S + (size_t)b * p.s_stride + (size_t)h * DK * DK;
+    // launched with programmatic dependent launch: wait for the input projection, then let
+    // the output projection start its weight prefetch
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     float4 st_regs[16];
     load_state(S, st_regs);  // 64 KB per CTA in flight while the prologue below runs
 
@@ -190,7 +194,7 @@ __global__ void __launch_bounds__(kDnThreads) gated_delta_kernel(float* S, const
 
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st) {
     dim3 grid(p.H, batch);
-    deltanet_fused_kernel<<<grid, kDnThreads, 0, st>>>(p);
+    launch_pdl(deltanet_fused_kernel, grid, dim3(kDnThreads), 0, st, p);
 }
 
 void launch_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,

@@ -71,6 +71,7 @@ __device__ __forceinline__ bool is_epi(int warp) { return warp >= 11; }
 __device__ __forceinline__ int epi_index(int warp) { return warp - 11; }
 constexpr int kUmmaThreads = 15 * 32;
 constexpr uint32_t kTmemCols = 512;               // two accumulators of 256 columns
+constexpr int kEpiBar = 1;                        // named barrier of the epilogue warps
 constexpr int kMinKTilesPerSplit = 4;
 static_assert(kConvWarps * 32 == kStageTiles * kRows, "one converter thread per weight row of a stage");
 
@@ -412,15 +413,69 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             tc_fence_after();
             const uint32_t dq = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((j & 1) * kPairRows);
             const int pr = u / KS;  // row-tile pair: rows pr*256 .. pr*256+255
+            if (u + G < U) {
+                // more units follow: the operand rings are busy, write from the TMEM rows
+#pragma unroll 1
+                for (int c = 0; c < kPairRows; c += 32) {
+                    float v[32];
+                    tmem_ld32(dq + c, v);
+                    if (row_ok) epi_out32(ep.y + (size_t)b * ep.ldy, pr * kPairRows + c, ep.m_out, how, v);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_free[j & 1]);
+                continue;
+            }
+            // the last unit: the f16 operand ring is idle (every MMA of the CTA has completed), so
+            // the accumulator goes through it as [64 rows][64 float4], float4 column index XOR
+            // (row % 8) against bank conflicts; then all 128 epilogue threads write whole rows
+            // with consecutive lanes on consecutive 16-byte pieces
+            float4* stage = reinterpret_cast<float4*>(smem + UmmaSmem::b_off(0));
+            const int r = q * 16 + (lane & 15);
 #pragma unroll 1
             for (int c = 0; c < kPairRows; c += 32) {
                 float v[32];
                 tmem_ld32(dq + c, v);
-                if (row_ok) epi_out32(ep.y + (size_t)b * ep.ldy, pr * kPairRows + c, ep.m_out, how, v);
+                if (lane < 16)
+#pragma unroll
+                    for (int e = 0; e < 8; e++)
+                        stage[r * 64 + ((c / 4 + e) ^ (r & 7))] =
+                            make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
             }
             tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_free[j & 1]);
+            asm volatile("bar.sync %0, %1;" ::"n"(kEpiBar), "n"(kEpiWarps * 32) : "memory");
+            const int et = threadIdx.x - 11 * 32;  // 0..127
+            const bool vec = (ep.ldy & 3) == 0;
+            for (int rr = et >> 6; rr < batch; rr += 2) {  // two rows per pass, 64 float4 each
+                const int c4 = et & 63;
+                const int m = pr * kPairRows + c4 * 4;
+                if (m >= ep.m_out) continue;
+                const float4 v = stage[rr * 64 + (c4 ^ (rr & 7))];
+                float* yp = ep.y + (size_t)rr * ep.ldy + m;
+                if (vec && m + 4 <= ep.m_out) {
+                    if (how == 2) {
+                        red_add_v4(yp, v.x, v.y, v.z, v.w);
+                    } else {
+                        float4 o = v;
+                        if (how == 1) {
+                            const float4 a = *reinterpret_cast<const float4*>(yp);
+                            o.x += a.x;
+                            o.y += a.y;
+                            o.z += a.z;
+                            o.w += a.w;
+                        }
+                        *reinterpret_cast<float4*>(yp) = o;
+                    }
+                } else {
+                    const float vv[4] = {v.x, v.y, v.z, v.w};
+                    for (int e = 0; e < 4 && m + e < ep.m_out; e++) {
+                        if (how == 2)
+                            atomicAdd(yp + e, vv[e]);
+                        else
+                            yp[e] = how == 1 ? yp[e] + vv[e] : vv[e];
+                    }
+                }
+            }
         }
     }
 
