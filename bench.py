@@ -138,6 +138,7 @@ def cpu_reference_tokps(gguf, shape, ctx_len: int, n_tokens: int = 0, seconds: f
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     from ane_infer_b200 import synth
+    oracle.lib().oracle_set_threads(len(os.sched_getaffinity(0)))
     om = oracle.Model(gguf, ctx_cap=ctx_len + 64)
     s = om.new_seq(kv_bf16=True)
     for l in range(shape.n_layers):
@@ -162,12 +163,15 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    load_pkg()
     from ane_infer_b200 import synth
     shape = synth.shape_2b()
     gguf = synth.build_model_gguf(shape, seed=0)
     total_steps = args.warmup + args.steps
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
+    # all host cores (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    oracle.lib().oracle_set_threads(len(os.sched_getaffinity(0)))
     om = oracle.Model(gguf, ctx_cap=args.ctx + total_steps + 8)
     s = om.new_seq(kv_bf16=True)
     for l in range(shape.n_layers):
@@ -281,6 +285,10 @@ def run_ours(args):
     dec = None
     if world > 1:
         dec = ShardedDecoder(lambda t: ctx.decode_step(t, want_logits=False)[1], B * world)
+        for _ in range(2):  # warm-up: the first scatter / gather set up their NCCL channels
+            host_tok = dec.step(host_tok if rank == 0 else None)
+    else:
+        _, host_tok = ctx.decode_step(host_tok, want_logits=False)
     barrier()
     t0 = time.perf_counter()
     for _ in range(n_e2e):
@@ -377,16 +385,24 @@ def run_op(args):
                                      out, st)
         nbytes = B * Hkv * ctx * hd * 2 * 2
         label = f"gqa flash-decode B={B} ctx={ctx} Hq=8 Hkv=2 hd=256"
-    # L2 (126 MB) is flushed before every timed launch by writing a 256 MB buffer, so inputs
-    # that fit in L2 (small batches) are still read from HBM
-    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    # L2 (126 MB) is flushed before every timed launch by writing one 256 MB buffer and then
+    # reading another, so inputs that fit in L2 (small batches) are read from HBM and the
+    # write-back of the flush's own dirty lines is not charged to the timed launch
+    flush_w = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def flush_l2():
+        flush_w.fill_(1.0)
+        torch.sum(flush_r, dim=0, out=sink)
+
     for _ in range(args.warmup):
-        flush.fill_(1.0)
+        flush_l2()
         fn()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.iters)]
     for e0, e1 in ev:
-        flush.fill_(1.0)
+        flush_l2()
         e0.record(st)
         fn()
         e1.record(st)
