@@ -119,6 +119,7 @@ struct DnParams {
     int D, H;
     ActOut out;          // activations of the ssm_out GEMM (K = D)
     float* o_out;        // optional f32 copy of the gated output [B][D]
+    unsigned* err = nullptr;  // bit 1024 set when a state copy did not arrive in time
 };
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
 // recurrence core only (op API): q,k,v bf16 [B][H][128], beta/decay f32 [B][H], o f32 [B][H][128]

@@ -727,6 +727,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.H = (int)c.dn_heads;
         p.out = act(x, x->xfb, D, B);
         p.o_out = nullptr;
+        p.err = x->err_d;
         ProfScope ps(x, PC_DN, st);
         launch_deltanet(p, B, st);
     } else {
@@ -845,7 +846,7 @@ int take_device_error(ab2_ctx* x) {
     *x->err_h = 0;
     cudaMemsetAsync(x->err_d, 0, 4, x->stream);
     cudaStreamSynchronize(x->stream);
-    return seterr(AB2_ERR_CUDA, "tcgen05 GEMM pipeline wait timed out (code 0x%x); results of this step are invalid", e);
+    return seterr(AB2_ERR_CUDA, "device pipeline wait timed out (code 0x%x); results of this step are invalid", e);
 }
 
 int64_t launches_per_step(const ab2_ctx* x, int B) {
