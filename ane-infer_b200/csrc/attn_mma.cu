@@ -296,7 +296,6 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             qa0[ks] = lo_row ? pack_bf16(l0, l1) : pack_bf16(h0, h1);
             qa2[ks] = lo_row ? pack_bf16(l2, l3) : pack_bf16(h2, h3);
         }
-        mbar_arrive(&q_free[qs]);
         k++;
         float o[NPV][4];
 #pragma unroll
@@ -389,6 +388,10 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             }
             mbar_arrive(&empty[s]);
         }
+        // The query slot is released after the item's tiles: the MMAs above consumed the
+        // registers loaded from it, so those loads are complete before the next copy into the
+        // slot can start (an arrival right after issuing them would not guarantee that).
+        mbar_arrive(&q_free[qs]);
         if (!ok) {
             // a timed-out wait: report it and stop; the results of this launch are invalid
             if (ct == 0 && p.err) atomicOr(p.err, 256u);

@@ -134,12 +134,44 @@ __device__ __forceinline__ DnItem dn_item(int j, int H) {
     return {item / H, item % H};
 }
 
+// The inputs of a group that do not come from the input projection: the conv states and
+// conv weights of this thread's channels (conv_k = 4), and ssm_a / dt_bias of item jg + tid.
+struct DnGroupIn {
+    float4 st[kConvPerThread], w4[kConvPerThread];
+    float sa, dtb;
+};
+
+__device__ __forceinline__ void dn_group_load(const DnParams& p, int jg, int ng, DnGroupIn& g) {
+    const int tid = threadIdx.x;
+    const int D = p.D, H = p.H;
+    const int nconv = ng * 3 * DK;
+    g.sa = 0.0f;
+    g.dtb = 0.0f;
+    if (tid < ng) {
+        const DnItem it = dn_item(jg + tid, H);
+        g.sa = p.ssm_a[it.h];
+        g.dtb = p.dt_bias[it.h];
+    }
+    if (p.K != 4) return;
+#pragma unroll
+    for (int u = 0; u < kConvPerThread; u++) {
+        const int e = tid + u * kDnThreads;
+        if (e < nconv) {
+            const int i = e / (3 * DK), rem = e % (3 * DK);
+            const DnItem it = dn_item(jg + i, H);
+            const int ch = (rem / DK) * D + it.h * DK + rem % DK;
+            g.st[u] = *reinterpret_cast<const float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4);
+            g.w4[u] = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
+        }
+    }
+}
+
 // conv_shift_and_append + conv_apply + SiLU (deltanet_cache.rs:34-54, deltanet.rs:444-450),
 // SiLU(gate) (deltanet.rs:527-533), beta = sigmoid(W_beta x) and
 // decay = exp(ssm_a * softplus(W_alpha x + dt_bias)) (deltanet.rs:469-480) for items jg..jg+ng-1,
 // then the per-head L2 norms of q (times 1/sqrt(dk)) and k (deltanet.rs:459-467)
-__device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int ng, float (*qkv)[3][DK],
-                                                 float (*gs)[DK], float (*bd)[2]) {
+__device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int ng, const DnGroupIn& g,
+                                                 float (*qkv)[3][DK], float (*gs)[DK], float (*bd)[2]) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = p.D, H = p.H, K = p.K;
     const int nconv = ng * 3 * DK;
@@ -154,17 +186,14 @@ __device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int 
             graw[u] = p.proj[(size_t)it.b * p.ldp + 3 * D + it.h * DK + e % DK];
         }
     }
-    float br = 0.0f, ar = 0.0f, sa = 0.0f, dtb = 0.0f;
+    float br = 0.0f, ar = 0.0f;
     if (tid < ng) {
         const DnItem it = dn_item(jg + tid, H);
         const float* proj = p.proj + (size_t)it.b * p.ldp;
         br = proj[4 * D + it.h];
         ar = proj[4 * D + H + it.h];
-        sa = p.ssm_a[it.h];
-        dtb = p.dt_bias[it.h];
     }
     if (K == 4) {
-        float4 st[kConvPerThread], w4[kConvPerThread];
         float in[kConvPerThread];
 #pragma unroll
         for (int u = 0; u < kConvPerThread; u++) {
@@ -172,10 +201,7 @@ __device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int 
             if (e < nconv) {
                 const int i = e / (3 * DK), rem = e % (3 * DK);
                 const DnItem it = dn_item(jg + i, H);
-                const int ch = (rem / DK) * D + it.h * DK + rem % DK;
-                st[u] = *reinterpret_cast<const float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4);
-                w4[u] = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
-                in[u] = p.proj[(size_t)it.b * p.ldp + ch];
+                in[u] = p.proj[(size_t)it.b * p.ldp + (rem / DK) * D + it.h * DK + rem % DK];
             }
         }
 #pragma unroll
@@ -185,12 +211,12 @@ __device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int 
                 const int i = e / (3 * DK), rem = e % (3 * DK);
                 const DnItem it = dn_item(jg + i, H);
                 const int ch = (rem / DK) * D + it.h * DK + rem % DK;
-                const float4 s4 = make_float4(st[u].y, st[u].z, st[u].w, in[u]);
+                const float4 s4 = make_float4(g.st[u].y, g.st[u].z, g.st[u].w, in[u]);
                 *reinterpret_cast<float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4) = s4;
-                float sum = s4.x * w4[u].x;
-                sum += s4.y * w4[u].y;
-                sum += s4.z * w4[u].z;
-                sum += s4.w * w4[u].w;
+                float sum = s4.x * g.w4[u].x;
+                sum += s4.y * g.w4[u].y;
+                sum += s4.z * g.w4[u].z;
+                sum += s4.w * g.w4[u].w;
                 qkv[i][rem / DK][rem % DK] = ref_silu(sum);
             }
         }
@@ -215,7 +241,7 @@ __device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int 
     }
     if (tid < ng) {
         bd[tid][0] = ref_sigmoid(br);
-        bd[tid][1] = expf(sa * ref_softplus(ar + dtb));
+        bd[tid][1] = expf(g.sa * ref_softplus(ar + g.dtb));
     }
     __syncthreads();
     for (int v = warp; v < 2 * ng; v += kDnThreads / 32) {
@@ -260,9 +286,6 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
         mbar_fence_init();
     }
     __syncthreads();
-    // the input projection (previous kernel) and the states of the previous step are complete
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     auto state_of = [&](int j) {
         const DnItem it = dn_item(j, H);
         return p.S + (size_t)it.b * p.s_stride + (size_t)it.h * DK * DK;
@@ -276,15 +299,28 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
         for (int c = 0; c < 4; c++)
             bulk_g2s(dst + c * (DK * DK / 4), src + c * (DK * DK / 4), kStateBytes / 4, &full[s]);
     };
+    // Launched with programmatic dependent launch behind the input projection GEMM, which lets
+    // this grid start once the GEMM has set up. The GEMM itself started only after the kernel
+    // before it (the RMSNorm, which waits for its own predecessor before it lets the next
+    // kernel start) had waited, so every kernel before that RMSNorm has completed, among them
+    // this layer's mixer of the previous step: the head states, conv states and weights can be
+    // read now. Only the projection output needs the wait.
     int issued = 0;  // thread 0: items whose state load has been issued
     if (tid == 0)
         for (; issued < min(kDnSlots, nmy); issued++) load(issued);
+    DnGroupIn gin;
+    dn_group_load(p, 0, min(kDnGroup, nmy), gin);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int r0 = warp * 16, c0 = lane * 4;  // this thread's 16 rows x 4 columns of a head state
     for (int jg = 0; jg < nmy; jg += kDnGroup) {
         const int ng = min(kDnGroup, nmy - jg);
-        __syncthreads();  // the previous group's inputs are no longer read
-        dn_prepare_group(p, jg, ng, qkv, gs, bd);
+        if (jg > 0) {
+            __syncthreads();  // the previous group's inputs are no longer read
+            dn_group_load(p, jg, ng, gin);
+        }
+        dn_prepare_group(p, jg, ng, gin, qkv, gs, bd);
         for (int i = 0; i < ng; i++) {
             const int j = jg + i;
             const DnItem it = dn_item(j, H);

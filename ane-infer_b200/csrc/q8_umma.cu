@@ -210,10 +210,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         s_abort = 0;
         for (int s = 0; s < kWStages; s++) {
             mbar_init(&w_full[s], 1);
-            mbar_init(&w_free[s], kConvWarps);
+            mbar_init(&w_free[s], kConvWarps * 32);
         }
         for (int s = 0; s < kBStages; s++) {
-            mbar_init(&b_full[s], kConvWarps);
+            mbar_init(&b_full[s], kConvWarps * 32);
             mbar_init(&b_free[s], 1);
         }
         for (int s = 0; s < kAStages; s++) {
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         }
         for (int j = 0; j < 2; j++) {
             mbar_init(&acc_full[j], 1);
-            mbar_init(&acc_free[j], kEpiWarps);
+            mbar_init(&acc_free[j], kEpiWarps * 32);
         }
         mbar_init(mma_done, 1);
         mbar_fence_init();
@@ -356,8 +356,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     qv[c] = *reinterpret_cast<const uint4*>(wb + ((size_t)c * kRows + r) * 16);
                 dd = *reinterpret_cast<const uint32_t*>(wb + 4 * kRows * 16 + r * 4);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&w_free[sw]);  // the raw weight stage has been read
             uint32_t hv[4][8];
             if (mine) {
 #pragma unroll
@@ -392,8 +390,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 }
                 fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&b_full[sb]);
+            // The raw stage is released only after the converted values have been stored: those
+            // stores consume the registers loaded from it, so the loads have completed. Arriving
+            // right after issuing the loads let the next copy into the slot overwrite bytes that
+            // a load had not read yet. Every writing thread arrives after its own proxy fence, so
+            // the MMA issued after the phase completes reads what each of them wrote.
+            mbar_arrive(&w_free[sw]);
+            mbar_arrive(&b_full[sb]);
           }
         }
     } else if (is_epi(warp)) {
@@ -422,8 +425,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     if (row_ok) epi_out32(ep.y + (size_t)b * ep.ldy, pr * kPairRows + c, ep.m_out, how, v);
                 }
                 tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_free[j & 1]);
+                mbar_arrive(&acc_free[j & 1]);  // this thread's TMEM loads are done
                 continue;
             }
             // the last unit: the f16 operand ring is idle (every MMA of the CTA has completed), so
