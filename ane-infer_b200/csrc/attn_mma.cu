@@ -117,19 +117,49 @@ int attn_mma_launches(int max_len, int chunk) { return (max_len + chunk - 1) / c
 // k_norm and rotated, and the new key and value appended to the bf16 cache at `pos`.
 template <int HD>
 __global__ void __launch_bounds__(128) attn_prep_kernel(AttnParams p) {
-    __shared__ float q_s[kGQ * HD], kn_s[HD], sc[kGQ + 1];
-    const int kvh = blockIdx.x, b = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    static_assert(HD % 4 == 0 && kGQ * HD % (4 * 128) == 0 && HD / 4 <= 128, "prep tiling");
+    __shared__ __align__(16) float q_s[kGQ * HD];
+    __shared__ __align__(16) float kn_s[HD];
+    __shared__ __align__(16) float qw_s[HD], kw_s[HD];
+    __shared__ float2 rope_s[HD / 2];
+    __shared__ float sc[kGQ + 1];
+    const int kvh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    // the norm weights are constants: fetched before the grid dependency wait
+    if (tid < HD / 4) {
+        if (p.q_norm) reinterpret_cast<float4*>(qw_s)[tid] = reinterpret_cast<const float4*>(p.q_norm)[tid];
+        if (p.k_norm) reinterpret_cast<float4*>(kw_s)[tid] = reinterpret_cast<const float4*>(p.k_norm)[tid];
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // every input load in flight at once: position, queries, key, value
     const int pos = p.pos[b];
     const float* proj = p.proj + (size_t)b * p.ldp;
     const int koff = p.Hq * 2 * HD, voff = koff + p.Hkv * HD;
-    for (int e = threadIdx.x; e < kGQ * HD; e += 128) {
-        const int hh = e / HD, d = e % HD;
-        q_s[e] = proj[(size_t)(kvh * kGQ + hh) * 2 * HD + d];
+    constexpr int kQ4 = kGQ * HD / 4 / 128;  // float4 of queries per thread
+    float4 qv[kQ4], kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
+#pragma unroll
+    for (int i = 0; i < kQ4; i++) {
+        const int e = (tid + i * 128) * 4, hh = e / HD, d = e % HD;
+        qv[i] = *reinterpret_cast<const float4*>(proj + (size_t)(kvh * kGQ + hh) * 2 * HD + d);
     }
-    for (int d = threadIdx.x; d < HD; d += 128) kn_s[d] = proj[koff + kvh * HD + d];
+    if (tid < HD / 4) {
+        kv4 = *reinterpret_cast<const float4*>(proj + koff + kvh * HD + tid * 4);
+        vv4 = *reinterpret_cast<const float4*>(proj + voff + kvh * HD + tid * 4);
+    }
+    const int half_rot = p.rot / 2;
+    const float2* rope = p.rope + (size_t)pos * half_rot;
+    for (int j = tid; j < half_rot; j += 128) rope_s[j] = rope[j];
+#pragma unroll
+    for (int i = 0; i < kQ4; i++) reinterpret_cast<float4*>(q_s)[tid + i * 128] = qv[i];
+    const size_t cache_off = (size_t)b * p.kv_slot_stride + (size_t)kvh * p.cap * HD + (size_t)pos * HD;
+    if (tid < HD / 4) {
+        reinterpret_cast<float4*>(kn_s)[tid] = kv4;
+        // the value is appended as it is (deltanet.rs:618-625)
+        __nv_bfloat162* vc = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(p.vc) + cache_off);
+        vc[2 * tid] = __floats2bfloat162_rn(vv4.x, vv4.y);
+        vc[2 * tid + 1] = __floats2bfloat162_rn(vv4.z, vv4.w);
+    }
     __syncthreads();
     // warps 0..3: query heads; warp 0 also the key
     {
@@ -145,31 +175,30 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(AttnParams p) {
         }
     }
     __syncthreads();
-    if (p.q_norm)
-        for (int e = threadIdx.x; e < kGQ * HD; e += 128) q_s[e] = q_s[e] * sc[e / HD] * p.q_norm[e % HD];
-    if (p.k_norm)
-        for (int d = threadIdx.x; d < HD; d += 128) kn_s[d] = kn_s[d] * sc[kGQ] * p.k_norm[d];
-    __syncthreads();
-    const int half_rot = p.rot / 2;
-    const float2* rope = p.rope + (size_t)pos * half_rot;
-    for (int e = threadIdx.x; e < (kGQ + 1) * half_rot; e += 128) {
-        const int hh = e / half_rot, j = e % half_rot;
-        float* tv = hh < kGQ ? q_s + hh * HD : kn_s;
-        const float2 cs = rope[j];
-        const float a0 = tv[2 * j], a1 = tv[2 * j + 1];
-        tv[2 * j] = a0 * cs.x - a1 * cs.y;
-        tv[2 * j + 1] = a0 * cs.y + a1 * cs.x;
-    }
-    __syncthreads();
+    // RMSNorm then RoPE on the first `rot` dims, one (head, dim pair) per thread step; the
+    // queries go to qprep, the key to the cache (deltanet.rs:565-617)
     float* qo = p.qprep + ((size_t)b * p.Hkv + kvh) * kGQ * HD;
-    for (int e = threadIdx.x; e < kGQ * HD; e += 128) qo[e] = q_s[e];
-    __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(p.kc) + (size_t)b * p.kv_slot_stride +
-                        (size_t)kvh * p.cap * HD + (size_t)pos * HD;
-    __nv_bfloat16* vc = reinterpret_cast<__nv_bfloat16*>(p.vc) + (size_t)b * p.kv_slot_stride +
-                        (size_t)kvh * p.cap * HD + (size_t)pos * HD;
-    for (int d = threadIdx.x; d < HD; d += 128) {
-        kc[d] = __float2bfloat16_rn(kn_s[d]);
-        vc[d] = __float2bfloat16_rn(proj[voff + kvh * HD + d]);
+    __nv_bfloat162* kc = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(p.kc) + cache_off);
+    for (int e = tid; e < (kGQ + 1) * (HD / 2); e += 128) {
+        const int hh = e / (HD / 2), j = e % (HD / 2);
+        const bool is_q = hh < kGQ;
+        const float* src = is_q ? q_s + hh * HD : kn_s;
+        float a0 = src[2 * j], a1 = src[2 * j + 1];
+        if (is_q ? p.q_norm != nullptr : p.k_norm != nullptr) {
+            const float* nw = is_q ? qw_s : kw_s;
+            a0 = a0 * sc[hh] * nw[2 * j];
+            a1 = a1 * sc[hh] * nw[2 * j + 1];
+        }
+        if (j < half_rot) {
+            const float2 cs = rope_s[j];
+            const float r0 = a0 * cs.x - a1 * cs.y, r1 = a0 * cs.y + a1 * cs.x;
+            a0 = r0;
+            a1 = r1;
+        }
+        if (is_q)
+            *reinterpret_cast<float2*>(qo + hh * HD + 2 * j) = make_float2(a0, a1);
+        else
+            kc[j] = __floats2bfloat162_rn(a0, a1);
     }
 }
 
@@ -252,6 +281,9 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                 }
             }
             if (!ok && p.err) atomicOr(p.err, 256u);
+            // all K/V copies of this CTA are issued: pull its share of the output projection's
+            // weights into L2 for the GEMM that follows
+            prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
             // every issued copy lands before the CTA can exit
             for (int j = max(0, i - kAttnStages); j < i; j++) mbar_wait(&full[j % kAttnStages], (j / kAttnStages) & 1);
             for (int j = max(0, k - 2); j < k; j++) mbar_wait(&q_full[j & 1], (j >> 1) & 1);
@@ -453,33 +485,56 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
     const int L = p.pos[b] + 1;
     const int nsplit = (L + p.chunk - 1) / p.chunk;
     if (nsplit <= 1) return;
+    static_assert(kGQ * HD % 4 == 0 && kGQ * HD <= 4 * 256 && kMaxSplits <= 64, "merge tiling: a float4 of outputs per thread");
     const size_t part_floats = (size_t)kGQ * 2 + (size_t)kGQ * HD;
     const float* parts = p.ws + (((size_t)b * p.Hkv + kvh) * kMaxSplits) * part_floats;
     const float* proj = p.proj + (size_t)b * p.ldp;
+    // this thread's four outputs (head hh, dims d..d+3) and their output gates, loaded first
+    const int e4 = threadIdx.x * 4, hh = e4 / HD, d = e4 % HD, h = kvh * kGQ + hh;
+    const bool has = e4 < kGQ * HD;
+    float4 gt = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (has) gt = *reinterpret_cast<const float4*>(proj + (size_t)h * 2 * HD + HD + d);
     if (warp < kGQ) {
-        float M = -INFINITY;
-        for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, __ldcg(parts + s * part_floats + warp));
-        M = warp_max(M);
-        float Ls = 0.0f;
-        for (int s = lane; s < nsplit; s += 32) {
-            const float ms = __ldcg(parts + s * part_floats + warp);
-            const float e = (ms == -INFINITY) ? 0.0f : expf(ms - M);
-            e_s[s * kGQ + warp] = e;
-            Ls += __ldcg(parts + s * part_floats + kGQ + warp) * e;
+        // lane s and s + 32 hold split s's (m, l) for head `warp`
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+        if (lane < nsplit) {
+            m0 = __ldcg(parts + lane * part_floats + warp);
+            l0 = __ldcg(parts + lane * part_floats + kGQ + warp);
         }
+        if (lane + 32 < nsplit) {
+            m1 = __ldcg(parts + (lane + 32) * part_floats + warp);
+            l1 = __ldcg(parts + (lane + 32) * part_floats + kGQ + warp);
+        }
+        const float M = warp_max(fmaxf(m0, m1));
+        const float e0 = (m0 == -INFINITY) ? 0.0f : expf(m0 - M);
+        const float e1 = (m1 == -INFINITY) ? 0.0f : expf(m1 - M);
+        if (lane < nsplit) e_s[lane * kGQ + warp] = e0;
+        if (lane + 32 < nsplit) e_s[(lane + 32) * kGQ + warp] = e1;
+        float Ls = l0 * e0;
+        Ls += l1 * e1;
         Ls = warp_sum(Ls);
         if (lane == 0) lsum_s[warp] = Ls;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < kGQ * HD; e += blockDim.x) {
-        const int hh = e / HD, d = e % HD, h = kvh * kGQ + hh;
-        float A = 0.0f;
+    if (!has) return;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
-        for (int s = 0; s < nsplit; s++) A += __ldcg(parts + s * part_floats + 2 * kGQ + e) * e_s[s * kGQ + hh];
-        float ov = A / lsum_s[hh];
-        ov *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
-        act_store(p.out, b, h * HD + d, ov);
-        if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d] = ov;
+    for (int s = 0; s < nsplit; s++) {
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(parts + s * part_floats + 2 * kGQ + e4));
+        const float w = e_s[s * kGQ + hh];
+        A.x += o.x * w;
+        A.y += o.y * w;
+        A.z += o.z * w;
+        A.w += o.w * w;
+    }
+    const float inv_l = lsum_s[hh];
+    const float av[4] = {A.x, A.y, A.z, A.w}, gv[4] = {gt.x, gt.y, gt.z, gt.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float ov = av[i] / inv_l;
+        ov *= ref_sigmoid(gv[i]);
+        act_store(p.out, b, h * HD + d + i, ov);
+        if (p.o_out) p.o_out[(size_t)b * p.Hq * HD + h * HD + d + i] = ov;
     }
 }
 

@@ -306,8 +306,10 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
     // this layer's mixer of the previous step: the head states, conv states and weights can be
     // read now. Only the projection output needs the wait.
     int issued = 0;  // thread 0: items whose state load has been issued
-    if (tid == 0)
+    if (tid == 0) {
         for (; issued < min(kDnSlots, nmy); issued++) load(issued);
+        if (issued == nmy) prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, G);
+    }
     DnGroupIn gin;
     dn_group_load(p, 0, min(kDnGroup, nmy), gin);
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -353,7 +355,12 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
             }
             *reinterpret_cast<float4*>(red + warp * DK + c0) = sk;
             __syncthreads();  // the slot has been read into registers
-            if (tid == 0 && issued < nmy) load(issued++);
+            if (tid == 0 && issued < nmy) {
+                load(issued++);
+                // the last head-state copy of this CTA is on its way: pull this CTA's share of
+                // the output projection's weights into L2 for the GEMM that follows
+                if (issued == nmy) prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, G);
+            }
             if (tid < DK) {
                 float a = 0.0f;
 #pragma unroll

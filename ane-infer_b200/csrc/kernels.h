@@ -57,6 +57,8 @@ struct GemmEpi {
     int ldy = 0;
     int m_out = 0;       // valid output rows (M, or ffn for SWIGLU)
     ActOut out{};        // SWIGLU: activations of the next GEMM
+    const void* pf = nullptr;  // optional: the next GEMM's weights, prefetched into L2 by this launch
+    int64_t pf_bytes = 0;
 };
 
 // the batch above which the tcgen05 path (q8t weights, x16 activations) is used
@@ -120,6 +122,8 @@ struct DnParams {
     ActOut out;          // activations of the ssm_out GEMM (K = D)
     float* o_out;        // optional f32 copy of the gated output [B][D]
     unsigned* err = nullptr;  // bit 1024 set when a state copy did not arrive in time
+    const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
+    int64_t pf_bytes = 0;
 };
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
 // recurrence core only (op API): q,k,v bf16 [B][H][128], beta/decay f32 [B][H], o f32 [B][H][128]
@@ -147,6 +151,8 @@ struct AttnParams {
     ActOut out;          // activations of the wo GEMM (K = Hq*HD)
     float* o_out;        // optional f32 copy [B][Hq*HD]
     unsigned* err = nullptr;  // pipeline error word (tensor-core kernel)
+    const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
+    int64_t pf_bytes = 0;
 };
 // attn_mma.cu: tensor-core flash-decode over a bf16 cache read through two TMA tensor maps
 // (K and V viewed as [rows][hd]); row_base = row of (first slot, kv head 0, token 0)

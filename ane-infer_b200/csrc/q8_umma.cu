@@ -72,6 +72,7 @@ __device__ __forceinline__ int epi_index(int warp) { return warp - 11; }
 constexpr int kUmmaThreads = 15 * 32;
 constexpr uint32_t kTmemCols = 512;               // two accumulators of 256 columns
 constexpr int kEpiBar = 1;                        // named barrier of the epilogue warps
+constexpr int kStageLd = kPairRows + 4;           // floats per staged accumulator row (16-byte pad)
 constexpr int kMinKTilesPerSplit = 4;
 static_assert(kConvWarps * 32 == kStageTiles * kRows, "one converter thread per weight row of a stage");
 
@@ -118,6 +119,8 @@ struct UmmaSmem {  // offsets from the 1024-aligned dynamic shared-memory base
     static constexpr int bytes() { return bar_off() + n_bars() * 8 + 16; }
 };
 static_assert(kBTileBytes % 1024 == 0 && kATileBytes % 1024 == 0, "operand tiles must stay 1024-aligned");
+static_assert(kBatchRows * kStageLd * 4 <= UmmaSmem::bar_off() - UmmaSmem::b_off(0),
+              "the staged accumulator fits in the operand rings");
 
 // Unit u = (row tile u / KS, K split u % KS) covers the len K tiles from k0. A CTA takes
 // units blockIdx.x, blockIdx.x + G, ...; every role walks them with plain nested loops
@@ -245,6 +248,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 const uint8_t* src = wt + ((size_t)mt * KT + k0) * kWStageBytes;  // the unit's blocks are contiguous
                 for (int q = 0; q < len; q++, st++) {
                     const int s = st % kWStages;
+                    // once the ring is full, pull this CTA's share of the next GEMM's weights
+                    // into L2 (this launch is latency-bound, so the extra HBM reads are free)
+                    if (st == kWStages) prefetch_share_l2(ep.pf, ep.pf_bytes, blockIdx.x, G);
                     if (st >= kWStages && !mbar_wait(&w_free[s], ((st / kWStages) - 1) & 1)) {
                         atomicOr(err, 1u);
                         s_abort = 1;
@@ -255,6 +261,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     bulk_g2s(smem + UmmaSmem::w_off(s), src + (size_t)q * kWStageBytes, kWStageBytes, &w_full[s]);
                 }
             }
+            if (st <= kWStages) prefetch_share_l2(ep.pf, ep.pf_bytes, blockIdx.x, G);
             for (int j = max(0, st - kWStages); j < st; j++)  // issued copies land before exit
                 if (!mbar_wait(&w_full[j % kWStages], (j / kWStages) & 1)) atomicOr(err, 2u);
         }
@@ -428,11 +435,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 mbar_arrive(&acc_free[j & 1]);  // this thread's TMEM loads are done
                 continue;
             }
-            // the last unit: the f16 operand ring is idle (every MMA of the CTA has completed), so
-            // the accumulator goes through it as [64 rows][64 float4], float4 column index XOR
-            // (row % 8) against bank conflicts; then all 128 epilogue threads write whole rows
-            // with consecutive lanes on consecutive 16-byte pieces
-            float4* stage = reinterpret_cast<float4*>(smem + UmmaSmem::b_off(0));
+            // The last unit: the operand rings are idle (every MMA of the CTA has completed, and
+            // every copy into them landed before its MMA), so the accumulator is staged there as
+            // [64 rows][kStageLd floats]; the 16-byte pad per row keeps the lane-per-row stores at
+            // most 2-way bank conflicted. Each batch row's outputs then leave in one bulk
+            // operation: a bulk store, or a bulk f32 add at L2 when the output accumulates
+            // (K splits, residual). Per-thread 16-byte reductions of the same data were bound
+            // by the L2's atomic rate when all CTAs reached their epilogue together.
+            float* stage = reinterpret_cast<float*>(smem + UmmaSmem::b_off(0));
             const int r = q * 16 + (lane & 15);
 #pragma unroll 1
             for (int c = 0; c < kPairRows; c += 32) {
@@ -441,18 +451,34 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 if (lane < 16)
 #pragma unroll
                     for (int e = 0; e < 8; e++)
-                        stage[r * 64 + ((c / 4 + e) ^ (r & 7))] =
+                        *reinterpret_cast<float4*>(stage + r * kStageLd + c + 4 * e) =
                             make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
             }
+            fence_proxy_async_smem();  // the bulk operations read the staged rows through the async proxy
             tc_fence_before();
             asm volatile("bar.sync %0, %1;" ::"n"(kEpiBar), "n"(kEpiWarps * 32) : "memory");
             const int et = threadIdx.x - 11 * 32;  // 0..127
+            const int m0 = pr * kPairRows, valid = min(kPairRows, ep.m_out - m0);
             const bool vec = (ep.ldy & 3) == 0;
+            if (valid > 0 && (valid & 3) == 0 && vec && (reinterpret_cast<uintptr_t>(ep.y) & 15) == 0) {
+                if (et < 32) {
+                    for (int rr = et; rr < batch; rr += 32) {
+                        float* dst = ep.y + (size_t)rr * ep.ldy + m0;
+                        if (how == 0)
+                            bulk_s2g(dst, stage + rr * kStageLd, (uint32_t)valid * 4);
+                        else
+                            bulk_reduce_add_f32(dst, stage + rr * kStageLd, (uint32_t)valid * 4);
+                    }
+                    bulk_commit();
+                    bulk_wait_all();
+                }
+                continue;
+            }
             for (int rr = et >> 6; rr < batch; rr += 2) {  // two rows per pass, 64 float4 each
                 const int c4 = et & 63;
-                const int m = pr * kPairRows + c4 * 4;
+                const int m = m0 + c4 * 4;
                 if (m >= ep.m_out) continue;
-                const float4 v = stage[rr * 64 + (c4 ^ (rr & 7))];
+                const float4 v = *reinterpret_cast<const float4*>(stage + rr * kStageLd + c4 * 4);
                 float* yp = ep.y + (size_t)rr * ep.ldy + m;
                 if (vec && m + 4 <= ep.m_out) {
                     if (how == 2) {

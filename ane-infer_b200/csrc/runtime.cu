@@ -670,6 +670,21 @@ bool umma_for(const ab2_ctx* x, int B) { return x->use_umma && B >= kUmmaMinBatc
 
 ActOut act(const ab2_ctx* x, uint8_t* buf, int K, int B) { return act_out(buf, K, B, umma_for(x, B)); }
 
+// L2 prefetch hint for a launch that precedes the tcgen05 GEMM on weight `w` (none on the
+// mma.sync path, whose weights are in the other layout); at most `cap` bytes
+void set_prefetch(ab2_ctx* x, int B, const Q8Weight* w, const void** pf, int64_t* pf_bytes,
+                  int64_t cap = INT64_MAX) {
+    *pf = nullptr;
+    *pf_bytes = 0;
+    if (!w || !w->qt || !umma_for(x, B)) return;
+    *pf = w->qt;
+    *pf_bytes = std::min<int64_t>((int64_t)w->qt_bytes(), cap);
+}
+
+// the part of a weight that one launch prefetches for its successor: L2 holds 126 MB, and the
+// lm_head (330 MB for the 2B shape) streams from HBM anyway after its first stages
+constexpr int64_t kPrefetchCap = 32ll << 20;
+
 int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st) {
     ProfScope ps(x, PC_GEMM, st);
     if (umma_for(x, B)) {
@@ -728,6 +743,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.out = act(x, x->xfb, D, B);
         p.o_out = nullptr;
         p.err = x->err_d;
+        set_prefetch(x, B, &L.w_out, &p.pf, &p.pf_bytes);
         ProfScope ps(x, PC_DN, st);
         launch_deltanet(p, B, st);
     } else {
@@ -755,6 +771,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.out = act(x, x->xfb, (int)(c.n_heads * c.hd), B);
         p.o_out = nullptr;
         p.err = x->err_d;
+        set_prefetch(x, B, &L.w_out, &p.pf, &p.pf_bytes);
         ProfScope ps(x, PC_ATTN, st);
         if (x->kv_bf16) {
             // bf16 cache: TMA + tensor-core flash-decode; rows of (layer, slot s0, head 0, token 0)
@@ -766,10 +783,14 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         }
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
+    set_prefetch(x, B, &L.gate_up, &e.pf, &e.pf_bytes);
     return gemm(x, L.w_out, x->xfb, B, e, st);
 }
 
-int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st) {
+// next: the weight of the GEMM that follows this FFN on the stream (prefetched into L2 by the
+// down projection), or null
+int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st,
+            const Q8Weight* next = nullptr) {
     const int D = (int)x->c.dim, F = (int)x->c.ffn;
     if (umma_for(x, B)) {
         // K-split gate/up sums into the zeroed f32 scratch, then silu(g)*u (which re-zeroes it)
@@ -778,6 +799,7 @@ int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cu
         e.y = x->h2;
         e.ldy = 2 * F;
         e.m_out = 2 * F;
+        set_prefetch(x, B, &L.down, &e.pf, &e.pf_bytes);
         RET(gemm(x, L.gate_up, x->xfa, B, e, st));
         ProfScope ps(x, PC_OTHER, st);
         launch_glu(x->h2, 2 * F, F, B, act(x, x->xfb, F, B), nullptr, 0, st);
@@ -785,6 +807,7 @@ int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cu
         RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
+    set_prefetch(x, B, next, &e.pf, &e.pf_bytes, kPrefetchCap);
     return gemm(x, L.down, x->xfb, B, e, st);
 }
 
@@ -809,7 +832,9 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
         launch_embed(x->embed, (int)c.vocab, tok_d, B, x->x, D, st);
     }
     const ActOut xa = act(x, x->xfa, D, B);
-    for (auto& L : x->layers) {
+    for (size_t li = 0; li < x->layers.size(); li++) {
+        const Layer& L = x->layers[li];
+        const Q8Weight* next = li + 1 < x->layers.size() ? &x->layers[li + 1].w_in : &x->lm_head;
         {
             // a K-split tcgen05 GEMM adds into its STORE output: clear the projection rows
             const bool zero = umma_for(x, B) && umma_nsplit(L.w_in.MT, L.w_in.KT, EPI_STORE, x->num_sms) > 1;
@@ -822,7 +847,7 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
             ProfScope ps(x, PC_OTHER, st);
             launch_rmsnorm_act(x->x, D, L.post_norm, D, c.eps, B, xa, st);
         }
-        RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st));
+        RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next));
     }
     {
         ProfScope ps(x, PC_OTHER, st);

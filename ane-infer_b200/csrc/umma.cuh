@@ -82,6 +82,40 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
         : "memory");
 }
 
+// L2 prefetch of [src, src + bytes) (16-byte aligned, size a multiple of 16), fire and forget
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// This CTA's share (CTA `part` of `parts`) of an L2 prefetch of `bytes` bytes at `src`, in
+// 32 KB pieces: how kernels pull the weights of the next GEMM on the stream into L2 while
+// their own work still runs, so that GEMM's pipeline fills from L2 instead of HBM.
+__device__ __forceinline__ void prefetch_share_l2(const void* src, int64_t bytes, int part, int parts) {
+    if (!src || bytes <= 0) return;
+    const int64_t per = ((bytes + parts - 1) / parts + 15) / 16 * 16;
+    const int64_t lo = (int64_t)part * per, hi = lo + per < bytes ? lo + per : bytes;
+    for (int64_t o = lo; o < hi; o += 32768) {
+        const int64_t n = hi - o < 32768 ? hi - o : 32768;
+        bulk_prefetch_l2(static_cast<const uint8_t*>(src) + o, (uint32_t)((n + 15) / 16 * 16));
+    }
+}
+
+// shared -> global bulk operations of the calling thread's bulk async-group (addresses 16-byte
+// aligned, size a multiple of 16): a plain copy, or an f32 add into global memory performed
+// at L2; bulk_commit closes the group and bulk_wait_all waits until its writes are complete
+__device__ __forceinline__ void bulk_s2g(void* dst_gmem, const void* src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem), "r"(smem_u32(src_smem)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_reduce_add_f32(float* dst_gmem, const float* src_smem, uint32_t bytes) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(dst_gmem),
+                 "r"(smem_u32(src_smem)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ------------------------------------------------------------------------------ tcgen05
