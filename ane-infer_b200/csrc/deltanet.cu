@@ -113,18 +113,24 @@ __global__ void __launch_bounds__(kDnThreads) gated_delta_kernel(float* S, const
 
 // ------------------------------------------------------------------------------------------
 // Persistent form of the fused mixer: CTA c takes the (sequence, head) items c, c + grid, ...
-// Each head's 64 KB state is copied into one of kDnSlots shared-memory slots with bulk copies
-// (four 16 KB pieces) issued kDnSlots heads ahead, read into registers (the same 16-row x
-// 4-column split as delta_rule_head), updated there and written back to global memory
-// with coalesced 16-byte stores, so the slot is refilled as soon as the registers hold it.
-// The per-head inputs (conv1d + SiLU of q/k/v, their L2 norms, beta, decay and SiLU(gate))
-// are prepared for kDnGroup heads at a time with every global load of the group in flight
-// at once, so their latency is paid once per group rather than once per head.
+// Two warp groups share the work:
+//   * eight update warps run the delta rule: each head's 64 KB state is copied into one of
+//     kDnSlots shared-memory slots with bulk copies (four 16 KB pieces) issued kDnSlots heads
+//     ahead, read into registers (the same 16-row x 4-column split as delta_rule_head),
+//     updated there and written back to global memory with coalesced 16-byte stores, so the
+//     slot is refilled as soon as the registers hold it;
+//   * four prep warps prepare the per-head inputs one or more heads ahead into a ring of
+//     kPrepSlots shared-memory slots: conv1d shift/append + SiLU of q/k/v, their L2 norms,
+//     beta, decay and SiLU(gate), with the global loads of the next head issued while the
+//     current one is computed.
+// The groups hand slots to each other through mbarriers and synchronise internally on their
+// own named barriers, so neither waits for the other's internal steps.
 constexpr int kDnSlots = 3;
-constexpr int kDnGroup = 8;
+constexpr int kPrepSlots = 3;
 constexpr int kStateBytes = DK * DK * 4;
-constexpr int kConvPerThread = kDnGroup * 3 * DK / kDnThreads;  // 12
-constexpr int kGatePerThread = kDnGroup * DK / kDnThreads;      // 4
+constexpr int kUpdThreads = 256, kPrepThreads = 128;
+constexpr int kDnPersistThreads = kUpdThreads + kPrepThreads;
+constexpr int kUpdBar = 1, kPrepBar = 2;  // named barriers (0 is __syncthreads)
 
 struct DnItem {
     int b, h;
@@ -134,147 +140,89 @@ __device__ __forceinline__ DnItem dn_item(int j, int H) {
     return {item / H, item % H};
 }
 
-// The inputs of a group that do not come from the input projection: the conv states and
-// conv weights of this thread's channels (conv_k = 4), and ssm_a / dt_bias of item jg + tid.
-struct DnGroupIn {
-    float4 st[kConvPerThread], w4[kConvPerThread];
-    float sa, dtb;
+struct PrepSlot {
+    float qkv[3][DK];  // q, k (normalised; q also scaled by 1/sqrt(dk)), v
+    float g[DK];       // SiLU(gate)
+    float beta, decay;
 };
 
-__device__ __forceinline__ void dn_group_load(const DnParams& p, int jg, int ng, DnGroupIn& g) {
-    const int tid = threadIdx.x;
-    const int D = p.D, H = p.H;
-    const int nconv = ng * 3 * DK;
-    g.sa = 0.0f;
-    g.dtb = 0.0f;
-    if (tid < ng) {
-        const DnItem it = dn_item(jg + tid, H);
-        g.sa = p.ssm_a[it.h];
-        g.dtb = p.dt_bias[it.h];
-    }
-    if (p.K != 4) return;
+// Global inputs of one head for one prep thread (channel `tid` of each of q, k, v).
+struct PrepIn {
+    float4 st[3], w4[3];  // conv states and conv weights (conv_k = 4)
+    float in[3], g;       // projection outputs: q/k/v channel and gate
+    float br, ar, sa, dtb;  // thread 0: beta/alpha inputs, ssm_a, dt_bias
+};
+
+// loads that do not depend on the input projection: conv states and weights, ssm_a, dt_bias
+__device__ __forceinline__ void prep_load_const(const DnParams& p, int j, int tid, PrepIn& in) {
+    const DnItem it = dn_item(j, p.H);
+    if (p.K == 4) {
 #pragma unroll
-    for (int u = 0; u < kConvPerThread; u++) {
-        const int e = tid + u * kDnThreads;
-        if (e < nconv) {
-            const int i = e / (3 * DK), rem = e % (3 * DK);
-            const DnItem it = dn_item(jg + i, H);
-            const int ch = (rem / DK) * D + it.h * DK + rem % DK;
-            g.st[u] = *reinterpret_cast<const float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4);
-            g.w4[u] = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
+        for (int i = 0; i < 3; i++) {
+            const int ch = i * p.D + it.h * DK + tid;
+            in.st[i] = *reinterpret_cast<const float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4);
+            in.w4[i] = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
         }
+    }
+    if (tid == 0) {
+        in.sa = p.ssm_a[it.h];
+        in.dtb = p.dt_bias[it.h];
+    }
+}
+// loads of the projection outputs (after the grid dependency wait)
+__device__ __forceinline__ void prep_load_proj(const DnParams& p, int j, int tid, PrepIn& in) {
+    const DnItem it = dn_item(j, p.H);
+    const float* proj = p.proj + (size_t)it.b * p.ldp;
+#pragma unroll
+    for (int i = 0; i < 3; i++) in.in[i] = proj[i * p.D + it.h * DK + tid];
+    in.g = proj[3 * p.D + it.h * DK + tid];
+    if (tid == 0) {
+        in.br = proj[4 * p.D + it.h];
+        in.ar = proj[4 * p.D + p.H + it.h];
     }
 }
 
 // conv_shift_and_append + conv_apply + SiLU (deltanet_cache.rs:34-54, deltanet.rs:444-450),
 // SiLU(gate) (deltanet.rs:527-533), beta = sigmoid(W_beta x) and
-// decay = exp(ssm_a * softplus(W_alpha x + dt_bias)) (deltanet.rs:469-480) for items jg..jg+ng-1,
-// then the per-head L2 norms of q (times 1/sqrt(dk)) and k (deltanet.rs:459-467)
-__device__ __forceinline__ void dn_prepare_group(const DnParams& p, int jg, int ng, const DnGroupIn& g,
-                                                 float (*qkv)[3][DK], float (*gs)[DK], float (*bd)[2]) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int D = p.D, H = p.H, K = p.K;
-    const int nconv = ng * 3 * DK;
-    // gate, beta and decay inputs: loads issued first, consumed after the conv loop
-    float graw[kGatePerThread];
+// decay = exp(ssm_a * softplus(W_alpha x + dt_bias)) (deltanet.rs:469-480) for head j
+__device__ __forceinline__ void prep_compute(const DnParams& p, int j, int tid, const PrepIn& in, PrepSlot& ps) {
+    const DnItem it = dn_item(j, p.H);
 #pragma unroll
-    for (int u = 0; u < kGatePerThread; u++) {
-        const int e = tid + u * kDnThreads;
-        graw[u] = 0.0f;
-        if (e < ng * DK) {
-            const DnItem it = dn_item(jg + e / DK, H);
-            graw[u] = p.proj[(size_t)it.b * p.ldp + 3 * D + it.h * DK + e % DK];
+    for (int i = 0; i < 3; i++) {
+        const int ch = i * p.D + it.h * DK + tid;
+        float* cs = p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * p.K;
+        float sum = 0.0f;
+        if (p.K == 4) {
+            const float4 s4 = make_float4(in.st[i].y, in.st[i].z, in.st[i].w, in.in[i]);
+            *reinterpret_cast<float4*>(cs) = s4;
+            sum = s4.x * in.w4[i].x;
+            sum += s4.y * in.w4[i].y;
+            sum += s4.z * in.w4[i].z;
+            sum += s4.w * in.w4[i].w;
+        } else {
+            const float* cw = p.conv_w + (size_t)ch * p.K;
+            for (int k = 0; k + 1 < p.K; k++) cs[k] = cs[k + 1];
+            cs[p.K - 1] = in.in[i];
+            for (int k = 0; k < p.K; k++) sum += cs[k] * cw[k];
         }
+        ps.qkv[i][tid] = ref_silu(sum);
     }
-    float br = 0.0f, ar = 0.0f;
-    if (tid < ng) {
-        const DnItem it = dn_item(jg + tid, H);
-        const float* proj = p.proj + (size_t)it.b * p.ldp;
-        br = proj[4 * D + it.h];
-        ar = proj[4 * D + H + it.h];
+    ps.g[tid] = in.g / (1.0f + expf(-in.g));
+    if (tid == 0) {
+        ps.beta = ref_sigmoid(in.br);
+        ps.decay = expf(in.sa * ref_softplus(in.ar + in.dtb));
     }
-    if (K == 4) {
-        float in[kConvPerThread];
-#pragma unroll
-        for (int u = 0; u < kConvPerThread; u++) {
-            const int e = tid + u * kDnThreads;
-            if (e < nconv) {
-                const int i = e / (3 * DK), rem = e % (3 * DK);
-                const DnItem it = dn_item(jg + i, H);
-                in[u] = p.proj[(size_t)it.b * p.ldp + (rem / DK) * D + it.h * DK + rem % DK];
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kConvPerThread; u++) {
-            const int e = tid + u * kDnThreads;
-            if (e < nconv) {
-                const int i = e / (3 * DK), rem = e % (3 * DK);
-                const DnItem it = dn_item(jg + i, H);
-                const int ch = (rem / DK) * D + it.h * DK + rem % DK;
-                const float4 s4 = make_float4(g.st[u].y, g.st[u].z, g.st[u].w, in[u]);
-                *reinterpret_cast<float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4) = s4;
-                float sum = s4.x * g.w4[u].x;
-                sum += s4.y * g.w4[u].y;
-                sum += s4.z * g.w4[u].z;
-                sum += s4.w * g.w4[u].w;
-                qkv[i][rem / DK][rem % DK] = ref_silu(sum);
-            }
-        }
-    } else {
-        for (int e = tid; e < nconv; e += kDnThreads) {
-            const int i = e / (3 * DK), rem = e % (3 * DK);
-            const DnItem it = dn_item(jg + i, H);
-            const int ch = (rem / DK) * D + it.h * DK + rem % DK;
-            float* cs = p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * K;
-            const float* cw = p.conv_w + (size_t)ch * K;
-            for (int k = 0; k + 1 < K; k++) cs[k] = cs[k + 1];
-            cs[K - 1] = p.proj[(size_t)it.b * p.ldp + ch];
-            float sum = 0.0f;
-            for (int k = 0; k < K; k++) sum += cs[k] * cw[k];
-            qkv[i][rem / DK][rem % DK] = ref_silu(sum);
-        }
-    }
-#pragma unroll
-    for (int u = 0; u < kGatePerThread; u++) {
-        const int e = tid + u * kDnThreads;
-        if (e < ng * DK) gs[e / DK][e % DK] = graw[u] / (1.0f + expf(-graw[u]));
-    }
-    if (tid < ng) {
-        bd[tid][0] = ref_sigmoid(br);
-        bd[tid][1] = expf(g.sa * ref_softplus(ar + g.dtb));
-    }
-    __syncthreads();
-    for (int v = warp; v < 2 * ng; v += kDnThreads / 32) {
-        float* x = qkv[v >> 1][v & 1];
-        float xs[4], ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            xs[i] = x[lane + 32 * i];
-            ss += xs[i] * xs[i];
-        }
-        ss = warp_sum(ss);
-        const float inv = 1.0f / sqrtf(ss + 1e-12f);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            float t = xs[i] * inv;
-            if ((v & 1) == 0) t *= 1.0f / sqrtf((float)DK);
-            x[lane + 32 * i] = t;
-        }
-    }
-    __syncthreads();
 }
 
-__global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParams p, int n_items) {
+__global__ void __launch_bounds__(kDnPersistThreads, 1) deltanet_persist_kernel(DnParams p, int n_items) {
     extern __shared__ uint8_t dn_smem_raw[];
     float* slots = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(dn_smem_raw) + 127) & ~(uintptr_t)127);
-    __shared__ __align__(16) float qkv[kDnGroup][3][DK];
-    __shared__ __align__(16) float gs[kDnGroup][DK];
-    __shared__ float bd[kDnGroup][2];
+    __shared__ __align__(16) PrepSlot prep[kPrepSlots];
     __shared__ __align__(16) float red[8 * DK];
     __shared__ __align__(16) float delta_s[DK];
     __shared__ float ssp[4];
-    __shared__ uint64_t full[kDnSlots];
-    __shared__ int s_abort;
+    __shared__ uint64_t full[kDnSlots], prep_full[kPrepSlots], prep_free[kPrepSlots];
+    __shared__ int s_abort, s_prep_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int H = p.H;
     const int G = gridDim.x;
@@ -282,7 +230,12 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
 
     if (tid == 0) {
         s_abort = 0;
+        s_prep_abort = 0;
         for (int s = 0; s < kDnSlots; s++) mbar_init(&full[s], 1);
+        for (int s = 0; s < kPrepSlots; s++) {
+            mbar_init(&prep_full[s], kPrepThreads);
+            mbar_init(&prep_free[s], kUpdThreads);
+        }
         mbar_fence_init();
     }
     __syncthreads();
@@ -290,6 +243,58 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
         const DnItem it = dn_item(j, H);
         return p.S + (size_t)it.b * p.s_stride + (size_t)it.h * DK * DK;
     };
+    // Launched with programmatic dependent launch behind the input projection GEMM, which lets
+    // this grid start once the GEMM has set up. The GEMM itself started only after the kernel
+    // before it (the RMSNorm, which waits for its own predecessor before it lets the next
+    // kernel start) had waited, so every kernel before that RMSNorm has completed, among them
+    // this layer's mixer of the previous step: the head states, conv states and weights can be
+    // read now. Only the projection output needs the wait.
+
+    if (tid >= kUpdThreads) {
+        // ---------------- prep warps: per-head inputs, one head ahead of the update warps
+        const int pt = tid - kUpdThreads;
+        PrepIn cur, nxt;
+        if (nmy > 0) prep_load_const(p, 0, pt, cur);
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+        if (nmy > 0) prep_load_proj(p, 0, pt, cur);
+        for (int j = 0; j < nmy; j++) {
+            const int s = j % kPrepSlots;
+            if (j + 1 < nmy) {  // the next head's loads overlap this head's math
+                prep_load_const(p, j + 1, pt, nxt);
+                prep_load_proj(p, j + 1, pt, nxt);
+            }
+            if (j >= kPrepSlots && !mbar_wait(&prep_free[s], ((j / kPrepSlots) - 1) & 1)) s_prep_abort = 1;
+            asm volatile("bar.sync %0, %1;" ::"n"(kPrepBar), "n"(kPrepThreads) : "memory");
+            if (s_prep_abort) break;
+            prep_compute(p, j, pt, cur, prep[s]);
+            asm volatile("bar.sync %0, %1;" ::"n"(kPrepBar), "n"(kPrepThreads) : "memory");
+            // per-head L2 norm of q (then * 1/sqrt(dk)) and k (deltanet.rs:459-467)
+            const int pw = pt >> 5;
+            if (pw < 2) {
+                float* v = prep[s].qkv[pw];
+                float xs[4], ss = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    xs[i] = v[lane + 32 * i];
+                    ss += xs[i] * xs[i];
+                }
+                ss = warp_sum(ss);
+                const float inv = 1.0f / sqrtf(ss + 1e-12f);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    float t = xs[i] * inv;
+                    if (pw == 0) t *= 1.0f / sqrtf((float)DK);
+                    v[lane + 32 * i] = t;
+                }
+            }
+            mbar_arrive(&prep_full[s]);
+            cur = nxt;
+        }
+        return;
+    }
+
+    // ---------------- update warps
     auto load = [&](int j) {  // thread 0
         const int s = j % kDnSlots;
         float* dst = slots + (size_t)s * DK * DK;
@@ -299,115 +304,101 @@ __global__ void __launch_bounds__(kDnThreads, 1) deltanet_persist_kernel(DnParam
         for (int c = 0; c < 4; c++)
             bulk_g2s(dst + c * (DK * DK / 4), src + c * (DK * DK / 4), kStateBytes / 4, &full[s]);
     };
-    // Launched with programmatic dependent launch behind the input projection GEMM, which lets
-    // this grid start once the GEMM has set up. The GEMM itself started only after the kernel
-    // before it (the RMSNorm, which waits for its own predecessor before it lets the next
-    // kernel start) had waited, so every kernel before that RMSNorm has completed, among them
-    // this layer's mixer of the previous step: the head states, conv states and weights can be
-    // read now. Only the projection output needs the wait.
     int issued = 0;  // thread 0: items whose state load has been issued
     if (tid == 0) {
         for (; issued < min(kDnSlots, nmy); issued++) load(issued);
         if (issued == nmy) prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, G);
     }
-    DnGroupIn gin;
-    dn_group_load(p, 0, min(kDnGroup, nmy), gin);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     const int r0 = warp * 16, c0 = lane * 4;  // this thread's 16 rows x 4 columns of a head state
-    for (int jg = 0; jg < nmy; jg += kDnGroup) {
-        const int ng = min(kDnGroup, nmy - jg);
-        if (jg > 0) {
-            __syncthreads();  // the previous group's inputs are no longer read
-            dn_group_load(p, jg, ng, gin);
-        }
-        dn_prepare_group(p, jg, ng, gin, qkv, gs, bd);
-        for (int i = 0; i < ng; i++) {
-            const int j = jg + i;
-            const DnItem it = dn_item(j, H);
-            const float* Ss = slots + (size_t)(j % kDnSlots) * DK * DK;
-            // every thread observes the copy's completion itself, so the bytes it reads from
-            // the slot are ones the bulk copy wrote
-            if (!mbar_wait(&full[j % kDnSlots], (j / kDnSlots) & 1)) s_abort = 1 + j;
-            __syncthreads();
-            if (s_abort) break;
-
-            // gated delta rule (deltanet.rs:485-512):
-            //   S *= decay; sk = S^T k; delta = beta (v - sk); S += k delta^T; o = S^T q
-            const float beta = bd[i][0], decay = bd[i][1];
-            const float* qv = qkv[i][0];
-            const float* kv = qkv[i][1];
-            float4 s[16];
-            float4 sk = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int r = 0; r < 16; r++) {
-                s[r] = *reinterpret_cast<const float4*>(Ss + (r0 + r) * DK + c0);
-                s[r].x *= decay;
-                s[r].y *= decay;
-                s[r].z *= decay;
-                s[r].w *= decay;
-                const float kr = kv[r0 + r];
-                sk.x += s[r].x * kr;
-                sk.y += s[r].y * kr;
-                sk.z += s[r].z * kr;
-                sk.w += s[r].w * kr;
-            }
-            *reinterpret_cast<float4*>(red + warp * DK + c0) = sk;
-            __syncthreads();  // the slot has been read into registers
-            if (tid == 0 && issued < nmy) {
-                load(issued++);
-                // the last head-state copy of this CTA is on its way: pull this CTA's share of
-                // the output projection's weights into L2 for the GEMM that follows
-                if (issued == nmy) prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, G);
-            }
-            if (tid < DK) {
-                float a = 0.0f;
-#pragma unroll
-                for (int w = 0; w < 8; w++) a += red[w * DK + tid];
-                delta_s[tid] = beta * (qkv[i][2][tid] - a);
-            }
-            __syncthreads();
-            float* Sg = const_cast<float*>(state_of(j));
-            const float4 dl = *reinterpret_cast<const float4*>(delta_s + c0);
-            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int r = 0; r < 16; r++) {
-                const float kr = kv[r0 + r], qr = qv[r0 + r];
-                s[r].x += kr * dl.x;
-                s[r].y += kr * dl.y;
-                s[r].z += kr * dl.z;
-                s[r].w += kr * dl.w;
-                __stcs(reinterpret_cast<float4*>(Sg + (size_t)(r0 + r) * DK + c0), s[r]);
-                o.x += s[r].x * qr;
-                o.y += s[r].y * qr;
-                o.z += s[r].z * qr;
-                o.w += s[r].w * qr;
-            }
-            *reinterpret_cast<float4*>(red + warp * DK + c0) = o;
-            __syncthreads();
-            // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533)
-            float ov = 0.0f;
-            if (tid < DK) {
-#pragma unroll
-                for (int w = 0; w < 8; w++) ov += red[w * DK + tid];
-                const float ss = warp_sum(ov * ov);
-                if (lane == 0) ssp[warp] = ss;
-            }
-            __syncthreads();
-            if (tid < DK) {
-                const float rms = 1.0f / sqrtf((ssp[0] + ssp[1] + ssp[2] + ssp[3]) / (float)DK + p.eps);
-                float nv = ov * rms * p.ssm_norm[tid];
-                nv *= gs[i][tid];
-                act_store(p.out, it.b, it.h * DK + tid, nv);
-                if (p.o_out) p.o_out[(size_t)it.b * p.D + it.h * DK + tid] = nv;
-            }
-        }
+    for (int j = 0; j < nmy; j++) {
+        const DnItem it = dn_item(j, H);
+        const int ps = j % kPrepSlots;
+        const float* Ss = slots + (size_t)(j % kDnSlots) * DK * DK;
+        // every thread observes the copy's and the prep slot's completion itself, so the bytes
+        // it reads are the ones the bulk copy and the prep warps wrote
+        if (!mbar_wait(&full[j % kDnSlots], (j / kDnSlots) & 1)) s_abort = 1 + j;
+        if (!mbar_wait(&prep_full[ps], (j / kPrepSlots) & 1)) s_abort = 1 + j;
+        asm volatile("bar.sync %0, %1;" ::"n"(kUpdBar), "n"(kUpdThreads) : "memory");
         if (s_abort) break;
+        const PrepSlot& in = prep[ps];
+
+        // gated delta rule (deltanet.rs:485-512):
+        //   S *= decay; sk = S^T k; delta = beta (v - sk); S += k delta^T; o = S^T q
+        const float beta = in.beta, decay = in.decay;
+        const float* qv = in.qkv[0];
+        const float* kv = in.qkv[1];
+        float4 s[16];
+        float4 sk = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+            s[r] = *reinterpret_cast<const float4*>(Ss + (r0 + r) * DK + c0);
+            s[r].x *= decay;
+            s[r].y *= decay;
+            s[r].z *= decay;
+            s[r].w *= decay;
+            const float kr = kv[r0 + r];
+            sk.x += s[r].x * kr;
+            sk.y += s[r].y * kr;
+            sk.z += s[r].z * kr;
+            sk.w += s[r].w * kr;
+        }
+        *reinterpret_cast<float4*>(red + warp * DK + c0) = sk;
+        asm volatile("bar.sync %0, %1;" ::"n"(kUpdBar), "n"(kUpdThreads) : "memory");  // the slot is in registers
+        if (tid == 0 && issued < nmy) {
+            load(issued++);
+            // the last head-state copy of this CTA is on its way: pull this CTA's share of
+            // the output projection's weights into L2 for the GEMM that follows
+            if (issued == nmy) prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, G);
+        }
+        if (tid < DK) {
+            float a = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; w++) a += red[w * DK + tid];
+            delta_s[tid] = beta * (in.qkv[2][tid] - a);
+        }
+        asm volatile("bar.sync %0, %1;" ::"n"(kUpdBar), "n"(kUpdThreads) : "memory");
+        float* Sg = const_cast<float*>(state_of(j));
+        const float4 dl = *reinterpret_cast<const float4*>(delta_s + c0);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+            const float kr = kv[r0 + r], qr = qv[r0 + r];
+            s[r].x += kr * dl.x;
+            s[r].y += kr * dl.y;
+            s[r].z += kr * dl.z;
+            s[r].w += kr * dl.w;
+            __stcs(reinterpret_cast<float4*>(Sg + (size_t)(r0 + r) * DK + c0), s[r]);
+            o.x += s[r].x * qr;
+            o.y += s[r].y * qr;
+            o.z += s[r].z * qr;
+            o.w += s[r].w * qr;
+        }
+        *reinterpret_cast<float4*>(red + warp * DK + c0) = o;
+        asm volatile("bar.sync %0, %1;" ::"n"(kUpdBar), "n"(kUpdThreads) : "memory");
+        // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533)
+        float ov = 0.0f;
+        if (tid < DK) {
+#pragma unroll
+            for (int w = 0; w < 8; w++) ov += red[w * DK + tid];
+            const float ss = warp_sum(ov * ov);
+            if (lane == 0) ssp[warp] = ss;
+        }
+        asm volatile("bar.sync %0, %1;" ::"n"(kUpdBar), "n"(kUpdThreads) : "memory");
+        if (tid < DK) {
+            const float rms = 1.0f / sqrtf((ssp[0] + ssp[1] + ssp[2] + ssp[3]) / (float)DK + p.eps);
+            float nv = ov * rms * p.ssm_norm[tid];
+            nv *= in.g[tid];
+            act_store(p.out, it.b, it.h * DK + tid, nv);
+            if (p.o_out) p.o_out[(size_t)it.b * p.D + it.h * DK + tid] = nv;
+        }
+        mbar_arrive(&prep_free[ps]);  // this thread's reads of the prep slot are done
     }
     if (tid == 0 && s_abort) {
-        // a state copy timed out: report it, then give the copies still in flight into the
-        // slots a bounded time to land before the CTA's shared memory is released
+        // a copy or a prep slot did not arrive in time: report it, then give the copies still in
+        // flight into the state slots a bounded time to land before shared memory is released
         if (p.err) atomicOr(p.err, 1024u);
         for (int k = s_abort - 1; k < issued; k++) mbar_wait(&full[k % kDnSlots], (k / kDnSlots) & 1);
     }
@@ -425,7 +416,7 @@ void launch_deltanet(const DnParams& p, int batch, cudaStream_t st) {
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int n_items = p.H * batch;
-    launch_pdl(deltanet_persist_kernel, dim3(std::min(n_items, nsm)), dim3(kDnThreads), smem, st, p, n_items);
+    launch_pdl(deltanet_persist_kernel, dim3(std::min(n_items, nsm)), dim3(kDnPersistThreads), smem, st, p, n_items);
 }
 
 void launch_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,
