@@ -156,6 +156,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t r[32]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// named barrier of the four epilogue warps that also returns the OR of `v` over them
+__device__ __forceinline__ bool epi_bar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kEpiBar), "n"(kEpiWarps * 32)
+        : "memory");
+    return r != 0;
+}
+
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, int MP, int KT, int KS, const uint8_t* __restrict__ x16,
                         int batch, unsigned* __restrict__ err, GemmEpi ep) {
@@ -369,12 +383,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         const int how = (KS > 1 || ep.mode == EPI_ADD) ? 2 : (ep.mode == EPI_RESID ? 1 : 0);
         pdl_wait();  // outputs may be read or written by earlier kernels of the stream
         for (int j = 0, u = blockIdx.x; u < U; j++, u += G) {
-            if (!mbar_wait(&acc_full[j & 1], (j >> 1) & 1)) {
+            const bool fail = !mbar_wait(&acc_full[j & 1], (j >> 1) & 1);
+            if (fail) {
                 atomicOr(err, 512u);
                 s_abort = 1;
-                break;
             }
-            if (*(volatile int*)&s_abort) break;
+            // one outcome for all epilogue threads, which meet at a named barrier below
+            if (epi_bar_or(fail || *(volatile int*)&s_abort)) break;
             tc_fence_after();
             const uint32_t dq = tmem + ((uint32_t)(q * 32) << 16) + kAccCol0 + (uint32_t)((j & 1) * kPairRows / 2);
             const int pr = u / KS;  // row-tile pair: rows pr*256 .. pr*256+255
