@@ -7,7 +7,10 @@ replica. The only traffic is the host plumbing the reference's caller does for o
 here for the whole batch: rank 0 scatters each rank's token ids and gathers the next ids.
 
 `torch.distributed` carries the two small messages (4 bytes per sequence); with the NCCL
-backend they travel as device tensors, with gloo (the CPU tests) as host tensors.
+backend they travel as device tensors, with gloo (the CPU tests) as host tensors. With a
+device step function (`step_fn_device`, NCCL) the ids stay on the device between the
+collectives: rank 0 makes one host-to-device copy of the batch's ids and one device-to-host
+copy of the next ids per step, and every rank decodes straight from the scattered tensor.
 """
 from __future__ import annotations
 
@@ -49,8 +52,8 @@ class ShardedDecoder:
     the same collective steps in the same order.
     """
 
-    def __init__(self, step_fn: Callable[[np.ndarray], np.ndarray], global_batch: int, group=None,
-                 device: Optional[str] = None):
+    def __init__(self, step_fn: Optional[Callable[[np.ndarray], np.ndarray]], global_batch: int, group=None,
+                 device: Optional[str] = None, step_fn_device: Optional[Callable] = None):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
@@ -63,6 +66,22 @@ class ShardedDecoder:
         if device is None:
             device = "cuda" if dist.get_backend(group) == "nccl" else "cpu"
         self.device = device
+        # step_fn_device(tokens_dev, next_dev): enqueue this rank's step on the current stream,
+        # reading int32 ids from tokens_dev [count] and writing the next ids to next_dev [count]
+        self.step_fn_device = step_fn_device
+        if step_fn is None and step_fn_device is None:
+            raise ValueError("a step function is required")
+        if step_fn_device is not None:
+            import torch
+            w = max(self.width, 1)
+            self._mine = torch.zeros(w, dtype=torch.int32, device=device)
+            self._next = torch.full((w,), -1, dtype=torch.int32, device=device)
+            if self.rank == 0:
+                self._send = torch.full((self.world, w), -1, dtype=torch.int32, device=device)
+                self._recv = torch.empty((self.world, w), dtype=torch.int32, device=device)
+                pin = device != "cpu"
+                self._send_h = torch.full((self.world, w), -1, dtype=torch.int32, pin_memory=pin)
+                self._recv_h = torch.empty((self.world, w), dtype=torch.int32, pin_memory=pin)
 
     def _padded(self, ids: np.ndarray):
         import torch
@@ -77,6 +96,8 @@ class ShardedDecoder:
         dist = self.dist
         if self.width == 0:
             return np.zeros(0, dtype=np.int32) if self.rank == 0 else None
+        if self.step_fn_device is not None:
+            return self._step_device(tokens)
         scatter_list = None
         if self.rank == 0:
             tokens = np.asarray(tokens, dtype=np.int32)
@@ -101,4 +122,35 @@ class ShardedDecoder:
         for r in range(self.world):
             s, c = shard_range(self.global_batch, self.world, r)
             res[s:s + c] = gather_list[r][:c].cpu().numpy()
+        return res
+
+    def _step_device(self, tokens: Optional[np.ndarray]) -> Optional[np.ndarray]:
+        import torch
+        dist = self.dist
+        scatter_list = gather_list = None
+        if self.rank == 0:
+            tokens = np.asarray(tokens, dtype=np.int32)
+            if tokens.shape != (self.global_batch,):
+                raise ValueError(f"expected {self.global_batch} token ids, got shape {tokens.shape}")
+            sh = self._send_h.numpy()
+            for r in range(self.world):
+                s, c = shard_range(self.global_batch, self.world, r)
+                sh[r, :c] = tokens[s:s + c]
+            self._send.copy_(self._send_h, non_blocking=True)
+            scatter_list = list(self._send.unbind(0))
+            gather_list = list(self._recv.unbind(0))
+        dist.scatter(self._mine, scatter_list, src=0, group=self.group)
+        if self.count:
+            self.step_fn_device(self._mine[: self.count], self._next[: self.count])
+        dist.gather(self._next, gather_list, dst=0, group=self.group)
+        if self.rank != 0:
+            return None
+        self._recv_h.copy_(self._recv, non_blocking=True)
+        if self.device != "cpu":
+            torch.cuda.current_stream().synchronize()
+        rh = self._recv_h.numpy()
+        res = np.empty(self.global_batch, dtype=np.int32)
+        for r in range(self.world):
+            s, c = shard_range(self.global_batch, self.world, r)
+            res[s:s + c] = rh[r, :c]
         return res

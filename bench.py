@@ -281,10 +281,13 @@ def run_ours(args):
 
     # ---- end to end through the host-buffer API: rank 0 holds every sequence's token id;
     # with N > 1 the ids are scattered to the ranks and the next ids gathered back each step
+    # (one host-to-device and one device-to-host copy of the batch's ids on rank 0)
     host_tok = synth.seeded_tokens(B * world, cfg["vocab"], seed=5)
     dec = None
     if world > 1:
-        dec = ShardedDecoder(lambda t: ctx.decode_step(t, want_logits=False)[1], B * world)
+        def dev_step(t, n):
+            ctx.decode_step_device(t, t.numel(), None, n, torch.cuda.current_stream())
+        dec = ShardedDecoder(None, B * world, step_fn_device=dev_step)
         for _ in range(2):  # warm-up: the first scatter / gather set up their NCCL channels
             host_tok = dec.step(host_tok if rank == 0 else None)
     else:
@@ -297,6 +300,7 @@ def run_ours(args):
         else:
             host_tok = dec.step(host_tok if rank == 0 else None)
     barrier()
+    ctx.sync()  # raises if a device pipeline wait timed out during the end-to-end steps
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = world * B * n_e2e / e2e_s
 
