@@ -850,8 +850,11 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
         RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next));
     }
     {
+        // a K-split lm_head adds into the logits (small vocabularies): clear them first
+        const bool zero = umma_for(x, B) && umma_nsplit(x->lm_head.MT, x->lm_head.KT, EPI_STORE, x->num_sms) > 1;
         ProfScope ps(x, PC_OTHER, st);
-        launch_rmsnorm_act(x->x, D, x->final_norm, D, c.eps, B, xa, st);
+        launch_rmsnorm_act(x->x, D, x->final_norm, D, c.eps, B, xa, st, zero ? logits_d : nullptr, (int)c.vocab,
+                           (int)c.vocab);
     }
     RET(gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st));
     {

@@ -59,6 +59,27 @@ def test_tiny_batched_slots_ragged(pkg, oracle, tiny_gguf, tiny_model):
     ctx.close()
 
 
+def test_small_vocab_batched_split_lm_head(pkg, oracle, synth):
+    # vocab 4096 is 16 row pairs, so with 9 slots (tcgen05 path) the lm_head runs K-split and
+    # adds into the logits: they must be cleared every step, not accumulate across steps
+    shape = synth.HybridShape(n_layers=4, dim=1024, vocab=4096, ffn=1024, dn_heads=8, attn_heads=8, kv_heads=2,
+                              head_dim=128)
+    gguf = synth.build_model_gguf(shape, seed=3)
+    om = oracle.Model(gguf, ctx_cap=64)
+    B = 9
+    seqs = [om.new_seq(kv_bf16=True) for _ in range(B)]
+    ctx = pkg.DecodeContext(gguf, max_batch=B, max_ctx=64, kv_bf16=True)
+    toks = [11 * b + 1 for b in range(B)]
+    for step in range(4):
+        lg, nx = ctx.decode_step(toks)
+        for b in range(B):
+            ref = seqs[b].forward(toks[b])
+            assert rel_err(lg[b], ref) < LOGIT_TOL, (step, b)
+            assert int(nx[b]) == oracle.greedy(lg[b]), (step, b)
+        toks = [int(t) for t in nx]
+    ctx.close()
+
+
 def test_state_io_and_capacity(pkg, tiny_gguf):
     ctx = pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=8, kv_bf16=True)
     rng = np.random.default_rng(4)
