@@ -94,8 +94,8 @@ void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out,
 // 128-row block the first 64 are gate rows, the next 64 the matching up rows): silu(g)*u for
 // the F outputs goes to `out` (and to y [batch][ldy] if y is set), and h2 is zeroed again.
 void launch_glu(float* h2, int ld, int F, int batch, const ActOut& out, float* y, int ldy, cudaStream_t st);
-void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st);
-// argmax split over nch chunks per row (part: [batch][nch] scratch), same tie rule
+// argmax under f32::total_cmp with ties going to the last index (greedy_sample,
+// crates/cli/src/main.rs:1767-1785), split over nch chunks per row (part: [batch][nch] scratch)
 constexpr int kArgmaxChunks = 32;
 void launch_argmax2(const float* logits, int ld, int V, int batch, int32_t* out, int2* part, int nch,
                     cudaStream_t st);

@@ -161,53 +161,9 @@ void launch_glu(float* h2, int ld, int F, int batch, const ActOut& out, float* y
     launch_pdl(glu_kernel, grid, dim3(threads), 0, st, h2, ld, F, out, y, ldy);
 }
 
-// argmax under f32::total_cmp with ties going to the last index, as Iterator::max_by
-// (greedy_sample, crates/cli/src/main.rs:1767-1785). One CTA per batch row.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int ld, int V,
-                                                      int32_t* __restrict__ out) {
-    __shared__ int32_t sk[32];
-    __shared__ int32_t si[32];
-    const int b = blockIdx.x;
-    const float* l = logits + (size_t)b * ld;
-    int32_t bk = INT32_MIN, bi = -1;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        int32_t k = total_key(l[i]);
-        if (k > bk || (k == bk && i > bi)) {
-            bk = k;
-            bi = i;
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
-        if (ok > bk || (ok == bk && oi > bi)) {
-            bk = ok;
-            bi = oi;
-        }
-    }
-    const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
-    if (ln == 0) {
-        sk[w] = bk;
-        si[w] = bi;
-    }
-    __syncthreads();
-    if (w == 0) {
-        const int nw = blockDim.x >> 5;
-        bk = ln < nw ? sk[ln] : INT32_MIN;
-        bi = ln < nw ? si[ln] : -1;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            int32_t ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
-            if (ok > bk || (ok == bk && oi > bi)) {
-                bk = ok;
-                bi = oi;
-            }
-        }
-        if (ln == 0) out[b] = bi < 0 ? 0 : bi;
-    }
-}
-
-// two-pass argmax: pass 1 reduces chunk c of row b to (key, index) in part[b][c]
+// Two-pass argmax under f32::total_cmp with ties going to the last index, as
+// Iterator::max_by (greedy_sample, crates/cli/src/main.rs:1767-1785): pass 1 reduces chunk c
+// of row b to (key, index) in part[b][c]
 __global__ void __launch_bounds__(512) argmax_part_kernel(const float* __restrict__ logits, int ld, int V,
                                                            int2* __restrict__ part) {
     __shared__ int32_t sk[16], si[16];
@@ -288,10 +244,6 @@ void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float ep
 
 void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st) {
     to_act_kernel<<<batch, 256, 0, st>>>(x, ldx, K, out);
-}
-
-void launch_argmax(const float* logits, int ld, int V, int batch, int32_t* out, cudaStream_t st) {
-    argmax_kernel<<<batch, 1024, 0, st>>>(logits, ld, V, out);
 }
 
 __global__ void pos_advance_kernel(int32_t* pos, int batch) {
