@@ -598,7 +598,7 @@ int attn_mma_nsplit_bound(int batch, int hkv, int cap, int num_sms) {
 
 template <int HD>
 static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch,
-                        int max_len, int num_sms, cudaStream_t st) {
+                        int max_len, int num_sms, cudaStream_t st, cudaEvent_t core_begin, cudaEvent_t core_end) {
     const int smem = AttnSmem<HD>::bytes() + 1024;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -614,19 +614,21 @@ static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, i
     const int n_items = pairs * splits;
     const int grid = std::min(n_items, num_sms);
     if (launch_pdl(attn_prep_kernel<HD>, dim3(p.Hkv, batch), dim3(128), 0, st, p) != cudaSuccess) return -2;
+    if (core_begin) cudaEventRecord(core_begin, st);
     if (launch_pdl(attn_mma_kernel<HD>, dim3(grid), dim3(kAttnMmaThreads), smem, st,
                    *reinterpret_cast<const CUtensorMap*>(tmk), *reinterpret_cast<const CUtensorMap*>(tmv), p, row_base,
                    pairs, n_items) != cudaSuccess)
         return -2;
+    if (core_end) cudaEventRecord(core_end, st);
     if (splits > 1) launch_pdl(attn_merge_kernel<HD>, dim3(p.Hkv, batch), dim3(256), 0, st, p);
     return 0;
 }
 
 int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,
-                         int max_len, int num_sms, cudaStream_t st) {
+                         int max_len, int num_sms, cudaStream_t st, cudaEvent_t core_begin, cudaEvent_t core_end) {
     if (p.Hq != kGQ * p.Hkv) return -1;
-    if (hd == 256) return launch_mma_t<256>(tmk, tmv, p, row_base, batch, max_len, num_sms, st);
-    if (hd == 128) return launch_mma_t<128>(tmk, tmv, p, row_base, batch, max_len, num_sms, st);
+    if (hd == 256) return launch_mma_t<256>(tmk, tmv, p, row_base, batch, max_len, num_sms, st, core_begin, core_end);
+    if (hd == 128) return launch_mma_t<128>(tmk, tmv, p, row_base, batch, max_len, num_sms, st, core_begin, core_end);
     return -1;
 }
 

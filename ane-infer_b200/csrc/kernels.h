@@ -160,8 +160,11 @@ int make_kv_tensor_map(void* map_out /*128 bytes, 64-aligned*/, void* base, int6
 int attn_mma_chunk(int batch, int hkv, int max_len, int num_sms);
 int attn_mma_nsplit_bound(int batch, int hkv, int cap, int num_sms);
 int attn_mma_launches(int max_len, int chunk);
+// core_begin / core_end (optional): events recorded around the attention kernel alone, not
+// its query-prep and split-merge kernels (per-kernel profiling)
 int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,
-                         int max_len, int num_sms, cudaStream_t st);
+                         int max_len, int num_sms, cudaStream_t st, cudaEvent_t core_begin = nullptr,
+                         cudaEvent_t core_end = nullptr);
 int attn_nsplit(int max_len, int chunk);
 int attn_chunk(int batch, int hkv, int max_len, int num_sms);
 int attn_nsplit_bound(int batch, int hkv, int cap, int num_sms);

@@ -628,23 +628,30 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
 }
 
 // --------------------------------------------------------------------------------- profiling
+// the next (begin, end) event pair of class cls while profiling, else (null, null)
+std::pair<cudaEvent_t, cudaEvent_t> prof_pair(ab2_ctx* x, int cls) {
+    if (!x->prof.on) return {nullptr, nullptr};
+    auto& v = x->prof.ev[cls];
+    size_t i = x->prof.used[cls]++;
+    if (i >= v.size()) {
+        cudaEvent_t a, b;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        v.push_back({a, b});
+    }
+    return v[i];
+}
+
 struct ProfScope {
     ab2_ctx* x;
     int cls;
     cudaStream_t st;
     cudaEvent_t stop = nullptr;
     ProfScope(ab2_ctx* x_, int cls_, cudaStream_t st_) : x(x_), cls(cls_), st(st_) {
-        if (!x->prof.on) return;
-        auto& v = x->prof.ev[cls];
-        size_t i = x->prof.used[cls]++;
-        if (i >= v.size()) {
-            cudaEvent_t a, b;
-            cudaEventCreate(&a);
-            cudaEventCreate(&b);
-            v.push_back({a, b});
-        }
-        cudaEventRecord(v[i].first, st);
-        stop = v[i].second;
+        const auto e = prof_pair(x, cls);
+        if (!e.first) return;
+        cudaEventRecord(e.first, st);
+        stop = e.second;
     }
     ~ProfScope() {
         if (stop) cudaEventRecord(stop, st);
@@ -772,14 +779,19 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.o_out = nullptr;
         p.err = x->err_d;
         set_prefetch(x, B, &L.w_out, &p.pf, &p.pf_bytes);
-        ProfScope ps(x, PC_ATTN, st);
         if (x->kv_bf16) {
-            // bf16 cache: TMA + tensor-core flash-decode; rows of (layer, slot s0, head 0, token 0)
+            // bf16 cache: TMA + tensor-core flash-decode; rows of (layer, slot s0, head 0, token 0).
+            // Profiling times the attention kernel alone (its query prep and split merge are
+            // small launches of their own).
             const int64_t row_base = ((int64_t)L.local * x->max_batch + s0) * c.n_kv * x->cap;
-            if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, x->num_sms, st))
+            const auto ev = prof_pair(x, PC_ATTN);
+            if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, x->num_sms, st,
+                                     ev.first, ev.second))
                 return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
-        } else if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st)) {
-            return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
+        } else {
+            ProfScope ps(x, PC_ATTN, st);
+            if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st))
+                return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
         }
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
