@@ -77,6 +77,8 @@ SIGNATURES = {
     "ab2_launches_per_step": (C.c_int, [_vp, C.c_int, C.POINTER(_i64)]),
     "ab2_profile": (C.c_int, [_vp, C.c_int]),
     "ab2_profile_read": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(_i64)]),
+    "ab2_step_graph": (C.c_int, [_vp, C.c_int]),
+    "ab2_step_graph_captures": (C.c_int, [_vp, C.POINTER(_i64)]),
     "ab2_mixer_layer": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp]),
     "ab2_ffn_layer": (C.c_int, [_vp, C.c_int, _vp, _vp]),
     "ab2_q8_create": (C.c_int, [_vp, _i64, _i64, C.c_int, C.POINTER(_vp)]),
@@ -241,6 +243,15 @@ class DecodeContext:
     def launches_per_step(self, batch: int) -> int:
         v = C.c_int64()
         _check(load_library().ab2_launches_per_step(self._h, batch, C.byref(v)))
+        return v.value
+
+    def step_graph(self, enable: bool):
+        """Replay decode steps from captured CUDA graphs (one per launch plan)."""
+        _check(load_library().ab2_step_graph(self._h, int(enable)))
+
+    def step_graph_captures(self) -> int:
+        v = C.c_int64()
+        _check(load_library().ab2_step_graph_captures(self._h, C.byref(v)))
         return v.value
 
     def profile(self, enable: bool):

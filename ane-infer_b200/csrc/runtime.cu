@@ -327,6 +327,19 @@ struct Layer {
     int local = 0;  // index among layers of the same kind
 };
 
+// One captured decode step (CUDA graph), replayable while everything its launches were
+// planned from holds: the batch, the attention split plan (chunk length and split count,
+// which follow the longest context) and the token / logit / next-token buffers.
+struct StepGraph {
+    int B = 0, chunk = 0, splits = 0;
+    const int32_t* tok = nullptr;
+    float* logits = nullptr;
+    int32_t* next = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t last = 0;  // least recently used goes first
+};
+constexpr int kStepGraphs = 4;
+
 struct Profile {
     bool on = false;
     std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev[4];
@@ -383,6 +396,11 @@ struct ab2_ctx {
     unsigned* err_h = nullptr;
     float* logits_h = nullptr;
     Profile prof;
+    // whole-step CUDA graphs (off by default)
+    bool graph_on = false;
+    StepGraph graphs[kStepGraphs];
+    uint64_t graph_tick = 0;
+    int64_t graph_captures = 0;
 
     template <typename T>
     int dalloc(T** p, size_t bytes, bool zero = true) {
@@ -724,6 +742,14 @@ GemmEpi epi_swiglu(const ActOut& out, int F) {
     return e;
 }
 
+// attention chunk length (tokens per split) of a step over B slots whose longest context is
+// max_len; 0 without attention layers
+int step_attn_chunk(const ab2_ctx* x, int B, int max_len) {
+    if (x->c.n_attn == 0) return 0;
+    const int hkv = (int)x->c.n_kv;
+    return x->kv_bf16 ? attn_mma_chunk(B, hkv, max_len, x->num_sms) : attn_chunk(B, hkv, max_len, x->num_sms);
+}
+
 // mixer of layer L on the activation fragments in xfa (batch B starting at slot s0);
 // the mixer output goes to `out` with epilogue `mode` (RESID into x, or STORE)
 int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out, int ldo, int mode,
@@ -769,7 +795,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.pos = x->pos_d + s0;
         p.Hq = (int)c.n_heads;
         p.Hkv = (int)c.n_kv;
-        p.chunk = x->kv_bf16 ? attn_mma_chunk(B, p.Hkv, max_len, x->num_sms) : attn_chunk(B, p.Hkv, max_len, x->num_sms);
+        p.chunk = step_attn_chunk(x, B, max_len);
         if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv) > x->aws_floats)
             return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
         p.ws = x->aws;
@@ -835,8 +861,9 @@ int check_capacity(ab2_ctx* x, int B, int* max_len) {
     return 0;
 }
 
-int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
-                 cudaStream_t st) {
+// the kernels of one decode step, enqueued on st (or captured, when st is capturing)
+int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
+                    cudaStream_t st) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
     {
@@ -875,6 +902,68 @@ int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* lo
         launch_pos_advance(x->pos_d, B, st);
     }
     CK(cudaGetLastError());
+    return 0;
+}
+
+void graphs_clear(ab2_ctx* x) {
+    for (StepGraph& g : x->graphs) {
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+        g = StepGraph{};
+    }
+}
+
+// Replay the captured step for this plan, capturing it first (on the context's stream) when
+// no cached graph matches; the graph keeps the kernels' programmatic (PDL) dependencies.
+int graph_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
+               cudaStream_t st) {
+    const int chunk = step_attn_chunk(x, B, max_len);
+    const int splits = chunk ? attn_nsplit(max_len, chunk) : 0;
+    StepGraph* g = nullptr;
+    for (StepGraph& e : x->graphs)
+        if (e.exec && e.B == B && e.chunk == chunk && e.splits == splits && e.tok == tok_d &&
+            e.logits == logits_d && e.next == next_d)
+            g = &e;
+    if (!g) {
+        g = &x->graphs[0];
+        for (StepGraph& e : x->graphs)
+            if (!e.exec || (g->exec && e.last < g->last)) g = &e;
+        if (g->exec) cudaGraphExecDestroy(g->exec);
+        *g = StepGraph{};
+        cudaGraph_t graph = nullptr;
+        CK(cudaStreamBeginCapture(x->stream, cudaStreamCaptureModeRelaxed));
+        const int rc = enqueue_kernels(x, tok_d, B, max_len, logits_d, next_d, x->stream);
+        const cudaError_t ce = cudaStreamEndCapture(x->stream, &graph);
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (ce != cudaSuccess) return seterr(AB2_ERR_CUDA, "step graph capture failed: %s", cudaGetErrorString(ce));
+        const cudaError_t ie = cudaGraphInstantiate(&g->exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) {
+            g->exec = nullptr;
+            return seterr(AB2_ERR_CUDA, "step graph instantiation failed: %s", cudaGetErrorString(ie));
+        }
+        g->B = B;
+        g->chunk = chunk;
+        g->splits = splits;
+        g->tok = tok_d;
+        g->logits = logits_d;
+        g->next = next_d;
+        x->graph_captures++;
+    }
+    g->last = ++x->graph_tick;
+    CK(cudaGraphLaunch(g->exec, st));
+    return 0;
+}
+
+int enqueue_step(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
+                 cudaStream_t st) {
+    // profiling records events between launches, so it always runs the plain stream form
+    if (x->graph_on && !x->prof.on)
+        RET(graph_step(x, tok_d, B, max_len, logits_d, next_d, st));
+    else
+        RET(enqueue_kernels(x, tok_d, B, max_len, logits_d, next_d, st));
     for (int b = 0; b < B; b++) x->pos_h[b] += 1;
     return 0;
 }
@@ -1005,6 +1094,7 @@ AB2_API void ab2_destroy(ab2_ctx* x) {
             cudaEventDestroy(e.first);
             cudaEventDestroy(e.second);
         }
+    graphs_clear(x);
     if (x->stream) cudaStreamDestroy(x->stream);
     delete x;
 }
@@ -1227,6 +1317,21 @@ AB2_API int ab2_profile(ab2_ctx* x, int enable) {
     CK(cudaStreamSynchronize(x->stream));
     prof_collect(x);
     x->prof.on = enable != 0;
+    return 0;
+}
+
+AB2_API int ab2_step_graph(ab2_ctx* x, int enable) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    CK(cudaSetDevice(x->device));
+    CK(cudaStreamSynchronize(x->stream));
+    if (!enable) graphs_clear(x);
+    x->graph_on = enable != 0;
+    return 0;
+}
+
+AB2_API int ab2_step_graph_captures(ab2_ctx* x, int64_t* out) {
+    if (!x || !out) return seterr(AB2_ERR_ARG, "null argument");
+    *out = x->graph_captures;
     return 0;
 }
 

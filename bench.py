@@ -231,6 +231,7 @@ def run_ours(args):
     ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap, kv_bf16=True)
     cfg = ctx.config
     ctx.seed_state(seed=1 + rank, n_slots=B, n_tokens=args.ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
+    ctx.step_graph(bool(args.graph))
     # an explicit stream: every kernel of the step and the timing events share it
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
@@ -323,6 +324,7 @@ def run_ours(args):
                                    f"prefilled bf16 KV", "model": "qwen35-hybrid-2B-shape (random init)",
                        "global_batch": B * world, "seq_len": args.ctx,
                        "parallelism": f"sequence-sharded x{world}, no collective",
+                       "step_graph": bool(args.graph),
                        "l2": "inputs larger than L2 (each step reads ~%.1f GB)" % (step_bytes / 1e9)},
             "step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms_max / args.steps) / 1e6, 1),
                          "frac": round(step_bytes / (ms_max / args.steps) / 1e6 / peak, 4)},
@@ -432,6 +434,8 @@ def main():
     ap.add_argument("--strong", action="store_true", help="split --batch across the GPUs instead")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--graph", type=int, choices=[0, 1], default=1,
+                    help="1: replay each decode step from a captured CUDA graph; 0: stream launches")
     ap.add_argument("--op", choices=["gemm", "recurrence", "attention"], default=None,
                     help="time one op (BASELINE configs 2-4) instead of the decode step")
     ap.add_argument("--m", type=int, default=6144)

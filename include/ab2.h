@@ -113,6 +113,15 @@ int ab2_launches_per_step(ab2_ctx* ctx, int batch, int64_t* out);
  * (classes: 0 attention, 1 deltanet, 2 q8 gemm, 3 other), read and reset the sums. */
 int ab2_profile(ab2_ctx* ctx, int enable);
 int ab2_profile_read(ab2_ctx* ctx, double ms[4], int64_t launches[4]);
+/* Whole-step CUDA graphs: when enabled, a decode step is captured once per launch plan
+ * (batch, attention split plan, token/logit/next-token buffers; up to 4 plans cached) and
+ * replayed with one graph launch instead of ~200 kernel launches: the same kernels with
+ * the same arguments as the stream form. Replaces the per-token command-buffer encoding of
+ * encode_full_token_gpu (crates/engine/src/gpu_full_decode.rs:221-1044). Profiling
+ * (ab2_profile) runs the stream form. */
+int ab2_step_graph(ab2_ctx* ctx, int enable);
+/* Number of step graphs captured so far (a capture happens when no cached plan matches). */
+int ab2_step_graph_captures(ab2_ctx* ctx, int64_t* out);
 
 /* ---- per-layer parity entry points (one slot, host buffers) ------------------------- */
 /* Mixer of one layer on an already RMS-normed hidden vector x[dim] -> out[dim]:
