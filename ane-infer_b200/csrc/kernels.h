@@ -47,8 +47,8 @@ struct Q8Weight {
     size_t qt_bytes() const { return (size_t)(MT + 1) / 2 * 2 * KT * kUTileBytes; }
 };
 
-// EPI_ADD: y += Wx with reductions; the caller keeps y zeroed between uses (the tcgen05 path
-// runs the SwiGLU gate/up projection this way, K-split, and applies silu(g)*u with launch_glu)
+// EPI_ADD: y += Wx with reductions into a y the caller zeroed (the tcgen05 path runs the
+// SwiGLU gate/up projection this way, K-split, and the down projection applies silu(g)*u)
 enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ADD = 3 };
 
 struct GemmEpi {
@@ -82,18 +82,16 @@ void launch_embed(const Q8Weight& w, int vocab, const int32_t* tokens, int batch
 int umma_nsplit(int MT, int KT, int mode, int num_sms);
 void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
                        int64_t stride, cudaStream_t st);
+// h2 (optional): the activations are silu(g) * u of this f32 gate/up scratch ([batch][h2_ld],
+// gate and up interleaved per 64 columns) instead of the x16 image
 int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
-                   cudaStream_t st);
+                   cudaStream_t st, const float* h2 = nullptr, int h2_ld = 0);
 
 // misc.cu
 // zero (optional): rows [0, batch) x [0, zero_n) of zero_ptr (leading dim zero_ld) are cleared
 void launch_rmsnorm_act(const float* x, int ldx, const float* w, int D, float eps, int batch, const ActOut& out,
                         cudaStream_t st, float* zero_ptr = nullptr, int zero_ld = 0, int zero_n = 0);
 void launch_to_act(const float* x, int ldx, int K, int batch, const ActOut& out, cudaStream_t st);
-// SwiGLU of a gate/up projection summed in h2 [batch][ld] (rows interleaved per 64: in each
-// 128-row block the first 64 are gate rows, the next 64 the matching up rows): silu(g)*u for
-// the F outputs goes to `out` (and to y [batch][ldy] if y is set), and h2 is zeroed again.
-void launch_glu(float* h2, int ld, int F, int batch, const ActOut& out, float* y, int ldy, cudaStream_t st);
 // argmax under f32::total_cmp with ties going to the last index (greedy_sample,
 // crates/cli/src/main.rs:1767-1785), split over nch chunks per row (part: [batch][nch] scratch)
 constexpr int kArgmaxChunks = 32;

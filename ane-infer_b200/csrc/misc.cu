@@ -113,54 +113,6 @@ __global__ void to_act_kernel(const float* __restrict__ x, int ldx, int K, ActOu
     for (int i = threadIdx.x; i < kp; i += blockDim.x) act_store(out, b, i, i < K ? x[(size_t)b * ldx + i] : 0.0f);
 }
 
-// silu(g) * u (vec_silu_mul_inplace, crates/engine/src/scratch.rs:181-186) of a gate/up
-// projection that a K-split GEMM summed into h2, whose rows interleave per 64 (in each
-// 128-row block 64 gate rows, then the 64 matching up rows). Each thread takes 8 consecutive
-// outputs: two 32-byte loads of gate and of up, one 16-byte activation store, and h2 is
-// zeroed behind it for the next projection.
-__global__ void __launch_bounds__(256) glu_kernel(float* __restrict__ h2, int ld, int F, ActOut out,
-                                                  float* __restrict__ y, int ldy) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int b = blockIdx.y;
-    const int o8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
-    if (o8 >= F) return;
-    float4* g = reinterpret_cast<float4*>(h2 + (size_t)b * ld + (o8 / 64) * 128 + o8 % 64);
-    float4* u = g + 16;  // 64 floats further: the matching up rows
-    const float4 g0 = g[0], g1 = g[1], u0 = u[0], u1 = u[1];
-    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-    const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-    float h[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) h[j] = (gv[j] / (1.0f + expf(-gv[j]))) * uv[j];
-    if (out.x16) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            __half2 t = __floats2half2_rn(h[2 * e], h[2 * e + 1]);
-            pk[e] = *reinterpret_cast<uint32_t*>(&t);
-        }
-        *reinterpret_cast<uint4*>(out.buf + x16_offset(out.npad, b, o8)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; j++) act_store(out, b, o8 + j, h[j]);
-    }
-    if (y)
-#pragma unroll
-        for (int j = 0; j < 8; j++) y[(size_t)b * ldy + o8 + j] = h[j];
-    const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-    g[0] = z;
-    g[1] = z;
-    u[0] = z;
-    u[1] = z;
-}
-
-void launch_glu(float* h2, int ld, int F, int batch, const ActOut& out, float* y, int ldy, cudaStream_t st) {
-    const int threads = 256;
-    const dim3 grid((F / 8 + threads - 1) / threads, batch);
-    launch_pdl(glu_kernel, grid, dim3(threads), 0, st, h2, ld, F, out, y, ldy);
-}
-
 // Two-pass argmax under f32::total_cmp with ties going to the last index, as
 // Iterator::max_by (greedy_sample, crates/cli/src/main.rs:1767-1785): pass 1 reduces chunk c
 // of row b to (key, index) in part[b][c]

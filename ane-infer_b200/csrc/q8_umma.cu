@@ -25,8 +25,12 @@
 //   * warps 8-11 drain the accumulators (TMEM lane = weight row, column = batch row). A unit
 //     covering all of K writes its outputs (STORE y = Wx, RESID y += Wx); units of a K split,
 //     and every unit of an EPI_ADD call, add their partial sums into y (the caller zeroes a
-//     STORE output; an EPI_ADD output is kept zeroed by its consumer). The SwiGLU gate/up
-//     projection runs as EPI_ADD into an f32 scratch, followed by launch_glu.
+//     STORE output or an EPI_ADD output before the launch).
+// SwiGLU FFN: the gate/up projection runs as EPI_ADD into an f32 scratch h2 (gate and up rows
+// interleaved per 64), and the down projection takes its activations from h2 itself: warps
+// 8-11, idle until the first accumulator is ready, compute x = silu(g) * u per K tile straight
+// into the swizzled f16 image in shared memory (the activation ring as 8 one-tile slots), in
+// place of warp 14's copies of a prepared image.
 // Every mbarrier wait is bounded; on a timeout the CTA records an error code, drains its
 // own copies and MMAs (again bounded), frees its TMEM and returns.
 #include <algorithm>
@@ -46,6 +50,7 @@ constexpr int kWStageBytes = kStageTiles * kUTileBytes;
 constexpr int kWStages = 8;                       // raw weight ring (136 KB)
 constexpr int kAGroup = 4;                        // activation K tiles per copy
 constexpr int kXStages = 2;                       // activation ring (64 KB)
+constexpr int kXSlots = kXStages * kAGroup;       // the same ring as one-tile slots (SwiGLU source)
 constexpr int kXTileBytes = kBatchRows * kTileK * 2;  // 8 KB
 constexpr int kOpStages = 4;                      // f16 weight operand ring in TMEM
 // TMEM columns: the operand ring in [0, 256) (stage s, tile t at s*64 + t*32: 32 columns hold
@@ -99,10 +104,11 @@ void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, in
 struct UmmaSmem {  // offsets from the 1024-aligned dynamic shared-memory base
     static constexpr int w_off(int s) { return s * kWStageBytes; }
     static constexpr int x_base() { return (kWStages * kWStageBytes + 1023) / 1024 * 1024; }
-    static constexpr int x_off(int s) { return x_base() + s * kAGroup * kXTileBytes; }
-    static constexpr int bar_off() { return x_off(kXStages); }
-    // w_full/w_free[W], op_full/op_free[Op], x_full/x_free[X], acc_full/acc_free[2], mma_done, tmem slot
-    static constexpr int n_bars() { return 2 * kWStages + 2 * kOpStages + 2 * kXStages + 4 + 1; }
+    // activation stage s of xg K tiles (xg = kAGroup for copied images, 1 for the SwiGLU source)
+    static constexpr int x_off(int s, int xg) { return x_base() + s * xg * kXTileBytes; }
+    static constexpr int bar_off() { return x_base() + kXSlots * kXTileBytes; }
+    // w_full/w_free[W], op_full/op_free[Op], x_full/x_free[kXSlots], acc_full/acc_free[2], mma_done, tmem slot
+    static constexpr int n_bars() { return 2 * kWStages + 2 * kOpStages + 2 * kXSlots + 4 + 1; }
     static constexpr int bytes() { return bar_off() + n_bars() * 8 + 16; }
 };
 static_assert(kXTileBytes % 1024 == 0 && UmmaSmem::x_base() % 1024 == 0, "operand tiles must stay 1024-aligned");
@@ -170,9 +176,55 @@ __device__ __forceinline__ bool epi_bar_or(bool v) {
     return r != 0;
 }
 
+// silu(g) * u of 8 consecutive K (two float4 of gate, two of up) as 4 packed f16 pairs, for
+// the swizzled activation image (vec_silu_mul_inplace, crates/engine/src/scratch.rs:181-186)
+__device__ __forceinline__ uint4 glu8(float4 g0, float4 g1, float4 u0, float4 u1) {
+    const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+    const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const float a = __fdividef(gv[2 * e], 1.0f + __expf(-gv[2 * e])) * uv[2 * e];
+        const float b = __fdividef(gv[2 * e + 1], 1.0f + __expf(-gv[2 * e + 1])) * uv[2 * e + 1];
+        __half2 t = __floats2half2_rn(a, b);
+        pk[e] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    return make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+
+// the gate and up halves (8 K each) of activation chunk j of batch row n in K tile kt of h2;
+// zeros for rows past the batch
+struct GluLoad {
+    float4 g[2][2], u[2][2];  // two chunks (rows n and n + 16)
+};
+__device__ __forceinline__ void glu_load(const float* __restrict__ h2, int ld, int batch, int kt, int n, int j,
+                                         GluLoad& r) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int nn = n + 16 * i;
+        if (nn < batch) {
+            const float4* g = reinterpret_cast<const float4*>(h2 + (size_t)nn * ld + (size_t)kt * 128 + 8 * j);
+            r.g[i][0] = g[0];
+            r.g[i][1] = g[1];
+            r.u[i][0] = g[16];  // the matching up rows: 64 floats further
+            r.u[i][1] = g[17];
+        } else {
+            r.g[i][0] = r.g[i][1] = r.u[i][0] = r.u[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+}
+__device__ __forceinline__ void glu_store(uint8_t* tile, int n, int j, const GluLoad& r) {
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int nn = n + 16 * i;
+        *reinterpret_cast<uint4*>(tile + nn * 128 + ((j ^ (nn & 7)) << 4)) =
+            glu8(r.g[i][0], r.g[i][1], r.u[i][0], r.u[i][1]);
+    }
+}
+
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, int MP, int KT, int KS, const uint8_t* __restrict__ x16,
-                        int batch, unsigned* __restrict__ err, GemmEpi ep) {
+                        const float* __restrict__ h2, int h2_ld, int batch, unsigned* __restrict__ err, GemmEpi ep) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + UmmaSmem::bar_off());
@@ -180,8 +232,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     uint64_t* op_full = w_free + kWStages;
     uint64_t* op_free = op_full + kOpStages;
     uint64_t* x_full = op_free + kOpStages;
-    uint64_t* x_free = x_full + kXStages;
-    uint64_t* acc_full = x_free + kXStages;
+    uint64_t* x_free = x_full + kXSlots;
+    uint64_t* acc_full = x_free + kXSlots;
     uint64_t* acc_free = acc_full + 2;
     uint64_t* mma_done = acc_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -201,8 +253,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             mbar_init(&op_full[s], kConvWarps * 32);
             mbar_init(&op_free[s], 1);
         }
-        for (int s = 0; s < kXStages; s++) {
-            mbar_init(&x_full[s], 1);
+        for (int s = 0; s < kXSlots; s++) {
+            // a copied stage completes on its bytes; a SwiGLU tile on all epilogue threads' stores
+            mbar_init(&x_full[s], h2 ? kEpiWarps * 32 : 1);
             mbar_init(&x_free[s], 1);
         }
         for (int j = 0; j < 2; j++) {
@@ -248,8 +301,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 if (!mbar_wait(&w_full[j % kWStages], (j / kWStages) & 1)) atomicOr(err, 2u);
         }
     } else if (warp == kWarpX) {
-        // ---------------- activation producer (after the predecessor has completed)
-        if (lane == 0) {
+        // ---------------- activation producer (after the predecessor has completed); with a
+        // SwiGLU source the epilogue warps produce the activations instead
+        if (lane == 0 && !h2) {
             pdl_wait();
             int g = 0;
             bool ok = true;
@@ -266,7 +320,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     }
                     const uint32_t bytes = (uint32_t)min(kAGroup, len - q) * kXTileBytes;
                     mbar_arrive_expect_tx(&x_full[s], bytes);
-                    bulk_g2s(smem + UmmaSmem::x_off(s), x16 + (size_t)(k0 + q) * kXTileBytes, bytes, &x_full[s]);
+                    bulk_g2s(smem + UmmaSmem::x_off(s, kAGroup), x16 + (size_t)(k0 + q) * kXTileBytes, bytes,
+                             &x_full[s]);
                 }
             }
             for (int j = max(0, g - kXStages); j < g; j++)
@@ -276,7 +331,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         // ---------------- MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = umma_idesc_f16(kRows, kBatchRows);
-            int st = 0, g = 0, j = 0;
+            const int xg = h2 ? 1 : kAGroup, xs = h2 ? kXSlots : kXStages;  // tiles per stage, stages
+            int st = 0, sx = 0, xph = 0, j = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < U && ok; u += G, j++) {
                 int mt, k0, len;
@@ -290,10 +346,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     tc_fence_after();  // the epilogue's TMEM loads of this accumulator are done
                 }
                 const uint32_t d = tmem + kAccCol0 + (uint32_t)((j & 1) * kPairRows / 2);
+                int ux = 0;  // K tile within the activation stage sx
                 for (int q = 0; q < len; q++, st++) {
-                    const int so = st % kOpStages, ux = q % kAGroup, sx = g % kXStages;
+                    const int so = st % kOpStages;
                     if (!mbar_wait(&op_full[so], (st / kOpStages) & 1) ||
-                        (ux == 0 && !mbar_wait(&x_full[sx], (g / kXStages) & 1))) {
+                        (ux == 0 && !mbar_wait(&x_full[sx], xph))) {
                         atomicOr(err, 32u);
                         ok = false;
                         break;
@@ -301,7 +358,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     tc_fence_after();  // the converters' TMEM stores of this stage are complete
                     // one descriptor per stage: a K16 step advances its start address by 32 bytes,
                     // i.e. 2 in the descriptor's 16-byte units
-                    const uint64_t xd = umma_desc_sw128(smem_u32(smem + UmmaSmem::x_off(sx) + ux * kXTileBytes));
+                    const uint64_t xd = umma_desc_sw128(smem_u32(smem + UmmaSmem::x_off(sx, xg) + ux * kXTileBytes));
                     const uint32_t a0 = tmem + kOpCol0 + (uint32_t)(so * kStageTiles * 32);
                     const uint32_t acc0 = q > 0 ? 1u : 0u;
 #pragma unroll
@@ -310,9 +367,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                         for (int t = 0; t < kStageTiles; t++)
                             umma_ts_f16(d + t * kBatchRows, a0 + t * 32 + k * 8, xd + (uint64_t)(2 * k), idesc,
                                         k > 0 ? 1u : acc0);
-                    if (ux == kAGroup - 1 || q == len - 1) {
+                    if (++ux == xg || q == len - 1) {
                         umma_commit(&x_free[sx]);
-                        g++;
+                        ux = 0;
+                        if (++sx == xs) {
+                            sx = 0;
+                            xph ^= 1;
+                        }
                     }
                     umma_commit(&op_free[so]);
                 }
@@ -381,10 +442,39 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         // ---------------- epilogue warps: TMEM lanes 32q .. 32q+31 = weight rows of each tile
         const int q = warp & 3;
         const int how = (KS > 1 || ep.mode == EPI_ADD) ? 2 : (ep.mode == EPI_RESID ? 1 : 0);
+        const int et = threadIdx.x - kWarpEpi0 * 32;  // 0..127
         pdl_wait();  // outputs may be read or written by earlier kernels of the stream
+        int gx = 0;  // SwiGLU source: activation tiles produced so far
         for (int j = 0, u = blockIdx.x; u < U; j++, u += G) {
-            const bool fail = !mbar_wait(&acc_full[j & 1], (j >> 1) & 1);
-            if (fail) {
+            bool fail = false;
+            if (h2) {
+                // this unit's activation tiles from the gate/up sums: thread et takes the
+                // 16-byte chunk jn = et % 8 (8 K) of rows et / 8 + 16 i, i = 0..3, as two loads
+                // of two rows, each issued half a tile ahead of its use
+                int mt, k0, len;
+                unit_range(u, KS, (KT + KS - 1) / KS, KT, mt, k0, len);
+                const int jn = et & 7, n0 = et >> 3;
+                GluLoad ra, rb;
+                glu_load(h2, h2_ld, batch, k0, n0, jn, ra);
+                for (int kq = 0; kq < len && !fail; kq++, gx++) {
+                    const int s = gx % kXSlots;
+                    glu_load(h2, h2_ld, batch, k0 + kq, n0 + 32, jn, rb);
+                    if (gx >= kXSlots && !mbar_wait(&x_free[s], ((gx / kXSlots) - 1) & 1)) {
+                        atomicOr(err, 2048u);
+                        s_abort = 1;
+                        fail = true;
+                        break;
+                    }
+                    uint8_t* tile = smem + UmmaSmem::x_off(s, 1);
+                    glu_store(tile, n0, jn, ra);
+                    if (kq + 1 < len) glu_load(h2, h2_ld, batch, k0 + kq + 1, n0, jn, ra);
+                    glu_store(tile, n0 + 32, jn, rb);
+                    fence_proxy_async_smem();  // the MMAs read the tile through the async proxy
+                    mbar_arrive(&x_full[s]);
+                }
+            }
+            if (!fail && !mbar_wait(&acc_full[j & 1], (j >> 1) & 1)) {
+                fail = true;
                 atomicOr(err, 512u);
                 s_abort = 1;
             }
@@ -435,7 +525,6 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             fence_proxy_async_smem();  // the bulk operations read the staged rows through the async proxy
             tc_fence_before();
             asm volatile("bar.sync %0, %1;" ::"n"(kEpiBar), "n"(kEpiWarps * 32) : "memory");
-            const int et = threadIdx.x - kWarpEpi0 * 32;  // 0..127
             const int m0 = pr * kPairRows, valid = min(kPairRows, ep.m_out - m0);
             const bool vec = (ep.ldy & 3) == 0;
             if (valid > 0 && (valid & 3) == 0 && vec && (reinterpret_cast<uintptr_t>(ep.y) & 15) == 0) {
@@ -493,7 +582,7 @@ int umma_nsplit(int MT, int KT, int mode, int num_sms) {
 }
 
 int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
-                   cudaStream_t st) {
+                   cudaStream_t st, const float* h2, int h2_ld) {
     const int smem = UmmaSmem::bytes() + 1024;
     static bool attr_set[64] = {};  // per device, before the first launch
     int dev = 0;
@@ -504,13 +593,15 @@ int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* e
             return -1;
         attr_set[dev & 63] = true;
     }
-    if (ep.mode == EPI_SWIGLU) return -3;  // SwiGLU runs as EPI_ADD + launch_glu on this path
+    if (ep.mode == EPI_SWIGLU) return -3;  // SwiGLU: EPI_ADD into h2, then a launch with the h2 source
     const int KS = umma_nsplit(w.MT, w.KT, ep.mode, num_sms);
     const int pairs = (w.MT + 1) / 2;
     const int U = pairs * KS;
     const int G = std::min(U, num_sms);
-    if (launch_pdl(q8_umma_gemm_kernel, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, pairs, w.KT, KS, x16, batch, err,
-                   ep) != cudaSuccess)
+    // the SwiGLU source reads whole 64-column gate/up groups of h2 (K = ffn a multiple of 64)
+    if (h2 && (w.KB % 2 != 0 || h2_ld < 2 * 32 * w.KB || (h2_ld & 3) != 0)) return -1;
+    if (launch_pdl(q8_umma_gemm_kernel, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, pairs, w.KT, KS, x16, h2, h2_ld,
+                   batch, err, ep) != cudaSuccess)
         return -2;
     return 0;
 }

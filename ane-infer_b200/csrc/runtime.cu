@@ -380,7 +380,7 @@ struct ab2_ctx {
     int2* amax_part = nullptr;  // [max_batch][kArgmaxChunks] partial (key, index) of the argmax
     float* gws = nullptr;       // GEMM split-K partials
     unsigned* gtk = nullptr;    // GEMM tickets
-    float* h2 = nullptr;        // tcgen05 path: f32 gate/up sums [max_batch][2*ffn], kept zeroed
+    float* h2 = nullptr;        // tcgen05 path: f32 gate/up sums [max_batch][2*ffn]
     float* aws = nullptr;       // attention split partials
     float* aqp = nullptr;       // tensor-core attention: prepared queries [max_batch][Hq][hd]
     size_t aws_floats = 0;
@@ -710,10 +710,12 @@ void set_prefetch(ab2_ctx* x, int B, const Q8Weight* w, const void** pf, int64_t
 // lm_head (330 MB for the 2B shape) streams from HBM anyway after its first stages
 constexpr int64_t kPrefetchCap = 32ll << 20;
 
-int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st) {
+// h2 (tcgen05 path only): take the activations as silu(g) * u of the gate/up scratch
+int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st,
+         const float* h2 = nullptr, int h2_ld = 0) {
     ProfScope ps(x, PC_GEMM, st);
     if (umma_for(x, B)) {
-        if (launch_q8_umma(w, xf, B, x->err_d, ep, x->num_sms, st))
+        if (launch_q8_umma(w, xf, B, x->err_d, ep, x->num_sms, st, h2, h2_ld))
             return seterr(AB2_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     } else {
         launch_q8_gemm(w, xf, B, x->gws, x->gtk, ep, x->num_sms, st);
@@ -830,22 +832,21 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
 int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st,
             const Q8Weight* next = nullptr) {
     const int D = (int)x->c.dim, F = (int)x->c.ffn;
-    if (umma_for(x, B)) {
-        // K-split gate/up sums into the zeroed f32 scratch, then silu(g)*u (which re-zeroes it)
-        GemmEpi e;
-        e.mode = EPI_ADD;
-        e.y = x->h2;
-        e.ldy = 2 * F;
-        e.m_out = 2 * F;
-        set_prefetch(x, B, &L.down, &e.pf, &e.pf_bytes);
-        RET(gemm(x, L.gate_up, x->xfa, B, e, st));
-        ProfScope ps(x, PC_OTHER, st);
-        launch_glu(x->h2, 2 * F, F, B, act(x, x->xfb, F, B), nullptr, 0, st);
-    } else {
-        RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
-    }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
     set_prefetch(x, B, next, &e.pf, &e.pf_bytes, kPrefetchCap);
+    if (umma_for(x, B)) {
+        // K-split gate/up sums into the f32 scratch (zeroed by the RMSNorm before), then the
+        // down projection computes silu(g)*u from it as its activations
+        GemmEpi gu;
+        gu.mode = EPI_ADD;
+        gu.y = x->h2;
+        gu.ldy = 2 * F;
+        gu.m_out = 2 * F;
+        set_prefetch(x, B, &L.down, &gu.pf, &gu.pf_bytes);
+        RET(gemm(x, L.gate_up, x->xfa, B, gu, st));
+        return gemm(x, L.down, nullptr, B, e, st, x->h2, 2 * F);
+    }
+    RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
     return gemm(x, L.down, x->xfb, B, e, st);
 }
 
@@ -883,8 +884,10 @@ int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float*
         }
         RET(run_mixer(x, L, 0, B, max_len, x->x, D, EPI_RESID, st));
         {
+            // on the tcgen05 path the gate/up projection adds into h2: clear it
+            const int F2 = 2 * (int)c.ffn;
             ProfScope ps(x, PC_OTHER, st);
-            launch_rmsnorm_act(x->x, D, L.post_norm, D, c.eps, B, xa, st);
+            launch_rmsnorm_act(x->x, D, L.post_norm, D, c.eps, B, xa, st, umma_for(x, B) ? x->h2 : nullptr, F2, F2);
         }
         RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next));
     }
@@ -979,9 +982,8 @@ int take_device_error(ab2_ctx* x) {
 }
 
 int64_t launches_per_step(const ab2_ctx* x, int B) {
-    // embed + 7 per layer (8 on the tcgen05 path: the SwiGLU kernel) + final norm + lm_head +
-    // 2 argmax passes + position advance
-    const int64_t per_layer = umma_for(x, B) ? 8 : 7;
+    // embed + 7 per layer + final norm + lm_head + 2 argmax passes + position advance
+    const int64_t per_layer = 7;
     int64_t n = 1 + (int64_t)x->layers.size() * per_layer + 1 + 1 + 2 + 1;
     if (x->kv_bf16 && x->c.n_attn > 0) {
         // the tensor-core attention adds a merge kernel when the current context is split

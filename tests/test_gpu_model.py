@@ -154,6 +154,27 @@ def test_step_graph_device_buffers(pkg, tiny_gguf, cuda):
     assert (outs[0] == outs[1]).mean() > 0.99
 
 
+def test_wide_ffn_swiglu_ring_wraps(pkg, oracle, synth):
+    """FFN 10240 on the tcgen05 path: the down projection (K = 10240) runs 18 K splits of up to
+    9 tiles, so the SwiGLU activation source cycles its 8-slot ring within a split."""
+    shape = synth.HybridShape(n_layers=2, dim=2048, vocab=4096, ffn=10240, dn_heads=16, attn_heads=8, kv_heads=2,
+                              head_dim=256, full_attn_interval=2)
+    gguf = synth.build_model_gguf(shape, seed=5)
+    om = oracle.Model(gguf, ctx_cap=16)
+    B = 9
+    seqs = [om.new_seq(kv_bf16=True) for _ in range(B)]
+    ctx = pkg.DecodeContext(gguf, max_batch=B, max_ctx=16, kv_bf16=True)
+    toks = [13 * b + 2 for b in range(B)]
+    for step in range(3):
+        lg, nx = ctx.decode_step(toks)
+        for b in range(B):
+            ref = seqs[b].forward(toks[b])
+            assert rel_err(lg[b], ref) < LOGIT_TOL, (step, b)
+            assert argmax_consistent(int(nx[b]), ref, lg[b]), (step, b)
+        toks = [int(t) for t in nx]
+    ctx.close()
+
+
 def test_state_io_and_capacity(pkg, tiny_gguf):
     ctx = pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=8, kv_bf16=True)
     rng = np.random.default_rng(4)
