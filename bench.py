@@ -195,8 +195,10 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"2B-shape Qwen3.5 hybrid decode, Q8_0, ctx {args.ctx} prefilled",
-                   "global_batch": 1, "seq_len": args.ctx, "parallelism": "host threads"},
+        "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {args.batch} seq/GPU, ctx {args.ctx} "
+                               f"prefilled bf16 KV", "model": "qwen35-hybrid-2B-shape (random init)",
+                   "global_batch": args.batch * args.gpus, "seq_len": args.ctx,
+                   "parallelism": "host threads; sequences one after another, as the reference decodes"},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
