@@ -349,6 +349,57 @@ def run_ours(args):
 
 
 # --------------------------------------------------------------------------- op benchmarks
+def cpu_op_baseline(op: str, B: int, M: int = 0, K: int = 0, ctx: int = 0, seconds: float = 5.0, blocks=None):
+    """The oracle (CPU restatement of the reference, all host threads) on the op of BASELINE
+    configs 2-4, in the op line's unit (microseconds for the whole batch B): the reference
+    runs these per sequence, so a bounded sample of sequences is timed and scaled to B."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from ane_infer_b200 import synth
+    L = oracle.lib()
+    L.oracle_set_threads(len(os.sched_getaffinity(0)))
+    rng = np.random.default_rng(1)
+    if op == "gemm":
+        # q8_gemv is one vector per call (q8_gemv.rs:130): B calls per batch
+        if blocks is None:
+            blocks = synth.random_q8_0(rng, M, K, std=0.01)
+        x = synth.bf16_round(rng.normal(size=K).astype(np.float32))
+        y = np.empty(M, dtype=np.float32)
+        call = lambda: L.oracle_q8_gemv(blocks, M, K, x, y)
+        per, n_seq, what = B, 1, f"q8_gemv {M}x{K}, one vector per call"
+        cores = L.oracle_max_threads() if M * K > 65536 else 1
+    elif op == "recurrence":
+        H, d, n_seq = 16, 128, min(B, 8)
+        S = rng.normal(0, 0.1, size=(n_seq, H, d, d)).astype(np.float32)
+        q, k, v = (synth.bf16_round(rng.normal(size=(n_seq, H, d)).astype(np.float32)) for _ in range(3))
+        beta = rng.random((n_seq, H), dtype=np.float32)
+        decay = rng.random((n_seq, H), dtype=np.float32)
+        o = np.empty((n_seq, H, d), dtype=np.float32)
+        call = lambda: L.oracle_gated_delta(S, q, k, v, beta, decay, n_seq, H, d, d, o)
+        per, what = B / n_seq, f"gated delta rule, {n_seq} sequences x 16 heads per call"
+        cores = L.oracle_max_threads()
+    else:
+        Hq, Hkv, hd, n_seq = 8, 2, 256, 1
+        kc = rng.normal(size=(Hkv, ctx + 1, hd)).astype(np.float32)
+        vc = rng.normal(size=(Hkv, ctx + 1, hd)).astype(np.float32)
+        kv = oracle.KvOp(synth.bf16_round(kc), synth.bf16_round(vc))
+        del kc, vc
+        q, gate = rng.normal(size=(Hq, hd)), rng.normal(size=(Hq, hd))
+        kn, vn = rng.normal(size=(Hkv, hd)), rng.normal(size=(Hkv, hd))
+        call = lambda: kv(q, gate, kn, vn, ctx - 1, 1e7, 64, kv_bf16=True)
+        per, what = B, f"GQA decode attention over {ctx} tokens, one sequence per call"
+        cores = 1  # the restatement's attention runs on one thread, as the reference's loop does
+    call()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while n == 0 or time.perf_counter() - t0 < seconds:
+        call()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(dt * per * 1e6, 2), "unit": "us per launch (whole batch)", "cores": cores,
+            "kind": "port", "sample": f"{what}; {n} calls in {dt * n:.1f} s, scaled to batch {B}"}
+
+
 def run_op(args):
     """One op of BASELINE configs 2-4 on cuda:0, timed with CUDA events; one JSON line."""
     import numpy as np
@@ -363,7 +414,8 @@ def run_op(args):
     B = args.batch
     if args.op == "gemm":
         M, K = args.m, args.k
-        w = pkg.Q8Tensor(synth.random_q8_0(rng, M, K, std=0.01), M, K)
+        blocks = synth.random_q8_0(rng, M, K, std=0.01)
+        w = pkg.Q8Tensor(blocks, M, K)
         x = torch.from_numpy(synth.bf16_round(rng.normal(size=(B, K)).astype(np.float32))).cuda()
         y = torch.empty((B, M), dtype=torch.float32, device="cuda")
         fn = lambda: pkg.q8_gemv(w, x, y, B, st)
@@ -419,9 +471,14 @@ def run_op(args):
         raise RuntimeError("tensor-core pipeline timeout")
     ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.iters
     gbs = nbytes / (ms / 1e3) / 1e9
+    cpu = None
+    if not args.no_cpu:
+        cpu = cpu_op_baseline(args.op, B, M=args.m, K=args.k, ctx=args.ctx, seconds=min(args.cpu_seconds, 10.0),
+                              blocks=blocks if args.op == "gemm" else None)
     print(json.dumps({"op": label, "us_per_launch": round(ms * 1e3, 2), "algorithmic_bytes": nbytes,
                       "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": peak_kind,
-                      "frac": round(gbs / peak, 4), "iters": args.iters, "l2": "flushed before each launch"}),
+                      "frac": round(gbs / peak, 4), "iters": args.iters, "l2": "flushed before each launch",
+                      "cpu_baseline": cpu}),
           flush=True)
 
 

@@ -861,6 +861,26 @@ OX int oracle_attn_op(float* q, const float* gate, float* k_new, const float* v_
     return 0;
 }
 
+// The same op over a cache that lives across calls, for timing the op without the two
+// whole-cache copies per call above: oracle_kv_new copies k/v [n_kv][cap][hd] in once.
+OX void* oracle_kv_new(int64_t n_kv, int64_t hd, int64_t cap, const float* k_cache, const float* v_cache) {
+    auto* kv = new KvCache{(size_t)n_kv, (size_t)hd, (size_t)cap, {}, {}};
+    const size_t n = (size_t)n_kv * cap * hd;
+    kv->k.assign(k_cache, k_cache + n);
+    kv->v.assign(v_cache, v_cache + n);
+    return kv;
+}
+OX void oracle_kv_free(void* h) { delete static_cast<KvCache*>(h); }
+OX int oracle_attn_op_kv(void* h, float* q, const float* gate, float* k_new, const float* v_new, int64_t pos,
+                         int64_t n_heads, float rope_base, int64_t rotary_dim, int kv_bf16, float* out) {
+    auto* kv = static_cast<KvCache*>(h);
+    if (pos < 0 || pos >= (int64_t)kv->max_seq) return fail("pos out of range");
+    if (rotary_dim % 2 || rotary_dim > (int64_t)kv->hd) return fail("bad rotary_dim");
+    attn_core(q, gate, k_new, v_new, n_heads, kv->n_kv, kv->hd, nullptr, 0, nullptr, 0, rope_base, rotary_dim, pos,
+              *kv, kv_bf16 != 0, out);
+    return 0;
+}
+
 // ---------------------------------------------------------------------------------------
 struct OracleModel {
     Model md;

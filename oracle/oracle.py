@@ -53,6 +53,9 @@ def lib():
         "oracle_gated_delta": (None, [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, f32p]),
         "oracle_attn_op": (C.c_int, [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, i64,
                                      vp, vp, C.c_float, i64, C.c_int, f32p]),
+        "oracle_kv_new": (vp, [i64, i64, i64, f32p, f32p]),
+        "oracle_kv_free": (None, [vp]),
+        "oracle_attn_op_kv": (C.c_int, [vp, f32p, f32p, f32p, f32p, i64, i64, C.c_float, i64, C.c_int, f32p]),
         "oracle_model_load": (vp, [u8p, i64, i64]),
         "oracle_model_free": (None, [vp]),
         "oracle_model_config": (None, [vp, C.POINTER(OracleConfig)]),
@@ -137,6 +140,33 @@ def attn_op(q, gate, k_new, v_new, k_cache, v_cache, pos, rope_base, rotary_dim,
     if rc:
         raise RuntimeError(_err())
     return out.reshape(Hq, hd), kc, vc
+
+
+class KvOp:
+    """attn_op without q/k norms over a cache kept across calls ([Hkv][cap][hd], copied in
+    once), for timing the op: each call appends at pos and attends over pos + 1 tokens."""
+
+    def __init__(self, k_cache, v_cache):
+        kc = np.ascontiguousarray(k_cache, dtype=np.float32)
+        vc = np.ascontiguousarray(v_cache, dtype=np.float32)
+        self.n_kv, self.cap, self.hd = kc.shape
+        self._h = lib().oracle_kv_new(self.n_kv, self.hd, self.cap, kc, vc)
+
+    def __call__(self, q, gate, k_new, v_new, pos, rope_base, rotary_dim, kv_bf16=False):
+        q = np.array(q, dtype=np.float32, copy=True).reshape(-1)
+        out = np.empty(q.size, dtype=np.float32)
+        rc = lib().oracle_attn_op_kv(self._h, q, np.ascontiguousarray(gate, dtype=np.float32).reshape(-1),
+                                     np.array(k_new, dtype=np.float32, copy=True).reshape(-1),
+                                     np.ascontiguousarray(v_new, dtype=np.float32).reshape(-1), pos,
+                                     q.size // self.hd, float(rope_base), rotary_dim, int(kv_bf16), out)
+        if rc:
+            raise RuntimeError(_err())
+        return out.reshape(-1, self.hd)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().oracle_kv_free(self._h)
+            self._h = None
 
 
 class Model:

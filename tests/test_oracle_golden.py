@@ -136,6 +136,25 @@ def test_oracle_attention_matches_numpy(oracle, rot):
     assert np.array_equal(kc2[:, :pos], kc[:, :pos])
 
 
+@pytest.mark.parametrize("kv_bf16", [False, True])
+def test_oracle_attn_op_kv_matches_attn_op(oracle, kv_bf16):
+    """The persistent-cache form used for CPU op timing computes what attn_op computes,
+    step after step as it appends to its own cache."""
+    rng = np.random.default_rng(12)
+    Hq, Hkv, hd, cap, pos = 8, 2, 64, 24, 9
+    kc = rng.normal(size=(Hkv, cap, hd)).astype(np.float32)
+    vc = rng.normal(size=(Hkv, cap, hd)).astype(np.float32)
+    op = oracle.KvOp(kc, vc)
+    for step in range(4):
+        q = rng.normal(size=(Hq, hd)).astype(np.float32)
+        gate = rng.normal(size=(Hq, hd)).astype(np.float32)
+        kn = rng.normal(size=(Hkv, hd)).astype(np.float32)
+        vn = rng.normal(size=(Hkv, hd)).astype(np.float32)
+        ref, kc, vc = oracle.attn_op(q, gate, kn, vn, kc, vc, pos + step, 1e7, 32, kv_bf16=kv_bf16)
+        got = op(q, gate, kn, vn, pos + step, 1e7, 32, kv_bf16=kv_bf16)
+        assert np.array_equal(got, ref), step
+
+
 def test_oracle_forward_matches_numpy(oracle, tiny_gguf, tiny_model):
     ref = numpy_ref.Model(tiny_gguf)
     st = ref.new_state(64)
