@@ -1,0 +1,240 @@
+// ab2_bench -- command-line decode benchmark over the C ABI of include/ab2.h.
+//
+// The B200 counterpart of the reference CLI's `bench` command (crates/cli/src/main.rs:251-508;
+// its GPU section, :418-498, times encode_full_token_gpu one token at a time). It loads a
+// qwen35 GGUF, runs a prompt of -pp tokens through the decode path, and then times -tg greedy
+// tokens. Flags follow the reference (-m/--model, -pp/--prompt-tokens, -tg/--gen-tokens,
+// defaults 128/128). The additions are the batch, the device, the KV cache type and the
+// step-graph switch.
+//
+// Differences, since no tokenizer is part of this path:
+// * Prompt ids are synthetic: a seeded hash of (seed, sequence, position) modulo the
+//   vocabulary.
+// * Generation does not stop at EOS.
+// * With -b B, B independent sequences decode together; the reference decodes one.
+//
+// The timing also follows the reference. The first generated token is a warm-up. Speed is
+// (tokens - 1) / time over the rest, summed over the batch, and wall-clock timed around the
+// synchronous ab2_decode_step calls (host buffers in and out).
+//
+// Output: the reference's human-readable lines on stderr, and one JSON line on stdout with
+// the rates and sequence 0's prompt and generated ids (`prompt`, `tokens`). Exit
+// status: 0 on success, 1 if a file or ab2 call fails (the ab2 message is printed), 2 on bad
+// usage.
+#include <chrono>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "ab2.h"
+
+namespace {
+
+struct Args {
+    std::string model;
+    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1;
+    bool kv_bf16 = true;
+    uint64_t seed = 0;
+};
+
+void usage(FILE* f) {
+    std::fprintf(f,
+                 "usage: ab2_bench -m MODEL.gguf [-pp N] [-tg N] [-b B] [-d DEVICE] [--kv bf16|f32]\n"
+                 "                 [--graph 0|1] [--seed S]\n"
+                 "  -m, --model          qwen35 GGUF with Q8_0 weights (required)\n"
+                 "  -pp, --prompt-tokens prompt tokens per sequence (default 128)\n"
+                 "  -tg, --gen-tokens    greedy tokens per sequence (default 128)\n"
+                 "  -b, --batch          sequences decoded together (default 1)\n"
+                 "  -d, --device         CUDA device (default 0)\n"
+                 "  --kv                 KV cache type (default bf16; f32 as the reference)\n"
+                 "  --graph              replay each step as one CUDA graph (default 1)\n"
+                 "  --seed               seed of the synthetic prompt ids (default 0)\n");
+}
+
+bool parse_long(const char* s, long lo, long* out) {
+    char* end = nullptr;
+    const long v = std::strtol(s, &end, 10);
+    if (!s[0] || *end || v < lo) return false;
+    *out = v;
+    return true;
+}
+
+// 0: parsed; 1: help was asked for; 2: bad usage (message printed)
+int parse(int argc, char** argv, Args* a) {
+    for (int i = 1; i < argc; i++) {
+        const std::string k = argv[i];
+        if (k == "-h" || k == "--help") return 1;
+        if (i + 1 >= argc) {
+            std::fprintf(stderr, "ab2_bench: %s needs a value\n", k.c_str());
+            return 2;
+        }
+        const char* v = argv[++i];
+        bool ok = true;
+        if (k == "-m" || k == "--model") {
+            a->model = v;
+        } else if (k == "-pp" || k == "--prompt-tokens") {
+            ok = parse_long(v, 1, &a->pp);
+        } else if (k == "-tg" || k == "--gen-tokens") {
+            ok = parse_long(v, 1, &a->tg);
+        } else if (k == "-b" || k == "--batch") {
+            ok = parse_long(v, 1, &a->batch);
+        } else if (k == "-d" || k == "--device") {
+            ok = parse_long(v, 0, &a->device);
+        } else if (k == "--graph") {
+            ok = parse_long(v, 0, &a->graph) && a->graph <= 1;
+        } else if (k == "--seed") {
+            long s = 0;
+            ok = parse_long(v, 0, &s);
+            a->seed = (uint64_t)s;
+        } else if (k == "--kv") {
+            ok = !std::strcmp(v, "bf16") || !std::strcmp(v, "f32");
+            a->kv_bf16 = !std::strcmp(v, "bf16");
+        } else {
+            std::fprintf(stderr, "ab2_bench: unknown option %s\n", k.c_str());
+            return 2;
+        }
+        if (!ok) {
+            std::fprintf(stderr, "ab2_bench: bad value for %s: %s\n", k.c_str(), v);
+            return 2;
+        }
+    }
+    if (a->model.empty()) {
+        std::fprintf(stderr, "ab2_bench: -m MODEL.gguf is required\n");
+        return 2;
+    }
+    return 0;
+}
+
+bool read_file(const std::string& path, std::vector<uint8_t>* out) {
+    FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return false;
+    bool ok = std::fseek(f, 0, SEEK_END) == 0;
+    const long n = ok ? std::ftell(f) : -1;
+    ok = ok && n > 0 && std::fseek(f, 0, SEEK_SET) == 0;
+    if (ok) {
+        out->resize((size_t)n);
+        ok = std::fread(out->data(), 1, (size_t)n, f) == (size_t)n;
+    }
+    std::fclose(f);
+    return ok;
+}
+
+// splitmix64 finaliser
+uint64_t mix(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+int fail(const char* what) {
+    std::fprintf(stderr, "ab2_bench: %s failed: %s\n", what, ab2_last_error());
+    return 1;
+}
+
+// a JSON string body: quotes, backslashes and control characters escaped
+std::string json_escape(const std::string& s) {
+    std::string o;
+    for (const char c : s) {
+        if (c == '"' || c == '\\') {
+            o += '\\';
+            o += c;
+        } else if ((unsigned char)c < 0x20) {
+            char buf[8];
+            std::snprintf(buf, sizeof(buf), "\\u%04x", (unsigned)(unsigned char)c);
+            o += buf;
+        } else {
+            o += c;
+        }
+    }
+    return o;
+}
+
+double seconds_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    Args a;
+    const int pr = parse(argc, argv, &a);
+    if (pr == 1) {
+        usage(stdout);
+        return 0;
+    }
+    if (pr) {
+        usage(stderr);
+        return 2;
+    }
+    std::vector<uint8_t> gguf;
+    if (!read_file(a.model, &gguf)) {
+        std::fprintf(stderr, "ab2_bench: cannot read %s\n", a.model.c_str());
+        return 1;
+    }
+    ab2_config cfg;
+    if (ab2_gguf_inspect(gguf.data(), gguf.size(), &cfg)) return fail("reading the GGUF");
+    std::fprintf(stderr, "  Model: %lld layers (%lld DeltaNet, %lld attention), dim %lld, vocab %lld\n",
+                 (long long)cfg.n_layers, (long long)cfg.n_dn, (long long)cfg.n_attn, (long long)cfg.dim,
+                 (long long)cfg.vocab);
+
+    const int B = (int)a.batch;
+    const long max_ctx = a.pp + a.tg + 2;
+    ab2_options opt;
+    std::memset(&opt, 0, sizeof(opt));
+    opt.kv_bf16 = a.kv_bf16 ? 1 : 0;
+    ab2_ctx* ctx = nullptr;
+    std::fprintf(stderr, "  Uploading model weights to GPU %ld...\n", a.device);
+    const auto t_up = std::chrono::steady_clock::now();
+    if (ab2_create(gguf.data(), gguf.size(), (int)a.device, B, (int)max_ctx, &opt, &ctx)) return fail("ab2_create");
+    std::fprintf(stderr, "  Uploaded in %.1fms\n", 1e3 * seconds_since(t_up));
+    int rc = 0;
+    std::vector<int32_t> tok((size_t)B), next((size_t)B), prompt0, gen0;
+    double pp_s = 0, tg_s = 0;
+    do {
+        if (ab2_step_graph(ctx, (int)a.graph)) {
+            rc = fail("ab2_step_graph");
+            break;
+        }
+        // prompt: one decode step per position for all sequences
+        const auto t_pp = std::chrono::steady_clock::now();
+        for (long i = 0; i < a.pp && !rc; i++) {
+            for (int b = 0; b < B; b++) tok[b] = (int32_t)(mix(a.seed ^ mix(((uint64_t)b << 32) + i)) % cfg.vocab);
+            prompt0.push_back(tok[0]);
+            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) rc = fail("ab2_decode_step (prompt)");
+        }
+        if (rc) break;
+        pp_s = seconds_since(t_pp);
+        // generation: the first token is the warm-up, then (tg - 1) timed greedy steps
+        auto t_tg = std::chrono::steady_clock::now();
+        for (long i = 0; i < a.tg && !rc; i++) {
+            if (i == 1) t_tg = std::chrono::steady_clock::now();
+            tok = next;
+            gen0.push_back(tok[0]);
+            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) rc = fail("ab2_decode_step");
+        }
+        if (rc) break;
+        tg_s = a.tg > 1 ? seconds_since(t_tg) : 0.0;
+    } while (false);
+    ab2_destroy(ctx);
+    if (rc) return rc;
+
+    const double pp_tps = pp_s > 0 ? (double)B * a.pp / pp_s : 0.0;
+    const double tg_tps = tg_s > 0 ? (double)B * (a.tg - 1) / tg_s : 0.0;
+    std::fprintf(stderr, "  Prompt: %ld tokens x %d sequences in %.1fms (%.1f tok/s)\n", a.pp, B, 1e3 * pp_s, pp_tps);
+    std::fprintf(stderr, "  Tokens: %ld\n", a.tg);
+    std::fprintf(stderr, "  Time: %.1fms\n", 1e3 * tg_s);
+    std::fprintf(stderr, "  Speed: %.1f tok/s (B200 tg%ld, %d sequences)\n", tg_tps, a.tg, B);
+    std::printf("{\"model\": \"%s\", \"batch\": %d, \"prompt_tokens\": %ld, \"gen_tokens\": %ld, "
+                "\"prompt_tok_s\": %.2f, \"gen_tok_s\": %.2f, \"gen_ms\": %.3f, \"kv\": \"%s\", \"graph\": %ld, "
+                "\"prompt\": [",
+                json_escape(a.model).c_str(), B, a.pp, a.tg, pp_tps, tg_tps, 1e3 * tg_s, a.kv_bf16 ? "bf16" : "f32", a.graph);
+    for (size_t i = 0; i < prompt0.size(); i++) std::printf("%s%d", i ? ", " : "", prompt0[i]);
+    std::printf("], \"tokens\": [");
+    for (size_t i = 0; i < gen0.size(); i++) std::printf("%s%d", i ? ", " : "", gen0[i]);
+    std::printf("]}\n");
+    return 0;
+}

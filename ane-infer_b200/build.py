@@ -4,8 +4,9 @@
 
 Each csrc/*.cu is compiled to _build/*.o with
 ``-gencode arch=compute_100a,code=sm_100a -lineinfo -O3`` and linked into
-ane-infer_b200/libab2.so with a static CUDA runtime. Objects are rebuilt only when a source
-or header is newer.
+ane-infer_b200/libab2.so with a static CUDA runtime. The command-line benchmark
+ane-infer_b200/ab2_bench (ab2_bench.cpp, a plain C++ caller of the C ABI) is linked against
+it. Targets are rebuilt only when a source or header is newer.
 """
 from __future__ import annotations
 
@@ -22,6 +23,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libab2.so")
+CLI_SRC = os.path.join(HERE, "ab2_bench.cpp")
+CLI = os.path.join(HERE, "ab2_bench")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-fvisibility=hidden",
@@ -66,7 +69,25 @@ def build(verbose_ptxas: bool = False, jobs: int = 8) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
+    build_cli()
     return LIB
+
+
+def build_cli(out: str = CLI, lib_dir: str = HERE, lib: str = "ab2", extra: tuple = ()) -> str:
+    """Compile ab2_bench.cpp with g++ and link it against lib{lib}.so in lib_dir; at run time
+    the binary looks for the library in its own directory. `extra` adds sources."""
+    header = os.path.join(ROOT, "include", "ab2.h")
+    deps = [CLI_SRC, header, *extra]
+    if os.path.exists(out) and os.path.getmtime(out) >= max(os.path.getmtime(d) for d in deps) and not extra:
+        return out
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-Wextra", "-I", os.path.join(ROOT, "include"), CLI_SRC, *extra,
+           "-o", out]
+    if lib:  # the library is looked up beside the binary first
+        cmd += ["-L", lib_dir, f"-l{lib}", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ failed on {CLI_SRC}:\n{r.stderr}")
+    return out
 
 
 if __name__ == "__main__":

@@ -1,0 +1,102 @@
+/* stub_ab2.c -- test double of libab2.so for the command-line benchmark's CPU tests: the
+ * entry points ab2_bench calls, with a deterministic stand-in for decoding (next token =
+ * (7 * token + position + slot) mod vocab) and a call log written to $STUB_LOG. Built only
+ * by tests/test_cli.py. */
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "ab2.h"
+
+#define STUB_VOCAB 1000
+
+struct ab2_ctx {
+    int max_batch, max_ctx;
+    long long pos[256];
+};
+
+static const char* g_msg = "";
+
+static void logf_(const char* fmt, long long a, long long b, long long c, long long d) {
+    const char* path = getenv("STUB_LOG");
+    if (!path) return;
+    FILE* f = fopen(path, "a");
+    if (!f) return;
+    fprintf(f, fmt, a, b, c, d);
+    fputc('\n', f);
+    fclose(f);
+}
+
+const char* ab2_last_error(void) { return g_msg; }
+
+int ab2_gguf_inspect(const uint8_t* gguf, uint64_t len, ab2_config* out) {
+    memset(out, 0, sizeof(*out));
+    if (len < 4 || memcmp(gguf, "GGUF", 4) != 0) {
+        g_msg = "stub: not a GGUF file";
+        return AB2_ERR_FORMAT;
+    }
+    out->n_layers = 4;
+    out->n_dn = 3;
+    out->n_attn = 1;
+    out->dim = 64;
+    out->vocab = STUB_VOCAB;
+    return 0;
+}
+
+int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
+               const ab2_options* opt, ab2_ctx** out) {
+    (void)gguf;
+    (void)len;
+    logf_("create %lld %lld %lld %lld", device, max_batch, max_ctx, opt ? opt->kv_bf16 : -1);
+    if (getenv("STUB_FAIL_CREATE")) {
+        g_msg = "stub: no CUDA device available";
+        return AB2_ERR_DEVICE;
+    }
+    if (max_batch < 1 || max_batch > 256) {
+        g_msg = "stub: bad max_batch";
+        return AB2_ERR_ARG;
+    }
+    ab2_ctx* x = (ab2_ctx*)calloc(1, sizeof(ab2_ctx));
+    x->max_batch = max_batch;
+    x->max_ctx = max_ctx;
+    *out = x;
+    return 0;
+}
+
+void ab2_destroy(ab2_ctx* ctx) {
+    logf_("destroy %lld %lld %lld %lld", 0, 0, 0, 0);
+    free(ctx);
+}
+
+int ab2_step_graph(ab2_ctx* ctx, int enable) {
+    (void)ctx;
+    logf_("graph %lld %lld %lld %lld", enable, 0, 0, 0);
+    return 0;
+}
+
+int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int batch, float* logits, int32_t* next) {
+    if (batch < 1 || batch > x->max_batch) {
+        g_msg = "stub: batch outside [1, max_batch]";
+        return AB2_ERR_CAPACITY;
+    }
+    for (int b = 0; b < batch; b++) {
+        if (x->pos[b] >= x->max_ctx) {
+            g_msg = "stub: slot is full";
+            return AB2_ERR_CAPACITY;
+        }
+        if (tokens[b] < 0 || tokens[b] >= STUB_VOCAB) {
+            g_msg = "stub: token out of range";
+            return AB2_ERR_ARG;
+        }
+    }
+    (void)logits;
+    int32_t n0 = 0;
+    for (int b = 0; b < batch; b++) {
+        const int32_t n = (int32_t)((7LL * tokens[b] + x->pos[b] + b) % STUB_VOCAB);
+        if (next) next[b] = n;
+        if (b == 0) n0 = n;
+        x->pos[b]++;
+    }
+    logf_("step %lld %lld %lld %lld", batch, tokens[0], n0, batch > 1 ? tokens[batch - 1] : -1);
+    return 0;
+}

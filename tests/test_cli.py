@@ -1,0 +1,126 @@
+"""The command-line benchmark ab2_bench (the counterpart of the reference CLI's `bench`,
+crates/cli/src/main.rs:251-508), on CPU: its argument handling, and its prompt and greedy
+feedback loop, run against a test double of libab2.so (tests/stub_ab2.c) that logs every call.
+Without a GPU, the real library must make it fail cleanly."""
+import importlib.util
+import json
+import os
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "ane-infer_b200")
+
+
+def _build_mod():
+    spec = importlib.util.spec_from_file_location("ab2_build_cli", os.path.join(PKG, "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.fixture(scope="module")
+def stub_cli(tmp_path_factory):
+    d = tmp_path_factory.mktemp("cli")
+    subprocess.run(["gcc", "-O1", "-shared", "-fPIC", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "stub_ab2.c"), "-o", str(d / "libab2.so")], check=True)
+    exe = _build_mod().build_cli(out=str(d / "ab2_bench"), lib_dir=str(d))
+    model = d / "model.gguf"
+    model.write_bytes(b"GGUF" + bytes(60))
+    return exe, str(model), d
+
+
+def run(exe, *args, env=None):
+    e = dict(os.environ)
+    e.update(env or {})
+    return subprocess.run([exe, *args], capture_output=True, text=True, env=e, timeout=60)
+
+
+def read_log(path):
+    return [line.split() for line in open(path).read().splitlines()]
+
+
+@pytest.mark.parametrize("B,pp,tg,kv,graph", [(1, 4, 6, "bf16", 1), (3, 2, 5, "f32", 0)])
+def test_prompt_then_greedy_feedback(stub_cli, tmp_path, B, pp, tg, kv, graph):
+    exe, model, _ = stub_cli
+    log = tmp_path / "calls.log"
+    r = run(exe, "-m", model, "-pp", str(pp), "-tg", str(tg), "-b", str(B), "--kv", kv, "--graph", str(graph),
+            "--seed", "3", env={"STUB_LOG": str(log)})
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    assert (out["batch"], out["prompt_tokens"], out["gen_tokens"], out["kv"], out["graph"]) == (B, pp, tg, kv, graph)
+    assert "Speed:" in r.stderr and "Tokens: %d" % tg in r.stderr
+    calls = read_log(log)
+    # create(device 0, max_batch B, max_ctx pp + tg + 2, kv flag), graph switch, steps, destroy
+    assert calls[0] == ["create", "0", str(B), str(pp + tg + 2), "1" if kv == "bf16" else "0"]
+    assert calls[1] == ["graph", str(graph), "0", "0", "0"]
+    steps = [c for c in calls if c[0] == "step"]
+    assert calls[-1][0] == "destroy" and len(steps) == pp + tg
+    assert all(int(s[1]) == B for s in steps)
+    tok0 = [int(s[2]) for s in steps]
+    nxt0 = [int(s[3]) for s in steps]
+    assert all(0 <= t < 1000 for t in tok0[:pp])
+    # each generated step feeds the previous step's greedy token, and the reported tokens
+    # are slot 0's generated ids in order
+    for k in range(pp, pp + tg):
+        assert tok0[k] == nxt0[k - 1], k
+    assert out["tokens"] == tok0[pp:]
+    assert out["prompt"] == tok0[:pp]
+
+
+def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
+    exe, model, _ = stub_cli
+    firsts = []
+    for seed in ("0", "1"):
+        log = tmp_path / f"s{seed}.log"
+        assert run(exe, "-m", model, "-pp", "3", "-tg", "1", "-b", "2", "--seed", seed,
+                   env={"STUB_LOG": str(log)}).returncode == 0
+        steps = [c for c in read_log(log) if c[0] == "step"]
+        firsts.append([(int(s[2]), int(s[4])) for s in steps[:3]])
+    assert firsts[0] != firsts[1]
+    assert any(a != b for a, b in firsts[0])  # slots 0 and 1 get different prompts
+
+
+@pytest.mark.parametrize("args,code,msg", [
+    ((), 2, "-m MODEL.gguf is required"),
+    (("-m",), 2, "needs a value"),
+    (("-m", "x", "-pp", "0"), 2, "bad value for -pp"),
+    (("-m", "x", "--graph", "2"), 2, "bad value for --graph"),
+    (("-m", "x", "--kv", "f16"), 2, "bad value for --kv"),
+    (("-m", "x", "--frobnicate", "1"), 2, "unknown option"),
+])
+def test_bad_usage(stub_cli, args, code, msg):
+    r = run(stub_cli[0], *args)
+    assert r.returncode == code and msg in r.stderr and "usage:" in r.stderr
+
+
+def test_help(stub_cli):
+    r = run(stub_cli[0], "--help")
+    assert r.returncode == 0 and r.stdout.startswith("usage: ab2_bench")
+
+
+def test_failures_report_the_ab2_message(stub_cli, tmp_path):
+    exe, model, d = stub_cli
+    r = run(exe, "-m", str(tmp_path / "missing.gguf"))
+    assert r.returncode == 1 and "cannot read" in r.stderr
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOPE" + bytes(8))
+    r = run(exe, "-m", str(bad))
+    assert r.returncode == 1 and "reading the GGUF failed: stub: not a GGUF file" in r.stderr
+    r = run(exe, "-m", model, env={"STUB_FAIL_CREATE": "1"})
+    assert r.returncode == 1 and "ab2_create failed: stub: no CUDA device available" in r.stderr
+
+
+def test_real_library_without_gpu_fails_cleanly(tiny_gguf, tmp_path):
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: this checks the no-device path")
+    exe = os.path.join(PKG, "ab2_bench")
+    if not os.path.exists(exe):
+        _build_mod().build()
+    model = tmp_path / "tiny.gguf"
+    model.write_bytes(bytes(tiny_gguf))
+    r = run(exe, "-m", str(model), "-pp", "2", "-tg", "2")
+    assert r.returncode == 1 and "ab2_create failed" in r.stderr
+    assert "Model: 4 layers (3 DeltaNet, 1 attention)" in r.stderr
