@@ -11,12 +11,26 @@ backend they travel as device tensors, with gloo (the CPU tests) as host tensors
 device step function (`step_fn_device`, NCCL) the ids stay on the device between the
 collectives: rank 0 makes one host-to-device copy of the batch's ids and one device-to-host
 copy of the next ids per step, and every rank decodes straight from the scattered tensor.
+
+Failures: in the host-array form, each rank's result carries a status word. The results
+travel by all-gather, so when one rank's step raises (or returns the wrong shape), every
+rank raises `ShardStepError` at the same point of the same step. No collective is left
+pending, and the group stays usable. In the device form a rank whose step raises takes no
+part in the gather, and the other ranks' gather ends with the process group's timeout.
 """
 from __future__ import annotations
 
 from typing import Callable, Optional
 
 import numpy as np
+
+
+class ShardStepError(RuntimeError):
+    """A decode step failed on one or more ranks; raised on every rank of the group."""
+
+    def __init__(self, failed_ranks: list[int]):
+        super().__init__(f"decode step failed on rank(s) {failed_ranks}")
+        self.failed_ranks = failed_ranks
 
 
 def shard_range(global_batch: int, world: int, rank: int) -> tuple[int, int]:
@@ -49,7 +63,8 @@ class ShardedDecoder:
     step_fn(local_tokens: np.ndarray[int32]) -> np.ndarray[int32] decodes this rank's
     sequences one step (for example `DecodeContext.decode_step(...)[1]`); it is called on
     every rank, also with an empty array when the rank owns no sequence, so all ranks take
-    the same collective steps in the same order.
+    the same collective steps in the same order. If it raises on any rank, `step` raises
+    ShardStepError on every rank (chained to the original exception where it happened).
     """
 
     def __init__(self, step_fn: Optional[Callable[[np.ndarray], np.ndarray]], global_batch: int, group=None,
@@ -83,12 +98,6 @@ class ShardedDecoder:
                 self._send_h = torch.full((self.world, w), -1, dtype=torch.int32, pin_memory=pin)
                 self._recv_h = torch.empty((self.world, w), dtype=torch.int32, pin_memory=pin)
 
-    def _padded(self, ids: np.ndarray):
-        import torch
-        t = torch.full((self.width,), -1, dtype=torch.int32)
-        t[: len(ids)] = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.int32))
-        return t.to(self.device)
-
     def step(self, tokens: Optional[np.ndarray]) -> Optional[np.ndarray]:
         """tokens: int32 [global_batch] on rank 0 (ignored elsewhere). Returns the next ids
         [global_batch] on rank 0 and None on the other ranks."""
@@ -98,30 +107,51 @@ class ShardedDecoder:
             return np.zeros(0, dtype=np.int32) if self.rank == 0 else None
         if self.step_fn_device is not None:
             return self._step_device(tokens)
+        # each rank's ids padded to the shard width, then a control word: 1 = rank 0 could not
+        # form the batch, so no rank runs its step
+        w = self.width
+        err = None
         scatter_list = None
         if self.rank == 0:
             tokens = np.asarray(tokens, dtype=np.int32)
             if tokens.shape != (self.global_batch,):
-                raise ValueError(f"expected {self.global_batch} token ids, got shape {tokens.shape}")
+                err = ValueError(f"expected {self.global_batch} token ids, got shape {tokens.shape}")
             scatter_list = []
             for r in range(self.world):
-                s, c = shard_range(self.global_batch, self.world, r)
-                scatter_list.append(self._padded(tokens[s:s + c]))
-        mine = torch.empty(self.width, dtype=torch.int32, device=self.device)
+                t = torch.full((w + 1,), -1, dtype=torch.int32)
+                if err is None:
+                    s0, c = shard_range(self.global_batch, self.world, r)
+                    t[:c] = torch.from_numpy(tokens[s0:s0 + c])
+                t[w] = 0 if err is None else 1
+                scatter_list.append(t.to(self.device))
+        mine = torch.empty(w + 1, dtype=torch.int32, device=self.device)
         dist.scatter(mine, scatter_list, src=0, group=self.group)
-        local = mine[: self.count].cpu().numpy()
-        nxt = np.asarray(self.step_fn(local), dtype=np.int32)
-        if nxt.shape != (self.count,):
-            raise ValueError(f"step_fn returned shape {nxt.shape} for {self.count} sequences")
-        out = self._padded(nxt)
-        gather_list = [torch.empty_like(out) for _ in range(self.world)] if self.rank == 0 else None
-        dist.gather(out, gather_list, dst=0, group=self.group)
+        mine = mine.cpu()
+        nxt = np.full(self.count, -1, dtype=np.int32)
+        if int(mine[w]) == 0:
+            try:
+                nxt = np.asarray(self.step_fn(mine[: self.count].numpy()), dtype=np.int32)
+                if nxt.shape != (self.count,):
+                    raise ValueError(f"step_fn returned shape {nxt.shape} for {self.count} sequences")
+            except Exception as e:  # reported to every rank below, then raised here
+                err = e
+                nxt = np.full(self.count, -1, dtype=np.int32)
+        # the next ids padded to the shard width, then this rank's status (0 ok, 1 failed)
+        out = torch.full((w + 1,), -1, dtype=torch.int32)
+        out[: self.count] = torch.from_numpy(nxt)
+        out[w] = 0 if err is None else 1
+        out = out.to(self.device)
+        outs = [torch.empty_like(out) for _ in range(self.world)]
+        dist.all_gather(outs, out, group=self.group)
+        failed = [r for r in range(self.world) if int(outs[r][w].item()) != 0]
+        if failed:
+            raise ShardStepError(failed) from err
         if self.rank != 0:
             return None
         res = np.empty(self.global_batch, dtype=np.int32)
         for r in range(self.world):
             s, c = shard_range(self.global_batch, self.world, r)
-            res[s:s + c] = gather_list[r][:c].cpu().numpy()
+            res[s:s + c] = outs[r][:c].cpu().numpy()
         return res
 
     def _step_device(self, tokens: Optional[np.ndarray]) -> Optional[np.ndarray]:

@@ -87,3 +87,68 @@ def test_sharded_decode_gloo_world2(tmp_path):
     assert lines[-1] == "max 2.5"
     checks = lines[:-1]
     assert len(checks) == 24 and all(l.endswith(" 1") for l in checks), checks
+
+
+def _fail_worker(rank, world, port, result_dir):
+    """Injected failures on the host: a rank whose step raises, a step returning the wrong
+    shape, and a malformed batch on rank 0. Every rank must see the same ShardStepError at
+    the same step, and the group must keep working afterwards."""
+    import sys
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        from conftest import load_pkg as lp
+        lp()
+        from ane_infer_b200.shard import ShardedDecoder, ShardStepError, shard_range
+        B = 6
+        start, _ = shard_range(B, world, rank)
+        calls = {"n": 0}
+        good = fake_step(start)
+
+        def flaky(toks):
+            calls["n"] += 1
+            if rank == 1 and calls["n"] == 2:
+                raise RuntimeError("injected worker failure")
+            if rank == 0 and calls["n"] == 4:
+                return good(toks)[:-1]  # wrong shape
+            return good(toks)
+
+        dec = ShardedDecoder(flaky, B)
+        toks = np.arange(B, dtype=np.int32) * 5 + 1
+        lines = []
+        for step in range(6):
+            feed = toks if rank == 0 else None
+            if rank == 0 and step == 4:
+                feed = toks[:-1]  # malformed batch on rank 0
+            try:
+                nxt = dec.step(feed)
+                ok = "ok"
+                if rank == 0:
+                    want = ((toks.astype(np.int64) * 31 + 7 + np.arange(B)) % 1000).astype(np.int32)
+                    ok += " 1" if np.array_equal(nxt, want) else " 0"
+                    toks = nxt
+                lines.append(ok)
+            except ShardStepError as e:
+                cause = type(e.__cause__).__name__ if e.__cause__ is not None else "-"
+                lines.append(f"fail {e.failed_ranks} {cause}")
+        with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
+            f.write("\n".join(lines))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_decode_failure_gloo_world2(tmp_path):
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_fail_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    r0 = (tmp_path / "rank0.txt").read_text().split("\n")
+    r1 = (tmp_path / "rank1.txt").read_text().split("\n")
+    # step 1: rank 1's step raises; step 3: rank 0's step returns the wrong shape; step 4:
+    # rank 0's batch is malformed, so no rank steps; the steps between and after succeed
+    assert r0 == ["ok 1", "fail [1] -", "ok 1", "fail [0] ValueError", "fail [0] ValueError", "ok 1"], r0
+    assert r1 == ["ok", "fail [1] RuntimeError", "ok", "fail [0] -", "fail [0] -", "ok"], r1
