@@ -315,6 +315,70 @@ int read_f32(const Gguf& g, const std::string& name, int64_t n, std::vector<floa
     return 0;
 }
 
+// an F32 or F16 tensor of n elements (the checks of read_f32, without reading)
+int check_f32(const Gguf& g, const std::string& name, int64_t n) {
+    const GTensor* t = g.tensor(name);
+    if (!t) return seterr(AB2_ERR_FORMAT, "tensor not found: %s", name.c_str());
+    int64_t ne = 1;
+    for (auto d : t->dims) ne *= (int64_t)d;
+    if (ne != n) return seterr(AB2_ERR_SHAPE, "%s: %lld elements, expected %lld", name.c_str(), (long long)ne, (long long)n);
+    if (t->type != 0 && t->type != 1) return seterr(AB2_ERR_SHAPE, "%s: expected an F32 or F16 tensor", name.c_str());
+    return 0;
+}
+
+// Everything the context build needs from the file, checked on the host before any device
+// work: the shapes this build's kernels support (rot = rotated dims per head, 0 = head_dim)
+// and the presence, type and shape of every tensor the build reads (tensor list of
+// load_qwen35_weights, crates/cli/src/main.rs:1874-1994).
+int validate_model(const Gguf& g, const Cfg& c, int rot) {
+    const int64_t D = c.dim, F = c.ffn, H = c.dn_heads, hd = c.hd, Hq = c.n_heads, Hkv = c.n_kv;
+    if (D % 128) return seterr(AB2_ERR_SHAPE, "embedding_length must be a multiple of 128");
+    if (F % 32 || F % 8) return seterr(AB2_ERR_SHAPE, "feed_forward_length must be a multiple of 32");
+    if (c.n_dn > 0) {
+        if (c.dn_state != 128 || H <= 0 || D % H || D / H != 128)
+            return seterr(AB2_ERR_SHAPE, "DeltaNet heads must have dk = dv = dim/heads = 128");
+        if (c.conv_k < 1 || c.conv_k > 8) return seterr(AB2_ERR_SHAPE, "ssm.conv_kernel must be in [1, 8]");
+    }
+    if (c.n_attn > 0) {
+        if (hd != 128 && hd != 256) return seterr(AB2_ERR_SHAPE, "attention head_dim must be 128 or 256");
+        if (Hkv <= 0 || Hq % Hkv || Hq / Hkv != 4) return seterr(AB2_ERR_SHAPE, "GQA group must be 4 query heads per KV head");
+        if ((Hq * hd) % 32) return seterr(AB2_ERR_SHAPE, "q dim must be a multiple of 32");
+        const int r = rot > 0 ? rot : (int)hd;
+        if (r % 2 || r > hd) return seterr(AB2_ERR_SHAPE, "rope_dims must be even and <= head_dim");
+    }
+    const GTensor* t;
+    RET(find_q8(g, "token_embd.weight", c.vocab, D, &t));
+    if (g.tensor("output.weight")) RET(find_q8(g, "output.weight", c.vocab, D, &t));
+    RET(check_f32(g, "output_norm.weight", D));
+    for (int64_t l = 0; l < c.n_layers; l++) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        RET(check_f32(g, p + "attn_norm.weight", D));
+        RET(check_f32(g, p + "post_attention_norm.weight", D));
+        if (c.is_dn[l]) {
+            RET(find_q8(g, p + "attn_qkv.weight", 3 * D, D, &t));
+            RET(find_q8(g, p + "attn_gate.weight", D, D, &t));
+            RET(find_q8(g, p + "ssm_beta.weight", H, D, &t));
+            RET(find_q8(g, p + "ssm_alpha.weight", H, D, &t));
+            RET(find_q8(g, p + "ssm_out.weight", D, D, &t));
+            RET(check_f32(g, p + "ssm_conv1d.weight", 3 * D * c.conv_k));
+            RET(check_f32(g, p + "ssm_a", H));
+            RET(check_f32(g, p + "ssm_dt.bias", H));
+            RET(check_f32(g, p + "ssm_norm.weight", 128));
+        } else {
+            RET(find_q8(g, p + "attn_q.weight", 2 * Hq * hd, D, &t));
+            RET(find_q8(g, p + "attn_k.weight", Hkv * hd, D, &t));
+            RET(find_q8(g, p + "attn_v.weight", Hkv * hd, D, &t));
+            RET(find_q8(g, p + "attn_output.weight", D, Hq * hd, &t));
+            RET(check_f32(g, p + "attn_q_norm.weight", hd));
+            RET(check_f32(g, p + "attn_k_norm.weight", hd));
+        }
+        RET(find_q8(g, p + "ffn_gate.weight", F, D, &t));
+        RET(find_q8(g, p + "ffn_up.weight", F, D, &t));
+        RET(find_q8(g, p + "ffn_down.weight", D, F, &t));
+    }
+    return 0;
+}
+
 // ------------------------------------------------------------------------------------- context
 enum { PC_ATTN = 0, PC_DN = 1, PC_GEMM = 2, PC_OTHER = 3 };
 
@@ -463,21 +527,8 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     RET(derive_config(g, &x->c));
     Cfg& c = x->c;
     const int64_t D = c.dim, F = c.ffn, H = c.dn_heads, hd = c.hd, Hq = c.n_heads, Hkv = c.n_kv;
-    // what the kernels of this build support
-    if (D % 128) return seterr(AB2_ERR_SHAPE, "embedding_length must be a multiple of 128");
-    if (F % 32 || F % 8) return seterr(AB2_ERR_SHAPE, "feed_forward_length must be a multiple of 32");
-    if (c.n_dn > 0) {
-        if (c.dn_state != 128 || H <= 0 || D % H || D / H != 128)
-            return seterr(AB2_ERR_SHAPE, "DeltaNet heads must have dk = dv = dim/heads = 128");
-        if (c.conv_k < 1 || c.conv_k > 8) return seterr(AB2_ERR_SHAPE, "ssm.conv_kernel must be in [1, 8]");
-    }
-    if (c.n_attn > 0) {
-        if (hd != 128 && hd != 256) return seterr(AB2_ERR_SHAPE, "attention head_dim must be 128 or 256");
-        if (Hkv <= 0 || Hq % Hkv || Hq / Hkv != 4) return seterr(AB2_ERR_SHAPE, "GQA group must be 4 query heads per KV head");
-        if ((Hq * hd) % 32) return seterr(AB2_ERR_SHAPE, "q dim must be a multiple of 32");
-    }
+    RET(validate_model(g, c, x->rot));
     x->rot = x->rot > 0 ? x->rot : (int)hd;
-    if (c.n_attn > 0 && (x->rot % 2 || x->rot > hd)) return seterr(AB2_ERR_SHAPE, "rope_dims must be even and <= head_dim");
 
     // staging buffer for the largest Q8 tensor
     uint64_t maxb = 0;
@@ -1053,6 +1104,15 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
     *out = nullptr;
     if (max_batch < 1 || max_batch > 64) return seterr(AB2_ERR_ARG, "max_batch must be in [1, 64]");
     if (max_ctx < 1) return seterr(AB2_ERR_ARG, "max_ctx must be positive");
+    {
+        // the file is checked on the host first, so a bad model fails the same way with or
+        // without a GPU
+        Gguf g;
+        Cfg c;
+        RET(parse_gguf(gguf, len, &g));
+        RET(derive_config(g, &c));
+        RET(validate_model(g, c, opt ? opt->rope_dims : 0));
+    }
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
         cudaGetLastError();

@@ -115,6 +115,54 @@ def test_unsupported_ggml_type(pkg, synth):
     assert _err(pkg, g.tobytes()) == -2
 
 
+def _edit_tensor_info(gguf, name, new_name=None, dims=None):
+    """Copy of GGUF bytes with one tensor's info edited in place: its name (same length) or
+    its dims (same number of dims)."""
+    b = bytearray(np.asarray(gguf, dtype=np.uint8).tobytes())
+    key = name.encode()
+    i = b.find(struct.pack("<Q", len(key)) + key)
+    assert i >= 0, name
+    j = i + 8 + len(key)
+    if new_name is not None:
+        assert len(new_name) == len(name)
+        b[i + 8:j] = new_name.encode()
+    if dims is not None:
+        assert struct.unpack_from("<I", b, j)[0] == len(dims)
+        for k, d in enumerate(dims):
+            struct.pack_into("<Q", b, j + 4 + 8 * k, d)
+    return np.frombuffer(bytes(b), dtype=np.uint8)
+
+
+def _create_err(pkg, gguf, **kw):
+    with pytest.raises(pkg.Ab2Error) as ei:
+        pkg.DecodeContext(gguf, max_batch=1, max_ctx=8, **kw)
+    return ei.value.code, str(ei.value)
+
+
+# The model file is checked on the host before any device work, so these fail the same way
+# with or without a GPU.
+def test_create_rejects_wrong_tensor_shape(pkg, tiny_gguf):
+    # ffn_down is D x F (GGUF dims F, D); transposed dims keep the byte size
+    code, msg = _create_err(pkg, _edit_tensor_info(tiny_gguf, "blk.2.ffn_down.weight", dims=(1024, 3072)))
+    assert code == -3 and "blk.2.ffn_down.weight: shape 3072x1024, expected 1024x3072" in msg
+    code, msg = _create_err(pkg, _edit_tensor_info(tiny_gguf, "blk.0.ssm_a", dims=(4,)))
+    assert code == -3 and "blk.0.ssm_a: 4 elements, expected 8" in msg
+
+
+def test_create_rejects_missing_tensor(pkg, tiny_gguf):
+    code, msg = _create_err(pkg, _edit_tensor_info(tiny_gguf, "blk.3.attn_k_norm.weight",
+                                                   new_name="blk.3.attn_k_xxxx.weight"))
+    assert code == -2 and "tensor not found: blk.3.attn_k_norm.weight" in msg
+
+
+def test_create_rejects_unsupported_shapes(pkg, tiny_gguf, synth):
+    g = synth.build_model_gguf(synth.HybridShape(head_dim=64, attn_heads=8, kv_heads=2), seed=1)
+    code, msg = _create_err(pkg, g)
+    assert code == -3 and "head_dim must be 128 or 256" in msg
+    code, msg = _create_err(pkg, tiny_gguf, rope_dims=3)
+    assert code == -3 and "rope_dims" in msg
+
+
 def test_create_without_gpu_fails_cleanly(pkg, tiny_gguf):
     torch = pytest.importorskip("torch")
     if torch.cuda.is_available():
