@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                     }
                 }
             }
-            if (!ok && p.err) atomicOr(p.err, 256u);
+            if (!ok && p.err) atomicOr(p.err, 4096u);
             // all K/V copies of this CTA are issued: pull its share of the output projection's
             // weights into L2 for the GEMM that follows
             prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
         // Q A-fragments for every k16 step: a0 = (row g, k 2t..2t+1), a2 = (row g, k 2t+8..+9)
         const int qs = k & 1;
         if (!mbar_wait(&q_full[qs], (k >> 1) & 1)) {
-            if (ct == 0 && p.err) atomicOr(p.err, 256u);
+            if (ct == 0 && p.err) atomicOr(p.err, 4096u);
             break;
         }
         const float* q_s = reinterpret_cast<const float*>(smem + L::q_off(qs));
@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
         mbar_arrive(&q_free[qs]);
         if (!ok) {
             // a timed-out wait: report it and stop; the results of this launch are invalid
-            if (ct == 0 && p.err) atomicOr(p.err, 256u);
+            if (ct == 0 && p.err) atomicOr(p.err, 4096u);
             break;
         }
         // merge hi/lo rows: lanes g < 4 hold head g for dims d0 + 8n + 2t, +1

@@ -148,7 +148,7 @@ struct AttnParams {
     unsigned* tickets;   // [B*Hkv]
     ActOut out;          // activations of the wo GEMM (K = Hq*HD)
     float* o_out;        // optional f32 copy [B][Hq*HD]
-    unsigned* err = nullptr;  // pipeline error word (tensor-core kernel)
+    unsigned* err = nullptr;  // pipeline error word: bit 4096 when a wait of the tensor-core kernel timed out
     const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
     int64_t pf_bytes = 0;
 };
