@@ -1345,6 +1345,9 @@ AB2_API int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int B, float* log
     CK(cudaSetDevice(x->device));
     int max_len;
     RET(check_capacity(x, B, &max_len));
+    for (int b = 0; b < B; b++)  // the reference indexes its embedding with the id (a panic when out of range)
+        if (tokens[b] < 0 || tokens[b] >= x->c.vocab)
+            return seterr(AB2_ERR_ARG, "token id %d of slot %d is outside [0, %lld)", tokens[b], b, (long long)x->c.vocab);
     memcpy(x->tok_h, tokens, (size_t)B * 4);
     CK(cudaMemcpyAsync(x->tok_d, x->tok_h, (size_t)B * 4, cudaMemcpyHostToDevice, x->stream));
     RET(enqueue_step(x, x->tok_d, B, max_len, x->logits, x->next_d, x->stream));

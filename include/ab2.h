@@ -97,10 +97,12 @@ int ab2_seed_state(ab2_ctx* ctx, uint64_t seed, int n_slots, int64_t n_tokens, f
  * each slot's position advanced by one. Host buffers; synchronous.
  * Batched replacement of encode_full_token_gpu (crates/engine/src/gpu_full_decode.rs:221)
  * and of qwen35_forward_token + greedy_sample (crates/cli/src/main.rs:953, :1767).
- * logits: [batch][vocab] or NULL; next_tokens: [batch] or NULL. */
+ * logits: [batch][vocab] or NULL; next_tokens: [batch] or NULL. Token ids outside
+ * [0, vocab) are rejected with AB2_ERR_ARG before any work is queued. */
 int ab2_decode_step(ab2_ctx* ctx, const int32_t* tokens, int batch, float* logits, int32_t* next_tokens);
 /* Same with device buffers, enqueued on `stream` (a cudaStream_t; NULL = the context's own
- * stream) without synchronising. tokens_dev may alias next_dev of the previous step. */
+ * stream) without synchronising. tokens_dev may alias next_dev of the previous step. The
+ * ids are not checked on the host here: an id outside [0, vocab) embeds as a zero vector. */
 int ab2_decode_step_device(ab2_ctx* ctx, const int32_t* tokens_dev, int batch, float* logits_dev,
                            int32_t* next_dev, void* stream);
 /* Wait for all work of the context (including ab2_decode_step_device calls) and report a

@@ -191,6 +191,11 @@ def test_state_io_and_capacity(pkg, tiny_gguf):
     with pytest.raises(pkg.Ab2Error) as ei:
         ctx.decode_step([1, 2, 3])                  # batch 3 > max_batch 2
     assert ei.value.code == -6
+    for bad in (32000, -5):                         # token ids outside the vocabulary
+        with pytest.raises(pkg.Ab2Error) as ei:
+            ctx.decode_step([bad])
+        assert ei.value.code == -1 and "outside [0, 32000)" in str(ei.value)
+    assert ctx.get_pos(0) == 0                      # nothing was queued
     ctx.set_pos(0, 8)
     with pytest.raises(pkg.Ab2Error) as ei:
         ctx.decode_step([1])                        # slot 0 is full
