@@ -70,7 +70,10 @@ int ab2_get_config(ab2_ctx* ctx, ab2_config* out);
 /* 1 if `layer` is a Gated DeltaNet layer (GgufFile::is_deltanet_layer, parser.rs:483). */
 int ab2_layer_is_deltanet(ab2_ctx* ctx, int layer);
 
-/* ---- per-slot state (host buffers). Layer indices are model layer indices. ---------- */
+/* ---- per-slot state (host buffers). Layer indices are model layer indices. ---------- *
+ * These calls are synchronous, but they do not wait for steps queued with
+ * ab2_decode_step_device on other streams: call ab2_sync (or synchronise those streams)
+ * first. */
 /* Zero a slot's states and set its position to 0 (HybridCache::new for one sequence). */
 int ab2_reset_slot(ab2_ctx* ctx, int slot);
 /* Position of the next token of a slot (HybridCache::pos, deltanet_cache.rs:72). */
