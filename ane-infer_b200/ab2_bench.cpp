@@ -13,6 +13,11 @@
 // * Generation does not stop at EOS.
 // * With -b B, B independent sequences decode together; the reference decodes one.
 //
+// --ctx N seeds every sequence's state as N tokens already processed (ab2_seed_state: DeltaNet
+// and conv state, KV cache), the prefilled workload of the backend's own benchmark (64
+// sequences at ctx 8192 on the 2B shape). The prompt then continues from position N; with
+// -pp 0 generation starts straight from a synthetic id.
+//
 // The timing also follows the reference. The first generated token is a warm-up. Speed is
 // (tokens - 1) / time over the rest, summed over the batch, and wall-clock timed around the
 // synchronous ab2_decode_step calls (host buffers in and out).
@@ -35,7 +40,7 @@ namespace {
 
 struct Args {
     std::string model;
-    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1;
+    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1, ctx = 0;
     bool kv_bf16 = true;
     uint64_t seed = 0;
 };
@@ -43,14 +48,15 @@ struct Args {
 void usage(FILE* f) {
     std::fprintf(f,
                  "usage: ab2_bench -m MODEL.gguf [-pp N] [-tg N] [-b B] [-d DEVICE] [--kv bf16|f32]\n"
-                 "                 [--graph 0|1] [--seed S]\n"
+                 "                 [--graph 0|1] [--ctx N] [--seed S]\n"
                  "  -m, --model          qwen35 GGUF with Q8_0 weights (required)\n"
-                 "  -pp, --prompt-tokens prompt tokens per sequence (default 128)\n"
+                 "  -pp, --prompt-tokens prompt tokens per sequence (default 128; 0 allowed)\n"
                  "  -tg, --gen-tokens    greedy tokens per sequence (default 128)\n"
                  "  -b, --batch          sequences decoded together (default 1)\n"
                  "  -d, --device         CUDA device (default 0)\n"
                  "  --kv                 KV cache type (default bf16; f32 as the reference)\n"
                  "  --graph              replay each step as one CUDA graph (default 1)\n"
+                 "  --ctx                seed every sequence as N tokens already processed (default 0)\n"
                  "  --seed               seed of the synthetic prompt ids (default 0)\n");
 }
 
@@ -76,13 +82,15 @@ int parse(int argc, char** argv, Args* a) {
         if (k == "-m" || k == "--model") {
             a->model = v;
         } else if (k == "-pp" || k == "--prompt-tokens") {
-            ok = parse_long(v, 1, &a->pp);
+            ok = parse_long(v, 0, &a->pp);
         } else if (k == "-tg" || k == "--gen-tokens") {
             ok = parse_long(v, 1, &a->tg);
         } else if (k == "-b" || k == "--batch") {
             ok = parse_long(v, 1, &a->batch);
         } else if (k == "-d" || k == "--device") {
             ok = parse_long(v, 0, &a->device);
+        } else if (k == "--ctx") {
+            ok = parse_long(v, 0, &a->ctx);
         } else if (k == "--graph") {
             ok = parse_long(v, 0, &a->graph) && a->graph <= 1;
         } else if (k == "--seed") {
@@ -182,7 +190,11 @@ int main(int argc, char** argv) {
                  (long long)cfg.vocab);
 
     const int B = (int)a.batch;
-    const long max_ctx = a.pp + a.tg + 2;
+    const long max_ctx = a.ctx + a.pp + a.tg + 2;
+    if (max_ctx > 0x7fffffffL) {
+        std::fprintf(stderr, "ab2_bench: --ctx + -pp + -tg is too large\n");
+        return 2;
+    }
     ab2_options opt;
     std::memset(&opt, 0, sizeof(opt));
     opt.kv_bf16 = a.kv_bf16 ? 1 : 0;
@@ -199,6 +211,12 @@ int main(int argc, char** argv) {
             rc = fail("ab2_step_graph");
             break;
         }
+        if (a.ctx > 0 && ab2_seed_state(ctx, a.seed, B, a.ctx, 0.1f, 1.0f, 1.0f)) {
+            rc = fail("ab2_seed_state");
+            break;
+        }
+        // the id each sequence starts generating from when there is no prompt
+        for (int b = 0; b < B; b++) next[b] = (int32_t)(mix(~a.seed ^ mix((uint64_t)b)) % cfg.vocab);
         // prompt: one decode step per position for all sequences
         const auto t_pp = std::chrono::steady_clock::now();
         for (long i = 0; i < a.pp && !rc; i++) {
@@ -228,10 +246,10 @@ int main(int argc, char** argv) {
     std::fprintf(stderr, "  Tokens: %ld\n", a.tg);
     std::fprintf(stderr, "  Time: %.1fms\n", 1e3 * tg_s);
     std::fprintf(stderr, "  Speed: %.1f tok/s (B200 tg%ld, %d sequences)\n", tg_tps, a.tg, B);
-    std::printf("{\"model\": \"%s\", \"batch\": %d, \"prompt_tokens\": %ld, \"gen_tokens\": %ld, "
+    std::printf("{\"model\": \"%s\", \"batch\": %d, \"ctx\": %ld, \"prompt_tokens\": %ld, \"gen_tokens\": %ld, "
                 "\"prompt_tok_s\": %.2f, \"gen_tok_s\": %.2f, \"gen_ms\": %.3f, \"kv\": \"%s\", \"graph\": %ld, "
                 "\"prompt\": [",
-                json_escape(a.model).c_str(), B, a.pp, a.tg, pp_tps, tg_tps, 1e3 * tg_s, a.kv_bf16 ? "bf16" : "f32", a.graph);
+                json_escape(a.model).c_str(), B, a.ctx, a.pp, a.tg, pp_tps, tg_tps, 1e3 * tg_s, a.kv_bf16 ? "bf16" : "f32", a.graph);
     for (size_t i = 0; i < prompt0.size(); i++) std::printf("%s%d", i ? ", " : "", prompt0[i]);
     std::printf("], \"tokens\": [");
     for (size_t i = 0; i < gen0.size(); i++) std::printf("%s%d", i ? ", " : "", gen0[i]);

@@ -74,6 +74,20 @@ int ab2_step_graph(ab2_ctx* ctx, int enable) {
     return 0;
 }
 
+int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tokens, float dn_std, float conv_std,
+                   float kv_std) {
+    (void)dn_std;
+    (void)conv_std;
+    (void)kv_std;
+    logf_("seed %lld %lld %lld %lld", (long long)seed, n_slots, n_tokens, 0);
+    if (n_slots < 1 || n_slots > x->max_batch || n_tokens < 0 || n_tokens >= x->max_ctx) {
+        g_msg = "stub: bad seed_state arguments";
+        return AB2_ERR_ARG;
+    }
+    for (int b = 0; b < n_slots; b++) x->pos[b] = n_tokens;
+    return 0;
+}
+
 int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int batch, float* logits, int32_t* next) {
     if (batch < 1 || batch > x->max_batch) {
         g_msg = "stub: batch outside [1, max_batch]";

@@ -69,6 +69,23 @@ def test_prompt_then_greedy_feedback(stub_cli, tmp_path, B, pp, tg, kv, graph):
     assert out["prompt"] == tok0[:pp]
 
 
+def test_seeded_context_without_prompt(stub_cli, tmp_path):
+    exe, model, _ = stub_cli
+    log = tmp_path / "calls.log"
+    r = run(exe, "-m", model, "--ctx", "5", "-pp", "0", "-tg", "3", "-b", "2", "--seed", "7",
+            env={"STUB_LOG": str(log)})
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    assert (out["ctx"], out["prompt_tokens"], out["prompt"]) == (5, 0, [])
+    calls = read_log(log)
+    assert calls[0] == ["create", "0", "2", str(5 + 0 + 3 + 2), "1"]
+    assert calls[2] == ["seed", "7", "2", "5", "0"]  # both slots start at position 5
+    steps = [c for c in calls if c[0] == "step"]
+    assert len(steps) == 3 and 0 <= int(steps[0][2]) < 1000
+    assert [int(s[2]) for s in steps[1:]] == [int(s[3]) for s in steps[:-1]]
+    assert out["tokens"] == [int(s[2]) for s in steps]
+
+
 def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
     exe, model, _ = stub_cli
     firsts = []
@@ -85,7 +102,8 @@ def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
 @pytest.mark.parametrize("args,code,msg", [
     ((), 2, "-m MODEL.gguf is required"),
     (("-m",), 2, "needs a value"),
-    (("-m", "x", "-pp", "0"), 2, "bad value for -pp"),
+    (("-m", "x", "-pp", "-1"), 2, "bad value for -pp"),
+    (("-m", "x", "--ctx", "x"), 2, "bad value for --ctx"),
     (("-m", "x", "--graph", "2"), 2, "bad value for --graph"),
     (("-m", "x", "--kv", "f16"), 2, "bad value for --kv"),
     (("-m", "x", "--frobnicate", "1"), 2, "unknown option"),
