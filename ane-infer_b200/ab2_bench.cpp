@@ -18,6 +18,10 @@
 // sequences at ctx 8192 on the 2B shape). The prompt then continues from position N; with
 // -pp 0 generation starts straight from a synthetic id.
 //
+// --gpus N runs the same workload on N GPUs at once, one host thread and context per GPU
+// (sequence sharding: nothing is exchanged), with seeds offset per GPU; the rates are
+// whole-job figures over the slowest GPU's time.
+//
 // The timing also follows the reference. The first generated token is a warm-up. Speed is
 // (tokens - 1) / time over the rest, summed over the batch, and wall-clock timed around the
 // synchronous ab2_decode_step calls (host buffers in and out).
@@ -31,7 +35,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
+#include <functional>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "ab2.h"
@@ -40,20 +47,22 @@ namespace {
 
 struct Args {
     std::string model;
-    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1, ctx = 0;
+    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1, ctx = 0, gpus = 1;
     bool kv_bf16 = true;
     uint64_t seed = 0;
 };
 
 void usage(FILE* f) {
     std::fprintf(f,
-                 "usage: ab2_bench -m MODEL.gguf [-pp N] [-tg N] [-b B] [-d DEVICE] [--kv bf16|f32]\n"
-                 "                 [--graph 0|1] [--ctx N] [--seed S]\n"
+                 "usage: ab2_bench -m MODEL.gguf [-pp N] [-tg N] [-b B] [-d DEVICE] [--gpus N]\n"
+                 "                 [--kv bf16|f32] [--graph 0|1] [--ctx N] [--seed S]\n"
                  "  -m, --model          qwen35 GGUF with Q8_0 weights (required)\n"
                  "  -pp, --prompt-tokens prompt tokens per sequence (default 128; 0 allowed)\n"
                  "  -tg, --gen-tokens    greedy tokens per sequence (default 128)\n"
                  "  -b, --batch          sequences decoded together (default 1)\n"
-                 "  -d, --device         CUDA device (default 0)\n"
+                 "  -d, --device         first CUDA device (default 0)\n"
+                 "  --gpus               GPUs from --device on, one host thread and context each,\n"
+                 "                       -b sequences per GPU (default 1)\n"
                  "  --kv                 KV cache type (default bf16; f32 as the reference)\n"
                  "  --graph              replay each step as one CUDA graph (default 1)\n"
                  "  --ctx                seed every sequence as N tokens already processed (default 0)\n"
@@ -89,6 +98,8 @@ int parse(int argc, char** argv, Args* a) {
             ok = parse_long(v, 1, &a->batch);
         } else if (k == "-d" || k == "--device") {
             ok = parse_long(v, 0, &a->device);
+        } else if (k == "--gpus") {
+            ok = parse_long(v, 1, &a->gpus) && a->gpus <= 64;
         } else if (k == "--ctx") {
             ok = parse_long(v, 0, &a->ctx);
         } else if (k == "--graph") {
@@ -165,6 +176,63 @@ double seconds_since(std::chrono::steady_clock::time_point t0) {
     return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
 }
 
+// one device's run: its own context, prompt and generation
+struct Run {
+    int rc = 0;
+    const char* what = "";
+    std::string msg;  // ab2_last_error() of the failing call, read on this thread
+    double pp_s = 0, tg_s = 0;
+    std::vector<int32_t> prompt0, gen0;  // sequence 0's prompt and generated ids
+};
+
+void run_device(const Args& a, const std::vector<uint8_t>& gguf, const ab2_config& cfg, int device, uint64_t seed,
+                int max_ctx, Run* out) {
+    const int B = (int)a.batch;
+    auto failed = [&](const char* what) {
+        out->rc = 1;
+        out->what = what;
+        out->msg = ab2_last_error();
+    };
+    ab2_options opt;
+    std::memset(&opt, 0, sizeof(opt));
+    opt.kv_bf16 = a.kv_bf16 ? 1 : 0;
+    ab2_ctx* ctx = nullptr;
+    if (ab2_create(gguf.data(), gguf.size(), device, B, max_ctx, &opt, &ctx)) return failed("ab2_create");
+    std::vector<int32_t> tok((size_t)B), next((size_t)B);
+    do {
+        if (ab2_step_graph(ctx, (int)a.graph)) {
+            failed("ab2_step_graph");
+            break;
+        }
+        if (a.ctx > 0 && ab2_seed_state(ctx, seed, B, a.ctx, 0.1f, 1.0f, 1.0f)) {
+            failed("ab2_seed_state");
+            break;
+        }
+        // the id each sequence starts generating from when there is no prompt
+        for (int b = 0; b < B; b++) next[b] = (int32_t)(mix(~seed ^ mix((uint64_t)b)) % cfg.vocab);
+        // prompt: one decode step per position for all sequences
+        const auto t_pp = std::chrono::steady_clock::now();
+        for (long i = 0; i < a.pp && !out->rc; i++) {
+            for (int b = 0; b < B; b++) tok[b] = (int32_t)(mix(seed ^ mix(((uint64_t)b << 32) + i)) % cfg.vocab);
+            out->prompt0.push_back(tok[0]);
+            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) failed("ab2_decode_step (prompt)");
+        }
+        if (out->rc) break;
+        out->pp_s = seconds_since(t_pp);
+        // generation: the first token is the warm-up, then (tg - 1) timed greedy steps
+        auto t_tg = std::chrono::steady_clock::now();
+        for (long i = 0; i < a.tg && !out->rc; i++) {
+            if (i == 1) t_tg = std::chrono::steady_clock::now();
+            tok = next;
+            out->gen0.push_back(tok[0]);
+            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) failed("ab2_decode_step");
+        }
+        if (out->rc) break;
+        out->tg_s = a.tg > 1 ? seconds_since(t_tg) : 0.0;
+    } while (false);
+    ab2_destroy(ctx);
+}
+
 }  // namespace
 
 int main(int argc, char** argv) {
@@ -189,70 +257,58 @@ int main(int argc, char** argv) {
                  (long long)cfg.n_layers, (long long)cfg.n_dn, (long long)cfg.n_attn, (long long)cfg.dim,
                  (long long)cfg.vocab);
 
-    const int B = (int)a.batch;
     const long max_ctx = a.ctx + a.pp + a.tg + 2;
     if (max_ctx > 0x7fffffffL) {
         std::fprintf(stderr, "ab2_bench: --ctx + -pp + -tg is too large\n");
         return 2;
     }
-    ab2_options opt;
-    std::memset(&opt, 0, sizeof(opt));
-    opt.kv_bf16 = a.kv_bf16 ? 1 : 0;
-    ab2_ctx* ctx = nullptr;
-    std::fprintf(stderr, "  Uploading model weights to GPU %ld...\n", a.device);
-    const auto t_up = std::chrono::steady_clock::now();
-    if (ab2_create(gguf.data(), gguf.size(), (int)a.device, B, (int)max_ctx, &opt, &ctx)) return fail("ab2_create");
-    std::fprintf(stderr, "  Uploaded in %.1fms\n", 1e3 * seconds_since(t_up));
+    // one host thread per GPU, each with its own context (contexts are per device and are
+    // driven from separate threads), started together
+    const int G = (int)a.gpus;
+    std::vector<Run> runs((size_t)G);
+    std::fprintf(stderr, "  Uploading model weights to %d GPU(s) from device %ld...\n", G, a.device);
+    std::vector<std::thread> threads;
+    for (int g = 0; g < G; g++)
+        threads.emplace_back(run_device, std::cref(a), std::cref(gguf), std::cref(cfg), (int)a.device + g,
+                             a.seed + (uint64_t)g, (int)max_ctx, &runs[(size_t)g]);
+    for (auto& t : threads) t.join();
     int rc = 0;
-    std::vector<int32_t> tok((size_t)B), next((size_t)B), prompt0, gen0;
-    double pp_s = 0, tg_s = 0;
-    do {
-        if (ab2_step_graph(ctx, (int)a.graph)) {
-            rc = fail("ab2_step_graph");
-            break;
+    for (int g = 0; g < G; g++)
+        if (runs[(size_t)g].rc) {
+            std::fprintf(stderr, "ab2_bench: GPU %ld: %s failed: %s\n", a.device + g, runs[(size_t)g].what,
+                         runs[(size_t)g].msg.c_str());
+            rc = 1;
         }
-        if (a.ctx > 0 && ab2_seed_state(ctx, a.seed, B, a.ctx, 0.1f, 1.0f, 1.0f)) {
-            rc = fail("ab2_seed_state");
-            break;
-        }
-        // the id each sequence starts generating from when there is no prompt
-        for (int b = 0; b < B; b++) next[b] = (int32_t)(mix(~a.seed ^ mix((uint64_t)b)) % cfg.vocab);
-        // prompt: one decode step per position for all sequences
-        const auto t_pp = std::chrono::steady_clock::now();
-        for (long i = 0; i < a.pp && !rc; i++) {
-            for (int b = 0; b < B; b++) tok[b] = (int32_t)(mix(a.seed ^ mix(((uint64_t)b << 32) + i)) % cfg.vocab);
-            prompt0.push_back(tok[0]);
-            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) rc = fail("ab2_decode_step (prompt)");
-        }
-        if (rc) break;
-        pp_s = seconds_since(t_pp);
-        // generation: the first token is the warm-up, then (tg - 1) timed greedy steps
-        auto t_tg = std::chrono::steady_clock::now();
-        for (long i = 0; i < a.tg && !rc; i++) {
-            if (i == 1) t_tg = std::chrono::steady_clock::now();
-            tok = next;
-            gen0.push_back(tok[0]);
-            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) rc = fail("ab2_decode_step");
-        }
-        if (rc) break;
-        tg_s = a.tg > 1 ? seconds_since(t_tg) : 0.0;
-    } while (false);
-    ab2_destroy(ctx);
     if (rc) return rc;
 
-    const double pp_tps = pp_s > 0 ? (double)B * a.pp / pp_s : 0.0;
-    const double tg_tps = tg_s > 0 ? (double)B * (a.tg - 1) / tg_s : 0.0;
-    std::fprintf(stderr, "  Prompt: %ld tokens x %d sequences in %.1fms (%.1f tok/s)\n", a.pp, B, 1e3 * pp_s, pp_tps);
+    // whole-job rates over the slowest device, as a multi-GPU timing is reported
+    const int B = (int)a.batch;
+    double pp_s = 0, tg_s = 0;
+    for (const Run& r : runs) {
+        pp_s = std::max(pp_s, r.pp_s);
+        tg_s = std::max(tg_s, r.tg_s);
+    }
+    const double pp_tps = pp_s > 0 ? (double)G * B * a.pp / pp_s : 0.0;
+    const double tg_tps = tg_s > 0 ? (double)G * B * (a.tg - 1) / tg_s : 0.0;
+    std::fprintf(stderr, "  Prompt: %ld tokens x %d sequences x %d GPU(s) in %.1fms (%.1f tok/s)\n", a.pp, B, G,
+                 1e3 * pp_s, pp_tps);
     std::fprintf(stderr, "  Tokens: %ld\n", a.tg);
     std::fprintf(stderr, "  Time: %.1fms\n", 1e3 * tg_s);
-    std::fprintf(stderr, "  Speed: %.1f tok/s (B200 tg%ld, %d sequences)\n", tg_tps, a.tg, B);
-    std::printf("{\"model\": \"%s\", \"batch\": %d, \"ctx\": %ld, \"prompt_tokens\": %ld, \"gen_tokens\": %ld, "
-                "\"prompt_tok_s\": %.2f, \"gen_tok_s\": %.2f, \"gen_ms\": %.3f, \"kv\": \"%s\", \"graph\": %ld, "
-                "\"prompt\": [",
-                json_escape(a.model).c_str(), B, a.ctx, a.pp, a.tg, pp_tps, tg_tps, 1e3 * tg_s, a.kv_bf16 ? "bf16" : "f32", a.graph);
-    for (size_t i = 0; i < prompt0.size(); i++) std::printf("%s%d", i ? ", " : "", prompt0[i]);
+    std::fprintf(stderr, "  Speed: %.1f tok/s (B200 tg%ld, %d sequences x %d GPU(s))\n", tg_tps, a.tg, B, G);
+    const Run& r0 = runs[0];
+    std::printf("{\"model\": \"%s\", \"gpus\": %d, \"batch\": %d, \"ctx\": %ld, \"prompt_tokens\": %ld, "
+                "\"gen_tokens\": %ld, \"prompt_tok_s\": %.2f, \"gen_tok_s\": %.2f, \"gen_ms\": %.3f, \"kv\": \"%s\", "
+                "\"graph\": %ld, \"gen_tok_s_per_gpu\": [",
+                json_escape(a.model).c_str(), G, B, a.ctx, a.pp, a.tg, pp_tps, tg_tps, 1e3 * tg_s,
+                a.kv_bf16 ? "bf16" : "f32", a.graph);
+    for (int g = 0; g < G; g++) {
+        const double t = runs[(size_t)g].tg_s;
+        std::printf("%s%.2f", g ? ", " : "", t > 0 ? (double)B * (a.tg - 1) / t : 0.0);
+    }
+    std::printf("], \"prompt\": [");
+    for (size_t i = 0; i < r0.prompt0.size(); i++) std::printf("%s%d", i ? ", " : "", r0.prompt0[i]);
     std::printf("], \"tokens\": [");
-    for (size_t i = 0; i < gen0.size(); i++) std::printf("%s%d", i ? ", " : "", gen0[i]);
+    for (size_t i = 0; i < r0.gen0.size(); i++) std::printf("%s%d", i ? ", " : "", r0.gen0[i]);
     std::printf("]}\n");
     return 0;
 }

@@ -80,7 +80,7 @@ def build_cli(out: str = CLI, lib_dir: str = HERE, lib: str = "ab2", extra: tupl
     deps = [CLI_SRC, header, *extra]
     if os.path.exists(out) and os.path.getmtime(out) >= max(os.path.getmtime(d) for d in deps) and not extra:
         return out
-    cmd = ["g++", "-O2", "-std=c++17", "-Wall", "-Wextra", "-I", os.path.join(ROOT, "include"), CLI_SRC, *extra,
+    cmd = ["g++", "-O2", "-std=c++17", "-pthread", "-Wall", "-Wextra", "-I", os.path.join(ROOT, "include"), CLI_SRC, *extra,
            "-o", out]
     if lib:  # the library is looked up beside the binary first
         cmd += ["-L", lib_dir, f"-l{lib}", "-Wl,-rpath,$ORIGIN"]

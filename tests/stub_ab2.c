@@ -2,6 +2,7 @@
  * entry points ab2_bench calls, with a deterministic stand-in for decoding (next token =
  * (7 * token + position + slot) mod vocab) and a call log written to $STUB_LOG. Built only
  * by tests/test_cli.py. */
+#include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -11,18 +12,22 @@
 #define STUB_VOCAB 1000
 
 struct ab2_ctx {
-    int max_batch, max_ctx;
+    int device, max_batch, max_ctx;
     long long pos[256];
 };
 
 static const char* g_msg = "";
 
-static void logf_(const char* fmt, long long a, long long b, long long c, long long d) {
+/* one line per call, appended to $STUB_LOG (long long arguments) */
+static void logf_(const char* fmt, ...) {
     const char* path = getenv("STUB_LOG");
     if (!path) return;
     FILE* f = fopen(path, "a");
     if (!f) return;
-    fprintf(f, fmt, a, b, c, d);
+    va_list ap;
+    va_start(ap, fmt);
+    vfprintf(f, fmt, ap);
+    va_end(ap);
     fputc('\n', f);
     fclose(f);
 }
@@ -47,7 +52,8 @@ int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int
                const ab2_options* opt, ab2_ctx** out) {
     (void)gguf;
     (void)len;
-    logf_("create %lld %lld %lld %lld", device, max_batch, max_ctx, opt ? opt->kv_bf16 : -1);
+    logf_("create %lld %lld %lld %lld", (long long)device, (long long)max_batch, (long long)max_ctx,
+          (long long)(opt ? opt->kv_bf16 : -1));
     if (getenv("STUB_FAIL_CREATE")) {
         g_msg = "stub: no CUDA device available";
         return AB2_ERR_DEVICE;
@@ -57,6 +63,7 @@ int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int
         return AB2_ERR_ARG;
     }
     ab2_ctx* x = (ab2_ctx*)calloc(1, sizeof(ab2_ctx));
+    x->device = device;
     x->max_batch = max_batch;
     x->max_ctx = max_ctx;
     *out = x;
@@ -64,13 +71,13 @@ int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int
 }
 
 void ab2_destroy(ab2_ctx* ctx) {
-    logf_("destroy %lld %lld %lld %lld", 0, 0, 0, 0);
+    logf_("destroy");
     free(ctx);
 }
 
 int ab2_step_graph(ab2_ctx* ctx, int enable) {
     (void)ctx;
-    logf_("graph %lld %lld %lld %lld", enable, 0, 0, 0);
+    logf_("graph %lld 0 0 0", (long long)enable);
     return 0;
 }
 
@@ -79,7 +86,8 @@ int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tokens, flo
     (void)dn_std;
     (void)conv_std;
     (void)kv_std;
-    logf_("seed %lld %lld %lld %lld", (long long)seed, n_slots, n_tokens, 0);
+    logf_("seed %lld %lld %lld 0 %lld", (long long)seed, (long long)n_slots, (long long)n_tokens,
+          (long long)x->device);
     if (n_slots < 1 || n_slots > x->max_batch || n_tokens < 0 || n_tokens >= x->max_ctx) {
         g_msg = "stub: bad seed_state arguments";
         return AB2_ERR_ARG;
@@ -111,6 +119,7 @@ int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int batch, float* logits,
         if (b == 0) n0 = n;
         x->pos[b]++;
     }
-    logf_("step %lld %lld %lld %lld", batch, tokens[0], n0, batch > 1 ? tokens[batch - 1] : -1);
+    logf_("step %lld %lld %lld %lld %lld", (long long)batch, (long long)tokens[0], (long long)n0,
+          (long long)(batch > 1 ? tokens[batch - 1] : -1), (long long)x->device);
     return 0;
 }

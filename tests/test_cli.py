@@ -79,11 +79,40 @@ def test_seeded_context_without_prompt(stub_cli, tmp_path):
     assert (out["ctx"], out["prompt_tokens"], out["prompt"]) == (5, 0, [])
     calls = read_log(log)
     assert calls[0] == ["create", "0", "2", str(5 + 0 + 3 + 2), "1"]
-    assert calls[2] == ["seed", "7", "2", "5", "0"]  # both slots start at position 5
+    assert calls[2] == ["seed", "7", "2", "5", "0", "0"]  # both slots start at position 5 (device 0)
     steps = [c for c in calls if c[0] == "step"]
     assert len(steps) == 3 and 0 <= int(steps[0][2]) < 1000
     assert [int(s[2]) for s in steps[1:]] == [int(s[3]) for s in steps[:-1]]
     assert out["tokens"] == [int(s[2]) for s in steps]
+
+
+def test_one_thread_and_context_per_gpu(stub_cli, tmp_path):
+    exe, model, _ = stub_cli
+    log = tmp_path / "calls.log"
+    G, B, pp, tg = 3, 2, 2, 4
+    r = run(exe, "-m", model, "--gpus", str(G), "-d", "1", "-b", str(B), "-pp", str(pp), "-tg", str(tg),
+            env={"STUB_LOG": str(log)})
+    assert r.returncode == 0, r.stderr
+    out = json.loads(r.stdout)
+    assert out["gpus"] == G and len(out["gen_tok_s_per_gpu"]) == G
+    calls = read_log(log)
+    creates = sorted(int(c[1]) for c in calls if c[0] == "create")
+    assert creates == [1, 2, 3]
+    assert sum(c[0] == "destroy" for c in calls) == G
+    by_dev = {}
+    for c in calls:
+        if c[0] == "step":
+            by_dev.setdefault(int(c[5]), []).append(c)
+    assert sorted(by_dev) == [1, 2, 3]
+    for dev, steps in by_dev.items():
+        assert len(steps) == pp + tg, dev
+        tok0 = [int(s[2]) for s in steps]
+        nxt0 = [int(s[3]) for s in steps]
+        assert all(tok0[k] == nxt0[k - 1] for k in range(pp, pp + tg)), dev
+    # each GPU decodes its own sequences: prompts are seeded per GPU; the output reports GPU 1's
+    prompts = {dev: [int(s[2]) for s in steps[:pp]] for dev, steps in by_dev.items()}
+    assert len({tuple(p) for p in prompts.values()}) == G
+    assert out["prompt"] == prompts[1]
 
 
 def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
@@ -104,6 +133,7 @@ def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
     (("-m",), 2, "needs a value"),
     (("-m", "x", "-pp", "-1"), 2, "bad value for -pp"),
     (("-m", "x", "--ctx", "x"), 2, "bad value for --ctx"),
+    (("-m", "x", "--gpus", "0"), 2, "bad value for --gpus"),
     (("-m", "x", "--graph", "2"), 2, "bad value for --graph"),
     (("-m", "x", "--kv", "f16"), 2, "bad value for --kv"),
     (("-m", "x", "--frobnicate", "1"), 2, "unknown option"),
