@@ -32,10 +32,10 @@ PKG_DIR = os.path.join(ROOT, "ane-infer_b200")
 METRIC = "decode tok/s, 2B-shape Q8_0 B=64 ctx8K at 1/2/4/8 B200; % HBM roofline"
 SHAPE_KEYS = dict(n_layers=24, dim=2048, vocab=151936, ffn=6144, dn_heads=16, dn_state=128, attn_heads=8,
                   kv_heads=2, head_dim=256)
-# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch, from the ncu capture
-# summarised in profiles/attn_mma_b8_ctx8k.md (B=8, ctx 8192: 134.32 MB read + 4.11 MB
-# written), scaled by 8 to the benchmark's B=64 launch; traffic grows with B (each sequence's
-# K/V is read once), so the scaling is proportional.
+# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch, from an ncu capture
+# of attn_mma_kernel on the op benchmark at B=8, ctx 8192 (134.32 MB read + 4.11 MB written),
+# scaled by 8 to the benchmark's B=64 launch; traffic grows with B (each sequence's K/V is
+# read once), so the scaling is proportional.
 NCU_TRAFFIC_ATTN_PER_LAUNCH = 8 * (134_317_568 + 4_110_080)
 
 
