@@ -172,3 +172,8 @@ def test_real_library_without_gpu_fails_cleanly(tiny_gguf, tmp_path):
     r = run(exe, "-m", str(model), "-pp", "2", "-tg", "2")
     assert r.returncode == 1 and "ab2_create failed" in r.stderr
     assert "Model: 4 layers (3 DeltaNet, 1 attention)" in r.stderr
+    # every device thread reports its own failure, read from its own thread's error slot
+    r = run(exe, "-m", str(model), "-pp", "2", "-tg", "2", "--gpus", "2")
+    assert r.returncode == 1
+    assert "GPU 0: ab2_create failed: no CUDA device available" in r.stderr
+    assert "GPU 1: ab2_create failed: no CUDA device available" in r.stderr
