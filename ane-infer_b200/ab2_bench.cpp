@@ -36,7 +36,9 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <condition_variable>
 #include <functional>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <vector>
@@ -172,26 +174,61 @@ std::string json_escape(const std::string& s) {
     return o;
 }
 
-double seconds_since(std::chrono::steady_clock::time_point t0) {
-    return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-}
+// A rendezvous of the device threads (C++17 has no std::barrier): wait() returns once every
+// thread still taking part has arrived; drop() leaves for good, so a thread whose device failed
+// does not hold the others back.
+class Gate {
+public:
+    explicit Gate(int n) : n_(n) {}
+    void wait() {
+        std::unique_lock<std::mutex> lk(mu_);
+        const long gen = gen_;
+        if (++arrived_ >= n_) {
+            open_locked();
+        } else {
+            cv_.wait(lk, [&] { return gen_ != gen; });
+        }
+    }
+    void drop() {
+        std::lock_guard<std::mutex> lk(mu_);
+        if (--n_ > 0 && arrived_ >= n_) open_locked();
+    }
+
+private:
+    void open_locked() {
+        arrived_ = 0;
+        gen_++;
+        cv_.notify_all();
+    }
+    std::mutex mu_;
+    std::condition_variable cv_;
+    int n_;
+    int arrived_ = 0;
+    long gen_ = 0;
+};
+
+using Clock = std::chrono::steady_clock;
 
 // one device's run: its own context, prompt and generation
 struct Run {
     int rc = 0;
     const char* what = "";
     std::string msg;  // ab2_last_error() of the failing call, read on this thread
-    double pp_s = 0, tg_s = 0;
-    std::vector<int32_t> prompt0, gen0;  // sequence 0's prompt and generated ids
+    Clock::time_point pp0, pp1, tg0, tg1;  // the timed prompt and generation phases
+    std::vector<int32_t> prompt0, gen0;    // sequence 0's prompt and generated ids
 };
 
+// Every device thread uploads and seeds its context, then all start the prompt together (one
+// gate) and the timed generation together (a second gate, after each thread's warm-up token),
+// so the whole-job rates are taken over the span from the first start to the last end.
 void run_device(const Args& a, const std::vector<uint8_t>& gguf, const ab2_config& cfg, int device, uint64_t seed,
-                int max_ctx, Run* out) {
+                int max_ctx, Gate* gate, Run* out) {
     const int B = (int)a.batch;
     auto failed = [&](const char* what) {
         out->rc = 1;
         out->what = what;
         out->msg = ab2_last_error();
+        gate->drop();
     };
     ab2_options opt;
     std::memset(&opt, 0, sizeof(opt));
@@ -211,24 +248,28 @@ void run_device(const Args& a, const std::vector<uint8_t>& gguf, const ab2_confi
         // the id each sequence starts generating from when there is no prompt
         for (int b = 0; b < B; b++) next[b] = (int32_t)(mix(~seed ^ mix((uint64_t)b)) % cfg.vocab);
         // prompt: one decode step per position for all sequences
-        const auto t_pp = std::chrono::steady_clock::now();
+        gate->wait();
+        out->pp0 = Clock::now();
         for (long i = 0; i < a.pp && !out->rc; i++) {
             for (int b = 0; b < B; b++) tok[b] = (int32_t)(mix(seed ^ mix(((uint64_t)b << 32) + i)) % cfg.vocab);
             out->prompt0.push_back(tok[0]);
             if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) failed("ab2_decode_step (prompt)");
         }
         if (out->rc) break;
-        out->pp_s = seconds_since(t_pp);
+        out->pp1 = Clock::now();
         // generation: the first token is the warm-up, then (tg - 1) timed greedy steps
-        auto t_tg = std::chrono::steady_clock::now();
         for (long i = 0; i < a.tg && !out->rc; i++) {
-            if (i == 1) t_tg = std::chrono::steady_clock::now();
+            if (i == 1) {
+                gate->wait();
+                out->tg0 = Clock::now();
+            }
             tok = next;
             out->gen0.push_back(tok[0]);
             if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) failed("ab2_decode_step");
         }
         if (out->rc) break;
-        out->tg_s = a.tg > 1 ? seconds_since(t_tg) : 0.0;
+        out->tg1 = Clock::now();
+        if (a.tg <= 1) out->tg0 = out->tg1;
     } while (false);
     ab2_destroy(ctx);
 }
@@ -268,9 +309,10 @@ int main(int argc, char** argv) {
     std::vector<Run> runs((size_t)G);
     std::fprintf(stderr, "  Uploading model weights to %d GPU(s) from device %ld...\n", G, a.device);
     std::vector<std::thread> threads;
+    Gate gate(G);
     for (int g = 0; g < G; g++)
         threads.emplace_back(run_device, std::cref(a), std::cref(gguf), std::cref(cfg), (int)a.device + g,
-                             a.seed + (uint64_t)g, (int)max_ctx, &runs[(size_t)g]);
+                             a.seed + (uint64_t)g, (int)max_ctx, &gate, &runs[(size_t)g]);
     for (auto& t : threads) t.join();
     int rc = 0;
     for (int g = 0; g < G; g++)
@@ -281,13 +323,17 @@ int main(int argc, char** argv) {
         }
     if (rc) return rc;
 
-    // whole-job rates over the slowest device, as a multi-GPU timing is reported
+    // whole-job rates over the span from the first device's start to the last device's end
     const int B = (int)a.batch;
-    double pp_s = 0, tg_s = 0;
+    Clock::time_point pp0 = runs[0].pp0, pp1 = runs[0].pp1, tg0 = runs[0].tg0, tg1 = runs[0].tg1;
     for (const Run& r : runs) {
-        pp_s = std::max(pp_s, r.pp_s);
-        tg_s = std::max(tg_s, r.tg_s);
+        pp0 = std::min(pp0, r.pp0);
+        pp1 = std::max(pp1, r.pp1);
+        tg0 = std::min(tg0, r.tg0);
+        tg1 = std::max(tg1, r.tg1);
     }
+    const double pp_s = std::chrono::duration<double>(pp1 - pp0).count();
+    const double tg_s = std::chrono::duration<double>(tg1 - tg0).count();
     const double pp_tps = pp_s > 0 ? (double)G * B * a.pp / pp_s : 0.0;
     const double tg_tps = tg_s > 0 ? (double)G * B * (a.tg - 1) / tg_s : 0.0;
     std::fprintf(stderr, "  Prompt: %ld tokens x %d sequences x %d GPU(s) in %.1fms (%.1f tok/s)\n", a.pp, B, G,
@@ -302,7 +348,7 @@ int main(int argc, char** argv) {
                 json_escape(a.model).c_str(), G, B, a.ctx, a.pp, a.tg, pp_tps, tg_tps, 1e3 * tg_s,
                 a.kv_bf16 ? "bf16" : "f32", a.graph);
     for (int g = 0; g < G; g++) {
-        const double t = runs[(size_t)g].tg_s;
+        const double t = std::chrono::duration<double>(runs[(size_t)g].tg1 - runs[(size_t)g].tg0).count();
         std::printf("%s%.2f", g ? ", " : "", t > 0 ? (double)B * (a.tg - 1) / t : 0.0);
     }
     std::printf("], \"prompt\": [");

@@ -85,6 +85,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) attn_decode_kernel(AttnParams
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z, nsplit = gridDim.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int pos = p.pos[b], L = pos + 1;
+    if (!attn_pos_ok(p, pos)) {  // nothing is appended or read at an out-of-range position
+        if (threadIdx.x == 0 && split == 0 && kvh == 0 && p.err) atomicOr(p.err, kAttnErrPos);
+        return;
+    }
     const int t0 = split * p.chunk, t1 = min(L, t0 + p.chunk);
     const float* proj = p.proj + (size_t)b * p.ldp;
     KV* kc = reinterpret_cast<KV*>(p.kc) + (size_t)b * p.kv_slot_stride + (size_t)kvh * p.cap * HD;

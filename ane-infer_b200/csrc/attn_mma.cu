@@ -99,6 +99,7 @@ __device__ __forceinline__ bool attn_item(const AttnParams& p, int item, int pai
     it.b = pair / p.Hkv;
     it.kvh = pair % p.Hkv;
     const int pos = p.pos[it.b], L = pos + 1;
+    if (!attn_pos_ok(p, pos)) return false;  // skipped; the prep kernel reports it
     it.t0 = it.split * p.chunk;
     if (it.t0 >= L) return false;
     it.t1 = min(L, it.t0 + p.chunk);
@@ -134,6 +135,10 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(AttnParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // every input load in flight at once: position, queries, key, value
     const int pos = p.pos[b];
+    if (!attn_pos_ok(p, pos)) {  // nothing is appended or read at an out-of-range position
+        if (tid == 0 && kvh == 0 && p.err) atomicOr(p.err, kAttnErrPos);
+        return;
+    }
     const float* proj = p.proj + (size_t)b * p.ldp;
     const int koff = p.Hq * 2 * HD, voff = koff + p.Hkv * HD;
     constexpr int kQ4 = kGQ * HD / 4 / 128;  // float4 of queries per thread
@@ -482,6 +487,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (!attn_pos_ok(p, p.pos[b])) return;
     const int L = p.pos[b] + 1;
     const int nsplit = (L + p.chunk - 1) / p.chunk;
     if (nsplit <= 1) return;

@@ -148,10 +148,19 @@ struct AttnParams {
     unsigned* tickets;   // [B*Hkv]
     ActOut out;          // activations of the wo GEMM (K = Hq*HD)
     float* o_out;        // optional f32 copy [B][Hq*HD]
-    unsigned* err = nullptr;  // pipeline error word: bit 4096 when a wait of the tensor-core kernel timed out
+    unsigned* err = nullptr;  // pipeline error word: bit 4096 when a wait of the tensor-core kernel timed out,
+                              // bit kAttnErrPos when a sequence's position is outside [0, max_pos]
+    // The largest position the launch plan covers (split count x chunk - 1, at most cap - 1).
+    // Every kernel checks 0 <= pos[b] <= max_pos < cap before it appends at pos or reads the
+    // rotation table at pos; a sequence outside that range is skipped and bit kAttnErrPos set.
+    int max_pos = 0;
     const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
     int64_t pf_bytes = 0;
 };
+constexpr unsigned kAttnErrPos = 8192;
+__host__ __device__ inline bool attn_pos_ok(const AttnParams& p, int pos) {
+    return pos >= 0 && pos <= p.max_pos && pos < p.cap;
+}
 // attn_mma.cu: tensor-core flash-decode over a bf16 cache read through two TMA tensor maps
 // (K and V viewed as [rows][hd]); row_base = row of (first slot, kv head 0, token 0)
 int make_kv_tensor_map(void* map_out /*128 bytes, 64-aligned*/, void* base, int64_t rows, int hd);

@@ -48,6 +48,23 @@ int seterr(int code, const char* fmt, ...) {
         if (r_ != 0) return r_; \
     } while (0)
 
+// Makes `dev` the calling thread's current device for the duration of an entry point and
+// restores the caller's device on every return path: a host thread that drives another GPU
+// (through torch, say) between calls into this library keeps its own current device.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        err = cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
 // ------------------------------------------------------------------------------------- GGUF
 // Same byte format and accessor semantics as the reference parser
 // (crates/gguf/src/parser.rs:17-347, :354-486), written for this runtime.
@@ -849,6 +866,9 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.Hq = (int)c.n_heads;
         p.Hkv = (int)c.n_kv;
         p.chunk = step_attn_chunk(x, B, max_len);
+        // a replayed step graph keeps this plan while the longest context stays within its
+        // split count, so every position up to the plan's last covered token is valid
+        p.max_pos = std::min(x->cap - 1, attn_nsplit(max_len, p.chunk) * p.chunk - 1);
         if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv) > x->aws_floats)
             return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
         p.ws = x->aws;
@@ -1119,7 +1139,8 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
         return seterr(AB2_ERR_DEVICE, "no CUDA device available");
     }
     if (device < 0 || device >= ndev) return seterr(AB2_ERR_ARG, "device %d out of range", device);
-    CK(cudaSetDevice(device));
+    DeviceGuard dev_guard(device);
+    CK(dev_guard.err);
     auto* x = new ab2_ctx();
     x->device = device;
     x->max_batch = max_batch;
@@ -1144,7 +1165,7 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
 
 AB2_API void ab2_destroy(ab2_ctx* x) {
     if (!x) return;
-    cudaSetDevice(x->device);
+    DeviceGuard dev_guard(x->device);
     if (x->stream) cudaStreamSynchronize(x->stream);
     for (void* p : x->allocs) cudaFree(p);
     if (x->tok_h) cudaFreeHost(x->tok_h);
@@ -1179,12 +1200,13 @@ AB2_API int ab2_layer_is_deltanet(ab2_ctx* x, int layer) {
 static int check_slot(ab2_ctx* x, int slot) {
     if (!x) return seterr(AB2_ERR_ARG, "null context");
     if (slot < 0 || slot >= x->max_batch) return seterr(AB2_ERR_ARG, "slot %d out of range", slot);
-    CK(cudaSetDevice(x->device));
     return 0;
 }
 
 AB2_API int ab2_reset_slot(ab2_ctx* x, int slot) {
     RET(check_slot(x, slot));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     const Cfg& c = x->c;
     const size_t kvel = x->kv_bf16 ? 2 : 4;
     for (int64_t i = 0; i < c.n_dn; i++) {
@@ -1203,6 +1225,8 @@ AB2_API int ab2_reset_slot(ab2_ctx* x, int slot) {
 
 AB2_API int ab2_set_pos(ab2_ctx* x, int slot, int64_t pos) {
     RET(check_slot(x, slot));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     if (pos < 0 || pos > x->cap) return seterr(AB2_ERR_ARG, "pos %lld outside [0, %d]", (long long)pos, x->cap);
     int32_t p = (int32_t)pos;
     CK(cudaMemcpyAsync(x->pos_d + slot, &p, 4, cudaMemcpyHostToDevice, x->stream));
@@ -1225,6 +1249,9 @@ static int dn_layer(ab2_ctx* x, int layer, const Layer** L) {
 }
 
 static int dn_state_io(ab2_ctx* x, int layer, int slot, float* rec, float* conv, bool set) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     RET(check_slot(x, slot));
     const Layer* L;
     RET(dn_layer(x, layer, &L));
@@ -1254,6 +1281,9 @@ static inline uint16_t f32_to_bf16_rne(float f) {
 }
 
 static int kv_io(ab2_ctx* x, int layer, int slot, float* k, float* v, int64_t n, bool set) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     RET(check_slot(x, slot));
     const Layer* L;
     RET(dn_layer(x, layer, &L));
@@ -1307,7 +1337,8 @@ AB2_API int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tok
     if (!x) return seterr(AB2_ERR_ARG, "null context");
     if (n_slots < 1 || n_slots > x->max_batch) return seterr(AB2_ERR_ARG, "n_slots outside [1, max_batch]");
     if (n_tokens < 0 || n_tokens >= x->cap) return seterr(AB2_ERR_ARG, "n_tokens outside [0, max_ctx)");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     const Cfg& c = x->c;
     for (int64_t i = 0; i < c.n_dn; i++) {
         launch_seed_f32(x->dn_S + (size_t)i * x->max_batch * x->s_stride, (int64_t)n_slots * x->s_stride, seed,
@@ -1333,7 +1364,8 @@ AB2_API int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tok
 AB2_API int ab2_decode_step_device(ab2_ctx* x, const int32_t* tok_d, int B, float* logits_d, int32_t* next_d,
                                    void* stream) {
     if (!x || !tok_d) return seterr(AB2_ERR_ARG, "null argument");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     int max_len;
     RET(check_capacity(x, B, &max_len));
     cudaStream_t st = stream ? (cudaStream_t)stream : x->stream;
@@ -1342,7 +1374,8 @@ AB2_API int ab2_decode_step_device(ab2_ctx* x, const int32_t* tok_d, int B, floa
 
 AB2_API int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int B, float* logits, int32_t* next_tokens) {
     if (!x || !tokens) return seterr(AB2_ERR_ARG, "null argument");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     int max_len;
     RET(check_capacity(x, B, &max_len));
     for (int b = 0; b < B; b++)  // the reference indexes its embedding with the id (a panic when out of range)
@@ -1363,7 +1396,8 @@ AB2_API int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int B, float* log
 
 AB2_API int ab2_sync(ab2_ctx* x) {
     if (!x) return seterr(AB2_ERR_ARG, "null context");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     CK(cudaMemcpyAsync(x->err_h, x->err_d, 4, cudaMemcpyDeviceToHost, x->stream));
     CK(cudaDeviceSynchronize());
     prof_collect(x);
@@ -1378,7 +1412,8 @@ AB2_API int ab2_launches_per_step(ab2_ctx* x, int B, int64_t* out) {
 
 AB2_API int ab2_profile(ab2_ctx* x, int enable) {
     if (!x) return seterr(AB2_ERR_ARG, "null context");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     CK(cudaStreamSynchronize(x->stream));
     prof_collect(x);
     x->prof.on = enable != 0;
@@ -1387,7 +1422,8 @@ AB2_API int ab2_profile(ab2_ctx* x, int enable) {
 
 AB2_API int ab2_step_graph(ab2_ctx* x, int enable) {
     if (!x) return seterr(AB2_ERR_ARG, "null context");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     CK(cudaStreamSynchronize(x->stream));
     if (!enable) graphs_clear(x);
     x->graph_on = enable != 0;
@@ -1402,7 +1438,8 @@ AB2_API int ab2_step_graph_captures(ab2_ctx* x, int64_t* out) {
 
 AB2_API int ab2_profile_read(ab2_ctx* x, double ms[4], int64_t n[4]) {
     if (!x || !ms || !n) return seterr(AB2_ERR_ARG, "null argument");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     CK(cudaDeviceSynchronize());
     prof_collect(x);
     for (int c = 0; c < 4; c++) {
@@ -1415,6 +1452,9 @@ AB2_API int ab2_profile_read(ab2_ctx* x, double ms[4], int64_t n[4]) {
 }
 
 AB2_API int ab2_mixer_layer(ab2_ctx* x, int layer, int slot, const float* xin, float* out) {
+    if (!x) return seterr(AB2_ERR_ARG, "null context");
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     RET(check_slot(x, slot));
     if (!xin || !out) return seterr(AB2_ERR_ARG, "null argument");
     const Layer* L;
@@ -1433,7 +1473,8 @@ AB2_API int ab2_mixer_layer(ab2_ctx* x, int layer, int slot, const float* xin, f
 
 AB2_API int ab2_ffn_layer(ab2_ctx* x, int layer, const float* xin, float* out) {
     if (!x) return seterr(AB2_ERR_ARG, "null context");
-    CK(cudaSetDevice(x->device));
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
     if (!xin || !out) return seterr(AB2_ERR_ARG, "null argument");
     const Layer* L;
     RET(dn_layer(x, layer, &L));
@@ -1458,7 +1499,8 @@ AB2_API int ab2_q8_create(const uint8_t* blocks, int64_t m, int64_t n, int devic
         cudaGetLastError();
         return seterr(AB2_ERR_DEVICE, "no CUDA device available");
     }
-    CK(cudaSetDevice(device));
+    DeviceGuard dev_guard(device);
+    CK(dev_guard.err);
     auto* w = new ab2_q8();
     w->device = device;
     w->n = n;
@@ -1495,7 +1537,7 @@ AB2_API int ab2_q8_create(const uint8_t* blocks, int64_t m, int64_t n, int devic
 
 AB2_API void ab2_q8_destroy(ab2_q8* w) {
     if (!w) return;
-    cudaSetDevice(w->device);
+    DeviceGuard dev_guard(w->device);
     if (w->w.qs) cudaFree(w->w.qs);
     if (w->w.d) cudaFree(w->w.d);
     if (w->w.qt) cudaFree(w->w.qt);
@@ -1505,7 +1547,8 @@ AB2_API void ab2_q8_destroy(ab2_q8* w) {
 AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* stream) {
     if (!w || !xin || !y) return seterr(AB2_ERR_ARG, "null argument");
     if (batch < 1 || batch > 64) return seterr(AB2_ERR_CAPACITY, "batch must be in [1, 64]");
-    CK(cudaSetDevice(w->device));
+    DeviceGuard dev_guard(w->device);
+    CK(dev_guard.err);
     OpCache& oc = g_ops[w->device & 63];
     std::lock_guard<std::mutex> lk(oc.mu);
     cudaStream_t st = (cudaStream_t)stream;
@@ -1550,7 +1593,8 @@ AB2_API int ab2_op_error(uint32_t* code) {
 
 AB2_API int ab2_q8_unpack(ab2_q8* w, float* out, void* stream) {
     if (!w || !out) return seterr(AB2_ERR_ARG, "null argument");
-    CK(cudaSetDevice(w->device));
+    DeviceGuard dev_guard(w->device);
+    CK(dev_guard.err);
     launch_q8p_dequant(w->w, w->w.M, out, (cudaStream_t)stream);
     CK(cudaGetLastError());
     return 0;
@@ -1634,6 +1678,7 @@ AB2_API int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int
     p.kv_slot_stride = (int64_t)Hkv * cap * hd;
     p.cap = (int)cap;
     p.pos = pos;
+    p.max_pos = max_pos;
     p.Hq = Hq;
     p.Hkv = Hkv;
     p.chunk = chunk;
@@ -1707,7 +1752,8 @@ AB2_API int ab2_q8_gemv_noalloc(ab2_q8* w, const float* xin, int batch, float* y
                       "activations %zu, split-K %zu); the fixed scratch holds %zu B (tickets at most %zu)",
                       (long long)w->w.M, (long long)w->n, batch, kNoAllocTicketBytes + xf_bytes + ws_bytes,
                       tk_bytes, xf_bytes, ws_bytes, kNoAllocScratchBytes, kNoAllocTicketBytes);
-    CK(cudaSetDevice(w->device));
+    DeviceGuard dev_guard(w->device);
+    CK(dev_guard.err);
     unsigned char* base = nullptr;
     RET(noalloc_scratch(w->device, &base));
     unsigned* tickets = (unsigned*)base;

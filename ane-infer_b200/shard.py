@@ -12,11 +12,13 @@ device step function (`step_fn_device`, NCCL) the ids stay on the device between
 collectives: rank 0 makes one host-to-device copy of the batch's ids and one device-to-host
 copy of the next ids per step, and every rank decodes straight from the scattered tensor.
 
-Failures: in the host-array form, each rank's result carries a status word. The results
-travel by all-gather, so when one rank's step raises (or returns the wrong shape), every
+Failures: each rank's result carries a status word, and the results travel by all-gather,
+so when one rank's step raises (or, in the host-array form, returns the wrong shape), every
 rank raises `ShardStepError` at the same point of the same step. No collective is left
-pending, and the group stays usable. In the device form a rank whose step raises takes no
-part in the gather, and the other ranks' gather ends with the process group's timeout.
+pending, and the group stays usable. When rank 0 cannot form the batch, the host-array form
+runs no step anywhere (a control word in the scatter); the device form, whose ranks do not
+read the scattered ids on the host, runs every rank's step on ids of -1 (which the decoder
+embeds as zeros, advancing those sequences by one step) and then raises on every rank.
 """
 from __future__ import annotations
 
@@ -89,14 +91,17 @@ class ShardedDecoder:
         if step_fn_device is not None:
             import torch
             w = max(self.width, 1)
+            pin = device != "cpu"
             self._mine = torch.zeros(w, dtype=torch.int32, device=device)
-            self._next = torch.full((w,), -1, dtype=torch.int32, device=device)
+            # the next ids padded to the shard width, then this rank's status word (0 ok, 1 failed)
+            self._next = torch.full((w + 1,), -1, dtype=torch.int32, device=device)
+            self._next[w] = 0
+            self._recv = torch.empty((self.world, w + 1), dtype=torch.int32, device=device)
+            self._recv_list = list(self._recv.unbind(0))
+            self._recv_h = torch.empty((self.world, w + 1), dtype=torch.int32, pin_memory=pin)
             if self.rank == 0:
                 self._send = torch.full((self.world, w), -1, dtype=torch.int32, device=device)
-                self._recv = torch.empty((self.world, w), dtype=torch.int32, device=device)
-                pin = device != "cpu"
                 self._send_h = torch.full((self.world, w), -1, dtype=torch.int32, pin_memory=pin)
-                self._recv_h = torch.empty((self.world, w), dtype=torch.int32, pin_memory=pin)
 
     def step(self, tokens: Optional[np.ndarray]) -> Optional[np.ndarray]:
         """tokens: int32 [global_batch] on rank 0 (ignored elsewhere). Returns the next ids
@@ -157,28 +162,42 @@ class ShardedDecoder:
     def _step_device(self, tokens: Optional[np.ndarray]) -> Optional[np.ndarray]:
         import torch
         dist = self.dist
-        scatter_list = gather_list = None
+        w = self.width
+        err = None
+        scatter_list = None
         if self.rank == 0:
-            tokens = np.asarray(tokens, dtype=np.int32)
-            if tokens.shape != (self.global_batch,):
-                raise ValueError(f"expected {self.global_batch} token ids, got shape {tokens.shape}")
             sh = self._send_h.numpy()
-            for r in range(self.world):
-                s, c = shard_range(self.global_batch, self.world, r)
-                sh[r, :c] = tokens[s:s + c]
+            try:
+                tokens = np.asarray(tokens, dtype=np.int32)
+                if tokens.shape != (self.global_batch,):
+                    raise ValueError(f"expected {self.global_batch} token ids, got shape {tokens.shape}")
+                for r in range(self.world):
+                    s, c = shard_range(self.global_batch, self.world, r)
+                    sh[r, :c] = tokens[s:s + c]
+            except Exception as e:  # every rank still steps (on -1 ids) and then raises
+                err = e
+                sh[:] = -1
             self._send.copy_(self._send_h, non_blocking=True)
             scatter_list = list(self._send.unbind(0))
-            gather_list = list(self._recv.unbind(0))
         dist.scatter(self._mine, scatter_list, src=0, group=self.group)
         if self.count:
-            self.step_fn_device(self._mine[: self.count], self._next[: self.count])
-        dist.gather(self._next, gather_list, dst=0, group=self.group)
-        if self.rank != 0:
-            return None
+            try:
+                self.step_fn_device(self._mine[: self.count], self._next[: self.count])
+            except Exception as e:  # reported to every rank below, then raised here
+                err = err or e
+        if err is not None:
+            self._next[w].fill_(1)
+        dist.all_gather(self._recv_list, self._next, group=self.group)
         self._recv_h.copy_(self._recv, non_blocking=True)
         if self.device != "cpu":
             torch.cuda.current_stream().synchronize()
         rh = self._recv_h.numpy()
+        failed = [r for r in range(self.world) if int(rh[r, w]) != 0]
+        if failed:
+            self._next[w].fill_(0)  # re-armed for the next step
+            raise ShardStepError(failed) from err
+        if self.rank != 0:
+            return None
         res = np.empty(self.global_batch, dtype=np.int32)
         for r in range(self.world):
             s, c = shard_range(self.global_batch, self.world, r)

@@ -4,13 +4,16 @@
     torchrun --nproc-per-node N bench.py --gpus N ...      (one process per GPU)
 
 Workload: 24 layers (every 4th GQA), hidden 2048, vocab 151936, random
-Q8_0 weights; per GPU 64 sequences whose bf16 KV cache is prefilled to 8192 tokens and whose
-DeltaNet / conv states are seeded; a step is one greedy decode token for every sequence
-(sequence-sharded across GPUs, no collective on the data path: weak scaling).
+Q8_0 weights; 64 sequences whose bf16 KV cache is prefilled to 8192 tokens and whose
+DeltaNet / conv states are seeded; a step is one greedy decode token for every sequence.
+With N GPUs the 64 sequences are split across them (sequence sharding, no collective on
+the data path: strong scaling, `--weak` runs 64 sequences per GPU instead); at N > 1 the
+line also carries the weak-scaling figure measured in the same run.
 
 Printed (rank 0): one JSON line with the whole-job tok/s measured on device with CUDA events
 (inputs resident, tokens fed back on device), the end-to-end tok/s through the host-buffer
-API, the roofline of the dominant kernel, the CPU baseline and the SM clocks seen.
+API, the roofline of the dominant kernel family with the other two beside it, the CPU
+baseline and the SM clocks seen.
 `--impl reference` times the CPU restatement of the reference decode path (oracle/) on the
 host cores for the same metric.
 """
@@ -129,7 +132,35 @@ def seq_bytes(cfg, ctx_len: int, kv_bytes: int = 2) -> int:
 
 
 def attn_launch_bytes(cfg, B: int, ctx_len: int) -> int:
+    """One flash-decode launch: every sequence's K and V (bf16) read once."""
     return B * cfg["n_kv_heads"] * ctx_len * cfg["head_dim"] * 2 * 2
+
+
+def gemm_shapes(cfg) -> list:
+    """(m, k) of every Q8_0 GEMM launch of one decode step, in launch order."""
+    D, F, V = cfg["dim"], cfg["ffn"], cfg["vocab"]
+    H, hd, Hq, Hkv = cfg["dn_heads"], cfg["head_dim"], cfg["n_heads"], cfg["n_kv_heads"]
+    out = []
+    for dn in cfg["layer_is_dn"]:
+        if dn:
+            out += [(3 * D + D + 2 * H, D), (D, D)]
+        else:
+            out += [(2 * Hq * hd + 2 * Hkv * hd, D), (D, Hq * hd)]
+        out += [(2 * F, D), (D, F)]
+    return out + [(V, D)]
+
+
+def gemm_step_bytes(cfg, B: int) -> int:
+    """Algorithmic bytes of one step's Q8_0 GEMMs: per launch m*k*34/32 of weights, B*k*2 of
+    activations and B*m*4 of outputs (the per-unit figure of the GEMM op benchmark)."""
+    return sum(m * k * 34 // 32 + B * k * 2 + B * m * 4 for m, k in gemm_shapes(cfg))
+
+
+def dn_launch_bytes(cfg, B: int) -> int:
+    """One DeltaNet mixer launch, per sequence: the f32 state read and written (H x 128 x 128),
+    the conv state read and written (3D x K), the projection inputs read and the f16 output."""
+    D, H, K = cfg["dim"], cfg["dn_heads"], cfg["conv_kernel"]
+    return B * (2 * H * 128 * 128 * 4 + 2 * 3 * D * K * 4 + (4 * D + 2 * H) * 4 + D * 2)
 
 
 # --------------------------------------------------------------------------- CPU reference
@@ -189,15 +220,19 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     v = args.steps / dt
     cores = oracle.lib().oracle_max_threads()
-    sample = (f"1 of the {args.batch} sequences, {args.steps} greedy tokens at ctx {args.ctx} "
-              f"(the reference decodes one sequence at a time; {args.batch} sequences = {args.batch} sequential runs)")
+    total = args.batch * args.gpus if args.weak else args.batch
+    per_gpu = args.batch if args.weak else args.batch // max(args.gpus, 1)
+    sample = (f"1 of the {total} sequences, {args.steps} greedy tokens at ctx {args.ctx} "
+              f"(the reference decodes one sequence at a time; {total} sequences = {total} sequential runs)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {args.batch} seq/GPU, ctx {args.ctx} "
-                               f"prefilled bf16 KV", "model": "qwen35-hybrid-2B-shape (random init)",
-                   "global_batch": args.batch * args.gpus, "seq_len": args.ctx,
+        "higher_is_better": True, "scaling": "weak" if args.weak else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {total} sequences "
+                               f"({per_gpu} per GPU), ctx {args.ctx} prefilled bf16 KV",
+                   "model": "qwen35-hybrid-2B-shape (random init)",
+                   "global_batch": total, "seq_len": args.ctx,
                    "parallelism": "host threads; sequences one after another, as the reference decodes"},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -227,24 +262,33 @@ def run_ours(args):
     from ane_infer_b200.shard import ShardedDecoder, max_over_ranks
     shape = synth.shape_2b()
     gguf = synth.build_model_gguf(shape, seed=0)
-    B = args.batch if not args.strong else args.batch // world
+    # strong scaling (default): the --batch sequences split across the ranks; --weak: --batch per rank
+    if args.weak:
+        B = args.batch
+    else:
+        from ane_infer_b200.shard import shard_range
+        B = shard_range(args.batch, world, rank)[1]
+        if args.batch % world:
+            raise SystemExit(f"--batch {args.batch} does not split evenly over {world} GPUs")
+    B_weak = args.batch if (world > 1 and not args.weak) else 0  # the extra weak-scaling figure
     n_e2e = max(2, args.steps // 2)
-    cap = args.ctx + args.warmup * 3 + args.steps * 3 + n_e2e + 16
-    ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap, kv_bf16=True)
-    cfg = ctx.config
-    ctx.seed_state(seed=1 + rank, n_slots=B, n_tokens=args.ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
+    cap = args.ctx + args.warmup * 4 + args.steps * 4 + n_e2e + 16
+    slots = max(B, B_weak)
+    ctx = pkg.DecodeContext(gguf, device=local, max_batch=slots, max_ctx=cap, kv_bf16=True)
+    cfg = dict(ctx.config, layer_is_dn=list(ctx.layer_is_deltanet))
+    ctx.seed_state(seed=1 + rank, n_slots=slots, n_tokens=args.ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
     ctx.step_graph(bool(args.graph))
     # an explicit stream: every kernel of the step and the timing events share it
     stream = torch.cuda.Stream(device=local)
     torch.cuda.set_stream(stream)
-    tok = [torch.from_numpy(synth.seeded_tokens(B, cfg["vocab"], seed=2 + rank)).cuda(),
-           torch.empty(B, dtype=torch.int32, device="cuda")]
-    logits = torch.empty((B, cfg["vocab"]), dtype=torch.float32, device="cuda")
+    tok = [torch.from_numpy(synth.seeded_tokens(slots, cfg["vocab"], seed=2 + rank)).cuda(),
+           torch.empty(slots, dtype=torch.int32, device="cuda")]
+    logits = torch.empty((slots, cfg["vocab"]), dtype=torch.float32, device="cuda")
 
-    def dev_steps(n, i0=0):
+    def dev_steps(n, i0=0, nb=B):
         for i in range(n):
             a, b = tok[(i0 + i) % 2], tok[(i0 + i + 1) % 2]
-            ctx.decode_step_device(a, B, logits, b, stream)
+            ctx.decode_step_device(a, nb, logits, b, stream)
 
     # ---- device-resident timed region
     dev_steps(args.warmup)
@@ -266,21 +310,41 @@ def run_ours(args):
     step_bytes = weight_bytes(cfg) + B * seq_bytes(cfg, int(mean_len))
     peak, peak_kind = measured_peaks()
 
-    # ---- per-kernel device time (CUDA events around each launch on the same stream)
+    # ---- per-kernel device time: CUDA events around each launch on the same stream (a pass
+    # of its own, since events between launches remove the overlap of dependent launches)
     ctx.profile(True)
     prof_pos0 = ctx.get_pos(0)
     dev_steps(args.steps, args.warmup + args.steps)
     torch.cuda.synchronize()
     prof = ctx.profile_read()
     ctx.profile(False)
-    a = prof["attention"]
-    attn_len = prof_pos0 + (args.steps + 1) / 2.0
-    attn_ms = a["ms"] / max(a["launches"], 1)
-    attn_bytes = attn_launch_bytes(cfg, B, int(attn_len))
-    attn_gbs = attn_bytes / (attn_ms / 1e3) / 1e9
-    traffic = None
-    if NCU_TRAFFIC_ATTN_PER_LAUNCH is not None:
-        traffic = NCU_TRAFFIC_ATTN_PER_LAUNCH
+    attn_len = int(prof_pos0 + (args.steps + 1) / 2.0)
+    fam_bytes = {  # algorithmic bytes per step of each kernel family
+        "q8_gemm": gemm_step_bytes(cfg, B),
+        "attention": cfg["n_attn"] * attn_launch_bytes(cfg, B, attn_len),
+        "deltanet": cfg["n_dn"] * dn_launch_bytes(cfg, B),
+    }
+    what = {"q8_gemm": "q8_umma_gemm_kernel (Q8_0 GEMM family on tcgen05: every projection and the lm_head)"
+                       if B >= 9 else "q8_gemm_kernel (Q8_0 GEMV family, mma.sync: every projection and the lm_head)",
+            "attention": "attn_mma_kernel (GQA split-KV flash-decode, bf16 KV via TMA)",
+            "deltanet": "deltanet_persist_kernel (fused conv1d, norms, gated delta rule, gated RMSNorm)"}
+    prof_total = sum(v["ms"] for v in prof.values())
+    kernels = {}
+    for fam, nbytes in fam_bytes.items():
+        f = prof[fam]
+        ms = f["ms"] / args.steps
+        gbs = nbytes / (ms / 1e3) / 1e9 if ms > 0 else 0.0
+        kernels[fam] = {"kernel": what[fam], "bound": "hbm", "achieved": round(gbs, 1), "peak": peak,
+                        "peak_kind": peak_kind, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                        "algorithmic_bytes_per_step": nbytes, "ms_per_step": round(ms, 4),
+                        "launches_per_step": f["launches"] // args.steps,
+                        "avg_launch_ms": round(f["ms"] / max(f["launches"], 1), 5),
+                        "share_of_profiled_step": round(f["ms"] / prof_total, 4) if prof_total else None}
+    kernels["attention"]["traffic"] = NCU_TRAFFIC_ATTN_PER_LAUNCH
+    kernels["attention"]["traffic_unit"] = "bytes per launch"
+    dominant = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
+    roofline = dict(kernels[dominant], family=dominant)
+    roofline.setdefault("traffic", None)
 
     # ---- end to end through the host-buffer API: rank 0 holds every sequence's token id;
     # with N > 1 the ids are scattered to the ranks and the next ids gathered back each step
@@ -307,6 +371,21 @@ def run_ours(args):
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = world * B * n_e2e / e2e_s
 
+    # ---- weak scaling at N > 1: --batch sequences per GPU, the same timing rules
+    weak = None
+    if B_weak:
+        dev_steps(args.warmup, 0, B_weak)
+        barrier()
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
+        dev_steps(args.steps, args.warmup, B_weak)
+        w1.record(stream)
+        barrier()
+        wms = max_over_ranks(w0.elapsed_time(w1))
+        weak = {"value": round(world * B_weak * args.steps / (wms / 1e3), 1), "unit": "tok/s",
+                "seq_per_gpu": B_weak, "global_batch": world * B_weak, "ms_per_step": round(wms / args.steps, 4),
+                "scaling": "weak"}
+
     # ---- CPU baseline (rank 0, N = 1): the oracle on one sequence of the same workload
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -320,21 +399,23 @@ def run_ours(args):
         print(json.dumps({
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
+            "dtype": "f16 MMA operands (q*d rounded once), f32 accumulate, bf16 KV" if B >= 9 else
+                     "exact Q8_0 weights x f16 hi/lo activations, f32 accumulate, bf16 KV",
             "data": "synthetic (seeded random Q8_0 weights, seeded DeltaNet/conv state, N(0,1) bf16 KV)",
-            "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {B} seq/GPU, ctx {args.ctx} "
-                                   f"prefilled bf16 KV", "model": "qwen35-hybrid-2B-shape (random init)",
+            "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {B * world} sequences "
+                                   f"({B} per GPU), ctx {args.ctx} prefilled bf16 KV",
+                       "model": "qwen35-hybrid-2B-shape (random init)",
                        "global_batch": B * world, "seq_len": args.ctx,
                        "parallelism": f"sequence-sharded x{world}, no collective",
                        "step_graph": bool(args.graph),
                        "l2": "inputs larger than L2 (each step reads ~%.1f GB)" % (step_bytes / 1e9)},
             "step_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(step_bytes / (ms_max / args.steps) / 1e6, 1),
                          "frac": round(step_bytes / (ms_max / args.steps) / 1e6 / peak, 4)},
-            "roofline": {"kernel": "attn_mma_kernel (GQA split-KV flash-decode, bf16 KV via TMA)", "bound": "hbm",
-                         "achieved": round(attn_gbs, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(attn_gbs / peak, 4), "traffic": traffic,
-                         "algorithmic_bytes_per_launch": attn_bytes, "avg_launch_ms": round(attn_ms, 5)},
+            "roofline": roofline,
+            "kernels": kernels,
             "kernel_ms_per_step": {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()},
+            "weak_scaling": weak,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B * world,
                     "d2h_bytes_per_step": 4 * B * world,
@@ -488,9 +569,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=64, help="sequences per GPU (weak scaling)")
+    ap.add_argument("--batch", type=int, default=64,
+                    help="sequences in total, split across the GPUs (with --weak: sequences per GPU)")
     ap.add_argument("--ctx", type=int, default=8192)
-    ap.add_argument("--strong", action="store_true", help="split --batch across the GPUs instead")
+    ap.add_argument("--weak", action="store_true", help="run --batch sequences on every GPU (weak scaling)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--graph", type=int, choices=[0, 1], default=1,

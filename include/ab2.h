@@ -179,7 +179,11 @@ int ab2_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16
  * [q | gate] then k then v as the attn_q/attn_k/attn_v projections produce them;
  * caches [B][Hkv][cap][hd] (bf16 bits if kv_bf16 else f32); pos [B] int32 (device) is the
  * position of the new token, which is appended. q_norm/k_norm may be NULL (no norm).
- * RoPE on adjacent pairs of the first rope_dims dims. out [B][Hq*hd] f32. */
+ * RoPE on adjacent pairs of the first rope_dims dims. out [B][Hq*hd] f32.
+ * max_pos (< cap, checked on the host) bounds the positions: the kernels check
+ * 0 <= pos[b] <= max_pos on the device, skip a sequence outside that range (nothing is
+ * appended or read for it, its output is left unwritten) and set bit 8192 of the word
+ * ab2_op_error returns. */
 int ab2_attn_decode(const float* proj, void* k_cache, void* v_cache, int64_t cap, const int32_t* pos, int B,
                     int Hq, int Hkv, int hd, int kv_bf16, const float* q_norm, const float* k_norm,
                     float rope_base, int rope_dims, int max_pos, float* out, void* stream);

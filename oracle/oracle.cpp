@@ -25,7 +25,12 @@
 //   * max_seq_len cap of 4096 (crates/engine/src/model.rs:50) can be lifted to run 8K ctx;
 //   * kv_bf16: round K/V to bf16 when they are appended, modelling the bf16 KV cache that
 //     the B200 backend stores (the reference cache is f32, crates/engine/src/kv_cache.rs:7-40);
-//   * attention op with rotary_dim < head_dim (RoPE on the first rotary_dim dims only).
+//   * attention op with rotary_dim < head_dim (RoPE on the first rotary_dim dims only);
+//   * oracle_q8_gemv_f16: q8_gemv with the operand rounding the B200 backend's batched
+//     tensor-core GEMM declares (every Q8_0 weight q*d rounded once to f16, the input
+//     vector rounded once to f16, products summed in f32). This is NOT the reference's
+//     arithmetic; tests use it to check that the device GEMM computes exactly that
+//     rounding, beside the comparisons with the unrounded reference GEMV.
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -382,10 +387,40 @@ inline float q8_row(const uint8_t* data, const float* x, size_t row, size_t bpr)
     return sum;
 }
 
+// f32 -> f16 -> f32, round to nearest even (overflow to infinity), as the device's
+// __float2half_rn / __hmul2 results
+inline float f16_round(float v) { return (float)(_Float16)v; }
+
+// Set only inside oracle_q8_gemv_f16 (see the header).
+thread_local bool t_f16_operands = false;
+
+// One row with the tensor-core operand rounding: f16(q*d) * f16(x) summed in f32. q*d is exact
+// in f32 (at most 8 + 11 significant bits), so rounding it to f16 gives the correctly rounded
+// f16 product the device's f16 multiply of q and d gives.
+inline float q8_row_f16(const uint8_t* data, const float* xh, size_t row, size_t bpr) {
+    const uint8_t* r = data + row * bpr * 34;
+    float sum = 0.0f;
+    for (size_t b = 0; b < bpr; b++) {
+        const uint8_t* blk = r + b * 34;
+        uint16_t h;
+        std::memcpy(&h, blk, 2);
+        const float scale = f16_to_f32(h);
+        for (int i = 0; i < 32; i++) sum += f16_round((float)(int8_t)blk[2 + i] * scale) * xh[b * 32 + i];
+    }
+    return sum;
+}
+
 // q8_gemv_impl: rows split across threads like rayon's par_iter_mut (q8_gemv.rs:138-148).
 // Every row is a sequential sum, so the result does not depend on the thread count.
 void q8_gemv(const uint8_t* data, size_t m, size_t n, const float* x, float* y) {
     size_t bpr = n / 32;
+    if (t_f16_operands) {
+        std::vector<float> xh(n);
+        for (size_t i = 0; i < n; i++) xh[i] = f16_round(x[i]);
+#pragma omp parallel for schedule(static) if (m * n > 65536)
+        for (long row = 0; row < (long)m; row++) y[row] = q8_row_f16(data, xh.data(), (size_t)row, bpr);
+        return;
+    }
 #pragma omp parallel for schedule(static) if (m * n > 65536)
     for (long row = 0; row < (long)m; row++) y[row] = q8_row(data, x, (size_t)row, bpr);
 }
@@ -797,6 +832,15 @@ OX void oracle_q8_dequant(const uint8_t* blocks, int64_t n_blocks, float* out) {
 OX int oracle_q8_gemv(const uint8_t* blocks, int64_t m, int64_t n, const float* x, float* y) {
     if (n % 32) return fail("n must be divisible by 32");
     q8_gemv(blocks, (size_t)m, (size_t)n, x, y);
+    return 0;
+}
+
+// q8_gemv with the tensor-core operand rounding (f16_operands test mode)
+OX int oracle_q8_gemv_f16(const uint8_t* blocks, int64_t m, int64_t n, const float* x, float* y) {
+    if (n % 32 != 0) return fail("n must be divisible by 32");
+    t_f16_operands = true;
+    q8_gemv(blocks, (size_t)m, (size_t)n, x, y);
+    t_f16_operands = false;
     return 0;
 }
 

@@ -49,6 +49,7 @@ def lib():
         "oracle_q8_dequant": (None, [u8p, i64, f32p]),
         "oracle_q8_gemv": (C.c_int, [u8p, i64, i64, f32p, f32p]),
         "oracle_q8_gemv_scalar": (C.c_int, [u8p, i64, i64, f32p, f32p]),
+        "oracle_q8_gemv_f16": (C.c_int, [u8p, i64, i64, f32p, f32p]),
         "oracle_greedy": (i32, [f32p, i64]),
         "oracle_gated_delta": (None, [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, f32p]),
         "oracle_attn_op": (C.c_int, [f32p, f32p, f32p, f32p, f32p, f32p, i64, i64, i64, i64, i64,
@@ -99,9 +100,11 @@ def q8_dequant(blocks: np.ndarray) -> np.ndarray:
     return out
 
 
-def q8_gemv(blocks: np.ndarray, m: int, n: int, x: np.ndarray, scalar: bool = False) -> np.ndarray:
+def q8_gemv(blocks: np.ndarray, m: int, n: int, x: np.ndarray, scalar: bool = False,
+            f16_operands: bool = False) -> np.ndarray:
+    """y = W x (q8_gemv.rs:130); f16_operands: the tensor-core GEMM's declared rounding instead."""
     y = np.empty(m, dtype=np.float32)
-    fn = lib().oracle_q8_gemv_scalar if scalar else lib().oracle_q8_gemv
+    fn = lib().oracle_q8_gemv_f16 if f16_operands else (lib().oracle_q8_gemv_scalar if scalar else lib().oracle_q8_gemv)
     if fn(np.ascontiguousarray(blocks, dtype=np.uint8), m, n, np.ascontiguousarray(x, dtype=np.float32), y):
         raise RuntimeError(_err())
     return y

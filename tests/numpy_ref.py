@@ -132,9 +132,20 @@ def attn_core(q, gate, k_new, v_new, kc, vc, pos, base, rot, q_norm=None, k_norm
     return out * sigmoid(gate)
 
 
+def f16(a):
+    return np.asarray(a).astype(np.float16).astype(np.float64)
+
+
 class Model:
-    def __init__(self, gguf):
+    """f16_operands: every Q8_0 weight and every GEMM input rounded once to f16 (the batched
+    tensor-core GEMM's declared rounding, a test mode; the default is the reference's f32 path)."""
+
+    def __init__(self, gguf, f16_operands=False):
         _, meta, t = read_gguf(gguf)
+        self.f16 = f16_operands
+        if f16_operands:  # the embedding gather reads exact rows; only GEMM weights are rounded
+            t = {k: (f16(v) if k.endswith(".weight") and v.ndim == 2 and "conv1d" not in k
+                     and k != "token_embd.weight" else v) for k, v in t.items()}
         a = meta["general.architecture"]
         self.t = t
         self.dim = meta[f"{a}.embedding_length"]
@@ -147,7 +158,11 @@ class Model:
         self.eps = meta[f"{a}.attention.layer_norm_rms_epsilon"]
         self.base = meta[f"{a}.rope.freq_base"]
         self.is_dn = [f"blk.{l}.ssm_a" in t for l in range(self.n_layers)]
-        self.lm = t.get("output.weight", t["token_embd.weight"])
+        self.lm = t.get("output.weight", f16(t["token_embd.weight"]) if f16_operands else t["token_embd.weight"])
+
+    def mv(self, w, x):
+        """One Q8_0 GEMV input: W @ x, x rounded to f16 in the f16_operands mode."""
+        return w @ (f16(x) if self.f16 else x)
 
     def new_state(self, cap):
         st = []
@@ -160,34 +175,34 @@ class Model:
 
     def dn_mixer(self, l, x, st):
         t, p, D, H = self.t, f"blk.{l}.", self.dim, self.H
-        qkv = t[p + "attn_qkv.weight"] @ x
+        qkv = self.mv(t[p + "attn_qkv.weight"], x)
         st["conv"] = np.concatenate([st["conv"][:, 1:], qkv[:, None]], axis=1)
         c = silu((st["conv"] * t[p + "ssm_conv1d.weight"]).sum(axis=1))
         q, k, v = c[:D].reshape(H, 128), c[D:2 * D].reshape(H, 128), c[2 * D:].reshape(H, 128)
         q = q / np.sqrt((q * q).sum(1, keepdims=True) + 1e-12) / np.sqrt(128)
         k = k / np.sqrt((k * k).sum(1, keepdims=True) + 1e-12)
-        beta = sigmoid(t[p + "ssm_beta.weight"] @ x)
-        a = t[p + "ssm_alpha.weight"] @ x + t[p + "ssm_dt.bias"]
+        beta = sigmoid(self.mv(t[p + "ssm_beta.weight"], x))
+        a = self.mv(t[p + "ssm_alpha.weight"], x) + t[p + "ssm_dt.bias"]
         decay = np.exp(t[p + "ssm_a"] * np.log1p(np.exp(a)))
         o = np.empty((H, 128))
         for h in range(H):
             o[h], st["S"][h] = gated_delta(st["S"][h], q[h], k[h], v[h], beta[h], decay[h])
-        gate = t[p + "attn_gate.weight"] @ x
+        gate = self.mv(t[p + "attn_gate.weight"], x)
         normed = np.concatenate([rmsnorm(o[h], t[p + "ssm_norm.weight"], self.eps) for h in range(H)])
-        return t[p + "ssm_out.weight"] @ (normed * silu(gate))
+        return self.mv(t[p + "ssm_out.weight"], normed * silu(gate))
 
     def attn_mixer(self, l, x, st, pos):
         t, p, hd = self.t, f"blk.{l}.", self.hd
-        qf = (t[p + "attn_q.weight"] @ x).reshape(self.Hq, 2 * hd)
-        k = (t[p + "attn_k.weight"] @ x).reshape(self.Hkv, hd)
-        v = (t[p + "attn_v.weight"] @ x).reshape(self.Hkv, hd)
+        qf = self.mv(t[p + "attn_q.weight"], x).reshape(self.Hq, 2 * hd)
+        k = self.mv(t[p + "attn_k.weight"], x).reshape(self.Hkv, hd)
+        v = self.mv(t[p + "attn_v.weight"], x).reshape(self.Hkv, hd)
         o = attn_core(qf[:, :hd], qf[:, hd:], k, v, st["k"], st["v"], pos, self.base, hd,
                       t[p + "attn_q_norm.weight"], t[p + "attn_k_norm.weight"])
-        return t[p + "attn_output.weight"] @ o.reshape(-1)
+        return self.mv(t[p + "attn_output.weight"], o.reshape(-1))
 
     def ffn(self, l, x):
         t, p = self.t, f"blk.{l}."
-        return t[p + "ffn_down.weight"] @ (silu(t[p + "ffn_gate.weight"] @ x) * (t[p + "ffn_up.weight"] @ x))
+        return self.mv(t[p + "ffn_down.weight"], silu(self.mv(t[p + "ffn_gate.weight"], x)) * self.mv(t[p + "ffn_up.weight"], x))
 
     def forward(self, st, token, pos):
         t = self.t
@@ -196,4 +211,4 @@ class Model:
             xn = rmsnorm(x, t[f"blk.{l}.attn_norm.weight"], self.eps)
             x = x + (self.dn_mixer(l, xn, st[l]) if self.is_dn[l] else self.attn_mixer(l, xn, st[l], pos))
             x = x + self.ffn(l, rmsnorm(x, t[f"blk.{l}.post_attention_norm.weight"], self.eps))
-        return self.lm @ rmsnorm(x, t["output_norm.weight"], self.eps)
+        return self.mv(self.lm, rmsnorm(x, t["output_norm.weight"], self.eps))

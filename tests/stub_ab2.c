@@ -6,6 +6,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #include "ab2.h"
 
@@ -54,10 +55,13 @@ int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int
     (void)len;
     logf_("create %lld %lld %lld %lld", (long long)device, (long long)max_batch, (long long)max_ctx,
           (long long)(opt ? opt->kv_bf16 : -1));
-    if (getenv("STUB_FAIL_CREATE")) {
+    const char* fail_dev = getenv("STUB_FAIL_CREATE_DEVICE");  /* only this device fails */
+    if (getenv("STUB_FAIL_CREATE") || (fail_dev && atoi(fail_dev) == device)) {
         g_msg = "stub: no CUDA device available";
         return AB2_ERR_DEVICE;
     }
+    const char* slow_dev = getenv("STUB_SLOW_CREATE_DEVICE");  /* this device uploads slowly */
+    if (slow_dev && atoi(slow_dev) == device) usleep(400000);
     if (max_batch < 1 || max_batch > 256) {
         g_msg = "stub: bad max_batch";
         return AB2_ERR_ARG;

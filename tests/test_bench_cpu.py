@@ -47,3 +47,21 @@ def test_roofline_accounting_matches_the_published_formulas(bench, synth):
     # one step at B=64, ctx 8192 (10.88 GB at the bench's mean context of ~8.2K tokens)
     step = bench.weight_bytes(cfg) + 64 * bench.seq_bytes(cfg, 8192)
     assert round(step / 1e9, 2) == 10.87
+
+
+def test_kernel_family_accounting(bench, synth):
+    """The per-family bytes of the `kernels` map: the GEMM family's weights are exactly the
+    step's Q8_0 weight bytes (every projection and the lm_head, in launch order), plus B*k*2 of
+    activations and B*m*4 of outputs per launch; one DeltaNet launch moves ~2.33 MB per
+    sequence (state and conv state read and written, projections in, f16 output out)."""
+    cfg = dict(_cfg_2b(synth))
+    s = synth.shape_2b()
+    cfg["layer_is_dn"] = [not s.layer_is_attn(l) for l in range(s.n_layers)]
+    shapes = bench.gemm_shapes(cfg)
+    assert len(shapes) == 4 * s.n_layers + 1
+    assert sum(m * k * 34 // 32 for m, k in shapes) == bench.weight_bytes(cfg)
+    extra = sum(64 * k * 2 + 64 * m * 4 for m, k in shapes)
+    assert bench.gemm_step_bytes(cfg, 64) == bench.weight_bytes(cfg) + extra
+    per_seq = bench.dn_launch_bytes(cfg, 1)
+    assert per_seq == 2 * 16 * 128 * 128 * 4 + 2 * 3 * 2048 * 4 * 4 + (4 * 2048 + 32) * 4 + 2048 * 2
+    assert round(per_seq / 1e6, 2) == 2.33

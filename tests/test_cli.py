@@ -115,6 +115,32 @@ def test_one_thread_and_context_per_gpu(stub_cli, tmp_path):
     assert out["prompt"] == prompts[1]
 
 
+def test_device_threads_start_together(stub_cli, tmp_path):
+    """The device threads pass a common gate after upload and seeding: no GPU starts decoding
+    while another is still uploading, so the whole-job rate spans first start to last end."""
+    exe, model, _ = stub_cli
+    log = tmp_path / "calls.log"
+    r = run(exe, "-m", model, "--gpus", "3", "-b", "2", "--ctx", "8", "-pp", "2", "-tg", "3",
+            env={"STUB_LOG": str(log), "STUB_SLOW_CREATE_DEVICE": "1"})
+    assert r.returncode == 0, r.stderr
+    calls = read_log(log)
+    kinds = [c[0] for c in calls]
+    last_seed = max(i for i, k in enumerate(kinds) if k == "seed")
+    first_step = min(i for i, k in enumerate(kinds) if k == "step")
+    assert last_seed < first_step, kinds
+
+
+def test_one_failing_device_does_not_hold_the_others(stub_cli, tmp_path):
+    exe, model, _ = stub_cli
+    log = tmp_path / "calls.log"
+    r = run(exe, "-m", model, "--gpus", "3", "-b", "2", "-pp", "2", "-tg", "3",
+            env={"STUB_LOG": str(log), "STUB_FAIL_CREATE_DEVICE": "1"})
+    assert r.returncode == 1
+    assert "GPU 1: ab2_create failed: stub: no CUDA device available" in r.stderr
+    steps = {int(c[5]) for c in read_log(log) if c[0] == "step"}
+    assert steps == {0, 2}  # the other devices ran to the end
+
+
 def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
     exe, model, _ = stub_cli
     firsts = []

@@ -100,6 +100,72 @@ def test_attn_decode_op(pkg, oracle, synth, cuda, B, ctx, hd, rot, kv_bf16, norm
         assert np.array_equal(kg[b][:, :p], kc[b][:, :p])
 
 
+@pytest.mark.parametrize("B,ctx", [(64, 4096), (64, 16384), (64, 32768), (1, 32768)])
+def test_attn_decode_op_config3(pkg, oracle, cuda, B, ctx):
+    """The flash-decode cells of BASELINE config 3 (Hq 8, Hkv 2, hd 256, bf16 KV N(0,1), RoPE
+    theta 1e7 on the first 64 dims, sigmoid gate N(0,1)) at B=64 and ctx 4K/16K/32K and at B=1,
+    ctx 32K. The caches are drawn on the device; sequences 0, B/2 and B-1 (ragged positions)
+    are checked against the oracle with their pre-call caches."""
+    torch = cuda
+    Hq, Hkv, hd, rot = 8, 2, 256, 64
+    cap = ctx + 8
+    g = torch.Generator(device="cuda").manual_seed(ctx + B)
+    proj = torch.randn(B, Hq * 2 * hd + 2 * Hkv * hd, device="cuda", generator=g)
+    kd = torch.randn(B, Hkv, cap, hd, device="cuda", generator=g).to(torch.bfloat16)
+    vd = torch.randn(B, Hkv, cap, hd, device="cuda", generator=g).to(torch.bfloat16)
+    pos = torch.tensor([ctx - 1 - (b % 3) for b in range(B)], dtype=torch.int32, device="cuda")
+    check = sorted({0, B // 2, B - 1})
+    pre = {b: (kd[b].float().cpu().numpy(), vd[b].float().cpu().numpy()) for b in check}
+    out = torch.empty((B, Hq * hd), dtype=torch.float32, device="cuda")
+    pkg.attn_decode(proj, kd, vd, cap, pos, B, Hq, Hkv, hd, True, None, None, 1e7, rot, int(pos.max().item()), out)
+    torch.cuda.synchronize()
+    assert pkg.op_error() == 0
+    og, pj, ph = out.cpu().numpy(), proj.cpu().numpy(), pos.cpu().numpy()
+    for b in check:
+        qf = pj[b, :Hq * 2 * hd].reshape(Hq, 2 * hd)
+        kn_ = pj[b, Hq * 2 * hd: Hq * 2 * hd + Hkv * hd].reshape(Hkv, hd)
+        vn_ = pj[b, Hq * 2 * hd + Hkv * hd:].reshape(Hkv, hd)
+        ref, _, _ = oracle.attn_op(qf[:, :hd], qf[:, hd:], kn_, vn_, pre[b][0], pre[b][1], int(ph[b]), 1e7, rot,
+                                   kv_bf16=True)
+        e = rel_err(og[b].reshape(Hq, hd), ref)
+        print(f"B={B} ctx={ctx} seq {b}: rel err {e:.2e}")
+        assert e < TOL, b
+
+
+@pytest.mark.parametrize("kv_bf16", [True, False])
+def test_attn_decode_rejects_position_above_max_pos(pkg, oracle, synth, cuda, kv_bf16):
+    """ab2_attn_decode's device-side position check: a sequence whose pos[b] is above the
+    declared max_pos (still inside the cache) is skipped, nothing is appended to its cache,
+    and ab2_op_error reports bit 8192; the other sequences are computed as usual."""
+    torch = cuda
+    B, Hq, Hkv, hd, rot, ctx = 3, 8, 2, 256, 64, 200
+    cap = ctx + 64
+    rng = np.random.default_rng(77)
+    proj, kc, vc, _ = attn_case(rng, synth, B, Hq, Hkv, hd, ctx, cap, kv_bf16)
+    max_pos = ctx - 1
+    pos = np.array([ctx - 1, ctx + 20, ctx - 2], dtype=np.int32)  # sequence 1 lies beyond max_pos
+    dt = torch.bfloat16 if kv_bf16 else torch.float32
+    kd, vd = torch.from_numpy(kc).to(dt).cuda(), torch.from_numpy(vc).to(dt).cuda()
+    k_before = kd[1].clone()
+    out = torch.zeros((B, Hq * hd), dtype=torch.float32, device="cuda")
+    assert pkg.op_error() == 0
+    pkg.attn_decode(torch.from_numpy(proj).cuda(), kd, vd, cap, torch.from_numpy(pos).cuda(), B, Hq, Hkv, hd, kv_bf16,
+                    None, None, 1e7, rot, max_pos, out)
+    code = pkg.op_error()
+    assert code & 8192, hex(code)
+    assert torch.equal(kd[1], k_before)  # no append at the rejected position
+    assert float(out[1].abs().max()) == 0.0
+    og = out.cpu().numpy()
+    for b in (0, 2):
+        qf = proj[b, :Hq * 2 * hd].reshape(Hq, 2 * hd)
+        kn_ = proj[b, Hq * 2 * hd: Hq * 2 * hd + Hkv * hd].reshape(Hkv, hd)
+        vn_ = proj[b, Hq * 2 * hd + Hkv * hd:].reshape(Hkv, hd)
+        ref, _, _ = oracle.attn_op(qf[:, :hd], qf[:, hd:], kn_, vn_, kc[b], vc[b], int(pos[b]), 1e7, rot,
+                                   kv_bf16=kv_bf16)
+        assert rel_err(og[b].reshape(Hq, hd), ref) < TOL, b
+    assert pkg.op_error() == 0  # the word was cleared by the read
+
+
 # ---------------------------------------------------------------------------- model layers
 @pytest.fixture(scope="module")
 def tiny_ctx(pkg, tiny_gguf, cuda):

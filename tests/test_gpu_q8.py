@@ -96,6 +96,31 @@ def test_gemv_matches_oracle(pkg, oracle, synth, cuda, m, n, batch):
     assert pkg.op_error() == 0
 
 
+# the tcgen05 path against the oracle's GEMV with the same declared operand rounding (weights
+# q*d and inputs rounded once to f16, f32 sums): only the f32 summation order differs
+TC_DECLARED_TOL = 2e-5
+
+
+@pytest.mark.parametrize("m,n", SHAPES)
+@pytest.mark.parametrize("batch", [9, 32, 64])
+def test_tc_gemm_matches_declared_rounding(pkg, oracle, synth, cuda, m, n, batch):
+    torch = cuda
+    rng = np.random.default_rng(m * 3 + n + batch)
+    blocks = synth.random_q8_0(rng, m, n, std=0.02)
+    w = pkg.Q8Tensor(blocks, m, n)
+    x = rng.normal(0, 1, size=(batch, n)).astype(np.float32)
+    y = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+    pkg.q8_gemv(w, torch.from_numpy(x).cuda(), y, batch)
+    torch.cuda.synchronize()
+    yg = y.cpu().numpy()
+    for b in (0, batch // 2, batch - 1):
+        ref = oracle.q8_gemv(blocks, m, n, x[b], f16_operands=True)
+        exact = oracle.q8_gemv(blocks, m, n, x[b])
+        assert rel_err(yg[b], ref) < TC_DECLARED_TOL, (b, rel_err(yg[b], ref))
+        assert rel_err(yg[b], exact) < TC_TOL, (b, rel_err(yg[b], exact))
+    assert pkg.op_error() == 0
+
+
 @pytest.mark.parametrize("batch", [2, 4, 5, 9, 16, 33, 64])
 def test_gemm_all_batch_modes(pkg, oracle, synth, cuda, batch):
     torch = cuda

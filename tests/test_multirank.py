@@ -116,26 +116,38 @@ def _fail_worker(rank, world, port, result_dir):
                 return good(toks)[:-1]  # wrong shape
             return good(toks)
 
-        dec = ShardedDecoder(flaky, B)
-        toks = np.arange(B, dtype=np.int32) * 5 + 1
-        lines = []
-        for step in range(6):
-            feed = toks if rank == 0 else None
-            if rank == 0 and step == 4:
-                feed = toks[:-1]  # malformed batch on rank 0
-            try:
-                nxt = dec.step(feed)
-                ok = "ok"
-                if rank == 0:
-                    want = ((toks.astype(np.int64) * 31 + 7 + np.arange(B)) % 1000).astype(np.int32)
-                    ok += " 1" if np.array_equal(nxt, want) else " 0"
-                    toks = nxt
-                lines.append(ok)
-            except ShardStepError as e:
-                cause = type(e.__cause__).__name__ if e.__cause__ is not None else "-"
-                lines.append(f"fail {e.failed_ranks} {cause}")
-        with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
-            f.write("\n".join(lines))
+        import torch
+        dev_calls = {"n": 0}
+
+        def flaky_dev(t, n):
+            # the tensor form (DecodeContext.decode_step_device on a GPU box): rank 1's second
+            # step raises after it was handed its ids
+            dev_calls["n"] += 1
+            if rank == 1 and dev_calls["n"] == 2:
+                raise RuntimeError("injected device-step failure")
+            n.copy_(torch.from_numpy(good(t.numpy())))
+
+        for mode in ("host", "device"):
+            dec = ShardedDecoder(flaky, B) if mode == "host" else ShardedDecoder(None, B, step_fn_device=flaky_dev)
+            toks = np.arange(B, dtype=np.int32) * 5 + 1
+            lines = []
+            for step in range(6):
+                feed = toks if rank == 0 else None
+                if rank == 0 and step == 4:
+                    feed = toks[:-1]  # malformed batch on rank 0
+                try:
+                    nxt = dec.step(feed)
+                    ok = "ok"
+                    if rank == 0:
+                        want = ((toks.astype(np.int64) * 31 + 7 + np.arange(B)) % 1000).astype(np.int32)
+                        ok += " 1" if np.array_equal(nxt, want) else " 0"
+                        toks = nxt
+                    lines.append(ok)
+                except ShardStepError as e:
+                    cause = type(e.__cause__).__name__ if e.__cause__ is not None else "-"
+                    lines.append(f"fail {e.failed_ranks} {cause}")
+            with open(os.path.join(result_dir, f"{mode}{rank}.txt"), "w") as f:
+                f.write("\n".join(lines))
     finally:
         dist.destroy_process_group()
 
@@ -146,9 +158,15 @@ def test_sharded_decode_failure_gloo_world2(tmp_path):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     mp.start_processes(_fail_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
-    r0 = (tmp_path / "rank0.txt").read_text().split("\n")
-    r1 = (tmp_path / "rank1.txt").read_text().split("\n")
+    r0 = (tmp_path / "host0.txt").read_text().split("\n")
+    r1 = (tmp_path / "host1.txt").read_text().split("\n")
     # step 1: rank 1's step raises; step 3: rank 0's step returns the wrong shape; step 4:
     # rank 0's batch is malformed, so no rank steps; the steps between and after succeed
     assert r0 == ["ok 1", "fail [1] -", "ok 1", "fail [0] ValueError", "fail [0] ValueError", "ok 1"], r0
     assert r1 == ["ok", "fail [1] RuntimeError", "ok", "fail [0] -", "fail [0] -", "ok"], r1
+    # the device (tensor) form: rank 1's step raises at step 1 and rank 0's batch is malformed
+    # at step 4; every rank raises at the same step instead of waiting out the group timeout
+    d0 = (tmp_path / "device0.txt").read_text().split("\n")
+    d1 = (tmp_path / "device1.txt").read_text().split("\n")
+    assert d0 == ["ok 1", "fail [1] -", "ok 1", "ok 1", "fail [0] ValueError", "ok 1"], d0
+    assert d1 == ["ok", "fail [1] RuntimeError", "ok", "ok", "fail [0] -", "ok"], d1

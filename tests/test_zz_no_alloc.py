@@ -44,6 +44,56 @@ def test_noalloc_matches_q8_gemv_twice(pkg, cuda, m, n, batch):
         row_close(got, ref)
 
 
+def test_noalloc_allocates_nothing(pkg, cuda):
+    """After a device's first call (the one-time address lookup of the fixed array, and the
+    first load of the kernels), a call on a shape never seen before leaves the device's free
+    memory exactly as it was."""
+    torch = cuda
+    rng = np.random.default_rng(11)
+    st = torch.cuda.Stream()
+    warm = pkg.Q8Tensor(blocks_for(rng, 64, 256), 64, 256)
+    xw = torch.zeros((7, 256), dtype=torch.float32, device="cuda")
+    yw = torch.zeros((7, 64), dtype=torch.float32, device="cuda")
+    m, n = 3008, 4096
+    w = pkg.Q8Tensor(blocks_for(rng, m, n), m, n)
+    x = torch.from_numpy(rng.normal(size=(7, n)).astype(np.float32)).cuda()
+    y = torch.empty((7, m), dtype=torch.float32, device="cuda")
+    pkg.q8_gemv_noalloc(warm, xw, yw, 7, st)
+    st.synchronize()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    pkg.q8_gemv_noalloc(w, x, y, 7, st)
+    st.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, (free0, free1)
+    ref = torch.empty_like(y)
+    pkg.q8_gemv(w, x, ref, 7, st)
+    st.synchronize()
+    row_close(y.cpu().numpy(), ref.cpu().numpy().astype(np.float64))
+
+
+def test_noalloc_keeps_the_callers_device(pkg, cuda):
+    """A call for a tensor on device 0 from a thread whose current device is 1 leaves the
+    thread's current device at 1."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    rng = np.random.default_rng(12)
+    w = pkg.Q8Tensor(blocks_for(rng, 256, 512), 256, 512)  # device 0
+    x = torch.zeros((2, 512), dtype=torch.float32, device="cuda:0")
+    y = torch.zeros((2, 256), dtype=torch.float32, device="cuda:0")
+    prev = torch.cuda.current_device()
+    try:
+        torch.cuda.set_device(1)
+        pkg.q8_gemv_noalloc(w, x, y, 2)
+        assert torch.cuda.current_device() == 1
+        pkg.q8_gemv(w, x, y, 2)
+        assert torch.cuda.current_device() == 1
+    finally:
+        torch.cuda.set_device(prev)
+    torch.cuda.synchronize(0)
+
+
 def test_noalloc_rejects_what_does_not_fit(pkg, cuda):
     torch = cuda
     rng = np.random.default_rng(3)
