@@ -77,8 +77,18 @@ void launch_q8p_dequant(const Q8Weight& w, int64_t rows, float* out, cudaStream_
 void launch_embed(const Q8Weight& w, int vocab, const int32_t* tokens, int batch, float* x, int ldx, cudaStream_t st);
 
 // q8_umma.cu
-// K splits of the tcgen05 GEMM; with more than one split the epilogue adds into y
-// (red.add), so a STORE-mode output must be zeroed first. SwiGLU is never split.
+// How the tcgen05 GEMM cuts a weight into work units: main_units units (row-tile pair, K
+// split) over the first pairs - tail_pairs pairs with ks splits each, then the last
+// tail_pairs pairs cut into ks_tail K pieces each. A launch with more whole-pair units than
+// CTAs would otherwise leave its last round to a few CTAs (the 2B lm_head: 594 pairs on 148
+// SMs); those last pairs are split instead. A unit of a split pair adds its partial sums into
+// y, so for a STORE the output rows from zero_row0 on must start at zero (zero_row0 = M: none).
+struct UmmaPlan {
+    int pairs = 0, ks = 1, kper = 0, main_units = 0, tail_pairs = 0, ks_tail = 1, kper_tail = 0, units = 0;
+    int64_t zero_row0 = 0;
+};
+UmmaPlan umma_plan(int MT, int KT, int64_t M, int num_sms);
+// K splits of the main units
 int umma_nsplit(int MT, int KT, int mode, int num_sms);
 void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
                        int64_t stride, cudaStream_t st);

@@ -30,8 +30,11 @@ __global__ void __launch_bounds__(256) rmsnorm_act_kernel(const float* __restric
             }
         }
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    // The GEMM that follows may start (and stream its constant weights into shared memory on
+    // the SMs the previous GEMM leaves idle) while this kernel still waits for its own input:
+    // its activation loads wait for this grid to complete.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const float* xb = x + (size_t)b * ldx;
     if (!fast) {
         if (zero_ptr)
@@ -56,7 +59,7 @@ __global__ void __launch_bounds__(256) rmsnorm_act_kernel(const float* __restric
     // a K-split GEMM that follows adds into these projection rows: clear them
     if (zero_ptr) {
         float* zr = zero_ptr + (size_t)b * zero_ld;
-        if ((zero_n & 3) == 0 && (zero_ld & 3) == 0) {
+        if ((zero_n & 3) == 0 && (zero_ld & 3) == 0 && (reinterpret_cast<uintptr_t>(zero_ptr) & 15) == 0) {
             for (int i = tid * 4; i < zero_n; i += 256 * 4) *reinterpret_cast<float4*>(zr + i) = make_float4(0.f, 0.f, 0.f, 0.f);
         } else {
             for (int i = tid; i < zero_n; i += 256) zr[i] = 0.0f;

@@ -115,14 +115,28 @@ static_assert(kXTileBytes % 1024 == 0 && UmmaSmem::x_base() % 1024 == 0, "operan
 // the last unit's accumulator is staged over the raw weight ring, idle by then
 static_assert(kBatchRows * kStageLd * 4 <= UmmaSmem::x_base(), "the staged accumulator fits in the weight ring");
 
-// Unit u = (row tile u / KS, K split u % KS) covers the len K tiles from k0. A CTA takes
-// units blockIdx.x, blockIdx.x + G, ...; every role walks them with plain nested loops
-// (pipeline stages and activation groups never span two units), because per-tile
-// bookkeeping in the issuing threads sits directly on the pipeline's critical path.
-__device__ __forceinline__ void unit_range(int u, int KS, int kper, int KT, int& mt, int& k0, int& len) {
-    mt = u / KS;
-    k0 = (u % KS) * kper;
-    len = min(KT, k0 + kper) - k0;
+// Unit u covers the len K tiles from k0 of row-tile pair mt: a main unit (pair u / ks, K split
+// u % ks) or, from main_units on, a K piece of one of the tail pairs. A CTA takes units
+// blockIdx.x, blockIdx.x + G, ...; every role walks them with plain nested loops (pipeline
+// stages and activation groups never span two units), because per-tile bookkeeping in the
+// issuing threads sits directly on the pipeline's critical path. `split`: other units cover
+// the same pair, so this one adds its partial sums into the output.
+struct UnitPlan {
+    int KT, ks, kper, main_units, first_tail, ks_tail, kper_tail, units;
+};
+__device__ __forceinline__ void unit_range(int u, const UnitPlan& P, int& mt, int& k0, int& len, bool& split) {
+    if (u < P.main_units) {
+        mt = u / P.ks;
+        k0 = (u % P.ks) * P.kper;
+        len = min(P.KT, k0 + P.kper) - k0;
+        split = P.ks > 1;
+    } else {
+        const int t = u - P.main_units;
+        mt = P.first_tail + t / P.ks_tail;
+        k0 = (t % P.ks_tail) * P.kper_tail;
+        len = min(P.KT, k0 + P.kper_tail) - k0;
+        split = true;
+    }
 }
 
 // 32 lanes x 32 columns of f32 from TMEM (this warp's lane quarter)
@@ -223,7 +237,7 @@ __device__ __forceinline__ void glu_store(uint8_t* tile, int n, int j, const Glu
 }
 
 __global__ void __launch_bounds__(kUmmaThreads, 1)
-    q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, int MP, int KT, int KS, const uint8_t* __restrict__ x16,
+    q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, UnitPlan P, const uint8_t* __restrict__ x16,
                         const float* __restrict__ h2, int h2_ld, int batch, unsigned* __restrict__ err, GemmEpi ep) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -240,8 +254,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     __shared__ int s_abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = gridDim.x, U = MP * KS;  // MP row-tile pairs
-    const int kper = (KT + KS - 1) / KS;
+    const int G = gridDim.x, U = P.units, KT = P.KT;
 
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -279,7 +292,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             bool ok = true;
             for (int u = blockIdx.x; u < U && ok; u += G) {
                 int mt, k0, len;
-                unit_range(u, KS, kper, KT, mt, k0, len);
+                bool split;
+                unit_range(u, P, mt, k0, len, split);
                 const uint8_t* src = wt + ((size_t)mt * KT + k0) * kWStageBytes;  // the unit's blocks are contiguous
                 for (int q = 0; q < len; q++, st++) {
                     const int s = st % kWStages;
@@ -309,7 +323,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             bool ok = true;
             for (int u = blockIdx.x; u < U && ok; u += G) {
                 int mt, k0, len;
-                unit_range(u, KS, kper, KT, mt, k0, len);
+                bool split;
+                unit_range(u, P, mt, k0, len, split);
                 for (int q = 0; q < len; q += kAGroup, g++) {
                     const int s = g % kXStages;
                     if (g >= kXStages && !mbar_wait(&x_free[s], ((g / kXStages) - 1) & 1)) {
@@ -336,7 +351,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             bool ok = true;
             for (int u = blockIdx.x; u < U && ok; u += G, j++) {
                 int mt, k0, len;
-                unit_range(u, KS, kper, KT, mt, k0, len);
+                bool split;
+                unit_range(u, P, mt, k0, len, split);
                 if (j >= 2) {
                     if (!mbar_wait(&acc_free[j & 1], ((j >> 1) - 1) & 1)) {
                         atomicOr(err, 16u);
@@ -392,7 +408,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
         bool ok = true;
         for (int u = blockIdx.x; u < U && ok; u += G) {
           int mt, k0, len;
-          unit_range(u, KS, kper, KT, mt, k0, len);
+          bool split;
+          unit_range(u, P, mt, k0, len, split);
           for (int q = 0; q < len; q++, st++) {
             const int sw = st % kWStages, so = st % kOpStages;
             // warp-uniform outcome: tcgen05.st below is a whole-warp instruction
@@ -441,18 +458,20 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + kEpiWarps) {
         // ---------------- epilogue warps: TMEM lanes 32q .. 32q+31 = weight rows of each tile
         const int q = warp & 3;
-        const int how = (KS > 1 || ep.mode == EPI_ADD) ? 2 : (ep.mode == EPI_RESID ? 1 : 0);
         const int et = threadIdx.x - kWarpEpi0 * 32;  // 0..127
         pdl_wait();  // outputs may be read or written by earlier kernels of the stream
         int gx = 0;  // SwiGLU source: activation tiles produced so far
         for (int j = 0, u = blockIdx.x; u < U; j++, u += G) {
             bool fail = false;
+            int mt, k0, len;
+            bool split;
+            unit_range(u, P, mt, k0, len, split);
+            // 2: add into y (split units, EPI_ADD), 1: y += Wx (RESID), 0: y = Wx
+            const int how = (split || ep.mode == EPI_ADD) ? 2 : (ep.mode == EPI_RESID ? 1 : 0);
             if (h2) {
                 // this unit's activation tiles from the gate/up sums: thread et takes the
                 // 16-byte chunk jn = et % 8 (8 K) of rows et / 8 + 16 i, i = 0..3, as two loads
                 // of two rows, each issued half a tile ahead of its use
-                int mt, k0, len;
-                unit_range(u, KS, (KT + KS - 1) / KS, KT, mt, k0, len);
                 const int jn = et & 7, n0 = et >> 3;
                 GluLoad ra, rb;
                 glu_load(h2, h2_ld, batch, k0, n0, jn, ra);
@@ -482,7 +501,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             if (epi_bar_or(fail || *(volatile int*)&s_abort)) break;
             tc_fence_after();
             const uint32_t dq = tmem + ((uint32_t)(q * 32) << 16) + kAccCol0 + (uint32_t)((j & 1) * kPairRows / 2);
-            const int pr = u / KS;  // row-tile pair: rows pr*256 .. pr*256+255
+            const int pr = mt;  // row-tile pair: rows pr*256 .. pr*256+255
             if (u + G < U) {
                 // more units follow: write straight from TMEM, lanes on consecutive rows m
 #pragma unroll 1
@@ -537,7 +556,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                             bulk_reduce_add_f32(dst, stage + rr * kStageLd, (uint32_t)valid * 4);
                     }
                     bulk_commit();
-                    bulk_wait_all();
+                    // the CTA may leave once the staged rows have been read out; the writes
+                    // themselves complete with the grid, before any dependent grid reads them
+                    bulk_wait_read();
                 }
                 continue;
             }
@@ -581,6 +602,30 @@ int umma_nsplit(int MT, int KT, int mode, int num_sms) {
     return (KT + per - 1) / per;
 }
 
+// The unit plan of a weight with MT row tiles and KT K tiles on num_sms SMs. Layer weights
+// (fewer pairs than SMs) are K-split so the units cover the SMs about once. A weight with more
+// pairs than SMs runs whole pairs, several rounds per CTA; when the last round would hold only
+// a few pairs (at most a quarter of the SMs), those pairs are cut into K pieces of at least
+// two tiles spread over as many CTAs, so no CTA runs a whole extra pair at the end.
+UmmaPlan umma_plan(int MT, int KT, int64_t M, int num_sms) {
+    UmmaPlan p;
+    p.pairs = (MT + 1) / 2;
+    p.ks = umma_nsplit(MT, KT, EPI_STORE, num_sms);
+    p.kper = (KT + p.ks - 1) / p.ks;
+    const int rem = p.ks == 1 && p.pairs > num_sms ? p.pairs % num_sms : 0;
+    if (rem > 0 && rem * 4 <= num_sms && KT >= 4) {
+        p.tail_pairs = rem;
+        const int want = std::min(num_sms / rem, KT / 2);
+        p.kper_tail = (KT + want - 1) / want;
+        p.ks_tail = (KT + p.kper_tail - 1) / p.kper_tail;
+    }
+    p.main_units = (p.pairs - p.tail_pairs) * p.ks;
+    p.units = p.main_units + p.tail_pairs * p.ks_tail;
+    p.zero_row0 = p.ks > 1 ? 0 : (p.tail_pairs ? (int64_t)(p.pairs - p.tail_pairs) * kPairRows : M);
+    if (p.zero_row0 > M) p.zero_row0 = M;
+    return p;
+}
+
 int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
                    cudaStream_t st, const float* h2, int h2_ld) {
     const int smem = UmmaSmem::bytes() + 1024;
@@ -594,14 +639,21 @@ int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* e
         attr_set[dev & 63] = true;
     }
     if (ep.mode == EPI_SWIGLU) return -3;  // SwiGLU: EPI_ADD into h2, then a launch with the h2 source
-    const int KS = umma_nsplit(w.MT, w.KT, ep.mode, num_sms);
-    const int pairs = (w.MT + 1) / 2;
-    const int U = pairs * KS;
-    const int G = std::min(U, num_sms);
+    const UmmaPlan pl = umma_plan(w.MT, w.KT, w.M, num_sms);
+    UnitPlan P;
+    P.KT = w.KT;
+    P.ks = pl.ks;
+    P.kper = pl.kper;
+    P.main_units = pl.main_units;
+    P.first_tail = pl.pairs - pl.tail_pairs;
+    P.ks_tail = pl.ks_tail;
+    P.kper_tail = pl.kper_tail;
+    P.units = pl.units;
+    const int G = std::min(pl.units, num_sms);
     // the SwiGLU source reads whole 64-column gate/up groups of h2 (K = ffn a multiple of 64)
     if (h2 && (w.KB % 2 != 0 || h2_ld < 2 * 32 * w.KB || (h2_ld & 3) != 0)) return -1;
-    if (launch_pdl(q8_umma_gemm_kernel, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, pairs, w.KT, KS, x16, h2, h2_ld,
-                   batch, err, ep) != cudaSuccess)
+    if (launch_pdl(q8_umma_gemm_kernel, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, P, x16, h2, h2_ld, batch, err,
+                   ep) != cudaSuccess)
         return -2;
     return 0;
 }

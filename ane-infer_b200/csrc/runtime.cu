@@ -947,11 +947,11 @@ int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float*
         const Layer& L = x->layers[li];
         const Q8Weight* next = li + 1 < x->layers.size() ? &x->layers[li + 1].w_in : &x->lm_head;
         {
-            // a K-split tcgen05 GEMM adds into its STORE output: clear the projection rows
-            const bool zero = umma_for(x, B) && umma_nsplit(L.w_in.MT, L.w_in.KT, EPI_STORE, x->num_sms) > 1;
+            // units of a split pair add into the STORE output: clear those projection rows
+            const int64_t z0 = umma_for(x, B) ? umma_plan(L.w_in.MT, L.w_in.KT, L.w_in.M, x->num_sms).zero_row0 : L.w_in.M;
             ProfScope ps(x, PC_OTHER, st);
-            launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st, zero ? x->proj : nullptr, x->ldp,
-                               (int)L.w_in.M);
+            launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st, z0 < L.w_in.M ? x->proj + z0 : nullptr,
+                               x->ldp, (int)(L.w_in.M - z0));
         }
         RET(run_mixer(x, L, 0, B, max_len, x->x, D, EPI_RESID, st));
         {
@@ -963,11 +963,13 @@ int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float*
         RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next));
     }
     {
-        // a K-split lm_head adds into the logits (small vocabularies): clear them first
-        const bool zero = umma_for(x, B) && umma_nsplit(x->lm_head.MT, x->lm_head.KT, EPI_STORE, x->num_sms) > 1;
+        // the lm_head's split units (all of them for small vocabularies, the K pieces of its
+        // last pairs for large ones) add into the logits: clear those columns first
+        const int64_t V = c.vocab;
+        const int64_t z0 = umma_for(x, B) ? umma_plan(x->lm_head.MT, x->lm_head.KT, V, x->num_sms).zero_row0 : V;
         ProfScope ps(x, PC_OTHER, st);
-        launch_rmsnorm_act(x->x, D, x->final_norm, D, c.eps, B, xa, st, zero ? logits_d : nullptr, (int)c.vocab,
-                           (int)c.vocab);
+        launch_rmsnorm_act(x->x, D, x->final_norm, D, c.eps, B, xa, st, z0 < V ? logits_d + z0 : nullptr, (int)V,
+                           (int)(V - z0));
     }
     RET(gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st));
     {
@@ -1565,8 +1567,10 @@ AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* 
     launch_to_act(xin, (int)w->n, (int)w->n, batch, in, st);
     const GemmEpi ep = epi_store(y, (int)w->w.M, w->w.M);
     if (tc) {
-        if (umma_nsplit(w->w.MT, w->w.KT, EPI_STORE, w->num_sms) > 1)
-            CK(cudaMemsetAsync(y, 0, (size_t)batch * w->w.M * 4, st));
+        // units of a split pair add into y: clear the rows they cover
+        const int64_t z0 = umma_plan(w->w.MT, w->w.KT, w->w.M, w->num_sms).zero_row0;
+        if (z0 < w->w.M)
+            CK(cudaMemset2DAsync(y + z0, (size_t)w->w.M * 4, 0, (size_t)(w->w.M - z0) * 4, batch, st));
         if (launch_q8_umma(w->w, oc.xf, batch, oc.err, ep, w->num_sms, st))
             return seterr(AB2_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     } else {

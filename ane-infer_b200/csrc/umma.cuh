@@ -102,7 +102,10 @@ __device__ __forceinline__ void prefetch_share_l2(const void* src, int64_t bytes
 
 // shared -> global bulk operations of the calling thread's bulk async-group (addresses 16-byte
 // aligned, size a multiple of 16): a plain copy, or an f32 add into global memory performed
-// at L2; bulk_commit closes the group and bulk_wait_all waits until its writes are complete
+// at L2; bulk_commit closes the group; bulk_wait_all waits until its writes are complete, and
+// bulk_wait_read only until its shared-memory sources have been read (then the staging buffer
+// may be reused or the CTA may exit; the writes are visible to dependent grids once this grid
+// has completed)
 __device__ __forceinline__ void bulk_s2g(void* dst_gmem, const void* src_smem, uint32_t bytes) {
     asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem), "r"(smem_u32(src_smem)),
                  "r"(bytes)
@@ -115,6 +118,7 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* dst_gmem, const float
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
