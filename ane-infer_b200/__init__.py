@@ -74,6 +74,7 @@ SIGNATURES = {
     "ab2_decode_step_device": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp, _vp]),
     "ab2_sync": (C.c_int, [_vp]),
     "ab2_op_error": (C.c_int, [C.POINTER(C.c_uint32)]),
+    "ab2_debug_arm_wait_timeout": (C.c_int, [C.c_int, C.c_int, C.c_uint32]),
     "ab2_launches_per_step": (C.c_int, [_vp, C.c_int, C.POINTER(_i64)]),
     "ab2_profile": (C.c_int, [_vp, C.c_int]),
     "ab2_profile_read": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(_i64)]),
@@ -318,6 +319,18 @@ def op_error() -> int:
     v = C.c_uint32()
     _check(load_library().ab2_op_error(C.byref(v)))
     return v.value
+
+
+# kernel families for debug_arm_wait_timeout
+WAIT_TEST_GEMM, WAIT_TEST_ATTENTION, WAIT_TEST_DELTANET = 1, 2, 3
+
+
+def debug_arm_wait_timeout(which: int, copy_index: int, wait_ns: int):
+    """Test hook: the next launch of kernel family `which` (not under stream capture) leaves
+    its asynchronous copy number `copy_index` (per CTA) unissued and bounds its waits at
+    `wait_ns`, so those waits expire and the kernel reports its error bit and returns.
+    wait_ns=0 disarms."""
+    _check(load_library().ab2_debug_arm_wait_timeout(int(which), int(copy_index), int(wait_ns)))
 
 
 def q8_dequant(blocks, n_blocks: int, out, stream=None):

@@ -208,6 +208,20 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(AttnParams p) {
 }
 
 __device__ __forceinline__ void comp_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kCompWarps * 32) : "memory"); }
+// comp_bar that also returns the OR of `v` over the compute threads: a wait outcome that every
+// compute thread then acts on alike, so none of them is left at a later barrier alone
+__device__ __forceinline__ bool comp_bar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.or.pred p, 1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kCompWarps * 32)
+        : "memory");
+    return r != 0;
+}
 
 // Persistent kernel: CTA c takes items c, c + gridDim.x, ...; the producer warp streams the
 // tiles of all of them through one ring, so the pipeline does not drain between items, and
@@ -236,6 +250,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr uint32_t kStageTx = 2u * L::kTileBytes;
+    const uint32_t WL = p.wt.wait_ns;  // the limit of every wait below
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kAttnStages; s++) {
@@ -263,7 +278,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                 if (!attn_item(p, item, pairs, it)) continue;
                 const int pair = it.b * p.Hkv + it.kvh;
                 const int qs = k & 1;
-                if (k >= 2 && !mbar_wait(&q_free[qs], ((k >> 1) - 1) & 1)) {
+                if (k >= 2 && !mbar_wait(&q_free[qs], ((k >> 1) - 1) & 1, WL)) {
                     ok = false;
                     break;
                 }
@@ -273,10 +288,11 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                 const int rows0 = (int)(row_base + (int64_t)pair * p.cap + it.t0);
                 for (int t = 0; t < it.ntiles; t++, i++) {
                     const int s = i % kAttnStages;
-                    if (i >= kAttnStages && !mbar_wait(&empty[s], ((i / kAttnStages) - 1) & 1)) {
+                    if (i >= kAttnStages && !mbar_wait(&empty[s], ((i / kAttnStages) - 1) & 1, WL)) {
                         ok = false;
                         break;
                     }
+                    if (i == p.wt.withhold) continue;  // test hook: this tile is never copied
                     mbar_arrive_expect_tx(&full[s], kStageTx);
 #pragma unroll
                     for (int d = 0; d < NDB; d++) {
@@ -290,8 +306,9 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             // weights into L2 for the GEMM that follows
             prefetch_share_l2(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
             // every issued copy lands before the CTA can exit
-            for (int j = max(0, i - kAttnStages); j < i; j++) mbar_wait(&full[j % kAttnStages], (j / kAttnStages) & 1);
-            for (int j = max(0, k - 2); j < k; j++) mbar_wait(&q_full[j & 1], (j >> 1) & 1);
+            for (int j = max(0, i - kAttnStages); j < i; j++)
+                if (j != p.wt.withhold) mbar_wait(&full[j % kAttnStages], (j / kAttnStages) & 1, WL);
+            for (int j = max(0, k - 2); j < k; j++) mbar_wait(&q_full[j & 1], (j >> 1) & 1, WL);
         }
         __syncwarp();
         return;
@@ -314,11 +331,11 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
         const float* proj = p.proj + (size_t)b * p.ldp;
 
         // Q A-fragments for every k16 step: a0 = (row g, k 2t..2t+1), a2 = (row g, k 2t+8..+9)
+        // A wait that times out is not acted on alone: the outcome is combined over the compute
+        // threads at the tile's first barrier (below), and all of them stop there together.
+        // Until then a thread whose wait timed out reads stale (in-bounds) shared memory.
         const int qs = k & 1;
-        if (!mbar_wait(&q_full[qs], (k >> 1) & 1)) {
-            if (ct == 0 && p.err) atomicOr(p.err, 4096u);
-            break;
-        }
+        const bool q_ok = mbar_wait(&q_full[qs], (k >> 1) & 1, WL);
         const float* q_s = reinterpret_cast<const float*>(smem + L::q_off(qs));
         uint32_t qa0[HD / 16], qa2[HD / 16];
 #pragma unroll
@@ -342,10 +359,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
         bool ok = true;
         for (int tt0 = 0; tt0 < it.ntiles; tt0++, i++) {
             const int s = i % kAttnStages;
-            if (!mbar_wait(&full[s], (i / kAttnStages) & 1)) {
-                ok = false;
-                break;
-            }
+            const bool w_ok = mbar_wait(&full[s], (i / kAttnStages) & 1, WL);
             const uint32_t kb = smem_u32(smem + L::k_off(s)), vb = smem_u32(smem + L::v_off(s));
             const int tbase = it.t0 + tt0 * kT;
             // S = Q K^T for tokens [16w, 16w+16) of the tile
@@ -371,7 +385,10 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                     S_s[g * kT + tt + 1] = (tbase + tt + 1 < it.t1) ? s1 / sq : -INFINITY;
                 }
             }
-            comp_bar();
+            if (comp_bar_or(!(q_ok && w_ok))) {
+                ok = false;
+                break;
+            }
             // online softmax for head `warp` over the tile's 64 tokens
             {
                 const float v0 = S_s[warp * kT + lane], v1 = S_s[warp * kT + lane + 32];
@@ -621,9 +638,11 @@ static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, i
     const int grid = std::min(n_items, num_sms);
     if (launch_pdl(attn_prep_kernel<HD>, dim3(p.Hkv, batch), dim3(128), 0, st, p) != cudaSuccess) return -2;
     if (core_begin) cudaEventRecord(core_begin, st);
+    AttnParams pm = p;
+    pm.wt = take_wait_test(kWaitTestAttention, st);
     if (launch_pdl(attn_mma_kernel<HD>, dim3(grid), dim3(kAttnMmaThreads), smem, st,
-                   *reinterpret_cast<const CUtensorMap*>(tmk), *reinterpret_cast<const CUtensorMap*>(tmv), p, row_base,
-                   pairs, n_items) != cudaSuccess)
+                   *reinterpret_cast<const CUtensorMap*>(tmk), *reinterpret_cast<const CUtensorMap*>(tmv), pm,
+                   row_base, pairs, n_items) != cudaSuccess)
         return -2;
     if (core_end) cudaEventRecord(core_end, st);
     if (splits > 1) launch_pdl(attn_merge_kernel<HD>, dim3(p.Hkv, batch), dim3(256), 0, st, p);

@@ -264,7 +264,8 @@ __global__ void __launch_bounds__(kDnPersistThreads, 1) deltanet_persist_kernel(
                 prep_load_const(p, j + 1, pt, nxt);
                 prep_load_proj(p, j + 1, pt, nxt);
             }
-            if (j >= kPrepSlots && !mbar_wait(&prep_free[s], ((j / kPrepSlots) - 1) & 1)) s_prep_abort = 1;
+            if (j >= kPrepSlots && !mbar_wait(&prep_free[s], ((j / kPrepSlots) - 1) & 1, p.wt.wait_ns))
+                s_prep_abort = 1;
             asm volatile("bar.sync %0, %1;" ::"n"(kPrepBar), "n"(kPrepThreads) : "memory");
             if (s_prep_abort) break;
             prep_compute(p, j, pt, cur, prep[s]);
@@ -295,7 +296,9 @@ __global__ void __launch_bounds__(kDnPersistThreads, 1) deltanet_persist_kernel(
     }
 
     // ---------------- update warps
+    const uint32_t WL = p.wt.wait_ns;  // the limit of every wait below
     auto load = [&](int j) {  // thread 0
+        if (j == p.wt.withhold) return;  // test hook: this state copy is never issued
         const int s = j % kDnSlots;
         float* dst = slots + (size_t)s * DK * DK;
         const float* src = state_of(j);
@@ -319,8 +322,8 @@ __global__ void __launch_bounds__(kDnPersistThreads, 1) deltanet_persist_kernel(
         const float* Ss = slots + (size_t)(j % kDnSlots) * DK * DK;
         // every thread observes the copy's and the prep slot's completion itself, so the bytes
         // it reads are the ones the bulk copy and the prep warps wrote
-        if (!mbar_wait(&full[j % kDnSlots], (j / kDnSlots) & 1)) s_abort = 1 + j;
-        if (!mbar_wait(&prep_full[ps], (j / kPrepSlots) & 1)) s_abort = 1 + j;
+        if (!mbar_wait(&full[j % kDnSlots], (j / kDnSlots) & 1, WL)) s_abort = 1 + j;
+        if (!mbar_wait(&prep_full[ps], (j / kPrepSlots) & 1, WL)) s_abort = 1 + j;
         asm volatile("bar.sync %0, %1;" ::"n"(kUpdBar), "n"(kUpdThreads) : "memory");
         if (s_abort) break;
         const PrepSlot& in = prep[ps];
@@ -400,7 +403,8 @@ __global__ void __launch_bounds__(kDnPersistThreads, 1) deltanet_persist_kernel(
         // a copy or a prep slot did not arrive in time: report it, then give the copies still in
         // flight into the state slots a bounded time to land before shared memory is released
         if (p.err) atomicOr(p.err, 1024u);
-        for (int k = s_abort - 1; k < issued; k++) mbar_wait(&full[k % kDnSlots], (k / kDnSlots) & 1);
+        for (int k = s_abort - 1; k < issued; k++)
+            if (k != p.wt.withhold) mbar_wait(&full[k % kDnSlots], (k / kDnSlots) & 1, WL);
     }
 }
 
@@ -416,7 +420,9 @@ void launch_deltanet(const DnParams& p, int batch, cudaStream_t st) {
     int nsm = 148;
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
     const int n_items = p.H * batch;
-    launch_pdl(deltanet_persist_kernel, dim3(std::min(n_items, nsm)), dim3(kDnPersistThreads), smem, st, p, n_items);
+    DnParams q = p;
+    q.wt = take_wait_test(kWaitTestDeltaNet, st);
+    launch_pdl(deltanet_persist_kernel, dim3(std::min(n_items, nsm)), dim3(kDnPersistThreads), smem, st, q, n_items);
 }
 
 void launch_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,

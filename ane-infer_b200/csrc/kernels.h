@@ -25,6 +25,20 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// The bounded waits of the pipelined kernels (tcgen05 GEMM, tensor-core attention, DeltaNet):
+// each mbarrier wait gives up after wait_ns (2 s) and the kernel reports an error bit, drains
+// its copies in flight and returns. A test can arm one launch to withhold its asynchronous
+// copy number `withhold` (counted per CTA) with a short wait_ns, so that those waits expire
+// without any fault (ab2_debug_arm_wait_timeout); otherwise nothing is withheld.
+struct WaitTest {
+    uint32_t wait_ns = 2000000000u;
+    int withhold = -1;
+};
+enum { kWaitTestGemm = 1, kWaitTestAttention = 2, kWaitTestDeltaNet = 3 };
+// the armed setting for the next launch of kernel family `which` on a stream that is not
+// capturing (then disarmed), else the production setting
+WaitTest take_wait_test(int which, cudaStream_t st);
+
 // A Q8_0 weight on the device, in one or both packed layouts:
 //   q8p (qs, d): mma.sync fragment order, used for batches <= 8 (exact weights);
 //   q8u (qt):    128-row x 64-column tiles for the tcgen05 GEMM, used for larger batches:
@@ -59,6 +73,7 @@ struct GemmEpi {
     ActOut out{};        // SWIGLU: activations of the next GEMM
     const void* pf = nullptr;  // optional: the next GEMM's weights, prefetched into L2 by this launch
     int64_t pf_bytes = 0;
+    WaitTest wt{};             // wait limit and the test hook (tcgen05 path)
 };
 
 // the batch above which the tcgen05 path (q8t weights, x16 activations) is used
@@ -132,6 +147,7 @@ struct DnParams {
     unsigned* err = nullptr;  // bit 1024 set when a state copy did not arrive in time
     const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
     int64_t pf_bytes = 0;
+    WaitTest wt{};             // wait limit and the test hook
 };
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
 // recurrence core only (op API): q,k,v bf16 [B][H][128], beta/decay f32 [B][H], o f32 [B][H][128]
@@ -164,6 +180,7 @@ struct AttnParams {
     // Every kernel checks 0 <= pos[b] <= max_pos < cap before it appends at pos or reads the
     // rotation table at pos; a sequence outside that range is skipped and bit kAttnErrPos set.
     int max_pos = 0;
+    WaitTest wt{};       // wait limit and the test hook (tensor-core kernel)
     const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
     int64_t pf_bytes = 0;
 };

@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, U = P.units, KT = P.KT;
+    const uint32_t WL = ep.wt.wait_ns;  // the limit of every wait below
 
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -300,19 +301,21 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     // once the ring is full, pull this CTA's share of the next GEMM's weights
                     // into L2 (this launch is latency-bound, so the extra HBM reads are free)
                     if (st == kWStages) prefetch_share_l2(ep.pf, ep.pf_bytes, blockIdx.x, G);
-                    if (st >= kWStages && !mbar_wait(&w_free[s], ((st / kWStages) - 1) & 1)) {
+                    if (st >= kWStages && !mbar_wait(&w_free[s], ((st / kWStages) - 1) & 1, WL)) {
                         atomicOr(err, 1u);
                         s_abort = 1;
                         ok = false;
                         break;
                     }
+                    if (st == ep.wt.withhold) continue;  // test hook: this copy is never issued
                     mbar_arrive_expect_tx(&w_full[s], kWStageBytes);
                     bulk_g2s(smem + UmmaSmem::w_off(s), src + (size_t)q * kWStageBytes, kWStageBytes, &w_full[s]);
                 }
             }
             if (st <= kWStages) prefetch_share_l2(ep.pf, ep.pf_bytes, blockIdx.x, G);
             for (int j = max(0, st - kWStages); j < st; j++)  // issued copies land before exit
-                if (!mbar_wait(&w_full[j % kWStages], (j / kWStages) & 1)) atomicOr(err, 2u);
+                if (j != ep.wt.withhold && !mbar_wait(&w_full[j % kWStages], (j / kWStages) & 1, WL))
+                    atomicOr(err, 2u);
         }
     } else if (warp == kWarpX) {
         // ---------------- activation producer (after the predecessor has completed); with a
@@ -327,7 +330,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 unit_range(u, P, mt, k0, len, split);
                 for (int q = 0; q < len; q += kAGroup, g++) {
                     const int s = g % kXStages;
-                    if (g >= kXStages && !mbar_wait(&x_free[s], ((g / kXStages) - 1) & 1)) {
+                    if (g >= kXStages && !mbar_wait(&x_free[s], ((g / kXStages) - 1) & 1, WL)) {
                         atomicOr(err, 4u);
                         s_abort = 1;
                         ok = false;
@@ -340,7 +343,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 }
             }
             for (int j = max(0, g - kXStages); j < g; j++)
-                if (!mbar_wait(&x_full[j % kXStages], (j / kXStages) & 1)) atomicOr(err, 8u);
+                if (!mbar_wait(&x_full[j % kXStages], (j / kXStages) & 1, WL)) atomicOr(err, 8u);
         }
     } else if (warp == kWarpMma) {
         // ---------------- MMA issuer
@@ -354,7 +357,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 bool split;
                 unit_range(u, P, mt, k0, len, split);
                 if (j >= 2) {
-                    if (!mbar_wait(&acc_free[j & 1], ((j >> 1) - 1) & 1)) {
+                    if (!mbar_wait(&acc_free[j & 1], ((j >> 1) - 1) & 1, WL)) {
                         atomicOr(err, 16u);
                         ok = false;
                         break;
@@ -365,8 +368,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 int ux = 0;  // K tile within the activation stage sx
                 for (int q = 0; q < len; q++, st++) {
                     const int so = st % kOpStages;
-                    if (!mbar_wait(&op_full[so], (st / kOpStages) & 1) ||
-                        (ux == 0 && !mbar_wait(&x_full[sx], xph))) {
+                    if (!mbar_wait(&op_full[so], (st / kOpStages) & 1, WL) ||
+                        (ux == 0 && !mbar_wait(&x_full[sx], xph, WL))) {
                         atomicOr(err, 32u);
                         ok = false;
                         break;
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             }
             if (!ok) s_abort = 1;
             umma_commit(mma_done);  // every MMA issued above has completed before TMEM is freed
-            if (!mbar_wait(mma_done, 0)) atomicOr(err, 64u);
+            if (!mbar_wait(mma_done, 0, WL)) atomicOr(err, 64u);
         }
     } else if (warp < kConvWarps) {
         // ---------------- converters: weight row r of tile t -> 32 TMEM columns of f16 pairs
@@ -413,7 +416,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
           for (int q = 0; q < len; q++, st++) {
             const int sw = st % kWStages, so = st % kOpStages;
             // warp-uniform outcome: tcgen05.st below is a whole-warp instruction
-            if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], (st / kWStages) & 1))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&w_full[sw], (st / kWStages) & 1, WL))) {
                 if (lane == 0) atomicOr(err, 128u);
                 s_abort = 1;
                 ok = false;
@@ -438,7 +441,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 }
             }
             if (st >= kOpStages &&
-                !__all_sync(0xffffffffu, mbar_wait(&op_free[so], ((st / kOpStages) - 1) & 1))) {
+                !__all_sync(0xffffffffu, mbar_wait(&op_free[so], ((st / kOpStages) - 1) & 1, WL))) {
                 if (lane == 0) atomicOr(err, 256u);
                 s_abort = 1;
                 ok = false;
@@ -478,7 +481,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 for (int kq = 0; kq < len && !fail; kq++, gx++) {
                     const int s = gx % kXSlots;
                     glu_load(h2, h2_ld, batch, k0 + kq, n0 + 32, jn, rb);
-                    if (gx >= kXSlots && !mbar_wait(&x_free[s], ((gx / kXSlots) - 1) & 1)) {
+                    if (gx >= kXSlots && !mbar_wait(&x_free[s], ((gx / kXSlots) - 1) & 1, WL)) {
                         atomicOr(err, 2048u);
                         s_abort = 1;
                         fail = true;
@@ -492,7 +495,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     mbar_arrive(&x_full[s]);
                 }
             }
-            if (!fail && !mbar_wait(&acc_full[j & 1], (j >> 1) & 1)) {
+            if (!fail && !mbar_wait(&acc_full[j & 1], (j >> 1) & 1, WL)) {
                 fail = true;
                 atomicOr(err, 512u);
                 s_abort = 1;
@@ -652,8 +655,10 @@ int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* e
     const int G = std::min(pl.units, num_sms);
     // the SwiGLU source reads whole 64-column gate/up groups of h2 (K = ffn a multiple of 64)
     if (h2 && (w.KB % 2 != 0 || h2_ld < 2 * 32 * w.KB || (h2_ld & 3) != 0)) return -1;
+    GemmEpi e = ep;
+    e.wt = take_wait_test(kWaitTestGemm, st);
     if (launch_pdl(q8_umma_gemm_kernel, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, P, x16, h2, h2_ld, batch, err,
-                   ep) != cudaSuccess)
+                   e) != cudaSuccess)
         return -2;
     return 0;
 }

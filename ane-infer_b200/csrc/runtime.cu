@@ -3,6 +3,7 @@
 // Owns the GGUF parse, the Qwen3.5 hybrid configuration, the packed device weights, the
 // per-slot recurrent / conv / KV state and the decode-step driver that launches the kernels
 // of q8.cu, deltanet.cu, attention.cu and misc.cu on a context-owned stream.
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -1108,7 +1109,41 @@ struct ab2_q8 {
 };
 
 // ================================================================================== C ABI
+// ------------------------------------------------------------------------- wait-timeout test hook
+static std::mutex g_wt_mu;
+static std::atomic<bool> g_wt_any{false};
+static WaitTest g_wt_armed[4];
+static bool g_wt_on[4] = {false, false, false, false};
+
+namespace ab2 {
+WaitTest take_wait_test(int which, cudaStream_t st) {
+    WaitTest w;
+    if (!g_wt_any.load(std::memory_order_relaxed) || which < 1 || which > 3) return w;
+    std::lock_guard<std::mutex> lk(g_wt_mu);
+    if (!g_wt_on[which]) return w;
+    // never baked into a captured graph: a capture keeps the production setting and the arm
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return w;
+    g_wt_on[which] = false;
+    g_wt_any.store(g_wt_on[1] || g_wt_on[2] || g_wt_on[3]);
+    return g_wt_armed[which];
+}
+}  // namespace ab2
+
 AB2_API const char* ab2_last_error(void) { return g_err.c_str(); }
+
+AB2_API int ab2_debug_arm_wait_timeout(int which, int copy_index, uint32_t wait_ns) {
+    if (which < kWaitTestGemm || which > kWaitTestDeltaNet)
+        return seterr(AB2_ERR_ARG, "which must be 1 (GEMM), 2 (attention) or 3 (DeltaNet)");
+    if (copy_index < 0) return seterr(AB2_ERR_ARG, "copy_index must be >= 0");
+    if (wait_ns != 0 && wait_ns < 1000) return seterr(AB2_ERR_ARG, "wait_ns must be 0 (disarm) or >= 1000");
+    std::lock_guard<std::mutex> lk(g_wt_mu);
+    g_wt_on[which] = wait_ns != 0;
+    g_wt_armed[which].wait_ns = wait_ns;
+    g_wt_armed[which].withhold = copy_index;
+    g_wt_any.store(g_wt_on[1] || g_wt_on[2] || g_wt_on[3]);
+    return 0;
+}
 
 AB2_API int ab2_gguf_inspect(const uint8_t* gguf, uint64_t len, ab2_config* out) {
     if (!out) return seterr(AB2_ERR_ARG, "null config pointer");

@@ -59,16 +59,16 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
     return ok != 0;
 }
 
-// Wait for phase `parity` of `bar` for at most kWaitLimitNs; false on timeout. A timeout
-// means a lost arrival; the caller records an error code and abandons the tile instead of
-// waiting forever.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for phase `parity` of `bar` for at most limit_ns (2 s unless a test shortens it);
+// false on timeout. A timeout means a lost arrival; the caller records an error code and
+// abandons the tile instead of waiting forever.
+constexpr uint32_t kWaitLimitNs = 2000000000u;  // 2 s
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
         if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -163,6 +163,17 @@ int ab2_q8_gemv_noalloc(ab2_q8* w, const float* x, int batch, float* y, void* st
 /* Synchronise the current device and return (then clear) the error word of the op-level
  * tensor-core calls: 0, or the code of a pipeline wait that timed out. */
 int ab2_op_error(uint32_t* code);
+/* Test hook; no counterpart in the reference. Arms the next launch (from this process, on a
+ * stream that is not capturing) of one pipelined kernel to leave its asynchronous copy number
+ * copy_index (counted per CTA from 0) unissued and to give each of its waits wait_ns
+ * nanoseconds instead of 2 s. The waits on that copy then expire without any fault: the
+ * kernel sets its error bit (tcgen05 GEMM 128 with others of its pipeline, attention 4096,
+ * DeltaNet 1024), waits for the copies it did issue, frees its tensor memory and returns; that
+ * launch's results are invalid. The error is reported as any other: ab2_op_error for the
+ * op-level calls, AB2_ERR_CUDA from the context's step or ab2_sync. which: 1 the tcgen05
+ * GEMM's weight copy, 2 the tensor-core attention's K/V tile copy, 3 the DeltaNet state copy.
+ * wait_ns = 0 disarms; otherwise at least 1000. Nothing is withheld unless this is called. */
+int ab2_debug_arm_wait_timeout(int which, int copy_index, uint32_t wait_ns);
 /* The packed tensor expanded back to f32 [m][n] (exact). */
 int ab2_q8_unpack(ab2_q8* w, float* out, void* stream);
 /* n_blocks raw Q8_0 blocks (device) -> f32 (device), bit-exact with dequant_q8_0_block

@@ -178,3 +178,14 @@ def test_bad_arguments(pkg, lib):
     assert "null" in lib.ab2_last_error().decode()
     h = C.c_void_p()
     assert lib.ab2_create(None, 0, 0, 0, 16, None, C.byref(h)) == -1   # max_batch 0
+
+
+def test_wait_timeout_hook_arguments(pkg):
+    """The test hook that arms one pipelined-kernel launch to let its waits expire checks its
+    arguments on the host (no device work), and disarming is always accepted."""
+    for args in ((0, 0, 1000), (4, 0, 1000), (1, -1, 1000), (1, 0, 10)):
+        with pytest.raises(pkg.Ab2Error) as ei:
+            pkg.debug_arm_wait_timeout(*args)
+        assert ei.value.code == -1
+    for which in (1, 2, 3):
+        pkg.debug_arm_wait_timeout(which, 0, 0)

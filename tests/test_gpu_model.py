@@ -180,27 +180,47 @@ def test_step_graph_matches_stream(pkg, oracle, tiny_gguf, tiny_model, kv_bf16):
 
 def test_step_graph_device_buffers(pkg, tiny_gguf, cuda):
     """Graph replay through the device-buffer entry point, tokens fed back on the device
-    through two alternating id buffers (two cached plans), against the stream form."""
+    through two alternating id buffers (two cached plans), against the stream form. The
+    tcgen05 path's K-split adds land in a different order in every run, and its f16 operand
+    rounding turns that into ~1e-3 logit differences between two runs. So each slot's tokens
+    must agree up to that slot's first divergence, and a divergence may only come at a near-tie
+    of the stream form's logits (top-2 gap below 1e-2 of the logit scale), after which the two
+    runs decode different sequences."""
     import torch
-    B = 9
-    outs = []
+    B, steps, V = 9, 24, 32000
+    runs = []
     for graph in (False, True):
         ctx = pkg.DecodeContext(tiny_gguf, max_batch=B, max_ctx=40, kv_bf16=True)
         ctx.step_graph(graph)
         tok = [torch.arange(B, dtype=torch.int32, device="cuda") * 7 + 3,
                torch.empty(B, dtype=torch.int32, device="cuda")]
+        logits = torch.empty((B, V), dtype=torch.float32, device="cuda")
         torch.cuda.synchronize()  # the step runs on the context's own stream
-        seen = []
-        for i in range(24):
-            ctx.decode_step_device(tok[i % 2], B, None, tok[(i + 1) % 2])
+        seen, lg = [], []
+        for i in range(steps):
+            ctx.decode_step_device(tok[i % 2], B, logits, tok[(i + 1) % 2])
             ctx.sync()
             seen.append(tok[(i + 1) % 2].cpu().numpy().copy())
+            lg.append(logits.cpu().numpy().copy())
         if graph:
             assert ctx.step_graph_captures() <= 4  # one plan per id buffer (and split count)
         ctx.close()
-        outs.append(np.stack(seen))
-    # same greedy tokens, allowing for a near-tie flipped by the K-split add order
-    assert (outs[0] == outs[1]).mean() > 0.99
+        runs.append((np.stack(seen), np.stack(lg)))
+    (ta, la), (tb, lb) = runs
+    diverged = []
+    for b in range(B):
+        diff = np.nonzero(ta[:, b] != tb[:, b])[0]
+        first = int(diff[0]) if diff.size else steps
+        # same input tokens up to step `first`: the two runs' logits agree to the path's precision
+        for i in range(first + 1 if first < steps else steps):
+            assert rel_err(lb[i, b], la[i, b]) < 1e-2, (b, i)
+        if first < steps:
+            ref = np.sort(la[first, b].astype(np.float64))
+            gap = (ref[-1] - ref[-2]) / np.max(np.abs(ref))
+            print(f"slot {b} diverges at step {first}: top-2 gap {gap:.2e}")
+            assert gap < 1e-2, (b, first, gap)
+            diverged.append(b)
+    assert len(diverged) <= 3, diverged
 
 
 def test_wide_ffn_swiglu_ring_wraps(pkg, oracle, synth):
