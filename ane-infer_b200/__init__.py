@@ -39,7 +39,8 @@ class Ab2Error(RuntimeError):
 
 
 class Ab2Options(C.Structure):
-    _fields_ = [("kv_bf16", C.c_int32), ("rope_dims", C.c_int32), ("reserved", C.c_int32 * 6)]
+    _fields_ = [("kv_bf16", C.c_int32), ("rope_dims", C.c_int32), ("exact_max_batch", C.c_int32),
+                ("reserved", C.c_int32 * 5)]
 
 
 class Ab2Config(C.Structure):
@@ -156,10 +157,13 @@ class DecodeContext:
     """A model resident on one GPU plus per-slot decode state for up to max_batch sequences."""
 
     def __init__(self, gguf, device: int = 0, max_batch: int = 1, max_ctx: int = 4096, kv_bf16: bool = True,
-                 rope_dims: int = 0):
+                 rope_dims: int = 0, exact_max_batch: int = 0):
+        """exact_max_batch: steps of at most this many sequences multiply the Q8_0 weights exactly
+        (mma.sync); larger steps use the tcgen05 path with f16 operands. 0 (default) = 1."""
         lib = load_library()
         buf = _host(gguf, np.uint8)
-        opt = Ab2Options(int(kv_bf16), int(rope_dims))
+        opt = Ab2Options(int(kv_bf16), int(rope_dims), int(exact_max_batch))
+        self.exact_max_batch = int(exact_max_batch) or 1
         h = C.c_void_p()
         _check(lib.ab2_create(_hp(buf), buf.size, device, max_batch, max_ctx, C.byref(opt), C.byref(h)))
         self._h = h
@@ -167,6 +171,10 @@ class DecodeContext:
         _check(lib.ab2_get_config(h, C.byref(cfg)))
         self.config = cfg.as_dict()
         self.layer_is_deltanet = [bool(lib.ab2_layer_is_deltanet(h, l)) for l in range(self.config["n_layers"])]
+
+    def tensor_core_gemm(self, batch: int) -> bool:
+        """Whether a step of `batch` sequences runs its Q8_0 GEMMs on the tcgen05 path."""
+        return batch > self.exact_max_batch
 
     def close(self):
         if getattr(self, "_h", None):

@@ -154,17 +154,34 @@ __global__ void __launch_bounds__(WARPS * 32) q8_gemm_kernel(const uint4* __rest
 #pragma unroll
     for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 
+    // Launched with programmatic dependent launch: the next kernel may start setting up now,
+    // and this one loads its first weight blocks (constants) before waiting for the kernel
+    // that produced its activations; every read of activations, split partials, tickets and
+    // outputs comes after the wait.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint4* qp = qs + (size_t)mt * KB * 32 + lane;
+    const uint32_t* dp = dsc + (size_t)mt * KB * 8 + (lane >> 2);
+    uint4 q[U];
+    uint32_t d[U];
     if (mt < M16) {
-        const uint4* qp = qs + (size_t)mt * KB * 32 + lane;
-        const uint32_t* dp = dsc + (size_t)mt * KB * 8 + (lane >> 2);
-        for (int kb = kb0; kb < kb1; kb += U) {
-            uint4 q[U];
-            uint32_t d[U];
 #pragma unroll
-            for (int u = 0; u < U; u++) {
-                if (kb + u < kb1) {
-                    q[u] = ld_stream(qp + (size_t)(kb + u) * 32);
-                    d[u] = ld_stream32(dp + (size_t)(kb + u) * 8);
+        for (int u = 0; u < U; u++) {
+            if (kb0 + u < kb1) {
+                q[u] = ld_stream(qp + (size_t)(kb0 + u) * 32);
+                d[u] = ld_stream32(dp + (size_t)(kb0 + u) * 8);
+            }
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (mt < M16) {
+        for (int kb = kb0; kb < kb1; kb += U) {
+            if (kb != kb0) {
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    if (kb + u < kb1) {
+                        q[u] = ld_stream(qp + (size_t)(kb + u) * 32);
+                        d[u] = ld_stream32(dp + (size_t)(kb + u) * 8);
+                    }
                 }
             }
 #pragma unroll
@@ -261,9 +278,9 @@ static void launch_gemm_t(const Q8Weight& w, const uint8_t* xf, int batch, float
     int ns = gemm_nsplit(w.M16, w.KB, num_sms);
     int kps = (w.KB + ns - 1) / ns;
     dim3 grid(gemm_grid_x(w.M16), ns);
-    q8_gemm_kernel<NT, PACKED, kGemmWarps><<<grid, kGemmWarps * 32, 0, st>>>(
-        reinterpret_cast<const uint4*>(w.qs), reinterpret_cast<const uint32_t*>(w.d), w.M16, w.KB,
-        reinterpret_cast<const uint4*>(xf), batch, kps, reinterpret_cast<float4*>(ws), tickets, ep);
+    launch_pdl(q8_gemm_kernel<NT, PACKED, kGemmWarps>, grid, dim3(kGemmWarps * 32), 0, st,
+               reinterpret_cast<const uint4*>(w.qs), reinterpret_cast<const uint32_t*>(w.d), w.M16, w.KB,
+               reinterpret_cast<const uint4*>(xf), batch, kps, reinterpret_cast<float4*>(ws), tickets, ep);
 }
 
 void launch_q8_gemm(const Q8Weight& w, const uint8_t* xf, int batch, float* ws, unsigned* tickets,

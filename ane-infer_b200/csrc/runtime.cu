@@ -472,7 +472,8 @@ struct ab2_ctx {
     unsigned* err_d = nullptr;  // tensor-core pipeline error word (0 = ok)
     alignas(64) uint8_t tmap_k[128];  // TMA tensor maps over the bf16 K / V caches ([rows][hd])
     alignas(64) uint8_t tmap_v[128];
-    bool use_umma = false;      // max_batch >= kUmmaMinBatch: q8t weights are packed too
+    int exact_max = 1;          // steps of at most this many sequences take the exact mma.sync GEMM
+    bool use_umma = false;      // max_batch > exact_max: q8t weights are packed too
     // pinned host staging
     int32_t *tok_h = nullptr, *next_h = nullptr;
     unsigned* err_h = nullptr;
@@ -759,8 +760,8 @@ void prof_collect(ab2_ctx* x) {
 }
 
 // --------------------------------------------------------------------------------- the step
-// batches of kUmmaMinBatch or more run on the tcgen05 path
-bool umma_for(const ab2_ctx* x, int B) { return x->use_umma && B >= kUmmaMinBatch; }
+// steps of more than exact_max sequences run on the tcgen05 path
+bool umma_for(const ab2_ctx* x, int B) { return x->use_umma && B > x->exact_max; }
 
 ActOut act(const ab2_ctx* x, uint8_t* buf, int K, int B) { return act_out(buf, K, B, umma_for(x, B)); }
 
@@ -1161,6 +1162,8 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
     *out = nullptr;
     if (max_batch < 1 || max_batch > 64) return seterr(AB2_ERR_ARG, "max_batch must be in [1, 64]");
     if (max_ctx < 1) return seterr(AB2_ERR_ARG, "max_ctx must be positive");
+    if (opt && (opt->exact_max_batch < 0 || opt->exact_max_batch > 64))
+        return seterr(AB2_ERR_ARG, "exact_max_batch must be in [0, 64]");
     {
         // the file is checked on the host first, so a bad model fails the same way with or
         // without a GPU
@@ -1184,7 +1187,8 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
     x->cap = max_ctx;
     x->kv_bf16 = opt ? opt->kv_bf16 != 0 : true;
     x->rot = opt ? opt->rope_dims : 0;
-    x->use_umma = max_batch >= kUmmaMinBatch;
+    x->exact_max = opt && opt->exact_max_batch > 0 ? opt->exact_max_batch : 1;
+    x->use_umma = max_batch > x->exact_max;
     cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device);
     int rc = 0;
     if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)

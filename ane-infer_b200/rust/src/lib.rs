@@ -42,7 +42,8 @@ pub mod ffi {
     pub struct ab2_options {
         pub kv_bf16: i32,
         pub rope_dims: i32,
-        pub reserved: [i32; 6],
+        pub exact_max_batch: i32,
+        pub reserved: [i32; 5],
     }
 
     #[repr(C)]
@@ -176,7 +177,7 @@ impl Decoder {
     /// Load a qwen35 GGUF (Q8_0 weights) onto `device` and allocate state for `max_batch`
     /// sequences of up to `max_ctx` tokens.
     pub fn new(gguf: &[u8], device: i32, max_batch: i32, max_ctx: i32, opt: &Options) -> Result<Self> {
-        let o = ffi::ab2_options { kv_bf16: opt.kv_bf16 as i32, rope_dims: opt.rope_dims, reserved: [0; 6] };
+        let o = ffi::ab2_options { kv_bf16: opt.kv_bf16 as i32, rope_dims: opt.rope_dims, exact_max_batch: 0, reserved: [0; 5] };
         let mut raw: *mut ffi::ab2_ctx = std::ptr::null_mut();
         check(unsafe { ffi::ab2_create(gguf.as_ptr(), gguf.len() as u64, device, max_batch, max_ctx, &o, &mut raw) })?;
         let ctx = NonNull::new(raw).ok_or_else(|| arg_error("ab2_create returned no context".into()))?;

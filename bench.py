@@ -324,8 +324,9 @@ def run_ours(args):
         "attention": cfg["n_attn"] * attn_launch_bytes(cfg, B, attn_len),
         "deltanet": cfg["n_dn"] * dn_launch_bytes(cfg, B),
     }
+    tc = ctx.tensor_core_gemm(B)
     what = {"q8_gemm": "q8_umma_gemm_kernel (Q8_0 GEMM family on tcgen05: every projection and the lm_head)"
-                       if B >= 9 else "q8_gemm_kernel (Q8_0 GEMV family, mma.sync: every projection and the lm_head)",
+                       if tc else "q8_gemm_kernel (Q8_0 GEMV family, mma.sync: every projection and the lm_head)",
             "attention": "attn_mma_kernel (GQA split-KV flash-decode, bf16 KV via TMA)",
             "deltanet": "deltanet_persist_kernel (fused conv1d, norms, gated delta rule, gated RMSNorm)"}
     prof_total = sum(v["ms"] for v in prof.values())
@@ -400,7 +401,7 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "weak" if args.weak else "strong", "vs_baseline": None,
-            "dtype": "f16 MMA operands (q*d rounded once), f32 accumulate, bf16 KV" if B >= 9 else
+            "dtype": "f16 MMA operands (q*d rounded once), f32 accumulate, bf16 KV" if tc else
                      "exact Q8_0 weights x f16 hi/lo activations, f32 accumulate, bf16 KV",
             "data": "synthetic (seeded random Q8_0 weights, seeded DeltaNet/conv state, N(0,1) bf16 KV)",
             "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {B * world} sequences "

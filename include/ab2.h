@@ -35,7 +35,12 @@ typedef struct ab2_q8 ab2_q8;
 typedef struct ab2_options {
     int32_t kv_bf16;   /* 1 (default): bf16 KV cache; 0: f32 KV cache like the reference  */
     int32_t rope_dims; /* rotated dims per head; 0 (default) = head_dim, the reference's  */
-    int32_t reserved[6];
+    /* Steps of at most this many sequences multiply the Q8_0 weights exactly (mma.sync, the
+     * weights q*d kept exact in f32 sums, activations as an f16 hi/lo pair); larger steps use
+     * the tcgen05 path, whose operands are rounded once to f16. 0 (default) = 1: one sequence
+     * exact, every batched step on the tensor-core path. At most 64. */
+    int32_t exact_max_batch;
+    int32_t reserved[5];
 } ab2_options;
 
 typedef struct ab2_config {

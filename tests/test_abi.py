@@ -189,3 +189,11 @@ def test_wait_timeout_hook_arguments(pkg):
         assert ei.value.code == -1
     for which in (1, 2, 3):
         pkg.debug_arm_wait_timeout(which, 0, 0)
+
+
+def test_create_rejects_bad_exact_max_batch(pkg, tiny_gguf):
+    """exact_max_batch is checked before any device work."""
+    for bad in (-1, 65):
+        with pytest.raises(pkg.Ab2Error) as ei:
+            pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=8, exact_max_batch=bad)
+        assert ei.value.code == -1 and "exact_max_batch" in str(ei.value)

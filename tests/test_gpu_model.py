@@ -244,6 +244,30 @@ def test_wide_ffn_swiglu_ring_wraps(pkg, oracle, synth):
     ctx.close()
 
 
+def test_exact_max_batch_option(pkg, oracle, tiny_gguf, tiny_model):
+    """A batched step takes the tcgen05 path by default (operands rounded once to f16) and the
+    exact-weight mma.sync path when exact_max_batch covers its batch; both meet the logit bar,
+    the exact one at the f32 level."""
+    B = 4
+    toks = [17, 301, 4444, 29999]
+    errs = {}
+    for exact in (0, 4):
+        ctx = pkg.DecodeContext(tiny_gguf, max_batch=B, max_ctx=16, kv_bf16=True, exact_max_batch=exact)
+        assert ctx.tensor_core_gemm(B) == (exact == 0) and not ctx.tensor_core_gemm(1)
+        seqs = [tiny_model.new_seq(kv_bf16=True) for _ in range(B)]
+        worst = 0.0
+        t = list(toks)
+        for step in range(3):
+            lg, nx = ctx.decode_step(t)
+            for b in range(B):
+                worst = max(worst, rel_err(lg[b], seqs[b].forward(t[b])))
+            t = [int(v) for v in nx]
+        ctx.close()
+        errs[exact] = worst
+    print(f"worst logit rel err: tcgen05 {errs[0]:.2e}, exact {errs[4]:.2e}")
+    assert errs[4] < 1e-4 and errs[0] < LOGIT_TOL and errs[0] > 10 * errs[4]
+
+
 def test_state_io_and_capacity(pkg, tiny_gguf):
     ctx = pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=8, kv_bf16=True)
     rng = np.random.default_rng(4)
@@ -286,10 +310,10 @@ def gguf_2b(synth):
 @pytest.mark.parametrize("B", [3, 16])
 def test_2b_prefilled_parity(pkg, oracle, synth, gguf_2b, cuda, B):
     """Config 5 shape: slots with seeded DeltaNet/conv state and a prefilled bf16 KV cache;
-    the device-seeded state is read back and loaded into the oracle. B=3 runs the mma.sync
-    GEMM path, B=16 the tcgen05 path."""
+    the device-seeded state is read back and loaded into the oracle. B=3 runs the exact
+    mma.sync GEMM path (exact_max_batch=8), B=16 the tcgen05 path."""
     n_ctx, steps = 1024, 2
-    ctx = pkg.DecodeContext(gguf_2b, max_batch=B, max_ctx=n_ctx + 16, kv_bf16=True)
+    ctx = pkg.DecodeContext(gguf_2b, max_batch=B, max_ctx=n_ctx + 16, kv_bf16=True, exact_max_batch=8)
     ctx.seed_state(seed=1, n_slots=B, n_tokens=n_ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
     om = oracle.Model(gguf_2b, ctx_cap=n_ctx + 16)
     seqs = []

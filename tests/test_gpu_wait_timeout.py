@@ -78,10 +78,10 @@ def test_deltanet_state_copy_timeout(pkg, tiny_gguf, cuda):
     # through the decode step (the DeltaNet kernel runs inside it): the first state copy of
     # every CTA is withheld in the first DeltaNet layer of the step; the step reports the
     # timeout, and after re-seeding the same state a normal step gives the reference logits
-    # (B=2: the exact mma.sync GEMM path, so the step is deterministic)
+    # (B=2 on the exact mma.sync GEMM path, exact_max_batch=2, so the step is deterministic)
     torch = cuda
     B, n_tok = 2, 40
-    ctx = pkg.DecodeContext(tiny_gguf, max_batch=B, max_ctx=64, kv_bf16=True)
+    ctx = pkg.DecodeContext(tiny_gguf, max_batch=B, max_ctx=64, kv_bf16=True, exact_max_batch=2)
     ctx.seed_state(seed=3, n_slots=B, n_tokens=n_tok, dn_std=0.1, conv_std=1.0, kv_std=1.0)
     ref, _ = ctx.decode_step([5, 77])
     ctx.seed_state(seed=3, n_slots=B, n_tokens=n_tok, dn_std=0.1, conv_std=1.0, kv_std=1.0)
@@ -100,7 +100,7 @@ def test_deltanet_state_copy_timeout(pkg, tiny_gguf, cuda):
 def test_attention_timeout_through_the_step(pkg, tiny_gguf, cuda):
     # the same through the decode step's attention layer (tensor-core kernel, bf16 KV)
     B, n_tok = 2, 300
-    ctx = pkg.DecodeContext(tiny_gguf, max_batch=B, max_ctx=400, kv_bf16=True)
+    ctx = pkg.DecodeContext(tiny_gguf, max_batch=B, max_ctx=400, kv_bf16=True, exact_max_batch=2)
     ctx.seed_state(seed=4, n_slots=B, n_tokens=n_tok, dn_std=0.1, conv_std=1.0, kv_std=1.0)
     ref, _ = ctx.decode_step([9, 11])
     ctx.seed_state(seed=4, n_slots=B, n_tokens=n_tok, dn_std=0.1, conv_std=1.0, kv_std=1.0)

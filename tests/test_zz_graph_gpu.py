@@ -1,8 +1,8 @@
 """Step-graph cache under pressure on a B200: more launch plans than the four cached ones (six
 batch sizes in rotation), so plans are evicted and captured again, with profiling (which
 runs the stream form) switched on and off in between. Every step must match a context that
-uses stream launches only. All batches are at most 8 slots (the fixed-order mma.sync path),
-so the two contexts' logits are bit-identical."""
+uses stream launches only. All batches are at most 8 slots, run on the fixed-order mma.sync
+path (exact_max_batch=8), so the two contexts' logits are bit-identical."""
 import numpy as np
 import pytest
 
@@ -10,7 +10,7 @@ pytestmark = pytest.mark.gpu
 
 
 def test_step_graph_eviction_and_profiling(pkg, tiny_gguf, cuda):
-    kw = dict(max_batch=8, max_ctx=64, kv_bf16=True)
+    kw = dict(max_batch=8, max_ctx=64, kv_bf16=True, exact_max_batch=8)
     ref = pkg.DecodeContext(tiny_gguf, **kw)
     gra = pkg.DecodeContext(tiny_gguf, **kw)
     gra.step_graph(True)
