@@ -35,11 +35,13 @@ PKG_DIR = os.path.join(ROOT, "ane-infer_b200")
 METRIC = "decode tok/s, 2B-shape Q8_0 B=64 ctx8K at 1/2/4/8 B200; % HBM roofline"
 SHAPE_KEYS = dict(n_layers=24, dim=2048, vocab=151936, ffn=6144, dn_heads=16, dn_state=128, attn_heads=8,
                   kv_heads=2, head_dim=256)
-# dram__bytes_read.sum + dram__bytes_write.sum of one attention launch, from an ncu capture
-# of attn_mma_kernel on the op benchmark at B=8, ctx 8192 (134.32 MB read + 4.11 MB written),
-# scaled by 8 to the benchmark's B=64 launch; traffic grows with B (each sequence's K/V is
-# read once), so the scaling is proportional.
-NCU_TRAFFIC_ATTN_PER_LAUNCH = 8 * (134_317_568 + 4_110_080)
+# dram__bytes_read.sum + dram__bytes_write.sum per decode step of each kernel family, from one
+# ncu capture of this benchmark's own step (2B shape, B=64, ctx ~8.2K: the launch list with
+# gpu__time_duration and the DRAM bytes, one pass per launch, ten steps averaged). The GEMM
+# family's figure includes the L2 prefetch of each following GEMM's weights and write-backs
+# of DeltaNet state evicted while the GEMMs run; DeltaNet's leaves part of its state writes
+# to later kernels.
+NCU_TRAFFIC_PER_STEP = {"q8_gemm": 3_275_100_000, "attention": 6_571_800_000, "deltanet": 1_639_700_000}
 
 
 def load_pkg():
@@ -341,8 +343,10 @@ def run_ours(args):
                         "launches_per_step": f["launches"] // args.steps,
                         "avg_launch_ms": round(f["ms"] / max(f["launches"], 1), 5),
                         "share_of_profiled_step": round(f["ms"] / prof_total, 4) if prof_total else None}
-    kernels["attention"]["traffic"] = NCU_TRAFFIC_ATTN_PER_LAUNCH
-    kernels["attention"]["traffic_unit"] = "bytes per launch"
+    if B == 64 and args.ctx == 8192:  # the captured workload
+        for fam, t in NCU_TRAFFIC_PER_STEP.items():
+            kernels[fam]["traffic"] = t
+            kernels[fam]["traffic_unit"] = "bytes per step (ncu, one decode step of this workload)"
     dominant = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
     roofline = dict(kernels[dominant], family=dominant)
     roofline.setdefault("traffic", None)
