@@ -61,6 +61,10 @@ SIGNATURES = {
     "ab2_gguf_inspect": (C.c_int, [_vp, _u64, C.POINTER(Ab2Config)]),
     "ab2_create": (C.c_int, [_vp, _u64, C.c_int, C.c_int, C.c_int, C.POINTER(Ab2Options), C.POINTER(_vp)]),
     "ab2_destroy": (None, [_vp]),
+    "ab2_tp_unique_id": (C.c_int, [_vp, _u64]),
+    "ab2_create_tp": (C.c_int, [_vp, _u64, C.c_int, C.c_int, C.c_int, C.POINTER(Ab2Options), C.c_int, C.c_int, _vp,
+                                _u64, C.POINTER(_vp)]),
+    "ab2_get_tp": (C.c_int, [_vp, C.POINTER(C.c_int32)]),
     "ab2_get_config": (C.c_int, [_vp, C.POINTER(Ab2Config)]),
     "ab2_layer_is_deltanet": (C.c_int, [_vp, C.c_int]),
     "ab2_reset_slot": (C.c_int, [_vp, C.c_int]),
@@ -145,6 +149,16 @@ def _stream(stream):
     return C.c_void_p(stream.cuda_stream)
 
 
+TP_ID_BYTES = 128
+
+
+def tp_unique_id() -> bytes:
+    """A fresh id for one head-parallel split (made on one rank, passed to every rank)."""
+    buf = (C.c_uint8 * TP_ID_BYTES)()
+    _check(load_library().ab2_tp_unique_id(C.cast(buf, C.c_void_p), TP_ID_BYTES))
+    return bytes(buf)
+
+
 def inspect_gguf(gguf) -> dict:
     """Parse GGUF bytes on the host and return the derived model configuration."""
     buf = _host(gguf, np.uint8)
@@ -157,20 +171,35 @@ class DecodeContext:
     """A model resident on one GPU plus per-slot decode state for up to max_batch sequences."""
 
     def __init__(self, gguf, device: int = 0, max_batch: int = 1, max_ctx: int = 4096, kv_bf16: bool = True,
-                 rope_dims: int = 0, exact_max_batch: int = 0):
+                 rope_dims: int = 0, exact_max_batch: int = 0, tp=None):
         """exact_max_batch: steps of at most this many sequences multiply the Q8_0 weights exactly
-        (mma.sync); larger steps use the tcgen05 path with f16 operands. 0 (default) = 1."""
+        (mma.sync); larger steps use the tcgen05 path with f16 operands. 0 (default) = 1.
+        tp: (rank, world, id) to join a head-parallel split of `world` GPUs (id from
+        tp_unique_id(), the same on every rank); returns once every rank has joined."""
         lib = load_library()
         buf = _host(gguf, np.uint8)
         opt = Ab2Options(int(kv_bf16), int(rope_dims), int(exact_max_batch))
         self.exact_max_batch = int(exact_max_batch) or 1
         h = C.c_void_p()
-        _check(lib.ab2_create(_hp(buf), buf.size, device, max_batch, max_ctx, C.byref(opt), C.byref(h)))
+        if tp is None:
+            _check(lib.ab2_create(_hp(buf), buf.size, device, max_batch, max_ctx, C.byref(opt), C.byref(h)))
+        else:
+            rank, world, tp_id = tp
+            idb = None if tp_id is None else (C.c_uint8 * len(tp_id)).from_buffer_copy(tp_id)
+            _check(lib.ab2_create_tp(_hp(buf), buf.size, device, max_batch, max_ctx, C.byref(opt), int(rank),
+                                     int(world), None if idb is None else C.cast(idb, C.c_void_p),
+                                     0 if tp_id is None else len(tp_id), C.byref(h)))
         self._h = h
         cfg = Ab2Config()
         _check(lib.ab2_get_config(h, C.byref(cfg)))
         self.config = cfg.as_dict()
         self.layer_is_deltanet = [bool(lib.ab2_layer_is_deltanet(h, l)) for l in range(self.config["n_layers"])]
+
+    def split(self) -> dict:
+        """This context's part of a head-parallel split (the whole model when not split)."""
+        v = (C.c_int32 * 6)()
+        _check(load_library().ab2_get_tp(self._h, v))
+        return {"rank": v[0], "world": v[1], "dn_h0": v[2], "dn_heads": v[3], "kv_h0": v[4], "kv_heads": v[5]}
 
     def tensor_core_gemm(self, batch: int) -> bool:
         """Whether a step of `batch` sequences runs its Q8_0 GEMMs on the tcgen05 path."""
@@ -210,8 +239,9 @@ class DecodeContext:
 
     def get_dn_state(self, layer: int, slot: int):
         cfg = self.config
-        rec = np.empty((cfg["dn_heads"], cfg["dn_state"], cfg["dn_state"]), dtype=np.float32)
-        conv = np.empty((3 * cfg["dim"], cfg["conv_kernel"]), dtype=np.float32)
+        # zeros: a head-parallel rank fills its own heads' part only
+        rec = np.zeros((cfg["dn_heads"], cfg["dn_state"], cfg["dn_state"]), dtype=np.float32)
+        conv = np.zeros((3 * cfg["dim"], cfg["conv_kernel"]), dtype=np.float32)
         _check(load_library().ab2_get_dn_state(self._h, layer, slot, _hp(rec), _hp(conv)))
         return rec, conv
 
@@ -222,8 +252,8 @@ class DecodeContext:
 
     def get_kv(self, layer: int, slot: int, n_tokens: int):
         cfg = self.config
-        k = np.empty((cfg["n_kv_heads"], n_tokens, cfg["head_dim"]), dtype=np.float32)
-        v = np.empty_like(k)
+        k = np.zeros((cfg["n_kv_heads"], n_tokens, cfg["head_dim"]), dtype=np.float32)
+        v = np.zeros_like(k)
         _check(load_library().ab2_get_kv(self._h, layer, slot, _hp(k), _hp(v), n_tokens))
         return k, v
 

@@ -325,6 +325,7 @@ size_t attn_ws_floats(int batch, int hkv, int nsplit, int hd, int gq) {
 int launch_attention(const AttnParams& p, int batch, int hd, bool kv_bf16, int max_len, cudaStream_t st) {
     const int gq = p.Hq / p.Hkv;
     if (gq != 4) return -1;
+    if (p.kvh0 != 0 || (p.Hkv_all && p.Hkv_all != p.Hkv)) return -1;  // the split runs the bf16 (tensor-core) path
     dim3 grid(attn_nsplit(max_len, p.chunk), p.Hkv, batch);
     const int nt = kAttnWarps * 32;
     if (hd == 256) {

@@ -140,17 +140,19 @@ __global__ void __launch_bounds__(128) attn_prep_kernel(AttnParams p) {
         return;
     }
     const float* proj = p.proj + (size_t)b * p.ldp;
-    const int koff = p.Hq * 2 * HD, voff = koff + p.Hkv * HD;
+    // the projection holds every head of the model; this launch runs kv heads kvh0 + kvh
+    const int kvg = p.kvh0 + kvh, Hkv_all = p.Hkv_all ? p.Hkv_all : p.Hkv;
+    const int koff = p.Hq * 2 * HD, voff = koff + Hkv_all * HD;
     constexpr int kQ4 = kGQ * HD / 4 / 128;  // float4 of queries per thread
     float4 qv[kQ4], kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
 #pragma unroll
     for (int i = 0; i < kQ4; i++) {
         const int e = (tid + i * 128) * 4, hh = e / HD, d = e % HD;
-        qv[i] = *reinterpret_cast<const float4*>(proj + (size_t)(kvh * kGQ + hh) * 2 * HD + d);
+        qv[i] = *reinterpret_cast<const float4*>(proj + (size_t)(kvg * kGQ + hh) * 2 * HD + d);
     }
     if (tid < HD / 4) {
-        kv4 = *reinterpret_cast<const float4*>(proj + koff + kvh * HD + tid * 4);
-        vv4 = *reinterpret_cast<const float4*>(proj + voff + kvh * HD + tid * 4);
+        kv4 = *reinterpret_cast<const float4*>(proj + koff + kvg * HD + tid * 4);
+        vv4 = *reinterpret_cast<const float4*>(proj + voff + kvg * HD + tid * 4);
     }
     const int half_rot = p.rot / 2;
     const float2* rope = p.rope + (size_t)pos * half_rot;
@@ -474,7 +476,7 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
         if (it.nsplit_b == 1) {
             // a lone split: the output itself
             for (int e = ct; e < kGQ * HD; e += kCT) {
-                const int hh = e / HD, d = e % HD, h = kvh * kGQ + hh;
+                const int hh = e / HD, d = e % HD, h = (p.kvh0 + kvh) * kGQ + hh;  // head in the model
                 float ov = o_s[e] / l_s[hh];
                 ov *= ref_sigmoid(proj[(size_t)h * 2 * HD + HD + d]);
                 act_store(p.out, b, h * HD + d, ov);
@@ -513,7 +515,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
     const float* parts = p.ws + (((size_t)b * p.Hkv + kvh) * kMaxSplits) * part_floats;
     const float* proj = p.proj + (size_t)b * p.ldp;
     // this thread's four outputs (head hh, dims d..d+3) and their output gates, loaded first
-    const int e4 = threadIdx.x * 4, hh = e4 / HD, d = e4 % HD, h = kvh * kGQ + hh;
+    const int e4 = threadIdx.x * 4, hh = e4 / HD, d = e4 % HD, h = (p.kvh0 + kvh) * kGQ + hh;
     const bool has = e4 < kGQ * HD;
     float4 gt = make_float4(0.f, 0.f, 0.f, 0.f);
     if (has) gt = *reinterpret_cast<const float4*>(proj + (size_t)h * 2 * HD + HD + d);
@@ -651,7 +653,7 @@ static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, i
 
 int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,
                          int max_len, int num_sms, cudaStream_t st, cudaEvent_t core_begin, cudaEvent_t core_end) {
-    if (p.Hq != kGQ * p.Hkv) return -1;
+    if (p.Hq != kGQ * (p.Hkv_all ? p.Hkv_all : p.Hkv)) return -1;
     if (hd == 256) return launch_mma_t<256>(tmk, tmv, p, row_base, batch, max_len, num_sms, st, core_begin, core_end);
     if (hd == 128) return launch_mma_t<128>(tmk, tmv, p, row_base, batch, max_len, num_sms, st, core_begin, core_end);
     return -1;

@@ -156,29 +156,31 @@ struct PrepIn {
 // loads that do not depend on the input projection: conv states and weights, ssm_a, dt_bias
 __device__ __forceinline__ void prep_load_const(const DnParams& p, int j, int tid, PrepIn& in) {
     const DnItem it = dn_item(j, p.H);
+    const int hg = p.h0 + it.h;  // the head's index in the model
     if (p.K == 4) {
 #pragma unroll
         for (int i = 0; i < 3; i++) {
-            const int ch = i * p.D + it.h * DK + tid;
+            const int ch = i * p.D + hg * DK + tid;
             in.st[i] = *reinterpret_cast<const float4*>(p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * 4);
             in.w4[i] = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
         }
     }
     if (tid == 0) {
-        in.sa = p.ssm_a[it.h];
-        in.dtb = p.dt_bias[it.h];
+        in.sa = p.ssm_a[hg];
+        in.dtb = p.dt_bias[hg];
     }
 }
 // loads of the projection outputs (after the grid dependency wait)
 __device__ __forceinline__ void prep_load_proj(const DnParams& p, int j, int tid, PrepIn& in) {
     const DnItem it = dn_item(j, p.H);
+    const int hg = p.h0 + it.h, H_all = p.H_all ? p.H_all : p.H;
     const float* proj = p.proj + (size_t)it.b * p.ldp;
 #pragma unroll
-    for (int i = 0; i < 3; i++) in.in[i] = proj[i * p.D + it.h * DK + tid];
-    in.g = proj[3 * p.D + it.h * DK + tid];
+    for (int i = 0; i < 3; i++) in.in[i] = proj[i * p.D + hg * DK + tid];
+    in.g = proj[3 * p.D + hg * DK + tid];
     if (tid == 0) {
-        in.br = proj[4 * p.D + it.h];
-        in.ar = proj[4 * p.D + p.H + it.h];
+        in.br = proj[4 * p.D + hg];
+        in.ar = proj[4 * p.D + H_all + hg];
     }
 }
 
@@ -187,9 +189,10 @@ __device__ __forceinline__ void prep_load_proj(const DnParams& p, int j, int tid
 // decay = exp(ssm_a * softplus(W_alpha x + dt_bias)) (deltanet.rs:469-480) for head j
 __device__ __forceinline__ void prep_compute(const DnParams& p, int j, int tid, const PrepIn& in, PrepSlot& ps) {
     const DnItem it = dn_item(j, p.H);
+    const int hg = p.h0 + it.h;
 #pragma unroll
     for (int i = 0; i < 3; i++) {
-        const int ch = i * p.D + it.h * DK + tid;
+        const int ch = i * p.D + hg * DK + tid;
         float* cs = p.conv + (size_t)it.b * p.conv_stride + (size_t)ch * p.K;
         float sum = 0.0f;
         if (p.K == 4) {
@@ -394,8 +397,8 @@ __global__ void __launch_bounds__(kDnPersistThreads, 1) deltanet_persist_kernel(
             const float rms = 1.0f / sqrtf((ssp[0] + ssp[1] + ssp[2] + ssp[3]) / (float)DK + p.eps);
             float nv = ov * rms * p.ssm_norm[tid];
             nv *= in.g[tid];
-            act_store(p.out, it.b, it.h * DK + tid, nv);
-            if (p.o_out) p.o_out[(size_t)it.b * p.D + it.h * DK + tid] = nv;
+            act_store(p.out, it.b, (p.h0 + it.h) * DK + tid, nv);  // the head's columns in the model
+            if (p.o_out) p.o_out[(size_t)it.b * p.D + (p.h0 + it.h) * DK + tid] = nv;
         }
         mbar_arrive(&prep_free[ps]);  // this thread's reads of the prep slot are done
     }

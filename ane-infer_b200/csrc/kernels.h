@@ -123,9 +123,10 @@ constexpr int kArgmaxChunks = 32;
 void launch_argmax2(const float* logits, int ld, int V, int batch, int32_t* out, int2* part, int nch,
                     cudaStream_t st);
 void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st);
-void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st);
+void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st,
+                     int64_t i0 = 0);
 void launch_seed_kv(void* dst, bool bf16, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
-                    uint64_t stream, float std, cudaStream_t st);
+                    uint64_t stream, float std, cudaStream_t st, int64_t i0 = 0);
 
 // deltanet.cu
 struct DnParams {
@@ -141,7 +142,9 @@ struct DnParams {
     const float* dt_bias;
     const float* ssm_norm;  // [128]
     float eps;
-    int D, H;
+    int D, H;            // H: heads this launch runs (the state buffer S holds exactly these)
+    int h0 = 0;          // index in the model of its first head (head-parallel split; 0 otherwise)
+    int H_all = 0;       // heads of the model (0: = H); the projection holds all of them
     ActOut out;          // activations of the ssm_out GEMM (K = D)
     float* o_out;        // optional f32 copy of the gated output [B][D]
     unsigned* err = nullptr;  // bit 1024 set when a state copy did not arrive in time
@@ -167,7 +170,9 @@ struct AttnParams {
     int64_t kv_slot_stride;  // elements between consecutive slots
     int cap;
     const int32_t* pos;  // [B] position of the new token per slot
-    int Hq, Hkv;
+    int Hq, Hkv;         // Hq: every query head (the projection layout); Hkv: the kv heads this launch runs
+    int kvh0 = 0;        // index in the model of its first kv head (head-parallel split; 0 otherwise)
+    int Hkv_all = 0;     // kv heads of the model (0: = Hkv); the caches hold only this launch's Hkv
     int chunk;           // tokens per split
     float* ws;           // split partials
     float* qprep = nullptr;  // tensor-core kernel: normed, rotated queries [B][Hkv][Hq/Hkv][HD]

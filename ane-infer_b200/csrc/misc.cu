@@ -220,21 +220,23 @@ __device__ __forceinline__ float hash_normal(uint64_t seed, uint64_t stream, uin
     return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
 }
 
-__global__ void seed_f32_kernel(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std) {
+// dst[i] = sample (i0 + i) of the stream
+__global__ void seed_f32_kernel(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, int64_t i0) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; i < n; i += (int64_t)gridDim.x * blockDim.x) dst[i] = std * hash_normal(seed, stream, (uint64_t)i);
+    for (; i < n; i += (int64_t)gridDim.x * blockDim.x) dst[i] = std * hash_normal(seed, stream, (uint64_t)(i0 + i));
 }
 
-// rows of hd values at [row][0, hd) for rows with (row % cap) < n_tokens, bf16-representable
+// rows of hd values at [row][0, hd) for rows with (row % cap) < n_tokens, bf16-representable;
+// element i takes sample (i0 + i) of the stream (i0 a multiple of cap * hd)
 template <typename T>
 __global__ void seed_kv_kernel(T* dst, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
-                               uint64_t stream, float std) {
+                               uint64_t stream, float std, int64_t i0) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t n = rows * hd;
     for (; i < n; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t row = i / hd;
         if (row % cap >= n_tokens) continue;
-        float v = __bfloat162float(__float2bfloat16_rn(std * hash_normal(seed, stream, (uint64_t)i)));
+        float v = __bfloat162float(__float2bfloat16_rn(std * hash_normal(seed, stream, (uint64_t)(i0 + i))));
         if constexpr (sizeof(T) == 4) dst[i] = v;
         else dst[i] = __float2bfloat16_rn(v);
     }
@@ -244,22 +246,23 @@ void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st) {
     pos_advance_kernel<<<(batch + 127) / 128, 128, 0, st>>>(pos, batch);
 }
 
-void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st) {
+void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st,
+                     int64_t i0) {
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 64) blocks = 148 * 64;
-    seed_f32_kernel<<<(unsigned)blocks, 256, 0, st>>>(dst, n, seed, stream, std);
+    seed_f32_kernel<<<(unsigned)blocks, 256, 0, st>>>(dst, n, seed, stream, std, i0);
 }
 
 void launch_seed_kv(void* dst, bool bf16, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
-                    uint64_t stream, float std, cudaStream_t st) {
+                    uint64_t stream, float std, cudaStream_t st, int64_t i0) {
     int64_t blocks = (rows * hd + 255) / 256;
     if (blocks > 148 * 64) blocks = 148 * 64;
     if (bf16)
         seed_kv_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>((__nv_bfloat16*)dst, rows, cap, n_tokens,
-                                                                       hd, seed, stream, std);
+                                                                       hd, seed, stream, std, i0);
     else
         seed_kv_kernel<float><<<(unsigned)blocks, 256, 0, st>>>((float*)dst, rows, cap, n_tokens, hd, seed, stream,
-                                                               std);
+                                                               std, i0);
 }
 
 }  // namespace ab2

@@ -3,6 +3,9 @@
 // Owns the GGUF parse, the Qwen3.5 hybrid configuration, the packed device weights, the
 // per-slot recurrent / conv / KV state and the decode-step driver that launches the kernels
 // of q8.cu, deltanet.cu, attention.cu and misc.cu on a context-owned stream.
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -65,6 +68,49 @@ struct DeviceGuard {
     DeviceGuard(const DeviceGuard&) = delete;
     DeviceGuard& operator=(const DeviceGuard&) = delete;
 };
+
+// ------------------------------------------------------------------------------------- NCCL
+// The head-parallel split all-gathers mixer outputs with NCCL, loaded at run time so that the
+// library links without it: "libnccl.so.2" (a copy the host process has loaded already, such
+// as PyTorch's, answers to that name first), or the file AB2_NCCL_LIB names.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+    std::string why;  // empty when loaded
+};
+
+const NcclApi& nccl_api() {
+    static NcclApi api = [] {
+        NcclApi a;
+        const char* env = getenv("AB2_NCCL_LIB");
+        const char* name = env && *env ? env : "libnccl.so.2";
+        void* h = dlopen(name, RTLD_NOW | RTLD_LOCAL);
+        if (!h) {
+            const char* e = dlerror();
+            a.why = std::string("cannot load ") + name + ": " + (e ? e : "?");
+            return a;
+        }
+        a.get_unique_id = (decltype(a.get_unique_id))dlsym(h, "ncclGetUniqueId");
+        a.comm_init_rank = (decltype(a.comm_init_rank))dlsym(h, "ncclCommInitRank");
+        a.comm_destroy = (decltype(a.comm_destroy))dlsym(h, "ncclCommDestroy");
+        a.all_gather = (decltype(a.all_gather))dlsym(h, "ncclAllGather");
+        a.error_string = (decltype(a.error_string))dlsym(h, "ncclGetErrorString");
+        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.all_gather || !a.error_string)
+            a.why = std::string(name) + " lacks an NCCL entry point";
+        return a;
+    }();
+    return api;
+}
+
+#define NCK(call)                                                                                   \
+    do {                                                                                            \
+        ncclResult_t n_ = (call);                                                                   \
+        if (n_ != ncclSuccess)                                                                      \
+            return seterr(AB2_ERR_CUDA, "%s: %s", #call, nccl_api().error_string(n_));              \
+    } while (0)
 
 // ------------------------------------------------------------------------------------- GGUF
 // Same byte format and accessor semantics as the reference parser
@@ -473,6 +519,13 @@ struct ab2_ctx {
     alignas(64) uint8_t tmap_k[128];  // TMA tensor maps over the bf16 K / V caches ([rows][hd])
     alignas(64) uint8_t tmap_v[128];
     int exact_max = 1;          // steps of at most this many sequences take the exact mma.sync GEMM
+    // head-parallel split over tp_world GPUs: this rank runs DeltaNet heads [dn_h0, dn_h0 +
+    // dn_hl) and kv heads [kv_h0, kv_h0 + kv_hl) and holds only their state; weights and the
+    // rest of the step are replicated (tp_world = 1: one GPU runs every head)
+    int tp_rank = 0, tp_world = 1;
+    int dn_h0 = 0, dn_hl = 0, kv_h0 = 0, kv_hl = 0;
+    bool dn_split = false, kv_split = false;  // which mixers are split (the others run replicated)
+    ncclComm_t nccl = nullptr;  // the communicator of the split
     bool use_umma = false;      // max_batch > exact_max: q8t weights are packed too
     // pinned host staging
     int32_t *tok_h = nullptr, *next_h = nullptr;
@@ -540,6 +593,25 @@ int upload_q8(ab2_ctx* x, int64_t M, int64_t K, const std::vector<RepackSrc>& sr
     return 0;
 }
 
+// Head-parallel split over tp_world ranks: rank r runs DeltaNet heads [r*H/W, (r+1)*H/W) and
+// kv heads [r*Hkv/W, (r+1)*Hkv/W) (with their query heads) and holds only their recurrent
+// state and KV cache. A mixer kind whose heads do not divide over the ranks (or whose output
+// slice would not be whole 64-column K tiles) runs replicated on every rank instead.
+int plan_split(ab2_ctx* x) {
+    const Cfg& c = x->c;
+    const int W = x->tp_world, r = x->tp_rank;
+    x->dn_split = c.n_dn > 0 && c.dn_heads % W == 0 && (c.dn_heads * 128 / W) % 64 == 0;
+    x->kv_split = c.n_attn > 0 && x->kv_bf16 && c.n_kv % W == 0 && (c.n_heads * c.hd / W) % 64 == 0;
+    if (!x->dn_split && !x->kv_split)
+        return seterr(AB2_ERR_ARG, "head-parallel split: neither %lld DeltaNet heads nor %lld kv heads (bf16 cache) "
+                      "divide over %d ranks", (long long)c.dn_heads, (long long)c.n_kv, W);
+    x->dn_hl = (int)(x->dn_split ? c.dn_heads / W : c.dn_heads);
+    x->dn_h0 = x->dn_split ? r * x->dn_hl : 0;
+    x->kv_hl = (int)(x->kv_split ? c.n_kv / W : c.n_kv);
+    x->kv_h0 = x->kv_split ? r * x->kv_hl : 0;
+    return 0;
+}
+
 int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     Gguf g;
     RET(parse_gguf(data, len, &g));
@@ -548,6 +620,7 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     const int64_t D = c.dim, F = c.ffn, H = c.dn_heads, hd = c.hd, Hq = c.n_heads, Hkv = c.n_kv;
     RET(validate_model(g, c, x->rot));
     x->rot = x->rot > 0 ? x->rot : (int)hd;
+    if (x->tp_world > 1) RET(plan_split(x));
 
     // staging buffer for the largest Q8 tensor
     uint64_t maxb = 0;
@@ -633,9 +706,13 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
 
     // ---- per-slot state
     const int B = x->max_batch;
-    x->s_stride = H * 128 * 128;
-    x->conv_stride = 3 * D * c.conv_k;
-    x->kv_slot = Hkv * (int64_t)x->cap * hd;
+    if (x->tp_world <= 1) {
+        x->dn_hl = (int)H;
+        x->kv_hl = (int)Hkv;
+    }
+    x->s_stride = (int64_t)x->dn_hl * 128 * 128;  // this rank's heads only
+    x->conv_stride = 3 * D * c.conv_k;             // every channel (a rank updates its heads')
+    x->kv_slot = x->kv_hl * (int64_t)x->cap * hd;
     const size_t kvel = x->kv_bf16 ? 2 : 4;
     RET(x->dalloc(&x->dn_S, (size_t)std::max<int64_t>(c.n_dn, 1) * B * x->s_stride * 4));
     RET(x->dalloc(&x->dn_conv, (size_t)std::max<int64_t>(c.n_dn, 1) * B * x->conv_stride * 4));
@@ -679,20 +756,21 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     if (x->use_umma) RET(x->dalloc(&x->h2, (size_t)B * 2 * F * 4));
     if (c.n_attn > 0) {
         size_t aws = 0;
+        const int hkl = x->kv_hl;
         for (int b = 1; b <= B; b++) {
-            const int ns = x->kv_bf16 ? attn_mma_nsplit_bound(b, (int)Hkv, x->cap, x->num_sms)
-                                      : attn_nsplit_bound(b, (int)Hkv, x->cap, x->num_sms);
-            aws = std::max(aws, attn_ws_floats(b, (int)Hkv, ns, (int)hd, (int)(Hq / Hkv)));
+            const int ns = x->kv_bf16 ? attn_mma_nsplit_bound(b, hkl, x->cap, x->num_sms)
+                                      : attn_nsplit_bound(b, hkl, x->cap, x->num_sms);
+            aws = std::max(aws, attn_ws_floats(b, hkl, ns, (int)hd, (int)(Hq / Hkv)));
         }
         x->aws_floats = aws;
         if (x->kv_bf16) {
-            const int64_t rows = c.n_attn * (int64_t)B * Hkv * x->cap;
+            const int64_t rows = c.n_attn * (int64_t)B * x->kv_hl * x->cap;
             if (make_kv_tensor_map(x->tmap_k, x->kc, rows, (int)hd) || make_kv_tensor_map(x->tmap_v, x->vc, rows, (int)hd))
                 return seterr(AB2_ERR_CUDA, "could not encode the TMA tensor maps of the KV cache");
         }
         RET(x->dalloc(&x->aws, aws * 4));
         if (x->kv_bf16) RET(x->dalloc(&x->aqp, (size_t)B * Hq * hd * 4));
-        RET(x->dalloc(&x->atk, (size_t)B * Hkv * 4));
+        RET(x->dalloc(&x->atk, (size_t)B * x->kv_hl * 4));
         // RoPE (cos, sin) table built with the host libm exactly as the reference computes it:
         // freq = 1 / base^(i / rot) for even i, angle = pos * freq (deltanet.rs:600-623)
         const int hr = x->rot / 2;
@@ -818,7 +896,7 @@ GemmEpi epi_swiglu(const ActOut& out, int F) {
 // max_len; 0 without attention layers
 int step_attn_chunk(const ab2_ctx* x, int B, int max_len) {
     if (x->c.n_attn == 0) return 0;
-    const int hkv = (int)x->c.n_kv;
+    const int hkv = x->kv_hl;
     return x->kv_bf16 ? attn_mma_chunk(B, hkv, max_len, x->num_sms) : attn_chunk(B, hkv, max_len, x->num_sms);
 }
 
@@ -844,7 +922,9 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.ssm_norm = L.ssm_norm;
         p.eps = c.eps;
         p.D = D;
-        p.H = (int)c.dn_heads;
+        p.H = x->dn_hl;
+        p.h0 = x->dn_h0;
+        p.H_all = (int)c.dn_heads;
         p.out = act(x, x->xfb, D, B);
         p.o_out = nullptr;
         p.err = x->err_d;
@@ -866,12 +946,14 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.cap = x->cap;
         p.pos = x->pos_d + s0;
         p.Hq = (int)c.n_heads;
-        p.Hkv = (int)c.n_kv;
+        p.Hkv = x->kv_hl;
+        p.kvh0 = x->kv_h0;
+        p.Hkv_all = (int)c.n_kv;
         p.chunk = step_attn_chunk(x, B, max_len);
         // a replayed step graph keeps this plan while the longest context stays within its
         // split count, so every position up to the plan's last covered token is valid
         p.max_pos = std::min(x->cap - 1, attn_nsplit(max_len, p.chunk) * p.chunk - 1);
-        if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv) > x->aws_floats)
+        if (attn_ws_floats(B, p.Hkv, attn_nsplit(max_len, p.chunk), (int)c.hd, p.Hq / p.Hkv_all) > x->aws_floats)
             return seterr(AB2_ERR_CAPACITY, "attention workspace too small for %d splits", attn_nsplit(max_len, p.chunk));
         p.ws = x->aws;
         p.qprep = x->aqp;
@@ -884,7 +966,7 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
             // bf16 cache: TMA + tensor-core flash-decode; rows of (layer, slot s0, head 0, token 0).
             // Profiling times the attention kernel alone (its query prep and split merge are
             // small launches of their own).
-            const int64_t row_base = ((int64_t)L.local * x->max_batch + s0) * c.n_kv * x->cap;
+            const int64_t row_base = ((int64_t)L.local * x->max_batch + s0) * x->kv_hl * x->cap;
             const auto ev = prof_pair(x, PC_ATTN);
             if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, x->num_sms, st,
                                      ev.first, ev.second))
@@ -894,6 +976,17 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
             if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st))
                 return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
         }
+    }
+    if (L.dn ? x->dn_split : x->kv_split) {
+        // head-parallel split: every rank wrote its heads' columns of the output projection's
+        // activations; gather the other ranks' columns in place. Both activation layouts are
+        // K-block-major, so a rank's columns are one contiguous byte range.
+        const int K = L.dn ? D : (int)(c.n_heads * c.hd);
+        const ActOut o = act(x, x->xfb, K, B);
+        const size_t chunk = o.x16 ? (size_t)(K / x->tp_world / 64) * o.npad * 128
+                                   : (size_t)(K / x->tp_world / 32) * o.xs.ntile * 512;
+        ProfScope ps(x, PC_OTHER, st);
+        NCK(nccl_api().all_gather(x->xfb + x->tp_rank * chunk, x->xfb, chunk, ncclUint8, x->nccl, st));
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
     set_prefetch(x, B, &L.gate_up, &e.pf, &e.pf_bytes);
@@ -1064,7 +1157,7 @@ int64_t launches_per_step(const ab2_ctx* x, int B) {
         // the tensor-core attention adds a merge kernel when the current context is split
         int max_len = 1;
         for (int b = 0; b < B && b < (int)x->pos_h.size(); b++) max_len = std::max(max_len, (int)x->pos_h[b] + 1);
-        const int chunk = attn_mma_chunk(B, (int)x->c.n_kv, max_len, x->num_sms);
+        const int chunk = attn_mma_chunk(B, x->kv_hl, max_len, x->num_sms);
         n += x->c.n_attn * (attn_mma_launches(max_len, chunk) - 1);
     }
     return n;
@@ -1156,8 +1249,8 @@ AB2_API int ab2_gguf_inspect(const uint8_t* gguf, uint64_t len, ab2_config* out)
     return 0;
 }
 
-AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
-                       const ab2_options* opt, ab2_ctx** out) {
+static int create_ctx(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
+                      const ab2_options* opt, int tp_rank, int tp_world, const uint8_t* tp_id, ab2_ctx** out) {
     if (!out) return seterr(AB2_ERR_ARG, "null output pointer");
     *out = nullptr;
     if (max_batch < 1 || max_batch > 64) return seterr(AB2_ERR_ARG, "max_batch must be in [1, 64]");
@@ -1189,11 +1282,23 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
     x->rot = opt ? opt->rope_dims : 0;
     x->exact_max = opt && opt->exact_max_batch > 0 ? opt->exact_max_batch : 1;
     x->use_umma = max_batch > x->exact_max;
+    x->tp_rank = tp_rank;
+    x->tp_world = tp_world;
     cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device);
     int rc = 0;
     if (cudaStreamCreateWithFlags(&x->stream, cudaStreamNonBlocking) != cudaSuccess)
         rc = seterr(AB2_ERR_CUDA, "cudaStreamCreate failed");
     if (!rc) rc = build_context(x, gguf, len);
+    if (!rc && tp_world > 1) {
+        // every rank reaches this call after its own (identical) model checks; it returns once
+        // all tp_world ranks have joined
+        ncclUniqueId id;
+        memcpy(id.internal, tp_id, sizeof id.internal);
+        ncclComm_t comm = nullptr;
+        const ncclResult_t nr = nccl_api().comm_init_rank(&comm, tp_world, id, tp_rank);
+        if (nr != ncclSuccess) rc = seterr(AB2_ERR_CUDA, "ncclCommInitRank: %s", nccl_api().error_string(nr));
+        else x->nccl = comm;
+    }
     if (rc) {
         std::string keep = g_err;
         ab2_destroy(x);
@@ -1204,10 +1309,57 @@ AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_ba
     return 0;
 }
 
+AB2_API int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
+                       const ab2_options* opt, ab2_ctx** out) {
+    return create_ctx(gguf, len, device, max_batch, max_ctx, opt, 0, 1, nullptr, out);
+}
+
+AB2_API int ab2_tp_unique_id(uint8_t* id, uint64_t len) {
+    if (!id || len < AB2_TP_ID_BYTES) return seterr(AB2_ERR_ARG, "the id buffer needs %d bytes", AB2_TP_ID_BYTES);
+    const NcclApi& n = nccl_api();
+    if (!n.why.empty()) return seterr(AB2_ERR_DEVICE, "%s", n.why.c_str());
+    ncclUniqueId u;
+    NCK(n.get_unique_id(&u));
+    static_assert(sizeof u.internal == AB2_TP_ID_BYTES, "NCCL unique id size");
+    memcpy(id, u.internal, AB2_TP_ID_BYTES);
+    return 0;
+}
+
+AB2_API int ab2_create_tp(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
+                          const ab2_options* opt, int tp_rank, int tp_world, const uint8_t* tp_id, uint64_t id_len,
+                          ab2_ctx** out) {
+    if (!out) return seterr(AB2_ERR_ARG, "null output pointer");
+    *out = nullptr;
+    if (tp_world < 1 || tp_world > 8) return seterr(AB2_ERR_ARG, "tp_world must be in [1, 8]");
+    if (tp_rank < 0 || tp_rank >= tp_world) return seterr(AB2_ERR_ARG, "tp_rank %d outside [0, %d)", tp_rank, tp_world);
+    if (tp_world > 1 && (!tp_id || id_len != AB2_TP_ID_BYTES))
+        return seterr(AB2_ERR_ARG, "tp_id must hold the %d bytes of ab2_tp_unique_id", AB2_TP_ID_BYTES);
+    if (tp_world > 1) {
+        const NcclApi& n = nccl_api();
+        if (!n.why.empty()) return seterr(AB2_ERR_DEVICE, "%s", n.why.c_str());
+    }
+    return create_ctx(gguf, len, device, max_batch, max_ctx, opt, tp_rank, tp_world, tp_id, out);
+}
+
+AB2_API int ab2_get_tp(ab2_ctx* x, int32_t out[6]) {
+    if (!x || !out) return seterr(AB2_ERR_ARG, "null argument");
+    out[0] = x->tp_rank;
+    out[1] = x->tp_world;
+    out[2] = x->dn_h0;
+    out[3] = x->dn_hl;
+    out[4] = x->kv_h0;
+    out[5] = x->kv_hl;
+    return 0;
+}
+
 AB2_API void ab2_destroy(ab2_ctx* x) {
     if (!x) return;
     DeviceGuard dev_guard(x->device);
     if (x->stream) cudaStreamSynchronize(x->stream);
+    // graphs that hold the split's collectives go before its communicator
+    graphs_clear(x);
+    if (x->nccl) nccl_api().comm_destroy(x->nccl);
+    x->nccl = nullptr;
     for (void* p : x->allocs) cudaFree(p);
     if (x->tok_h) cudaFreeHost(x->tok_h);
     if (x->next_h) cudaFreeHost(x->next_h);
@@ -1300,7 +1452,11 @@ static int dn_state_io(ab2_ctx* x, int layer, int slot, float* rec, float* conv,
     float* S = x->dn_S + ((size_t)L->local * x->max_batch + slot) * x->s_stride;
     float* C = x->dn_conv + ((size_t)L->local * x->max_batch + slot) * x->conv_stride;
     auto kind = set ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
-    if (rec) CK(cudaMemcpyAsync(set ? (void*)S : rec, set ? (const void*)rec : S, x->s_stride * 4, kind, x->stream));
+    // the host arrays hold every head; a head-parallel rank moves its own heads' part of the
+    // recurrent state [H][128][128] only (and the whole conv state, of which it updates the
+    // channels of its heads)
+    float* rec_h = rec ? rec + (size_t)x->dn_h0 * 128 * 128 : nullptr;
+    if (rec) CK(cudaMemcpyAsync(set ? (void*)S : rec_h, set ? (const void*)rec_h : S, x->s_stride * 4, kind, x->stream));
     if (conv) CK(cudaMemcpyAsync(set ? (void*)C : conv, set ? (const void*)conv : C, x->conv_stride * 4, kind, x->stream));
     CK(cudaStreamSynchronize(x->stream));
     return 0;
@@ -1331,16 +1487,17 @@ static int kv_io(ab2_ctx* x, int layer, int slot, float* k, float* v, int64_t n,
     if (L->dn) return seterr(AB2_ERR_ARG, "layer %d is not an attention layer", layer);
     if (n < 0 || n > x->cap) return seterr(AB2_ERR_ARG, "n_tokens %lld outside [0, %d]", (long long)n, x->cap);
     if (!k || !v) return seterr(AB2_ERR_ARG, "null k/v");
-    const int64_t Hkv = x->c.n_kv, hd = x->c.hd;
+    const int64_t hd = x->c.hd;
     const size_t kvel = x->kv_bf16 ? 2 : 4;
     const size_t rowb = (size_t)n * hd * kvel;
     std::vector<uint8_t> tmp(rowb);
     for (int which = 0; which < 2; which++) {
         float* host = which ? v : k;
         uint8_t* dev = (uint8_t*)(which ? x->vc : x->kc) + ((size_t)L->local * x->max_batch + slot) * x->kv_slot * kvel;
-        for (int64_t h = 0; h < Hkv; h++) {
+        // the host arrays hold every kv head; a head-parallel rank moves its own heads only
+        for (int64_t h = 0; h < x->kv_hl; h++) {
             uint8_t* d = dev + (size_t)h * x->cap * hd * kvel;
-            float* hp = host + (size_t)h * n * hd;
+            float* hp = host + (size_t)(x->kv_h0 + h) * n * hd;
             if (set) {
                 if (x->kv_bf16) {
                     uint16_t* t = (uint16_t*)tmp.data();
@@ -1381,20 +1538,33 @@ AB2_API int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tok
     DeviceGuard dev_guard(x->device);
     CK(dev_guard.err);
     const Cfg& c = x->c;
+    // every value is a function of its index in the full (all heads) state, so a head-parallel
+    // rank seeds exactly its heads' part of what one GPU seeds
+    const bool whole_dn = x->dn_hl == (int)c.dn_heads, whole_kv = x->kv_hl == (int)c.n_kv;
+    const int64_t s_all = c.dn_heads * 128 * 128;
     for (int64_t i = 0; i < c.n_dn; i++) {
-        launch_seed_f32(x->dn_S + (size_t)i * x->max_batch * x->s_stride, (int64_t)n_slots * x->s_stride, seed,
-                        (uint64_t)(3 * i), dn_std, x->stream);
+        float* S = x->dn_S + (size_t)i * x->max_batch * x->s_stride;
+        if (whole_dn) {
+            launch_seed_f32(S, (int64_t)n_slots * x->s_stride, seed, (uint64_t)(3 * i), dn_std, x->stream);
+        } else {
+            for (int s = 0; s < n_slots; s++)
+                launch_seed_f32(S + (size_t)s * x->s_stride, x->s_stride, seed, (uint64_t)(3 * i), dn_std, x->stream,
+                                s * s_all + (int64_t)x->dn_h0 * 128 * 128);
+        }
         launch_seed_f32(x->dn_conv + (size_t)i * x->max_batch * x->conv_stride, (int64_t)n_slots * x->conv_stride,
                         seed, (uint64_t)(3 * i + 1), conv_std, x->stream);
     }
     const size_t kvel = x->kv_bf16 ? 2 : 4;
-    const int64_t rows = (int64_t)n_slots * c.n_kv * x->cap;
     for (int64_t i = 0; i < c.n_attn; i++) {
-        size_t off = (size_t)i * x->max_batch * x->kv_slot * kvel;
-        launch_seed_kv((uint8_t*)x->kc + off, x->kv_bf16, rows, x->cap, n_tokens, (int)c.hd, seed,
-                       (uint64_t)(1000 + 2 * i), kv_std, x->stream);
-        launch_seed_kv((uint8_t*)x->vc + off, x->kv_bf16, rows, x->cap, n_tokens, (int)c.hd, seed,
-                       (uint64_t)(1001 + 2 * i), kv_std, x->stream);
+        for (int s = 0; s < (whole_kv ? 1 : n_slots); s++) {
+            const size_t off = ((size_t)i * x->max_batch + s) * x->kv_slot * kvel;
+            const int64_t rows = whole_kv ? (int64_t)n_slots * c.n_kv * x->cap : (int64_t)x->kv_hl * x->cap;
+            const int64_t i0 = whole_kv ? 0 : ((int64_t)s * c.n_kv + x->kv_h0) * x->cap * c.hd;
+            launch_seed_kv((uint8_t*)x->kc + off, x->kv_bf16, rows, x->cap, n_tokens, (int)c.hd, seed,
+                           (uint64_t)(1000 + 2 * i), kv_std, x->stream, i0);
+            launch_seed_kv((uint8_t*)x->vc + off, x->kv_bf16, rows, x->cap, n_tokens, (int)c.hd, seed,
+                           (uint64_t)(1001 + 2 * i), kv_std, x->stream, i0);
+        }
     }
     CK(cudaGetLastError());
     CK(cudaStreamSynchronize(x->stream));

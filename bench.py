@@ -16,6 +16,13 @@ API, the roofline of the dominant kernel family with the other two beside it, th
 baseline and the SM clocks seen.
 `--impl reference` times the CPU restatement of the reference decode path (oracle/) on the
 host cores for the same metric.
+
+    torchrun --nproc-per-node N bench.py --gpus N --split heads --batch 1 [--ctx C]
+
+times the head-parallel split instead (every rank runs the --batch sequences with 1/N of the
+DeltaNet and kv heads, the mixer outputs all-gathered with NCCL): one JSON line with the
+decode-step latency (max over ranks); with N = 1 the same step on one GPU, which is also what
+sequence sharding gives one sequence at any N.
 """
 from __future__ import annotations
 
@@ -434,6 +441,104 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_split(args):
+    """Decode-step latency of the head-parallel split over the torchrun ranks (N = 1: one GPU,
+    unsplit). Device-resident steps timed with CUDA events (max over ranks), plus the same
+    steps through the host-buffer API."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    pkg = load_pkg()
+    from ane_infer_b200 import synth
+    from ane_infer_b200.heads import open_split_context
+    from ane_infer_b200.shard import max_over_ranks
+    shape = synth.shape_2b()
+    gguf = synth.build_model_gguf(shape, seed=0)
+    B = args.batch
+    n_e2e = max(2, args.steps // 2)
+    cap = args.ctx + args.warmup + 2 * args.steps + n_e2e + 16
+    if world > 1:
+        ctx = open_split_context(gguf, local, B, cap)
+    else:
+        ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap)
+    split = ctx.split()
+    cfg = ctx.config
+    # every rank seeds its part of one state and feeds the same tokens
+    ctx.seed_state(seed=1, n_slots=B, n_tokens=args.ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
+    ctx.step_graph(bool(args.graph))
+    stream = torch.cuda.Stream(device=local)
+    torch.cuda.set_stream(stream)
+    tok = [torch.from_numpy(synth.seeded_tokens(B, cfg["vocab"], seed=2)).cuda(),
+           torch.empty(B, dtype=torch.int32, device="cuda")]
+    logits = torch.empty((B, cfg["vocab"]), dtype=torch.float32, device="cuda")
+
+    def dev_steps(n, i0=0):
+        for i in range(n):
+            ctx.decode_step_device(tok[(i0 + i) % 2], B, logits, tok[(i0 + i + 1) % 2], stream)
+
+    dev_steps(args.warmup)
+    barrier()
+    clock = ClockSampler(gpu_id_for(torch, local))
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    dev_steps(args.steps, args.warmup)
+    e1.record(stream)
+    barrier()
+    clocks = clock.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+
+    host_tok = synth.seeded_tokens(B, cfg["vocab"], seed=5)
+    _, host_tok = ctx.decode_step(host_tok, want_logits=False)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        _, host_tok = ctx.decode_step(host_tok, want_logits=False)
+    barrier()
+    ctx.sync()
+    e2e_ms = max_over_ranks(time.perf_counter() - t0) * 1e3 / n_e2e
+    if rank == 0:
+        tc = ctx.tensor_core_gemm(B)
+        print(json.dumps({
+            "metric": f"decode step latency, 2B-shape Q8_0 B={B} ctx {args.ctx}, head-parallel split",
+            "value": round(ms, 4), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "f16 MMA operands (q*d rounded once), f32 accumulate, bf16 KV" if tc else
+                     "exact Q8_0 weights x f16 hi/lo activations, f32 accumulate, bf16 KV",
+            "data": "synthetic (seeded random Q8_0 weights, seeded DeltaNet/conv state, N(0,1) bf16 KV)",
+            "config": {"workload": f"2B-shape Qwen3.5 hybrid greedy decode, Q8_0, {B} sequence(s), "
+                                   f"ctx {args.ctx} prefilled bf16 KV",
+                       "model": "qwen35-hybrid-2B-shape (random init)", "global_batch": B, "seq_len": args.ctx,
+                       "parallelism": (f"head-parallel x{world}: DeltaNet heads {split['dn_heads']} and kv heads "
+                                       f"{split['kv_heads']} per GPU, NCCL all-gather after each split mixer")
+                                      if world > 1 else "one GPU (sequence sharding of one sequence)",
+                       "step_graph": bool(args.graph)},
+            "e2e": {"value": round(e2e_ms, 4), "unit": "ms/step", "h2d_bytes_per_step": 4 * B,
+                    "d2h_bytes_per_step": 4 * B, "steps": n_e2e},
+            "gpu_launches": ctx.launches_per_step(B) * args.steps,
+            "clocks": clocks,
+        }), flush=True)
+    ctx.close()  # its step graphs and NCCL communicator go before the process group
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 # --------------------------------------------------------------------------- op benchmarks
 def cpu_op_baseline(op: str, B: int, M: int = 0, K: int = 0, ctx: int = 0, seconds: float = 5.0, blocks=None):
     """The oracle (CPU restatement of the reference, all host threads) on the op of BASELINE
@@ -587,11 +692,15 @@ def main():
     ap.add_argument("--m", type=int, default=6144)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--split", choices=["sequences", "heads"], default="sequences",
+                    help="heads: time the head-parallel split's decode-step latency (use --batch 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.op:
         run_op(args)
+    elif args.split == "heads" and args.impl == "ours":
+        run_split(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -72,6 +72,29 @@ int ab2_create(const uint8_t* gguf, uint64_t len, int device, int max_batch, int
                const ab2_options* opt, ab2_ctx** out);
 void ab2_destroy(ab2_ctx* ctx);
 int ab2_get_config(ab2_ctx* ctx, ab2_config* out);
+
+/* ---- head-parallel split over tp_world GPUs (one process or thread per GPU) ---------- *
+ * No reference counterpart: the reference runs one device (README.md:258). Each rank holds
+ * every weight, runs the DeltaNet heads [rank*H/W, (rank+1)*H/W) and the kv heads
+ * [rank*Hkv/W, (rank+1)*Hkv/W) with their query heads, and keeps only those heads'
+ * recurrent state and KV cache; after each split mixer the ranks all-gather its output over
+ * NCCL (loaded at run time: libnccl.so.2, or the file AB2_NCCL_LIB names). A mixer kind whose
+ * heads do not divide over the ranks, or attention with an f32 cache, runs replicated on
+ * every rank. Every rank makes the same calls with the same arguments (tokens, slots,
+ * positions) in the same order; each returns the full logits / next tokens.
+ * State I/O (ab2_{set,get}_dn_state, ab2_{set,get}_kv) keeps its full-size host arrays and
+ * moves the rank's own heads' part of them; ab2_seed_state seeds each rank's part of what
+ * one GPU seeds. */
+#define AB2_TP_ID_BYTES 128
+/* A fresh id for one split (ncclGetUniqueId); made on one rank and passed to all. */
+int ab2_tp_unique_id(uint8_t* id, uint64_t id_len);
+/* ab2_create for rank tp_rank of tp_world (1..8); returns once all ranks have joined.
+ * tp_world = 1 is ab2_create (id may be NULL). */
+int ab2_create_tp(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
+                  const ab2_options* opt, int tp_rank, int tp_world, const uint8_t* tp_id,
+                  uint64_t id_len, ab2_ctx** out);
+/* out = {tp_rank, tp_world, first DeltaNet head, DeltaNet heads, first kv head, kv heads}. */
+int ab2_get_tp(ab2_ctx* ctx, int32_t out[6]);
 /* 1 if `layer` is a Gated DeltaNet layer (GgufFile::is_deltanet_layer, parser.rs:483). */
 int ab2_layer_is_deltanet(ab2_ctx* ctx, int layer);
 

@@ -197,3 +197,16 @@ def test_create_rejects_bad_exact_max_batch(pkg, tiny_gguf):
         with pytest.raises(pkg.Ab2Error) as ei:
             pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=8, exact_max_batch=bad)
         assert ei.value.code == -1 and "exact_max_batch" in str(ei.value)
+
+
+def test_create_tp_rejects_bad_arguments_on_the_host(pkg, tiny_gguf):
+    """The head-parallel entry point checks rank, world and id before it loads NCCL or touches
+    a device."""
+    for tp, what in (((2, 2, bytes(128)), "tp_rank"), ((-1, 2, bytes(128)), "tp_rank"),
+                     ((0, 9, bytes(128)), "tp_world"), ((0, 0, bytes(128)), "tp_world"),
+                     ((0, 2, None), "tp_id"), ((1, 2, bytes(64)), "tp_id")):
+        with pytest.raises(pkg.Ab2Error) as ei:
+            pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=8, tp=tp)
+        assert ei.value.code == -1 and what in str(ei.value), (tp, str(ei.value))
+    buf = (C.c_uint8 * 64)()
+    assert pkg.load_library().ab2_tp_unique_id(C.cast(buf, C.c_void_p), 64) == -1  # needs 128 bytes
