@@ -287,7 +287,8 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
                 mbar_arrive_expect_tx(&q_full[qs], kQBytes);
                 bulk_g2s(smem + L::q_off(qs), p.qprep + (size_t)pair * kGQ * HD, kQBytes, &q_full[qs]);
                 k++;
-                const int rows0 = (int)(row_base + (int64_t)pair * p.cap + it.t0);
+                const int64_t seq_rows = p.seq_rows < 0 ? (int64_t)p.Hkv * p.cap : p.seq_rows;
+                const int rows0 = (int)(row_base + it.b * seq_rows + (int64_t)it.kvh * p.cap + it.t0);
                 for (int t = 0; t < it.ntiles; t++, i++) {
                     const int s = i % kAttnStages;
                     if (i >= kAttnStages && !mbar_wait(&empty[s], ((i / kAttnStages) - 1) & 1, WL)) {

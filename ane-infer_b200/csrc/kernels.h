@@ -123,6 +123,8 @@ constexpr int kArgmaxChunks = 32;
 void launch_argmax2(const float* logits, int ld, int V, int batch, int32_t* out, int2* part, int nch,
                     cudaStream_t st);
 void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st);
+// pos[i] = p0 + i for i < n (the positions of a prefill chunk's tokens)
+void launch_pos_fill(int32_t* pos, int p0, int n, cudaStream_t st);
 void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st,
                      int64_t i0 = 0);
 void launch_seed_kv(void* dst, bool bf16, int64_t rows, int cap, int64_t n_tokens, int hd, uint64_t seed,
@@ -153,6 +155,11 @@ struct DnParams {
     WaitTest wt{};             // wait limit and the test hook
 };
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
+// dn_prefill.cu: the DeltaNet mixer of `tokens` (<= kPrefillChunk) consecutive tokens of one
+// sequence (proj and out rows are tokens; S and conv point at that sequence's state); chunked
+// form of the recurrence. Returns 0, or -1 for an unsupported shape, -2 for a launch failure.
+constexpr int kPrefillChunk = 64;
+int launch_dn_prefill(const DnParams& p, int tokens, cudaStream_t st);
 // recurrence core only (op API): q,k,v bf16 [B][H][128], beta/decay f32 [B][H], o f32 [B][H][128]
 void launch_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,
                         const float* decay, int B, int H, float* o, cudaStream_t st);
@@ -172,6 +179,10 @@ struct AttnParams {
     const int32_t* pos;  // [B] position of the new token per slot
     int Hq, Hkv;         // Hq: every query head (the projection layout); Hkv: the kv heads this launch runs
     int kvh0 = 0;        // index in the model of its first kv head (head-parallel split; 0 otherwise)
+    // cache rows (tokens) between consecutive sequences in the tensor map of the bf16 cache:
+    // -1 = Hkv * cap (each sequence its own slot); 0 = every query row reads one shared slot
+    // (the prefill of one sequence's tokens, kv_slot_stride 0 likewise)
+    int64_t seq_rows = -1;
     int Hkv_all = 0;     // kv heads of the model (0: = Hkv); the caches hold only this launch's Hkv
     int chunk;           // tokens per split
     float* ws;           // split partials

@@ -246,6 +246,15 @@ void launch_pos_advance(int32_t* pos, int batch, cudaStream_t st) {
     pos_advance_kernel<<<(batch + 127) / 128, 128, 0, st>>>(pos, batch);
 }
 
+__global__ void pos_fill_kernel(int32_t* pos, int p0, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) pos[i] = p0 + i;
+}
+
+void launch_pos_fill(int32_t* pos, int p0, int n, cudaStream_t st) {
+    pos_fill_kernel<<<(n + 127) / 128, 128, 0, st>>>(pos, p0, n);
+}
+
 void launch_seed_f32(float* dst, int64_t n, uint64_t seed, uint64_t stream, float std, cudaStream_t st,
                      int64_t i0) {
     int64_t blocks = (n + 255) / 256;

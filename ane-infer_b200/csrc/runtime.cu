@@ -902,8 +902,10 @@ int step_attn_chunk(const ab2_ctx* x, int B, int max_len) {
 
 // mixer of layer L on the activation fragments in xfa (batch B starting at slot s0);
 // the mixer output goes to `out` with epilogue `mode` (RESID into x, or STORE)
+// With pf_p0 >= 0 the B rows are consecutive prompt tokens of sequence s0 at positions
+// pf_p0.. (a prefill chunk): the chunked DeltaNet kernel, and attention over one shared slot.
 int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out, int ldo, int mode,
-              cudaStream_t st) {
+              cudaStream_t st, int64_t pf_p0 = -1) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
     RET(gemm(x, L.w_in, x->xfa, B, epi_store(x->proj, x->ldp, L.w_in.M), st));
@@ -930,7 +932,8 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.err = x->err_d;
         set_prefetch(x, B, &L.w_out, &p.pf, &p.pf_bytes);
         ProfScope ps(x, PC_DN, st);
-        launch_deltanet(p, B, st);
+        if (pf_p0 < 0) launch_deltanet(p, B, st);
+        else if (launch_dn_prefill(p, B, st)) return seterr(AB2_ERR_SHAPE, "DeltaNet prefill: unsupported shape");
     } else {
         const size_t kvel = x->kv_bf16 ? 2 : 4;
         AttnParams p;
@@ -944,7 +947,13 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.vc = (uint8_t*)x->vc + ((size_t)L.local * x->max_batch + s0) * x->kv_slot * kvel;
         p.kv_slot_stride = x->kv_slot;
         p.cap = x->cap;
-        p.pos = x->pos_d + s0;
+        p.pos = pf_p0 >= 0 ? x->pf_pos : x->pos_d + s0;
+        if (pf_p0 >= 0) {
+            // the chunk's tokens are rows of one sequence: every row reads (and the query prep
+            // appends to) slot s0's cache
+            p.kv_slot_stride = 0;
+            p.seq_rows = 0;
+        }
         p.Hq = (int)c.n_heads;
         p.Hkv = x->kv_hl;
         p.kvh0 = x->kv_h0;
@@ -1028,14 +1037,16 @@ int check_capacity(ab2_ctx* x, int B, int* max_len) {
     return 0;
 }
 
-// the kernels of one decode step, enqueued on st (or captured, when st is capturing)
-int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
-                    cudaStream_t st) {
+// Embedding and every layer over B rows of the residual stream: the B sequences (slots
+// [0, B)) of a decode step, or, with pf_p0 >= 0, B consecutive prompt tokens of sequence
+// `slot` at positions pf_p0, pf_p0 + 1, ... (a prefill chunk)
+int enqueue_body(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, int slot, int64_t pf_p0, cudaStream_t st) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
     {
         ProfScope ps(x, PC_OTHER, st);
         launch_embed(x->embed, (int)c.vocab, tok_d, B, x->x, D, st);
+        if (pf_p0 >= 0) launch_pos_fill(x->pf_pos, (int)pf_p0, B, st);
     }
     const ActOut xa = act(x, x->xfa, D, B);
     for (size_t li = 0; li < x->layers.size(); li++) {
@@ -1048,7 +1059,7 @@ int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float*
             launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st, z0 < L.w_in.M ? x->proj + z0 : nullptr,
                                x->ldp, (int)(L.w_in.M - z0));
         }
-        RET(run_mixer(x, L, 0, B, max_len, x->x, D, EPI_RESID, st));
+        RET(run_mixer(x, L, pf_p0 >= 0 ? slot : 0, B, max_len, x->x, D, EPI_RESID, st, pf_p0));
         {
             // on the tcgen05 path the gate/up projection adds into h2: clear it
             const int F2 = 2 * (int)c.ffn;
@@ -1057,19 +1068,37 @@ int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float*
         }
         RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next));
     }
+    return 0;
+}
+
+// final norm of the B residual rows at xrows, lm_head into logits_d [B][vocab], argmax
+int enqueue_head(ab2_ctx* x, const float* xrows, int B, float* logits_d, int32_t* next_d, cudaStream_t st) {
+    const Cfg& c = x->c;
+    const int D = (int)c.dim;
     {
         // the lm_head's split units (all of them for small vocabularies, the K pieces of its
         // last pairs for large ones) add into the logits: clear those columns first
         const int64_t V = c.vocab;
         const int64_t z0 = umma_for(x, B) ? umma_plan(x->lm_head.MT, x->lm_head.KT, V, x->num_sms).zero_row0 : V;
         ProfScope ps(x, PC_OTHER, st);
-        launch_rmsnorm_act(x->x, D, x->final_norm, D, c.eps, B, xa, st, z0 < V ? logits_d + z0 : nullptr, (int)V,
-                           (int)(V - z0));
+        launch_rmsnorm_act(xrows, D, x->final_norm, D, c.eps, B, act(x, x->xfa, D, B), st,
+                           z0 < V ? logits_d + z0 : nullptr, (int)V, (int)(V - z0));
     }
     RET(gemm(x, x->lm_head, x->xfa, B, epi_store(logits_d, (int)c.vocab, c.vocab), st));
+    if (next_d) {
+        ProfScope ps(x, PC_OTHER, st);
+        launch_argmax2(logits_d, (int)c.vocab, (int)c.vocab, B, next_d, x->amax_part, kArgmaxChunks, st);
+    }
+    return 0;
+}
+
+// the kernels of one decode step, enqueued on st (or captured, when st is capturing)
+int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
+                    cudaStream_t st) {
+    RET(enqueue_body(x, tok_d, B, max_len, 0, -1, st));
+    RET(enqueue_head(x, x->x, B, logits_d, next_d, st));
     {
         ProfScope ps(x, PC_OTHER, st);
-        if (next_d) launch_argmax2(logits_d, (int)c.vocab, (int)c.vocab, B, next_d, x->amax_part, kArgmaxChunks, st);
         launch_pos_advance(x->pos_d, B, st);
     }
     CK(cudaGetLastError());
