@@ -77,6 +77,7 @@ SIGNATURES = {
     "ab2_seed_state": (C.c_int, [_vp, _u64, C.c_int, _i64, C.c_float, C.c_float, C.c_float]),
     "ab2_decode_step": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "ab2_decode_step_device": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp, _vp]),
+    "ab2_prefill": (C.c_int, [_vp, C.c_int, _vp, _i64, _vp, _vp]),
     "ab2_sync": (C.c_int, [_vp]),
     "ab2_op_error": (C.c_int, [C.POINTER(C.c_uint32)]),
     "ab2_debug_arm_wait_timeout": (C.c_int, [C.c_int, C.c_int, C.c_uint32]),
@@ -270,6 +271,16 @@ class DecodeContext:
         _check(load_library().ab2_decode_step(self._h, _hp(t), B, None if logits is None else _hp(logits),
                                               _hp(nxt)))
         return logits, nxt
+
+    def prefill(self, slot: int, tokens, want_logits: bool = True):
+        """Run a prompt through slot `slot` from its position on (chunks of 64 tokens on the
+        GPU); returns (logits of the last token [vocab] or None, its argmax)."""
+        t = _host(tokens, np.int32).reshape(-1)
+        nxt = np.zeros(1, dtype=np.int32)
+        logits = np.empty(self.config["vocab"], dtype=np.float32) if want_logits else None
+        _check(load_library().ab2_prefill(self._h, slot, _hp(t), t.size, None if logits is None else _hp(logits),
+                                          _hp(nxt)))
+        return logits, int(nxt[0])
 
     def decode_step_device(self, tokens_dev, batch: int, logits_dev=None, next_dev=None, stream=None):
         _check(load_library().ab2_decode_step_device(self._h, _dp(tokens_dev), batch, _dp(logits_dev),

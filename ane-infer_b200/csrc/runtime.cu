@@ -497,9 +497,13 @@ struct ab2_ctx {
     void* vc = nullptr;
     int32_t* pos_d = nullptr;   // [max_batch]
     std::vector<int64_t> pos_h;
+    int32_t* pf_pos = nullptr;  // [kPrefillChunk] positions of a prefill chunk's tokens
+    int32_t* pf_tok = nullptr;  // [kPrefillChunk] token ids of a prefill chunk
     int64_t s_stride = 0, conv_stride = 0, kv_slot = 0;
-    // scratch
-    float* x = nullptr;         // residual stream [max_batch][D]
+    // scratch, for `rows` = max(max_batch, kPrefillChunk) rows (sequences of a step, or
+    // tokens of a prefill chunk)
+    int rows = 0;
+    float* x = nullptr;         // residual stream [rows][D]
     float* proj = nullptr;      // [max_batch][ldp]
     int ldp = 0;
     uint8_t *xfa = nullptr, *xfb = nullptr;
@@ -721,15 +725,19 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     RET(x->dalloc(&x->pos_d, (size_t)B * 4));
     x->pos_h.assign(B, 0);
 
-    // ---- scratch
+    // ---- scratch (rows: the sequences of a step or the tokens of a prefill chunk)
+    const int R = std::max(B, kPrefillChunk);
+    x->rows = R;
+    RET(x->dalloc(&x->pf_pos, (size_t)kPrefillChunk * 4));
+    RET(x->dalloc(&x->pf_tok, (size_t)kPrefillChunk * 4));
     int64_t mproj = 0, maxk = D;
     for (auto& L : x->layers) mproj = std::max<int64_t>(mproj, L.w_in.M);
     maxk = std::max<int64_t>(maxk, F);
     maxk = std::max<int64_t>(maxk, Hq * hd);
     x->ldp = (int)((mproj + 3) / 4 * 4);
-    RET(x->dalloc(&x->x, (size_t)B * D * 4));
-    RET(x->dalloc(&x->proj, (size_t)B * x->ldp * 4));
-    const size_t actb = std::max(xfrag_bytes((int)maxk, B), x16_bytes((int)maxk, B));
+    RET(x->dalloc(&x->x, (size_t)R * D * 4));
+    RET(x->dalloc(&x->proj, (size_t)R * x->ldp * 4));
+    const size_t actb = std::max(xfrag_bytes((int)maxk, R), x16_bytes((int)maxk, R));
     RET(x->dalloc(&x->xfa, actb));
     RET(x->dalloc(&x->xfb, actb));
     RET(x->dalloc(&x->err_d, 16));
@@ -741,7 +749,7 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     size_t gws = 0;
     int gtk = 1;
     auto acc_gemm = [&](const Q8Weight& w) {
-        gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, B, x->num_sms));
+        gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, R, x->num_sms));
         gtk = std::max(gtk, gemm_grid_x(w.M16));
     };
     for (auto& L : x->layers) {
@@ -753,11 +761,11 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     acc_gemm(x->lm_head);
     RET(x->dalloc(&x->gws, gws * 4));
     RET(x->dalloc(&x->gtk, (size_t)gtk * 4));
-    if (x->use_umma) RET(x->dalloc(&x->h2, (size_t)B * 2 * F * 4));
+    if (x->use_umma) RET(x->dalloc(&x->h2, (size_t)R * 2 * F * 4));
     if (c.n_attn > 0) {
         size_t aws = 0;
         const int hkl = x->kv_hl;
-        for (int b = 1; b <= B; b++) {
+        for (int b = 1; b <= R; b++) {
             const int ns = x->kv_bf16 ? attn_mma_nsplit_bound(b, hkl, x->cap, x->num_sms)
                                       : attn_nsplit_bound(b, hkl, x->cap, x->num_sms);
             aws = std::max(aws, attn_ws_floats(b, hkl, ns, (int)hd, (int)(Hq / Hkv)));
@@ -769,8 +777,8 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
                 return seterr(AB2_ERR_CUDA, "could not encode the TMA tensor maps of the KV cache");
         }
         RET(x->dalloc(&x->aws, aws * 4));
-        if (x->kv_bf16) RET(x->dalloc(&x->aqp, (size_t)B * Hq * hd * 4));
-        RET(x->dalloc(&x->atk, (size_t)B * x->kv_hl * 4));
+        if (x->kv_bf16) RET(x->dalloc(&x->aqp, (size_t)R * Hq * hd * 4));
+        RET(x->dalloc(&x->atk, (size_t)R * x->kv_hl * 4));
         // RoPE (cos, sin) table built with the host libm exactly as the reference computes it:
         // freq = 1 / base^(i / rot) for even i, angle = pos * freq (deltanet.rs:600-623)
         const int hr = x->rot / 2;
@@ -1631,6 +1639,44 @@ AB2_API int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int B, float* log
     prof_collect(x);
     RET(take_device_error(x));
     if (next_tokens) memcpy(next_tokens, x->next_h, (size_t)B * 4);
+    return 0;
+}
+
+AB2_API int ab2_prefill(ab2_ctx* x, int slot, const int32_t* tokens, int64_t n, float* logits, int32_t* next_token) {
+    RET(check_slot(x, slot));
+    if (!tokens || n < 1) return seterr(AB2_ERR_ARG, "prefill needs at least one token");
+    DeviceGuard dev_guard(x->device);
+    CK(dev_guard.err);
+    const Cfg& c = x->c;
+    if (c.n_attn > 0 && !x->kv_bf16) return seterr(AB2_ERR_SHAPE, "prefill needs the bf16 KV cache");
+    if (c.n_dn > 0 && c.conv_k != 4) return seterr(AB2_ERR_SHAPE, "prefill supports conv kernel 4 only");
+    const int64_t p0 = x->pos_h[slot];
+    if (p0 + n > x->cap)
+        return seterr(AB2_ERR_CAPACITY, "slot %d: %lld prompt tokens at pos %lld exceed max_ctx %d", slot, (long long)n,
+                      (long long)p0, x->cap);
+    for (int64_t i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= c.vocab)
+            return seterr(AB2_ERR_ARG, "prompt token %lld (id %d) is outside [0, %lld)", (long long)i, tokens[i],
+                          (long long)c.vocab);
+    cudaStream_t st = x->stream;
+    // chunks of up to kPrefillChunk tokens, in stream order (each chunk's id copy follows the
+    // previous chunk's kernels on the stream)
+    for (int64_t t0 = 0; t0 < n; t0 += kPrefillChunk) {
+        const int T = (int)std::min<int64_t>(kPrefillChunk, n - t0);
+        CK(cudaMemcpyAsync(x->pf_tok, tokens + t0, (size_t)T * 4, cudaMemcpyHostToDevice, st));
+        RET(enqueue_body(x, x->pf_tok, T, (int)(p0 + t0 + T), slot, p0 + t0, st));
+        if (t0 + T == n) RET(enqueue_head(x, x->x + (size_t)(T - 1) * c.dim, 1, x->logits, x->next_d, st));
+    }
+    const int32_t pn = (int32_t)(p0 + n);
+    CK(cudaMemcpyAsync(x->pos_d + slot, &pn, 4, cudaMemcpyHostToDevice, st));
+    if (next_token) CK(cudaMemcpyAsync(x->next_h, x->next_d, 4, cudaMemcpyDeviceToHost, st));
+    if (logits) CK(cudaMemcpyAsync(logits, x->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(x->err_h, x->err_d, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    prof_collect(x);
+    x->pos_h[slot] = p0 + n;
+    RET(take_device_error(x));
+    if (next_token) *next_token = x->next_h[0];
     return 0;
 }
 

@@ -539,6 +539,57 @@ def run_split(args):
         dist.destroy_process_group()
 
 
+def run_prefill(args):
+    """Prefill throughput of one sequence on one GPU: --prefill N prompt tokens through
+    ab2_prefill (64-token chunks), prompt tokens per second from CUDA events on the context's
+    stream around each call (the call is synchronous; its host-to-device copy of the ids and
+    its device-to-host copy of the last logits are inside)."""
+    import torch
+    pkg = load_pkg()
+    from ane_infer_b200 import synth
+    shape = synth.shape_2b()
+    gguf = synth.build_model_gguf(shape, seed=0)
+    n = args.prefill
+    ctx = pkg.DecodeContext(gguf, device=0, max_batch=args.prefill_batch, max_ctx=n + 8, kv_bf16=True)
+    cfg = ctx.config
+    prompt = synth.seeded_tokens(n, cfg["vocab"], seed=3)
+    for _ in range(args.warmup):
+        ctx.reset_slot(0)
+        ctx.prefill(0, prompt, want_logits=False)
+    clock = ClockSampler(gpu_id_for(torch, 0))
+    time.sleep(0.3)
+    times = []
+    for _ in range(args.steps):
+        ctx.reset_slot(0)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ctx.prefill(0, prompt, want_logits=True)
+        times.append(time.perf_counter() - t0)
+    clocks = clock.stop()
+    ctx.profile(True)
+    ctx.reset_slot(0)
+    ctx.prefill(0, prompt, want_logits=False)
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    med = statistics.median(times)
+    tc = ctx.tensor_core_gemm(64)
+    print(json.dumps({
+        "metric": f"prefill tok/s, 2B-shape Q8_0, one sequence, {n}-token prompt",
+        "value": round(n / med, 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(med * 1e3, 3), "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+        "dtype": "f16 MMA operands (q*d rounded once), f32 accumulate, bf16 KV" if tc else
+                 "exact Q8_0 weights x f16 hi/lo activations, f32 accumulate, bf16 KV",
+        "data": "synthetic (seeded random Q8_0 weights and prompt ids)",
+        "config": {"workload": f"2B-shape Qwen3.5 hybrid prefill of {n} tokens in 64-token chunks",
+                   "model": "qwen35-hybrid-2B-shape (random init)", "max_batch": args.prefill_batch,
+                   "timing": "host wall clock around the synchronous call, median of steps"},
+        "kernel_ms": {k: round(v["ms"], 3) for k, v in prof.items()},
+        "gpu_launches_per_prefill": sum(v["launches"] for v in prof.values()),
+        "clocks": clocks,
+    }), flush=True)
+    ctx.close()
+
+
 # --------------------------------------------------------------------------- op benchmarks
 def cpu_op_baseline(op: str, B: int, M: int = 0, K: int = 0, ctx: int = 0, seconds: float = 5.0, blocks=None):
     """The oracle (CPU restatement of the reference, all host threads) on the op of BASELINE
@@ -692,6 +743,9 @@ def main():
     ap.add_argument("--m", type=int, default=6144)
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--prefill", type=int, default=0, help="time the prefill of this many prompt tokens instead")
+    ap.add_argument("--prefill-batch", type=int, default=64,
+                    help="max_batch of the prefill context (> 1: its GEMMs run on tcgen05)")
     ap.add_argument("--split", choices=["sequences", "heads"], default="sequences",
                     help="heads: time the head-parallel split's decode-step latency (use --batch 1)")
     args = ap.parse_args()
@@ -699,6 +753,8 @@ def main():
         args.warmup = 3
     if args.op:
         run_op(args)
+    elif args.prefill and args.impl == "ours":
+        run_prefill(args)
     elif args.split == "heads" and args.impl == "ours":
         run_split(args)
     elif args.impl == "reference":

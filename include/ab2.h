@@ -131,6 +131,16 @@ int ab2_seed_state(ab2_ctx* ctx, uint64_t seed, int n_slots, int64_t n_tokens, f
  * logits: [batch][vocab] or NULL; next_tokens: [batch] or NULL. Token ids outside
  * [0, vocab) are rejected with AB2_ERR_ARG before any work is queued. */
 int ab2_decode_step(ab2_ctx* ctx, const int32_t* tokens, int batch, float* logits, int32_t* next_tokens);
+/* Prefill: run n prompt tokens of one slot through the model from the slot's position on,
+ * updating its recurrent, conv and KV state and advancing its position by n; the last
+ * token's logits [vocab] and argmax come back (either pointer may be NULL). Host buffers;
+ * synchronous. Replaces the reference's prompt loop over qwen35_forward_token
+ * (crates/cli/src/main.rs:358-362) and ane_prefill_tokens (main.rs:1168). The tokens go
+ * through in chunks of 64: every projection as a 64-row GEMM, the DeltaNet recurrence in its
+ * chunkwise form (the plan of HANDOVER.md:67-72), each token's attention over the slot's
+ * cache. Needs the bf16 KV cache and conv kernel 4. Ids outside [0, vocab) and prompts that
+ * do not fit in max_ctx are rejected before any work is queued. */
+int ab2_prefill(ab2_ctx* ctx, int slot, const int32_t* tokens, int64_t n, float* logits, int32_t* next_token);
 /* Same with device buffers, enqueued on `stream` (a cudaStream_t; NULL = the context's own
  * stream) without synchronising. tokens_dev may alias next_dev of the previous step. The
  * ids are not checked on the host here: an id outside [0, vocab) embeds as a zero vector. */

@@ -1,0 +1,147 @@
+"""GPU: prefill of a prompt (ab2_prefill: chunks of 64 tokens, the DeltaNet recurrence in its
+chunkwise form, each token's attention over the slot's cache) against the oracle's
+token-by-token qwen35_forward_token, the reference's own prompt loop
+(crates/cli/src/main.rs:358-362).
+
+On the exact-weight path the prefill and the oracle differ only in the order of f32 sums
+(the 64-row GEMM's K order, the chunkwise recurrence), so the last token's logits and every
+state agree to PREFILL_TOL. On the tcgen05 path (a context whose batched steps run on the
+tensor cores) the GEMM operands are rounded to f16 and the decode parity bar applies."""
+import numpy as np
+import pytest
+
+from conftest import argmax_consistent, rel_err
+
+pytestmark = pytest.mark.gpu
+
+PREFILL_TOL = 1e-4   # max|d| <= PREFILL_TOL * max|ref|: logits and recurrent / conv state
+KV_TOL = 1e-2        # bf16 cache entries (one bf16 ulp is 2^-8 relative)
+LOGIT_TOL = 1e-2     # tcgen05 path (f16 operands), the decode parity bar
+
+
+def _oracle_run(model, tokens, seq=None):
+    seq = seq or model.new_seq(kv_bf16=True)
+    lo = None
+    for t in tokens:
+        lo = seq.forward(int(t))
+    return seq, lo
+
+
+def _check_states(ctx, seq, n, layers_dn, tol=PREFILL_TOL, slot=0):
+    for l, dn in enumerate(layers_dn):
+        if dn:
+            rec, conv = ctx.get_dn_state(l, slot)
+            rr, cr = seq.get_dn(l)
+            assert rel_err(rec, rr) < tol, (l, rel_err(rec, rr))
+            assert rel_err(conv, cr) < tol, (l, rel_err(conv, cr))
+        else:
+            k, v = ctx.get_kv(l, slot, n)
+            kr, vr = seq.get_kv(l, n)
+            assert rel_err(k, kr) < KV_TOL and rel_err(v, vr) < KV_TOL, l
+
+
+@pytest.mark.parametrize("n", [1, 63, 64, 65, 150])
+def test_prefill_tiny_matches_oracle(pkg, oracle, synth, tiny_gguf, tiny_model, n):
+    """Prompt lengths around the chunk size: the last token's logits and argmax, the position,
+    and every DeltaNet, conv and KV state equal the oracle's after the same prompt; then 16
+    greedy decode steps from the prefilled state follow the oracle's."""
+    prompt = synth.seeded_tokens(n, 32000, seed=40 + n)
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=n + 24, kv_bf16=True) as ctx:
+        lg, nx = ctx.prefill(0, prompt)
+        seq, lo = _oracle_run(tiny_model, prompt)
+        err = rel_err(lg, lo)
+        print(f"n={n}: last-token logit rel err {err:.2e}")
+        assert err < PREFILL_TOL
+        assert nx == oracle.greedy(lg) and argmax_consistent(nx, lo, lg)
+        assert ctx.get_pos(0) == n and seq.pos == n
+        _check_states(ctx, seq, n, ctx.layer_is_deltanet)
+        tg = to = nx
+        for i in range(16):
+            lgd, nxd = ctx.decode_step([tg])
+            lod = seq.forward(to)
+            assert rel_err(lgd[0], lod) < PREFILL_TOL, (i, rel_err(lgd[0], lod))
+            tg, to = int(nxd[0]), oracle.greedy(lod)
+            assert argmax_consistent(tg, lod, lgd[0]), i
+            if tg != to:
+                break  # a near tie: the two continuations are no longer comparable
+
+
+def test_prefill_continues_a_sequence(pkg, oracle, synth, tiny_gguf, tiny_model):
+    """Decode 5 tokens, then prefill 70 more from position 5 (a chunk that starts mid-sequence
+    and crosses the 64-token boundary), then prefill 3 more."""
+    toks = synth.seeded_tokens(78, 32000, seed=7)
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=96, kv_bf16=True) as ctx:
+        for t in toks[:5]:
+            ctx.decode_step([int(t)])
+        ctx.prefill(0, toks[5:75])
+        lg, nx = ctx.prefill(0, toks[75:])
+        seq, lo = _oracle_run(tiny_model, toks)
+        assert rel_err(lg, lo) < PREFILL_TOL
+        assert ctx.get_pos(0) == 78
+        _check_states(ctx, seq, 78, ctx.layer_is_deltanet)
+
+
+def test_prefill_matches_stepwise_decode(pkg, synth, tiny_gguf):
+    """Prefill of slot 1 against one decode step per token of the same prompt in slot 0 of
+    the same context: the same logits to PREFILL_TOL, and slot 1's prefill leaves slot 0 alone."""
+    prompt = synth.seeded_tokens(100, 32000, seed=3)
+    with pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=128, kv_bf16=True, exact_max_batch=2) as ctx:
+        lg1, _ = ctx.prefill(1, prompt)
+        assert ctx.get_pos(0) == 0
+        assert not ctx.get_dn_state(0, 0)[0].any()
+        for t in prompt:
+            lg0, _ = ctx.decode_step([int(t)])
+        assert rel_err(lg1, lg0[0]) < PREFILL_TOL
+        for l, dn in enumerate(ctx.layer_is_deltanet):
+            if dn:
+                assert rel_err(ctx.get_dn_state(l, 1)[0], ctx.get_dn_state(l, 0)[0]) < PREFILL_TOL
+
+
+def test_prefill_tensor_core_path(pkg, oracle, synth, tiny_gguf, tiny_model):
+    """A context whose batched steps run on tcgen05 prefills with that GEMM (64-row chunks):
+    within the decode parity bar of the oracle."""
+    prompt = synth.seeded_tokens(130, 32000, seed=11)
+    with pkg.DecodeContext(tiny_gguf, max_batch=16, max_ctx=140, kv_bf16=True) as ctx:
+        assert ctx.tensor_core_gemm(64)
+        lg, nx = ctx.prefill(0, prompt)
+        seq, lo = _oracle_run(tiny_model, prompt)
+        err = rel_err(lg, lo)
+        print(f"tcgen05 prefill: last-token logit rel err {err:.2e}")
+        assert err < LOGIT_TOL
+        _check_states(ctx, seq, 130, ctx.layer_is_deltanet, tol=LOGIT_TOL)
+
+
+def test_prefill_2b_matches_oracle(pkg, oracle, synth):
+    """The 2B shape (16 DeltaNet heads, hd-256 attention): 70 prompt tokens (two chunks)."""
+    gguf = synth.build_model_gguf(synth.shape_2b(), seed=0)
+    prompt = synth.seeded_tokens(70, 151936, seed=5)
+    with pkg.DecodeContext(gguf, max_batch=1, max_ctx=80, kv_bf16=True) as ctx:
+        lg, nx = ctx.prefill(0, prompt)
+        model = oracle.Model(gguf, ctx_cap=80)
+        seq, lo = _oracle_run(model, prompt)
+        err = rel_err(lg, lo)
+        print(f"2B prefill: last-token logit rel err {err:.2e}")
+        assert err < PREFILL_TOL
+        assert argmax_consistent(nx, lo, lg)
+        _check_states(ctx, seq, 70, ctx.layer_is_deltanet)
+
+
+def test_prefill_rejects_bad_requests(pkg, synth, tiny_gguf):
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=32, kv_bf16=True) as ctx:
+        with pytest.raises(pkg.Ab2Error) as ei:
+            ctx.prefill(0, synth.seeded_tokens(33, 32000))
+        assert ei.value.code == -6
+        with pytest.raises(pkg.Ab2Error) as ei:
+            ctx.prefill(0, np.array([1, 32000], dtype=np.int32))
+        assert ei.value.code == -1
+        with pytest.raises(pkg.Ab2Error) as ei:
+            ctx.prefill(0, np.zeros(0, dtype=np.int32))
+        assert ei.value.code == -1
+        with pytest.raises(pkg.Ab2Error) as ei:
+            ctx.prefill(1, [1, 2])
+        assert ei.value.code == -1
+        assert ctx.get_pos(0) == 0  # nothing ran
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=32, kv_bf16=False) as ctx:
+        with pytest.raises(pkg.Ab2Error) as ei:
+            ctx.prefill(0, [1, 2])
+        assert ei.value.code == -3
