@@ -49,7 +49,7 @@ namespace {
 
 struct Args {
     std::string model;
-    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1, ctx = 0, gpus = 1;
+    long pp = 128, tg = 128, batch = 1, device = 0, graph = 1, ctx = 0, gpus = 1, prefill = 1;
     bool kv_bf16 = true;
     uint64_t seed = 0;
 };
@@ -57,7 +57,7 @@ struct Args {
 void usage(FILE* f) {
     std::fprintf(f,
                  "usage: ab2_bench -m MODEL.gguf [-pp N] [-tg N] [-b B] [-d DEVICE] [--gpus N]\n"
-                 "                 [--kv bf16|f32] [--graph 0|1] [--ctx N] [--seed S]\n"
+                 "                 [--kv bf16|f32] [--graph 0|1] [--prefill 0|1] [--ctx N] [--seed S]\n"
                  "  -m, --model          qwen35 GGUF with Q8_0 weights (required)\n"
                  "  -pp, --prompt-tokens prompt tokens per sequence (default 128; 0 allowed)\n"
                  "  -tg, --gen-tokens    greedy tokens per sequence (default 128)\n"
@@ -67,6 +67,8 @@ void usage(FILE* f) {
                  "                       -b sequences per GPU (default 1)\n"
                  "  --kv                 KV cache type (default bf16; f32 as the reference)\n"
                  "  --graph              replay each step as one CUDA graph (default 1)\n"
+                 "  --prefill            1 (default): each sequence's prompt through ab2_prefill\n"
+                 "                       (bf16 cache); 0: one decode step per prompt position\n"
                  "  --ctx                seed every sequence as N tokens already processed (default 0)\n"
                  "  --seed               seed of the synthetic prompt ids (default 0)\n");
 }
@@ -104,6 +106,8 @@ int parse(int argc, char** argv, Args* a) {
             ok = parse_long(v, 1, &a->gpus) && a->gpus <= 64;
         } else if (k == "--ctx") {
             ok = parse_long(v, 0, &a->ctx);
+        } else if (k == "--prefill") {
+            ok = parse_long(v, 0, &a->prefill) && a->prefill <= 1;
         } else if (k == "--graph") {
             ok = parse_long(v, 0, &a->graph) && a->graph <= 1;
         } else if (k == "--seed") {
@@ -247,13 +251,25 @@ void run_device(const Args& a, const std::vector<uint8_t>& gguf, const ab2_confi
         }
         // the id each sequence starts generating from when there is no prompt
         for (int b = 0; b < B; b++) next[b] = (int32_t)(mix(~seed ^ mix((uint64_t)b)) % cfg.vocab);
-        // prompt: one decode step per position for all sequences
+        // the prompt id of sequence b at position i
+        auto prompt_id = [&](int b, long i) { return (int32_t)(mix(seed ^ mix(((uint64_t)b << 32) + i)) % cfg.vocab); };
         gate->wait();
         out->pp0 = Clock::now();
-        for (long i = 0; i < a.pp && !out->rc; i++) {
-            for (int b = 0; b < B; b++) tok[b] = (int32_t)(mix(seed ^ mix(((uint64_t)b << 32) + i)) % cfg.vocab);
-            out->prompt0.push_back(tok[0]);
-            if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) failed("ab2_decode_step (prompt)");
+        if (a.prefill && a.kv_bf16) {
+            // prompt: each sequence's tokens through one prefill call (chunks of 64 on the GPU)
+            std::vector<int32_t> ids((size_t)a.pp);
+            for (int b = 0; b < B && a.pp > 0 && !out->rc; b++) {
+                for (long i = 0; i < a.pp; i++) ids[(size_t)i] = prompt_id(b, i);
+                if (b == 0) out->prompt0 = ids;
+                if (ab2_prefill(ctx, b, ids.data(), a.pp, nullptr, &next[(size_t)b])) failed("ab2_prefill");
+            }
+        } else {
+            // prompt: one decode step per position for all sequences
+            for (long i = 0; i < a.pp && !out->rc; i++) {
+                for (int b = 0; b < B; b++) tok[b] = prompt_id(b, i);
+                out->prompt0.push_back(tok[0]);
+                if (ab2_decode_step(ctx, tok.data(), B, nullptr, next.data())) failed("ab2_decode_step (prompt)");
+            }
         }
         if (out->rc) break;
         out->pp1 = Clock::now();

@@ -15,7 +15,7 @@
 // SiLU(gate) are the decode mixer's, token by token, fused around it.
 //
 // One CTA per head holds the head's 128 x 128 state and the chunk's q, k, v in shared
-// memory (196 KB); the products run on the CUDA cores in f32, like the reference's.
+// memory (198 KB); the products run on the CUDA cores in f32, like the reference's.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -28,13 +28,14 @@ constexpr int DK = 128;             // key_dim = value_dim
 constexpr int kT = kPrefillChunk;   // tokens per launch
 constexpr int kPfThreads = 512;
 constexpr int kLd = DK + 4;         // padded row stride of q and k (conflict-free float4 rows)
+constexpr int kLv = DK + 8;         // padded row stride of v / R / Delta (conflict-free substitution)
 
 struct PfSmem {
     static constexpr int S = 0;                     // [DK][DK] state before the chunk
     static constexpr int K = S + DK * DK;           // [kT][kLd] normed keys
     static constexpr int Q = K + kT * kLd;          // [kT][kLd] normed, scaled queries; later O
-    static constexpr int V = Q + kT * kLd;          // [kT][DK] values; later R, then Delta
-    static constexpr int A = V + kT * DK;           // [kT][kT]
+    static constexpr int V = Q + kT * kLd;          // [kT][kLv] values; later R, then Delta
+    static constexpr int A = V + kT * kLv;          // [kT][kT]
     static constexpr int P = A + kT * kT;           // [kT][kT]
     static constexpr int G = P + kT * kT;           // [kT] cumulative log-decay
     static constexpr int BETA = G + kT;             // [kT]
@@ -87,14 +88,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         float* cs_g = p.conv + (size_t)ch * 4;
         float4 cs = *reinterpret_cast<const float4*>(cs_g);
         float* dst = ch_i == 0 ? Qb : ch_i == 1 ? Kb : Vb;
-        const int ld = ch_i == 2 ? DK : kLd;
-        for (int t = 0; t < T; t++) {
-            cs = make_float4(cs.y, cs.z, cs.w, p.proj[(size_t)t * p.ldp + ch]);
-            float sum = cs.x * cw.x;
-            sum += cs.y * cw.y;
-            sum += cs.z * cw.z;
-            sum += cs.w * cw.w;
-            dst[t * ld + ch_c] = ref_silu(sum);
+        const int ld = ch_i == 2 ? kLv : kLd;
+        // the chunk's inputs of this channel are loaded 16 at a time ahead of the window's
+        // serial dependency, so their latencies overlap
+        for (int t0 = 0; t0 < T; t0 += 16) {
+            float xin[16];
+#pragma unroll
+            for (int u = 0; u < 16; u++) xin[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                if (t0 + u >= T) break;
+                cs = make_float4(cs.y, cs.z, cs.w, xin[u]);
+                float sum = cs.x * cw.x;
+                sum += cs.y * cw.y;
+                sum += cs.z * cw.z;
+                sum += cs.w * cw.w;
+                dst[(t0 + u) * ld + ch_c] = ref_silu(sum);
+            }
         }
         *reinterpret_cast<float4*>(cs_g) = cs;
     } else if (tid - 3 * DK < T) {
@@ -191,26 +201,25 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         for (int u = 0; u < 16; u++) {
             const int t = tg * 16 + u;
             if (t < T) {
-                Vb[t * DK + j] = beta[t] * (Vb[t * DK + j] - eg[t] * ks0[u]);
+                Vb[t * kLv + j] = beta[t] * (Vb[t * kLv + j] - eg[t] * ks0[u]);
                 Qb[t * kLd + j] = eg[t] * qs0[u];
             }
         }
     }
     __syncthreads();
-    // (I + A) Delta = R by forward substitution, a column per thread
-    if (tid < DK) {
+    // (I + A) Delta = R by forward substitution. A column is four lanes of one warp (column
+    // tid / 4, part tid % 4 over s = part, part + 4, ...), so a row's result needs only the warp.
+    {
+        const int col = tid >> 2, part = tid & 3;
+        float* vc = Vb + col;
         for (int t = 1; t < T; t++) {
             const float* at = A + t * kT;
-            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-            int s = 0;
-            for (; s + 4 <= t; s += 4) {
-                a0 += at[s] * Vb[s * DK + tid];
-                a1 += at[s + 1] * Vb[(s + 1) * DK + tid];
-                a2 += at[s + 2] * Vb[(s + 2) * DK + tid];
-                a3 += at[s + 3] * Vb[(s + 3) * DK + tid];
-            }
-            for (; s < t; s++) a0 += at[s] * Vb[s * DK + tid];
-            Vb[t * DK + tid] -= (a0 + a1) + (a2 + a3);
+            float a = 0.0f;
+            for (int s = part; s < t; s += 4) a += at[s] * vc[s * kLv];
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            a += __shfl_xor_sync(0xffffffffu, a, 2);
+            if (part == 0) vc[t * kLv] -= a;
+            __syncwarp();
         }
     }
     __syncthreads();
@@ -223,10 +232,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         float o0 = Qb[t * kLd + j], o1 = 0.0f;
         int s = 0;
         for (; s + 2 <= t + 1; s += 2) {
-            o0 += pt[s] * Vb[s * DK + j];
-            o1 += pt[s + 1] * Vb[(s + 1) * DK + j];
+            o0 += pt[s] * Vb[s * kLv + j];
+            o1 += pt[s + 1] * Vb[(s + 1) * kLv + j];
         }
-        if (s <= t) o0 += pt[s] * Vb[s * DK + j];
+        if (s <= t) o0 += pt[s] * Vb[s * kLv + j];
         Qb[t * kLd + j] = o0 + o1;
     }
     // S_T = e^{g_{T-1}} S0 + K^T diag(w) Delta (column j, rows [32 tg, 32 tg + 32)), to HBM
@@ -236,7 +245,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
 #pragma unroll
         for (int r = 0; r < 32; r++) acc[r] = eT * S[(tg * 32 + r) * DK + j];
         for (int t = 0; t < T; t++) {
-            const float dw = w[t] * Vb[t * DK + j];
+            const float dw = w[t] * Vb[t * kLv + j];
             const float* kr = Kb + t * kLd + tg * 32;
 #pragma unroll
             for (int r = 0; r < 32; r += 4) {

@@ -92,6 +92,8 @@ pub mod ffi {
                           n_tokens: i64) -> c_int;
         pub fn ab2_decode_step(ctx: *mut ab2_ctx, tokens: *const i32, batch: c_int, logits: *mut f32,
                                next_tokens: *mut i32) -> c_int;
+        pub fn ab2_prefill(ctx: *mut ab2_ctx, slot: c_int, tokens: *const i32, n: i64, logits: *mut f32,
+                           next_token: *mut i32) -> c_int;
         pub fn ab2_decode_step_device(ctx: *mut ab2_ctx, tokens_dev: *const i32, batch: c_int,
                                       logits_dev: *mut f32, next_dev: *mut i32, stream: *mut c_void) -> c_int;
         pub fn ab2_sync(ctx: *mut ab2_ctx) -> c_int;
@@ -235,6 +237,18 @@ impl Decoder {
         let lp = logits.map_or(std::ptr::null_mut(), |l| l.as_mut_ptr());
         let np = next.map_or(std::ptr::null_mut(), |n| n.as_mut_ptr());
         check(unsafe { ffi::ab2_decode_step(self.raw(), tokens.as_ptr(), b as c_int, lp, np) })
+    }
+
+    /// The prompt loop of `cmd_bench` (`crates/cli/src/main.rs:358-362`) on the GPU: every
+    /// prompt token of `slot` in one call; returns the last token's logits and greedy id.
+    pub fn prefill(&mut self, slot: usize, tokens: &[u32]) -> Result<(Vec<f32>, u32)> {
+        let ids: Vec<i32> = tokens.iter().map(|&t| t as i32).collect();
+        let mut logits = vec![0f32; self.cfg.vocab as usize];
+        let mut next = 0i32;
+        check(unsafe {
+            ffi::ab2_prefill(self.raw(), slot as c_int, ids.as_ptr(), ids.len() as i64, logits.as_mut_ptr(), &mut next)
+        })?;
+        Ok((logits, next as u32))
     }
 
     /// `encode_full_token_gpu` for one sequence (slot 0): token in, logits out.

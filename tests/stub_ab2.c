@@ -100,6 +100,33 @@ int ab2_seed_state(ab2_ctx* x, uint64_t seed, int n_slots, int64_t n_tokens, flo
     return 0;
 }
 
+/* the prompt of one slot: the decode stand-in applied token by token */
+int ab2_prefill(ab2_ctx* x, int slot, const int32_t* tokens, int64_t n, float* logits, int32_t* next_token) {
+    if (slot < 0 || slot >= x->max_batch || n < 1) {
+        g_msg = "stub: bad prefill arguments";
+        return AB2_ERR_ARG;
+    }
+    if (x->pos[slot] + n > x->max_ctx) {
+        g_msg = "stub: prompt does not fit";
+        return AB2_ERR_CAPACITY;
+    }
+    for (int64_t i = 0; i < n; i++)
+        if (tokens[i] < 0 || tokens[i] >= STUB_VOCAB) {
+            g_msg = "stub: token out of range";
+            return AB2_ERR_ARG;
+        }
+    (void)logits;
+    int32_t nx = 0;
+    for (int64_t i = 0; i < n; i++) {
+        nx = (int32_t)((7LL * tokens[i] + x->pos[slot] + slot) % STUB_VOCAB);
+        x->pos[slot]++;
+    }
+    if (next_token) *next_token = nx;
+    logf_("prefill %lld %lld %lld %lld %lld %lld", (long long)slot, (long long)n, (long long)tokens[0],
+          (long long)tokens[n - 1], (long long)nx, (long long)x->device);
+    return 0;
+}
+
 int ab2_decode_step(ab2_ctx* x, const int32_t* tokens, int batch, float* logits, int32_t* next) {
     if (batch < 1 || batch > x->max_batch) {
         g_msg = "stub: batch outside [1, max_batch]";

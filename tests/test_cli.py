@@ -52,21 +52,47 @@ def test_prompt_then_greedy_feedback(stub_cli, tmp_path, B, pp, tg, kv, graph):
     assert (out["batch"], out["prompt_tokens"], out["gen_tokens"], out["kv"], out["graph"]) == (B, pp, tg, kv, graph)
     assert "Speed:" in r.stderr and "Tokens: %d" % tg in r.stderr
     calls = read_log(log)
-    # create(device 0, max_batch B, max_ctx pp + tg + 2, kv flag), graph switch, steps, destroy
+    # create(device 0, max_batch B, max_ctx pp + tg + 2, kv flag), graph switch, prompt, steps, destroy
     assert calls[0] == ["create", "0", str(B), str(pp + tg + 2), "1" if kv == "bf16" else "0"]
     assert calls[1] == ["graph", str(graph), "0", "0", "0"]
     steps = [c for c in calls if c[0] == "step"]
-    assert calls[-1][0] == "destroy" and len(steps) == pp + tg
+    prefills = [c for c in calls if c[0] == "prefill"]
+    assert calls[-1][0] == "destroy"
+    if kv == "bf16":
+        # the prompt of every sequence goes through one prefill call (slot, n, first id,
+        # last id, next id, device); the generation starts from slot 0's next id
+        assert [(int(c[1]), int(c[2])) for c in prefills] == [(b, pp) for b in range(B)]
+        assert len(steps) == tg
+        first_gen = int(prefills[0][5])
+        assert out["prompt"][0] == int(prefills[0][3]) and out["prompt"][-1] == int(prefills[0][4])
+        assert len(out["prompt"]) == pp and all(0 <= t < 1000 for t in out["prompt"])
+    else:
+        # the f32 cache has no prefill: one decode step per prompt position
+        assert not prefills and len(steps) == pp + tg
+        assert out["prompt"] == [int(s[2]) for s in steps[:pp]]
+        first_gen = int(steps[pp - 1][3])
+        steps = steps[pp:]
     assert all(int(s[1]) == B for s in steps)
     tok0 = [int(s[2]) for s in steps]
     nxt0 = [int(s[3]) for s in steps]
-    assert all(0 <= t < 1000 for t in tok0[:pp])
     # each generated step feeds the previous step's greedy token, and the reported tokens
     # are slot 0's generated ids in order
-    for k in range(pp, pp + tg):
+    assert tok0[0] == first_gen
+    for k in range(1, tg):
         assert tok0[k] == nxt0[k - 1], k
-    assert out["tokens"] == tok0[pp:]
-    assert out["prompt"] == tok0[:pp]
+    assert out["tokens"] == tok0
+
+
+def test_prompt_by_decode_steps(stub_cli, tmp_path):
+    """--prefill 0: the prompt runs as one decode step per position for all sequences."""
+    exe, model, _ = stub_cli
+    log = tmp_path / "calls.log"
+    r = run(exe, "-m", model, "-pp", "3", "-tg", "2", "-b", "2", "--prefill", "0", env={"STUB_LOG": str(log)})
+    assert r.returncode == 0, r.stderr
+    calls = read_log(log)
+    steps = [c for c in calls if c[0] == "step"]
+    assert not [c for c in calls if c[0] == "prefill"] and len(steps) == 5
+    assert json.loads(r.stdout)["prompt"] == [int(s[2]) for s in steps[:3]]
 
 
 def test_seeded_context_without_prompt(stub_cli, tmp_path):
@@ -99,20 +125,23 @@ def test_one_thread_and_context_per_gpu(stub_cli, tmp_path):
     creates = sorted(int(c[1]) for c in calls if c[0] == "create")
     assert creates == [1, 2, 3]
     assert sum(c[0] == "destroy" for c in calls) == G
-    by_dev = {}
+    by_dev, pf_dev = {}, {}
     for c in calls:
         if c[0] == "step":
             by_dev.setdefault(int(c[5]), []).append(c)
-    assert sorted(by_dev) == [1, 2, 3]
+        if c[0] == "prefill":
+            pf_dev.setdefault(int(c[6]), []).append(c)
+    assert sorted(by_dev) == [1, 2, 3] and sorted(pf_dev) == [1, 2, 3]
     for dev, steps in by_dev.items():
-        assert len(steps) == pp + tg, dev
+        assert len(steps) == tg and len(pf_dev[dev]) == B, dev
         tok0 = [int(s[2]) for s in steps]
         nxt0 = [int(s[3]) for s in steps]
-        assert all(tok0[k] == nxt0[k - 1] for k in range(pp, pp + tg)), dev
+        assert tok0[0] == int(pf_dev[dev][0][5])
+        assert all(tok0[k] == nxt0[k - 1] for k in range(1, tg)), dev
     # each GPU decodes its own sequences: prompts are seeded per GPU; the output reports GPU 1's
-    prompts = {dev: [int(s[2]) for s in steps[:pp]] for dev, steps in by_dev.items()}
-    assert len({tuple(p) for p in prompts.values()}) == G
-    assert out["prompt"] == prompts[1]
+    prompts = {dev: (int(pf[0][3]), int(pf[0][4])) for dev, pf in pf_dev.items()}
+    assert len(set(prompts.values())) == G
+    assert (out["prompt"][0], out["prompt"][-1]) == prompts[1]
 
 
 def test_device_threads_start_together(stub_cli, tmp_path):
@@ -126,7 +155,7 @@ def test_device_threads_start_together(stub_cli, tmp_path):
     calls = read_log(log)
     kinds = [c[0] for c in calls]
     last_seed = max(i for i, k in enumerate(kinds) if k == "seed")
-    first_step = min(i for i, k in enumerate(kinds) if k == "step")
+    first_step = min(i for i, k in enumerate(kinds) if k in ("step", "prefill"))
     assert last_seed < first_step, kinds
 
 
@@ -148,10 +177,10 @@ def test_prompt_ids_depend_on_seed_and_slot(stub_cli, tmp_path):
         log = tmp_path / f"s{seed}.log"
         assert run(exe, "-m", model, "-pp", "3", "-tg", "1", "-b", "2", "--seed", seed,
                    env={"STUB_LOG": str(log)}).returncode == 0
-        steps = [c for c in read_log(log) if c[0] == "step"]
-        firsts.append([(int(s[2]), int(s[4])) for s in steps[:3]])
+        pf = [c for c in read_log(log) if c[0] == "prefill"]
+        firsts.append([(int(c[3]), int(c[4])) for c in pf])  # each slot's first and last prompt id
     assert firsts[0] != firsts[1]
-    assert any(a != b for a, b in firsts[0])  # slots 0 and 1 get different prompts
+    assert firsts[0][0] != firsts[0][1]  # slots 0 and 1 get different prompts
 
 
 @pytest.mark.parametrize("args,code,msg", [
