@@ -14,37 +14,49 @@
 // SiLU over the chunk, the q/k L2 norms, beta, the decay and the gated RMSNorm times
 // SiLU(gate) are the decode mixer's, token by token, fused around it.
 //
-// One CTA per head holds the head's 128 x 128 state and the chunk's q, k, v in shared
-// memory (198 KB); the products run on the CUDA cores in f32, like the reference's.
+// Each head runs on a thread-block cluster of kPfCluster CTAs. Every CTA of the cluster
+// holds the chunk's normed q and k, computes kT / kPfCluster rows of A and P and stores them
+// into every CTA's shared memory (distributed shared memory), and owns 128 / kPfCluster of
+// the head's value columns: their slice of the state, of V, Delta and O. The gated RMSNorm's
+// sum of squares over the 128 columns is exchanged the same way. The products run on the
+// CUDA cores in f32, like the reference's.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
-
-#include <algorithm>
 
 namespace ab2 {
 namespace {
 
-constexpr int DK = 128;             // key_dim = value_dim
-constexpr int kT = kPrefillChunk;   // tokens per launch
+namespace cg = cooperative_groups;
+
+constexpr int DK = 128;                   // key_dim = value_dim
+constexpr int kT = kPrefillChunk;         // tokens per launch
 constexpr int kPfThreads = 512;
-constexpr int kLd = DK + 4;         // padded row stride of q and k (conflict-free float4 rows)
-constexpr int kLv = DK + 8;         // padded row stride of v / R / Delta (conflict-free substitution)
+constexpr int kPfCluster = 8;             // CTAs per head
+constexpr int kCols = DK / kPfCluster;    // value columns per CTA (16)
+constexpr int kRows = kT / kPfCluster;    // rows of A and P each CTA computes (8)
+constexpr int kLd = DK + 4;               // padded row stride of q and k (conflict-free float4 rows)
+constexpr int kLv = kCols + 1;            // padded row stride of the per-CTA column buffers
 
 struct PfSmem {
-    static constexpr int S = 0;                     // [DK][DK] state before the chunk
-    static constexpr int K = S + DK * DK;           // [kT][kLd] normed keys
-    static constexpr int Q = K + kT * kLd;          // [kT][kLd] normed, scaled queries; later O
-    static constexpr int V = Q + kT * kLd;          // [kT][kLv] values; later R, then Delta
-    static constexpr int A = V + kT * kLv;          // [kT][kT]
-    static constexpr int P = A + kT * kT;           // [kT][kT]
-    static constexpr int G = P + kT * kT;           // [kT] cumulative log-decay
-    static constexpr int BETA = G + kT;             // [kT]
-    static constexpr int EG = BETA + kT;            // [kT] e^{g_t}
-    static constexpr int W = EG + kT;               // [kT] e^{g_{T-1} - g_t}
-    static constexpr int floats = W + kT;
+    static constexpr int K = 0;                      // [kT][kLd] normed keys
+    static constexpr int Q = K + kT * kLd;           // [kT][kLd] normed, scaled queries
+    static constexpr int S = Q + kT * kLd;           // [DK][kCols] this CTA's columns of the state
+    static constexpr int V = S + DK * kCols;         // [kT][kLv] values; later R, then Delta
+    static constexpr int O = V + kT * kLv;           // [kT][kLv] outputs
+    static constexpr int A = O + kT * kLv;           // [kT][kT]
+    static constexpr int P = A + kT * kT;            // [kT][kT]
+    static constexpr int G = P + kT * kT;            // [kT] cumulative log-decay
+    static constexpr int BETA = G + kT;              // [kT]
+    static constexpr int EG = BETA + kT;             // [kT] e^{g_t}
+    static constexpr int W = EG + kT;                // [kT] e^{g_{T-1} - g_t}
+    static constexpr int SS = W + kT;                // [kPfCluster][kT] partial sums of squares of O
+    static constexpr int floats = SS + kPfCluster * kT;
     static constexpr int bytes = floats * 4;
 };
 static_assert(PfSmem::bytes <= 227 * 1024, "prefill shared memory");
+static_assert(kPfThreads == kCols * 32 && kRows * kT == kPfThreads, "prefill thread mapping");
 
 __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
     acc += a.x * b.x;
@@ -57,40 +69,56 @@ __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
 __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, int T) {
     extern __shared__ float4 pf_smem4[];
     float* sm = reinterpret_cast<float*>(pf_smem4);
-    float* S = sm + PfSmem::S;
     float* Kb = sm + PfSmem::K;
     float* Qb = sm + PfSmem::Q;
+    float* S = sm + PfSmem::S;
     float* Vb = sm + PfSmem::V;
+    float* Ob = sm + PfSmem::O;
     float* A = sm + PfSmem::A;
     float* P = sm + PfSmem::P;
     float* g = sm + PfSmem::G;
     float* beta = sm + PfSmem::BETA;
     float* eg = sm + PfSmem::EG;
     float* w = sm + PfSmem::W;
+    float* ssp = sm + PfSmem::SS;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int c = (int)cluster.block_rank();                  // this CTA's column block
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int h = blockIdx.x, hg = p.h0 + h, H_all = p.H_all ? p.H_all : p.H;
+    const int h = blockIdx.x / kPfCluster, hg = p.h0 + h, H_all = p.H_all ? p.H_all : p.H;
+    const int c0 = c * kCols;                                  // first value column of this CTA
     float* Sg = p.S + (size_t)h * DK * DK;
 
-    // constants, before the grid dependency wait: this thread's conv channel weights, ssm_a, dt_bias
-    const int ch_i = tid / DK, ch_c = tid % DK;                // q / k / v channel group and index
-    const int ch = tid < 3 * DK ? ch_i * p.D + hg * DK + ch_c : -1;
-    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+    // this thread's conv channel: q and k (every CTA: all 256), v (this CTA's 16 columns)
+    int ch = -1, ch_c = 0;
+    float* dst = nullptr;
+    int ld = 0;
+    if (tid < 2 * DK) {
+        ch_c = tid % DK;
+        ch = (tid / DK) * p.D + hg * DK + ch_c;
+        dst = tid < DK ? Qb : Kb;
+        ld = kLd;
+    } else if (tid < 2 * DK + kCols) {
+        ch_c = tid - 2 * DK;
+        ch = 2 * p.D + hg * DK + c0 + ch_c;
+        dst = Vb;
+        ld = kLv;
+    }
+    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f), cs = cw;
     if (ch >= 0) cw = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
     const float sa = p.ssm_a[hg], dtb = p.dt_bias[hg];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    for (int e = tid; e < DK * DK / 4; e += kPfThreads)
-        reinterpret_cast<float4*>(S)[e] = reinterpret_cast<const float4*>(Sg)[e];
+    // this CTA's columns of the head's state: [DK rows][kCols]
+    {
+        const int r = tid >> 2, q4 = tid & 3;  // 128 rows x 4 float4
+        reinterpret_cast<float4*>(S + r * kCols)[q4] = reinterpret_cast<const float4*>(Sg + (size_t)r * DK + c0)[q4];
+    }
     if (ch >= 0) {
         // conv_shift_and_append + conv_apply + SiLU per token (deltanet_cache.rs:34-54,
-        // deltanet.rs:444-450), the window carried in registers across the chunk
-        float* cs_g = p.conv + (size_t)ch * 4;
-        float4 cs = *reinterpret_cast<const float4*>(cs_g);
-        float* dst = ch_i == 0 ? Qb : ch_i == 1 ? Kb : Vb;
-        const int ld = ch_i == 2 ? kLv : kLd;
-        // the chunk's inputs of this channel are loaded 16 at a time ahead of the window's
-        // serial dependency, so their latencies overlap
+        // deltanet.rs:444-450), the window carried in registers; the chunk's inputs are
+        // loaded 16 at a time ahead of the window's serial dependency
+        cs = *reinterpret_cast<const float4*>(p.conv + (size_t)ch * 4);
         for (int t0 = 0; t0 < T; t0 += 16) {
             float xin[16];
 #pragma unroll
@@ -106,8 +134,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
                 dst[(t0 + u) * ld + ch_c] = ref_silu(sum);
             }
         }
-        *reinterpret_cast<float4*>(cs_g) = cs;
-    } else if (tid - 3 * DK < T) {
+    } else if (tid >= 3 * DK && tid - 3 * DK < T) {
         // beta = sigmoid(W_beta x) and log d = ssm_a * softplus(W_alpha x + dt_bias) (deltanet.rs:469-480)
         const int t = tid - 3 * DK;
         const float* pr = p.proj + (size_t)t * p.ldp;
@@ -135,9 +162,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         const float inv = 1.0f / sqrtf(ss + 1e-12f);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            float t = xs[i] * inv;
-            if (r < T) t *= 1.0f / sqrtf((float)DK);
-            v[lane + 32 * i] = t;
+            float x = xs[i] * inv;
+            if (r < T) x *= 1.0f / sqrtf((float)DK);
+            v[lane + 32 * i] = x;
         }
     }
     __syncthreads();
@@ -145,141 +172,138 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         eg[tid] = expf(g[tid]);
         w[tid] = expf(g[T - 1] - g[tid]);
     }
+    // every CTA of the cluster has started (its shared memory may now be written) and has
+    // read the conv windows before they are replaced
+    cluster.sync();
+    // the windows after the chunk: the q and k channels' by one CTA of the cluster, the v
+    // channels' by the CTA that owns them
+    if (ch >= 0 && (tid >= 2 * DK || c == 0)) *reinterpret_cast<float4*>(p.conv + (size_t)ch * 4) = cs;
 
-    // A and P: warp w holds rows t = w + 16a, lane holds columns s = lane + 32b
+    // rows [kRows c, kRows (c+1)) of A and P, one entry of each per thread, stored into every
+    // CTA of the cluster
     {
-        float kk[4][2], qk[4][2];
-#pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int b = 0; b < 2; b++) kk[a][b] = qk[a][b] = 0.0f;
-        for (int i = 0; i < DK; i += 4) {
-            float4 ks[2];
-#pragma unroll
-            for (int b = 0; b < 2; b++) ks[b] = *reinterpret_cast<const float4*>(Kb + (lane + 32 * b) * kLd + i);
-#pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const int t = warp + 16 * a;
-                const float4 kt = *reinterpret_cast<const float4*>(Kb + t * kLd + i);
-                const float4 qt = *reinterpret_cast<const float4*>(Qb + t * kLd + i);
-#pragma unroll
-                for (int b = 0; b < 2; b++) {
-                    kk[a][b] = dot4(kt, ks[b], kk[a][b]);
-                    qk[a][b] = dot4(qt, ks[b], qk[a][b]);
-                }
+        const int t = c * kRows + (tid >> 6), s = tid & (kT - 1);
+        float kk = 0.0f, qk = 0.0f;
+        if (t < T && s <= t) {
+            const float* kt = Kb + t * kLd;
+            const float* qt = Qb + t * kLd;
+            const float* ks = Kb + s * kLd;
+#pragma unroll 8
+            for (int i = 0; i < DK; i += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
+                kk = dot4(*reinterpret_cast<const float4*>(kt + i), k4, kk);
+                qk = dot4(*reinterpret_cast<const float4*>(qt + i), k4, qk);
             }
         }
+        const bool in = t < T && s <= t;  // rows and columns past T were never written
+        const float e = in ? expf(g[t] - g[s]) : 0.0f;
+        const float a_ts = in && s < t ? beta[t] * e * kk : 0.0f;
+        const float p_ts = in ? e * qk : 0.0f;
 #pragma unroll
-        for (int a = 0; a < 4; a++)
-#pragma unroll
-            for (int b = 0; b < 2; b++) {
-                const int t = warp + 16 * a, s = lane + 32 * b;
-                const bool in = t < T && s <= t;  // rows and columns past T were never written
-                const float e = in ? expf(g[t] - g[s]) : 0.0f;
-                A[t * kT + s] = in && s < t ? beta[t] * e * kk[a][b] : 0.0f;
-                P[t * kT + s] = in ? e * qk[a][b] : 0.0f;
-            }
+        for (int r = 0; r < kPfCluster; r++) {
+            cluster.map_shared_rank(A, r)[t * kT + s] = a_ts;
+            cluster.map_shared_rank(P, r)[t * kT + s] = p_ts;
+        }
     }
 
-    // R = beta (V - e^g K S0) and e^g Q S0; thread: column j, tokens [16 tg, 16 tg + 16)
-    const int j = tid & (DK - 1), tg = tid >> 7;
+    // R = beta (V - e^g K S0) and e^g Q S0 for this CTA's columns; thread: column j,
+    // tokens {tg, tg + 32}
+    const int j = tid & (kCols - 1), tg = tid >> 4;
     {
-        float ks0[16], qs0[16];
-#pragma unroll
-        for (int u = 0; u < 16; u++) ks0[u] = qs0[u] = 0.0f;
+        float ks0[2] = {0.f, 0.f}, qs0[2] = {0.f, 0.f};
         for (int i = 0; i < DK; i += 4) {
-            const float4 s4 = make_float4(S[i * DK + j], S[(i + 1) * DK + j], S[(i + 2) * DK + j], S[(i + 3) * DK + j]);
+            const float4 s4 = make_float4(S[i * kCols + j], S[(i + 1) * kCols + j], S[(i + 2) * kCols + j],
+                                          S[(i + 3) * kCols + j]);
 #pragma unroll
-            for (int u = 0; u < 16; u++) {
-                const int t = tg * 16 + u;
+            for (int u = 0; u < 2; u++) {
+                const int t = tg + 32 * u;
                 ks0[u] = dot4(*reinterpret_cast<const float4*>(Kb + t * kLd + i), s4, ks0[u]);
                 qs0[u] = dot4(*reinterpret_cast<const float4*>(Qb + t * kLd + i), s4, qs0[u]);
             }
         }
-        __syncthreads();  // every read of Q is done: it now holds O
 #pragma unroll
-        for (int u = 0; u < 16; u++) {
-            const int t = tg * 16 + u;
+        for (int u = 0; u < 2; u++) {
+            const int t = tg + 32 * u;
             if (t < T) {
                 Vb[t * kLv + j] = beta[t] * (Vb[t * kLv + j] - eg[t] * ks0[u]);
-                Qb[t * kLd + j] = eg[t] * qs0[u];
+                Ob[t * kLv + j] = eg[t] * qs0[u];
             }
         }
     }
-    __syncthreads();
-    // (I + A) Delta = R by forward substitution. A column is four lanes of one warp (column
-    // tid / 4, part tid % 4 over s = part, part + 4, ...), so a row's result needs only the warp.
-    {
-        const int col = tid >> 2, part = tid & 3;
+    cluster.sync();  // all of A and P has arrived; R is complete
+    // (I + A) Delta = R by forward substitution: a column is 8 lanes of one warp (column
+    // tid / 8, part tid % 8 over s = part, part + 8, ...), so a row needs only the warp
+    if (tid < kCols * 8) {
+        const int col = tid >> 3, part = tid & 7;
         float* vc = Vb + col;
         for (int t = 1; t < T; t++) {
             const float* at = A + t * kT;
             float a = 0.0f;
-            for (int s = part; s < t; s += 4) a += at[s] * vc[s * kLv];
+            for (int s = part; s < t; s += 8) a += at[s] * vc[s * kLv];
             a += __shfl_xor_sync(0xffffffffu, a, 1);
             a += __shfl_xor_sync(0xffffffffu, a, 2);
+            a += __shfl_xor_sync(0xffffffffu, a, 4);
             if (part == 0) vc[t * kLv] -= a;
             __syncwarp();
         }
     }
     __syncthreads();
-    // O += P Delta (column j, tokens of group tg)
-#pragma unroll 1
-    for (int u = 0; u < 16; u++) {
-        const int t = tg * 16 + u;
-        if (t >= T) break;
-        const float* pt = P + t * kT;
-        float o0 = Qb[t * kLd + j], o1 = 0.0f;
-        int s = 0;
-        for (; s + 2 <= t + 1; s += 2) {
-            o0 += pt[s] * Vb[s * kLv + j];
-            o1 += pt[s + 1] * Vb[(s + 1) * kLv + j];
+    // O += P Delta (column j, tokens tg, tg + 32)
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const int t = tg + 32 * u;
+        if (t < T) {
+            const float* pt = P + t * kT;
+            float o0 = Ob[t * kLv + j], o1 = 0.0f;
+            int s = 0;
+            for (; s + 2 <= t + 1; s += 2) {
+                o0 += pt[s] * Vb[s * kLv + j];
+                o1 += pt[s + 1] * Vb[(s + 1) * kLv + j];
+            }
+            if (s <= t) o0 += pt[s] * Vb[s * kLv + j];
+            Ob[t * kLv + j] = o0 + o1;
         }
-        if (s <= t) o0 += pt[s] * Vb[s * kLv + j];
-        Qb[t * kLd + j] = o0 + o1;
     }
-    // S_T = e^{g_{T-1}} S0 + K^T diag(w) Delta (column j, rows [32 tg, 32 tg + 32)), to HBM
+    // S_T = e^{g_{T-1}} S0 + K^T diag(w) Delta for this CTA's columns (column j, rows
+    // tg * 4 .. tg * 4 + 3), to HBM
     {
         const float eT = eg[T - 1];
-        float acc[32];
+        float acc[4];
 #pragma unroll
-        for (int r = 0; r < 32; r++) acc[r] = eT * S[(tg * 32 + r) * DK + j];
+        for (int r = 0; r < 4; r++) acc[r] = eT * S[(tg * 4 + r) * kCols + j];
         for (int t = 0; t < T; t++) {
             const float dw = w[t] * Vb[t * kLv + j];
-            const float* kr = Kb + t * kLd + tg * 32;
-#pragma unroll
-            for (int r = 0; r < 32; r += 4) {
-                const float4 k4 = *reinterpret_cast<const float4*>(kr + r);
-                acc[r] += k4.x * dw;
-                acc[r + 1] += k4.y * dw;
-                acc[r + 2] += k4.z * dw;
-                acc[r + 3] += k4.w * dw;
-            }
+            const float4 k4 = *reinterpret_cast<const float4*>(Kb + t * kLd + tg * 4);
+            acc[0] += k4.x * dw;
+            acc[1] += k4.y * dw;
+            acc[2] += k4.z * dw;
+            acc[3] += k4.w * dw;
         }
 #pragma unroll
-        for (int r = 0; r < 32; r++) Sg[(size_t)(tg * 32 + r) * DK + j] = acc[r];
+        for (int r = 0; r < 4; r++) Sg[(size_t)(tg * 4 + r) * DK + c0 + j] = acc[r];
     }
     __syncthreads();
-    // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533), a warp per token;
-    // the sum of squares adds the four 32-column partials in the decode mixer's order
+    // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533): this CTA's partial
+    // sums of squares of O per token go to every CTA; each adds the kPfCluster partials in
+    // rank order, so all CTAs of the head use the same rms
     for (int t = warp; t < T; t += kPfThreads / 32) {
-        float ov[4], ss[4];
+        const float o = lane < kCols ? Ob[t * kLv + lane] : 0.0f;
+        const float ss = warp_sum(o * o);
+        if (lane < kPfCluster) cluster.map_shared_rank(ssp, lane)[c * kT + t] = ss;
+    }
+    cluster.sync();
+    for (int e = tid; e < T * kCols; e += kPfThreads) {
+        const int t = e / kCols, col = e % kCols;
+        float tot = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-            ov[c] = Qb[t * kLd + lane + 32 * c];
-            ss[c] = warp_sum(ov[c] * ov[c]);
-        }
-        const float rms = 1.0f / sqrtf((ss[0] + ss[1] + ss[2] + ss[3]) / (float)DK + p.eps);
-        const float* gate = p.proj + (size_t)t * p.ldp + 3 * p.D + hg * DK;
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-            const int col = lane + 32 * c;
-            const float gt = gate[col];
-            float nv = ov[c] * rms * p.ssm_norm[col];
-            nv *= gt / (1.0f + expf(-gt));
-            act_store(p.out, t, hg * DK + col, nv);
-            if (p.o_out) p.o_out[(size_t)t * p.D + hg * DK + col] = nv;
-        }
+        for (int r = 0; r < kPfCluster; r++) tot += ssp[r * kT + t];
+        const float rms = 1.0f / sqrtf(tot / (float)DK + p.eps);
+        const int hc = c0 + col;  // the column in the head
+        const float gt = p.proj[(size_t)t * p.ldp + 3 * p.D + hg * DK + hc];
+        float nv = Ob[t * kLv + col] * rms * p.ssm_norm[hc];
+        nv *= gt / (1.0f + expf(-gt));
+        act_store(p.out, t, hg * DK + hc, nv);
+        if (p.o_out) p.o_out[(size_t)t * p.D + hg * DK + hc] = nv;
     }
 }
 
@@ -296,9 +320,21 @@ int launch_dn_prefill(const DnParams& p, int tokens, cudaStream_t st) {
             return -2;
         attr_set[dev & 63] = true;
     }
-    return launch_pdl(dn_prefill_kernel, dim3(p.H), dim3(kPfThreads), PfSmem::bytes, st, p, tokens) == cudaSuccess
-               ? 0
-               : -2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.H * kPfCluster);
+    cfg.blockDim = dim3(kPfThreads);
+    cfg.dynamicSmemBytes = PfSmem::bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kPfCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, dn_prefill_kernel, p, tokens) == cudaSuccess ? 0 : -2;
 }
 
 }  // namespace ab2
