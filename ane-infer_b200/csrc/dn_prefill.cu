@@ -33,9 +33,10 @@ namespace cg = cooperative_groups;
 constexpr int DK = 128;                   // key_dim = value_dim
 constexpr int kT = kPrefillChunk;         // tokens per launch
 constexpr int kPfThreads = 512;
-constexpr int kPfCluster = 8;             // CTAs per head
-constexpr int kCols = DK / kPfCluster;    // value columns per CTA (16)
-constexpr int kRows = kT / kPfCluster;    // rows of A and P each CTA computes (8)
+constexpr int kPfCluster = 4;             // CTAs per head (16 clusters of 8 do not fit at once)
+constexpr int kCols = DK / kPfCluster;    // value columns per CTA (32)
+constexpr int kRows = kT / kPfCluster;    // rows of A and P each CTA computes (16)
+constexpr int kTg = kPfThreads / kCols;   // thread groups of one column (16)
 constexpr int kLd = DK + 4;               // padded row stride of q and k (conflict-free float4 rows)
 constexpr int kLv = kCols + 1;            // padded row stride of the per-CTA column buffers
 
@@ -56,7 +57,7 @@ struct PfSmem {
     static constexpr int bytes = floats * 4;
 };
 static_assert(PfSmem::bytes <= 227 * 1024, "prefill shared memory");
-static_assert(kPfThreads == kCols * 32 && kRows * kT == kPfThreads, "prefill thread mapping");
+static_assert(kCols == 32 && kTg == 16 && kRows * kT == 2 * kPfThreads, "prefill thread mapping");
 
 __device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
     acc += a.x * b.x;
@@ -109,10 +110,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // this CTA's columns of the head's state: [DK rows][kCols]
-    {
-        const int r = tid >> 2, q4 = tid & 3;  // 128 rows x 4 float4
-        reinterpret_cast<float4*>(S + r * kCols)[q4] = reinterpret_cast<const float4*>(Sg + (size_t)r * DK + c0)[q4];
+    // this CTA's columns of the head's state: [DK rows][kCols], 8 float4 per row
+    for (int e = tid; e < DK * kCols / 4; e += kPfThreads)
+        reinterpret_cast<float4*>(S)[e] = reinterpret_cast<const float4*>(Sg + (size_t)(e >> 3) * DK + c0)[e & 7];
+    // the gate values of this thread's outputs (token e / kCols, column e % kCols), loaded now
+    float gate[kT * kCols / kPfThreads];
+#pragma unroll
+    for (int u = 0; u < kT * kCols / kPfThreads; u++) {
+        const int e = tid + u * kPfThreads, t = e / kCols;
+        gate[u] = t < T ? p.proj[(size_t)t * p.ldp + 3 * p.D + hg * DK + c0 + e % kCols] : 0.0f;
     }
     if (ch >= 0) {
         // conv_shift_and_append + conv_apply + SiLU per token (deltanet_cache.rs:34-54,
@@ -142,12 +148,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         g[t] = sa * ref_softplus(pr[4 * p.D + H_all + hg] + dtb);
     }
     __syncthreads();
-    if (tid == 0) {
-        float acc = 0.0f;
-        for (int t = 0; t < T; t++) {
-            acc += g[t];
-            g[t] = acc;
+    if (warp == 0) {
+        // inclusive prefix sum of the log-decays: lane l holds tokens 2l, 2l + 1
+        const float a0 = 2 * lane < T ? g[2 * lane] : 0.0f;
+        const float a1 = 2 * lane + 1 < T ? g[2 * lane + 1] : 0.0f;
+        float pre = a0 + a1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float n = __shfl_up_sync(0xffffffffu, pre, o);
+            if (lane >= o) pre += n;
         }
+        const float base = pre - (a0 + a1);
+        if (2 * lane < T) g[2 * lane] = base + a0;
+        if (2 * lane + 1 < T) g[2 * lane + 1] = pre;
     }
     // per-token L2 norm of q (then * 1/sqrt(dk)) and k (deltanet.rs:459-467), a warp per row
     for (int r = warp; r < 2 * T; r += kPfThreads / 32) {
@@ -181,8 +194,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
 
     // rows [kRows c, kRows (c+1)) of A and P, one entry of each per thread, stored into every
     // CTA of the cluster
-    {
-        const int t = c * kRows + (tid >> 6), s = tid & (kT - 1);
+#pragma unroll 1
+    for (int u = 0; u < 2; u++) {
+        const int e = tid + u * kPfThreads, t = c * kRows + (e >> 6), s = e & (kT - 1);
         float kk = 0.0f, qk = 0.0f;
         if (t < T && s <= t) {
             const float* kt = Kb + t * kLd;
@@ -196,9 +210,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
             }
         }
         const bool in = t < T && s <= t;  // rows and columns past T were never written
-        const float e = in ? expf(g[t] - g[s]) : 0.0f;
-        const float a_ts = in && s < t ? beta[t] * e * kk : 0.0f;
-        const float p_ts = in ? e * qk : 0.0f;
+        const float dec = in ? expf(g[t] - g[s]) : 0.0f;
+        const float a_ts = in && s < t ? beta[t] * dec * kk : 0.0f;
+        const float p_ts = in ? dec * qk : 0.0f;
 #pragma unroll
         for (int r = 0; r < kPfCluster; r++) {
             cluster.map_shared_rank(A, r)[t * kT + s] = a_ts;
@@ -207,23 +221,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     }
 
     // R = beta (V - e^g K S0) and e^g Q S0 for this CTA's columns; thread: column j,
-    // tokens {tg, tg + 32}
-    const int j = tid & (kCols - 1), tg = tid >> 4;
+    // tokens tg + kTg u
+    const int j = tid & (kCols - 1), tg = tid / kCols;
     {
-        float ks0[2] = {0.f, 0.f}, qs0[2] = {0.f, 0.f};
+        float ks0[4] = {0.f, 0.f, 0.f, 0.f}, qs0[4] = {0.f, 0.f, 0.f, 0.f};
         for (int i = 0; i < DK; i += 4) {
             const float4 s4 = make_float4(S[i * kCols + j], S[(i + 1) * kCols + j], S[(i + 2) * kCols + j],
                                           S[(i + 3) * kCols + j]);
 #pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int t = tg + 32 * u;
+            for (int u = 0; u < 4; u++) {
+                const int t = tg + kTg * u;
                 ks0[u] = dot4(*reinterpret_cast<const float4*>(Kb + t * kLd + i), s4, ks0[u]);
                 qs0[u] = dot4(*reinterpret_cast<const float4*>(Qb + t * kLd + i), s4, qs0[u]);
             }
         }
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int t = tg + 32 * u;
+        for (int u = 0; u < 4; u++) {
+            const int t = tg + kTg * u;
             if (t < T) {
                 Vb[t * kLv + j] = beta[t] * (Vb[t * kLv + j] - eg[t] * ks0[u]);
                 Ob[t * kLv + j] = eg[t] * qs0[u];
@@ -237,9 +251,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         const int col = tid >> 3, part = tid & 7;
         float* vc = Vb + col;
         for (int t = 1; t < T; t++) {
+            // the (at most 8) terms s = part + 8m < t: loads issued together, then a tree sum
             const float* at = A + t * kT;
-            float a = 0.0f;
-            for (int s = part; s < t; s += 8) a += at[s] * vc[s * kLv];
+            float pr[kT / 8];
+#pragma unroll
+            for (int m = 0; m < kT / 8; m++) {
+                const int s = part + 8 * m;
+                pr[m] = s < t ? at[s] * vc[s * kLv] : 0.0f;
+            }
+            float a = ((pr[0] + pr[1]) + (pr[2] + pr[3])) + ((pr[4] + pr[5]) + (pr[6] + pr[7]));
             a += __shfl_xor_sync(0xffffffffu, a, 1);
             a += __shfl_xor_sync(0xffffffffu, a, 2);
             a += __shfl_xor_sync(0xffffffffu, a, 4);
@@ -248,10 +268,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         }
     }
     __syncthreads();
-    // O += P Delta (column j, tokens tg, tg + 32)
+    // O += P Delta (column j, tokens tg + kTg u)
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-        const int t = tg + 32 * u;
+    for (int u = 0; u < 4; u++) {
+        const int t = tg + kTg * u;
         if (t < T) {
             const float* pt = P + t * kT;
             float o0 = Ob[t * kLv + j], o1 = 0.0f;
@@ -265,41 +285,48 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         }
     }
     // S_T = e^{g_{T-1}} S0 + K^T diag(w) Delta for this CTA's columns (column j, rows
-    // tg * 4 .. tg * 4 + 3), to HBM
+    // tg * 8 .. tg * 8 + 7), to HBM
     {
         const float eT = eg[T - 1];
-        float acc[4];
+        float acc[8];
 #pragma unroll
-        for (int r = 0; r < 4; r++) acc[r] = eT * S[(tg * 4 + r) * kCols + j];
+        for (int r = 0; r < 8; r++) acc[r] = eT * S[(tg * 8 + r) * kCols + j];
         for (int t = 0; t < T; t++) {
             const float dw = w[t] * Vb[t * kLv + j];
-            const float4 k4 = *reinterpret_cast<const float4*>(Kb + t * kLd + tg * 4);
-            acc[0] += k4.x * dw;
-            acc[1] += k4.y * dw;
-            acc[2] += k4.z * dw;
-            acc[3] += k4.w * dw;
+            const float4 ka = *reinterpret_cast<const float4*>(Kb + t * kLd + tg * 8);
+            const float4 kb = *reinterpret_cast<const float4*>(Kb + t * kLd + tg * 8 + 4);
+            acc[0] += ka.x * dw;
+            acc[1] += ka.y * dw;
+            acc[2] += ka.z * dw;
+            acc[3] += ka.w * dw;
+            acc[4] += kb.x * dw;
+            acc[5] += kb.y * dw;
+            acc[6] += kb.z * dw;
+            acc[7] += kb.w * dw;
         }
 #pragma unroll
-        for (int r = 0; r < 4; r++) Sg[(size_t)(tg * 4 + r) * DK + c0 + j] = acc[r];
+        for (int r = 0; r < 8; r++) Sg[(size_t)(tg * 8 + r) * DK + c0 + j] = acc[r];
     }
     __syncthreads();
-    // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533): this CTA's partial
-    // sums of squares of O per token go to every CTA; each adds the kPfCluster partials in
-    // rank order, so all CTAs of the head use the same rms
+    // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533): each CTA's sum of
+    // squares over its 32 columns (a warp sum, as the decode mixer's per-warp partials) goes
+    // to every CTA, which adds the four in rank order, as the decode mixer does
     for (int t = warp; t < T; t += kPfThreads / 32) {
-        const float o = lane < kCols ? Ob[t * kLv + lane] : 0.0f;
+        const float o = Ob[t * kLv + lane];
         const float ss = warp_sum(o * o);
         if (lane < kPfCluster) cluster.map_shared_rank(ssp, lane)[c * kT + t] = ss;
     }
     cluster.sync();
-    for (int e = tid; e < T * kCols; e += kPfThreads) {
-        const int t = e / kCols, col = e % kCols;
+#pragma unroll
+    for (int u = 0; u < kT * kCols / kPfThreads; u++) {
+        const int e = tid + u * kPfThreads, t = e / kCols, col = e % kCols;
+        if (t >= T) break;
         float tot = 0.0f;
 #pragma unroll
         for (int r = 0; r < kPfCluster; r++) tot += ssp[r * kT + t];
         const float rms = 1.0f / sqrtf(tot / (float)DK + p.eps);
         const int hc = c0 + col;  // the column in the head
-        const float gt = p.proj[(size_t)t * p.ldp + 3 * p.D + hg * DK + hc];
+        const float gt = gate[u];
         float nv = Ob[t * kLv + col] * rms * p.ssm_norm[hc];
         nv *= gt / (1.0f + expf(-gt));
         act_store(p.out, t, hg * DK + hc, nv);
