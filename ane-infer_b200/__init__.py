@@ -371,7 +371,7 @@ def op_error() -> int:
 
 
 # kernel families for debug_arm_wait_timeout
-WAIT_TEST_GEMM, WAIT_TEST_ATTENTION, WAIT_TEST_DELTANET, WAIT_TEST_GEMV = 1, 2, 3, 4
+WAIT_TEST_GEMM, WAIT_TEST_ATTENTION, WAIT_TEST_DELTANET = 1, 2, 3
 
 
 def debug_arm_wait_timeout(which: int, copy_index: int, wait_ns: int):

@@ -34,7 +34,7 @@ struct WaitTest {
     uint32_t wait_ns = 2000000000u;
     int withhold = -1;
 };
-enum { kWaitTestGemm = 1, kWaitTestAttention = 2, kWaitTestDeltaNet = 3, kWaitTestGemv = 4 };
+enum { kWaitTestGemm = 1, kWaitTestAttention = 2, kWaitTestDeltaNet = 3 };
 // the armed setting for the next launch of kernel family `which` on a stream that is not
 // capturing (then disarmed), else the production setting
 WaitTest take_wait_test(int which, cudaStream_t st);
@@ -74,7 +74,6 @@ struct GemmEpi {
     const void* pf = nullptr;  // optional: the next GEMM's weights, prefetched into L2 by this launch
     int64_t pf_bytes = 0;
     WaitTest wt{};             // wait limit and the test hook (tcgen05 path)
-    unsigned* err = nullptr;   // mma.sync ring path: bit 16384 set when a weight stage did not arrive in time
 };
 
 // the batch above which the tcgen05 path (q8t weights, x16 activations) is used
@@ -84,8 +83,6 @@ constexpr int kUmmaMinBatch = 9;
 int gemm_nsplit(int M16, int KB, int num_sms);
 int gemm_grid_x(int M16);
 size_t gemm_ws_floats(int M16, int KB, int batch, int num_sms);
-// split-K tickets (zero at rest) a launch of this batch needs
-int gemm_tickets(int M16, int KB, int batch, int num_sms);
 void launch_q8_gemm(const Q8Weight& w, const uint8_t* xf, int batch, float* ws, unsigned* tickets,
                     const GemmEpi& ep, int num_sms, cudaStream_t st);
 void launch_q8_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,

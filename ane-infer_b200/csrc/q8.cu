@@ -9,7 +9,6 @@
 // represents the f32 value to 2^-22, so the result tracks the f32 reference closely.
 #include "common.cuh"
 #include "kernels.h"
-#include "umma.cuh"
 
 namespace ab2 {
 
@@ -250,174 +249,6 @@ __global__ void __launch_bounds__(WARPS * 32) q8_gemm_kernel(const uint4* __rest
     gemm_epilogue<NT, PACKED>(acc, mt, lane, batch, ep);
 }
 
-// ------------------------------------------------------------------------------ ring GEMV
-// Batches 1..8 on a persistent grid (one CTA per SM, kRingWarps warps). The weight matrix
-// is cut into units of one m16 tile over kps = KB / ns blocks; each warp takes a contiguous
-// range of units, whose weight bytes are one contiguous range of the packed layout, and
-// streams it through its own ring of kRingStages shared-memory stages filled by
-// cp.async.bulk (lane 0 issues, the warp consumes and refills the slot it has just read).
-// The per-block arithmetic is q8_gemm_kernel's. A unit's sum goes straight to the epilogue
-// when ns == 1; otherwise it is a split-K partial, reduced in split order by the warp that
-// completes a tile's last split (an atomic ticket per tile, no waiting).
-constexpr int kRingWarps = 8;
-constexpr int kRingStages = 4;
-constexpr int kRingCB = 8;                                   // Q8_0 blocks per stage
-constexpr int kRingQBytes = kRingCB * 512;                   // q bytes of m16 x (32 kRingCB)
-constexpr int kRingDBytes = kRingCB * 32;                    // their f16 scales
-constexpr int kRingStageBytes = kRingQBytes + kRingDBytes;   // 4352
-constexpr int kRingSmem = kRingWarps * kRingStages * (kRingStageBytes + 8) + 128;
-
-struct RingPlan {
-    int ns = 0, kps = 0;  // ns = 0: the shape does not fit the ring kernel
-};
-// ns: the smallest divisor of KB / kRingCB that gives every warp of the grid two units or
-// more (the largest when none does)
-RingPlan ring_plan(int M16, int KB, int batch, int num_sms) {
-    RingPlan r;
-    if (batch < 1 || batch > 8 || KB % kRingCB != 0) return r;
-    const int nc = KB / kRingCB;
-    const int64_t want = 2LL * num_sms * kRingWarps;
-    r.ns = nc;
-    for (int d = 1; d <= nc; d++)
-        if (nc % d == 0 && (int64_t)M16 * d >= want) {
-            r.ns = d;
-            break;
-        }
-    r.kps = KB / r.ns;
-    return r;
-}
-
-template <int NT, bool PACKED>
-__global__ void __launch_bounds__(kRingWarps * 32, 1)
-    q8_gemv_ring_kernel(const uint8_t* __restrict__ qs, const uint8_t* __restrict__ dsc, int M16, int KB,
-                        const uint4* __restrict__ xf, int batch, int ns, int kps, float4* __restrict__ ws,
-                        unsigned* __restrict__ tickets, GemmEpi ep) {
-    constexpr int NTILE = PACKED ? 1 : 2 * NT;
-    extern __shared__ uint8_t ring_smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ring_smem_raw) + 127) & ~(uintptr_t)127);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint8_t* ring = smem + warp * kRingStages * kRingStageBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRingWarps * kRingStages * kRingStageBytes) + warp * kRingStages;
-    const int gw = blockIdx.x * kRingWarps + warp, GW = gridDim.x * kRingWarps;
-    const int units = M16 * ns;
-    const int u0 = (int)((int64_t)units * gw / GW), u1 = (int)((int64_t)units * (gw + 1) / GW);
-    const int spu = kps / kRingCB;             // stages per unit
-    const int nst = (u1 - u0) * spu;           // stages of this warp
-    const int64_t gb0 = (int64_t)u0 * kps;     // its first block: unit u covers blocks [u kps, (u+1) kps)
-    const uint32_t WL = ep.wt.wait_ns;
-
-    if (lane == 0)
-        for (int s = 0; s < kRingStages; s++) mbar_init(&full[s], 1);
-    mbar_fence_init();
-    __syncwarp();
-    auto issue = [&](int i) {  // lane 0: stage i into its slot
-        if (i == ep.wt.withhold) return;  // test hook: this copy is never issued
-        const int slot = i % kRingStages;
-        uint8_t* dst = ring + slot * kRingStageBytes;
-        const int64_t gb = gb0 + (int64_t)i * kRingCB;
-        mbar_arrive_expect_tx(&full[slot], kRingStageBytes);
-        bulk_g2s(dst, qs + gb * 512, kRingQBytes, &full[slot]);
-        bulk_g2s(dst + kRingQBytes, dsc + gb * 32, kRingDBytes, &full[slot]);
-    };
-    // weights are constants: the first stages are requested before the wait for the kernel
-    // that produced the activations; everything that reads them, the partials, the tickets or
-    // the outputs comes after it
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    int issued = min(kRingStages, nst);
-    if (lane == 0)
-        for (int i = 0; i < issued; i++) issue(i);
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-
-    float acc[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-    int failed_at = -1;
-    for (int i = 0; i < nst; i++) {
-        const int slot = i % kRingStages;
-        const bool got = mbar_wait(&full[slot], (i / kRingStages) & 1, WL);
-        if (!__all_sync(kFull, got)) {
-            failed_at = i;
-            break;
-        }
-        const uint8_t* stg = ring + slot * kRingStageBytes;
-        const int kb0 = (int)((gb0 + (int64_t)i * kRingCB) % KB);  // the stage's first block in its tile
-#pragma unroll
-        for (int c = 0; c < kRingCB; c++) {
-            const uint4 q = *reinterpret_cast<const uint4*>(stg + (c * 32 + lane) * 16);
-            const uint32_t d = *reinterpret_cast<const uint32_t*>(stg + kRingQBytes + c * 32 + (lane >> 2) * 4);
-            uint32_t a[8];
-            q8_unpack(q, a);
-            const float dg = f16bits_to_f32(d), dg8 = f16bits_to_f32(d >> 16);
-            const uint4* xp = xf + (size_t)(kb0 + c) * NTILE * 32 + lane;
-#pragma unroll
-            for (int j = 0; j < NT; j++) {
-                float tq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                const uint4 bh = __ldg(xp + j * 32);
-                mma_f16(tq, a, bh.x, bh.y);
-                mma_f16(tq, a + 4, bh.z, bh.w);
-                if (!PACKED) {
-                    const uint4 bl = __ldg(xp + (NT + j) * 32);
-                    mma_f16(tq, a, bl.x, bl.y);
-                    mma_f16(tq, a + 4, bl.z, bl.w);
-                }
-                acc[j][0] = fmaf(dg, tq[0], acc[j][0]);
-                acc[j][1] = fmaf(dg, tq[1], acc[j][1]);
-                acc[j][2] = fmaf(dg8, tq[2], acc[j][2]);
-                acc[j][3] = fmaf(dg8, tq[3], acc[j][3]);
-            }
-        }
-        __syncwarp();  // every lane has read the slot
-        if (issued < nst) {
-            if (lane == 0) {
-                fence_proxy_async_smem();
-                issue(issued);
-            }
-            issued++;
-        }
-        if ((i + 1) % spu != 0) continue;
-        // the unit ends with this stage
-        const int u = u0 + i / spu, mt = u / ns, sp = u % ns;
-        if (ns > 1) {
-#pragma unroll
-            for (int j = 0; j < NT; j++)
-                __stcg(&ws[(((size_t)sp * M16 + mt) * NT + j) * 32 + lane],
-                       make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]));
-            __threadfence();
-            unsigned last = 0;
-            if (lane == 0) last = atomicAdd(&tickets[mt], 1u) == (unsigned)ns - 1u ? 1u : 0u;
-            last = __shfl_sync(kFull, last, 0);
-            if (last) {
-                __threadfence();
-#pragma unroll
-                for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-                for (int s2 = 0; s2 < ns; s2++) {
-#pragma unroll
-                    for (int j = 0; j < NT; j++) {
-                        const float4 pp = __ldcg(&ws[(((size_t)s2 * M16 + mt) * NT + j) * 32 + lane]);
-                        acc[j][0] += pp.x;
-                        acc[j][1] += pp.y;
-                        acc[j][2] += pp.z;
-                        acc[j][3] += pp.w;
-                    }
-                }
-                if (lane == 0) tickets[mt] = 0u;  // re-armed for the next launch
-                gemm_epilogue<NT, PACKED>(acc, mt, lane, batch, ep);
-            }
-        } else {
-            gemm_epilogue<NT, PACKED>(acc, mt, lane, batch, ep);
-        }
-#pragma unroll
-        for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
-    }
-    if (failed_at >= 0 && lane == 0) {
-        // a stage did not arrive in time: report it, then give the copies still in flight into
-        // this warp's ring a bounded time to land before the CTA's shared memory is released
-        if (ep.err) atomicOr(ep.err, 16384u);
-        for (int k = failed_at; k < issued; k++)
-            if (k != ep.wt.withhold) mbar_wait(&full[k % kRingStages], (k / kRingStages) & 1, WL);
-    }
-}
-
 // ------------------------------------------------------------------------------ launchers
 constexpr int kGemmWarps = 8;
 
@@ -435,35 +266,10 @@ int gemm_nsplit(int M16, int KB, int num_sms) {
 }
 
 size_t gemm_ws_floats(int M16, int KB, int batch, int num_sms) {
-    const RingPlan rp = ring_plan(M16, KB, batch, num_sms);
-    if (rp.ns) return rp.ns > 1 ? (size_t)rp.ns * M16 * 32 * 4 : 0;  // batch <= 8: one n8 tile
     int ns = gemm_nsplit(M16, KB, num_sms);
     if (ns <= 1) return 0;
     int nt = batch <= 4 ? 1 : (batch + 7) / 8;
     return (size_t)ns * M16 * nt * 32 * 4;
-}
-
-int gemm_tickets(int M16, int KB, int batch, int num_sms) {
-    const RingPlan rp = ring_plan(M16, KB, batch, num_sms);
-    if (rp.ns) return rp.ns > 1 ? M16 : 1;
-    return gemm_grid_x(M16);
-}
-
-template <bool PACKED>
-static void launch_ring_t(const Q8Weight& w, const uint8_t* xf, int batch, float* ws, unsigned* tickets,
-                          const GemmEpi& ep, const RingPlan& rp, int num_sms, cudaStream_t st) {
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        cudaFuncSetAttribute(q8_gemv_ring_kernel<1, PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingSmem);
-        attr_set[dev & 63] = true;
-    }
-    GemmEpi e = ep;
-    e.wt = take_wait_test(kWaitTestGemv, st);
-    launch_pdl(q8_gemv_ring_kernel<1, PACKED>, dim3(num_sms), dim3(kRingWarps * 32), kRingSmem, st, w.qs,
-               reinterpret_cast<const uint8_t*>(w.d), w.M16, w.KB, reinterpret_cast<const uint4*>(xf), batch, rp.ns,
-               rp.kps, reinterpret_cast<float4*>(ws), tickets, e);
 }
 
 template <int NT, bool PACKED>
@@ -479,11 +285,6 @@ static void launch_gemm_t(const Q8Weight& w, const uint8_t* xf, int batch, float
 
 void launch_q8_gemm(const Q8Weight& w, const uint8_t* xf, int batch, float* ws, unsigned* tickets,
                     const GemmEpi& ep, int num_sms, cudaStream_t st) {
-    const RingPlan rp = ring_plan(w.M16, w.KB, batch, num_sms);
-    if (rp.ns) {
-        if (batch <= 4) return launch_ring_t<true>(w, xf, batch, ws, tickets, ep, rp, num_sms, st);
-        return launch_ring_t<false>(w, xf, batch, ws, tickets, ep, rp, num_sms, st);
-    }
     if (batch <= 4) return launch_gemm_t<1, true>(w, xf, batch, ws, tickets, ep, num_sms, st);
     switch ((batch + 7) / 8) {
         case 1: return launch_gemm_t<1, false>(w, xf, batch, ws, tickets, ep, num_sms, st);

@@ -749,11 +749,8 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     size_t gws = 0;
     int gtk = 1;
     auto acc_gemm = [&](const Q8Weight& w) {
-        // the largest step, and the largest one on the ring kernel (batches 1..8)
-        for (const int b : {R, std::min(R, 8)}) {
-            gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, b, x->num_sms));
-            gtk = std::max(gtk, gemm_tickets(w.M16, w.KB, b, x->num_sms));
-        }
+        gws = std::max(gws, gemm_ws_floats(w.M16, w.KB, R, x->num_sms));
+        gtk = std::max(gtk, gemm_grid_x(w.M16));
     };
     for (auto& L : x->layers) {
         acc_gemm(L.w_in);
@@ -877,9 +874,7 @@ int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi&
         if (launch_q8_umma(w, xf, B, x->err_d, ep, x->num_sms, st, h2, h2_ld))
             return seterr(AB2_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     } else {
-        GemmEpi e = ep;
-        e.err = x->err_d;
-        launch_q8_gemm(w, xf, B, x->gws, x->gtk, e, x->num_sms, st);
+        launch_q8_gemm(w, xf, B, x->gws, x->gtk, ep, x->num_sms, st);
     }
     return 0;
 }
@@ -1248,20 +1243,20 @@ struct ab2_q8 {
 // ------------------------------------------------------------------------- wait-timeout test hook
 static std::mutex g_wt_mu;
 static std::atomic<bool> g_wt_any{false};
-static WaitTest g_wt_armed[5];
-static bool g_wt_on[5] = {false, false, false, false, false};
+static WaitTest g_wt_armed[4];
+static bool g_wt_on[4] = {false, false, false, false};
 
 namespace ab2 {
 WaitTest take_wait_test(int which, cudaStream_t st) {
     WaitTest w;
-    if (!g_wt_any.load(std::memory_order_relaxed) || which < 1 || which > 4) return w;
+    if (!g_wt_any.load(std::memory_order_relaxed) || which < 1 || which > 3) return w;
     std::lock_guard<std::mutex> lk(g_wt_mu);
     if (!g_wt_on[which]) return w;
     // never baked into a captured graph: a capture keeps the production setting and the arm
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return w;
     g_wt_on[which] = false;
-    g_wt_any.store(g_wt_on[1] || g_wt_on[2] || g_wt_on[3] || g_wt_on[4]);
+    g_wt_any.store(g_wt_on[1] || g_wt_on[2] || g_wt_on[3]);
     return g_wt_armed[which];
 }
 }  // namespace ab2
@@ -1269,15 +1264,15 @@ WaitTest take_wait_test(int which, cudaStream_t st) {
 AB2_API const char* ab2_last_error(void) { return g_err.c_str(); }
 
 AB2_API int ab2_debug_arm_wait_timeout(int which, int copy_index, uint32_t wait_ns) {
-    if (which < kWaitTestGemm || which > kWaitTestGemv)
-        return seterr(AB2_ERR_ARG, "which must be 1 (tcgen05 GEMM), 2 (attention), 3 (DeltaNet) or 4 (ring GEMV)");
+    if (which < kWaitTestGemm || which > kWaitTestDeltaNet)
+        return seterr(AB2_ERR_ARG, "which must be 1 (GEMM), 2 (attention) or 3 (DeltaNet)");
     if (copy_index < 0) return seterr(AB2_ERR_ARG, "copy_index must be >= 0");
     if (wait_ns != 0 && wait_ns < 1000) return seterr(AB2_ERR_ARG, "wait_ns must be 0 (disarm) or >= 1000");
     std::lock_guard<std::mutex> lk(g_wt_mu);
     g_wt_on[which] = wait_ns != 0;
     g_wt_armed[which].wait_ns = wait_ns;
     g_wt_armed[which].withhold = copy_index;
-    g_wt_any.store(g_wt_on[1] || g_wt_on[2] || g_wt_on[3] || g_wt_on[4]);
+    g_wt_any.store(g_wt_on[1] || g_wt_on[2] || g_wt_on[3]);
     return 0;
 }
 
@@ -1848,7 +1843,7 @@ AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* 
     size_t wsf = gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms);
     RET(ensure(&oc.ws, &oc.ws_bytes, std::max<size_t>(16, wsf * 4)));
     size_t tkb = oc.tk_n * 4;
-    RET(ensure((void**)&oc.tk, &tkb, (size_t)gemm_tickets(w->w.M16, w->w.KB, batch, w->num_sms) * 4));
+    RET(ensure((void**)&oc.tk, &tkb, (size_t)gemm_grid_x(w->w.M16) * 4));
     oc.tk_n = tkb / 4;
     size_t errb = oc.err ? 16 : 0;
     RET(ensure((void**)&oc.err, &errb, 16));
@@ -1863,9 +1858,7 @@ AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* 
         if (launch_q8_umma(w->w, oc.xf, batch, oc.err, ep, w->num_sms, st))
             return seterr(AB2_ERR_CUDA, "tcgen05 GEMM launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     } else {
-        GemmEpi e = ep;
-        e.err = oc.err;
-        launch_q8_gemm(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, e, w->num_sms, st);
+        launch_q8_gemm(w->w, oc.xf, batch, (float*)oc.ws, oc.tk, ep, w->num_sms, st);
     }
     CK(cudaGetLastError());
     return 0;
@@ -2037,7 +2030,8 @@ AB2_API int ab2_q8_gemv_noalloc(ab2_q8* w, const float* xin, int batch, float* y
     if (batch < 1 || batch >= kUmmaMinBatch)
         return seterr(AB2_ERR_CAPACITY, "ab2_q8_gemv_noalloc: batch %d outside [1, %d]", batch, kUmmaMinBatch - 1);
     if (w->device < 0 || w->device >= 64) return seterr(AB2_ERR_ARG, "device index out of range");
-    const size_t tk_bytes = (size_t)gemm_tickets(w->w.M16, w->w.KB, batch, w->num_sms) * 4;
+    const int gx = gemm_grid_x(w->w.M16);
+    const size_t tk_bytes = (size_t)gx * 4;
     const size_t xf_bytes = (xfrag_bytes((int)w->n, batch) + 255) & ~(size_t)255;
     const size_t ws_bytes = gemm_ws_floats(w->w.M16, w->w.KB, batch, w->num_sms) * 4;
     if (tk_bytes > kNoAllocTicketBytes || kNoAllocTicketBytes + xf_bytes + ws_bytes > kNoAllocScratchBytes)

@@ -206,11 +206,10 @@ int ab2_op_error(uint32_t* code);
  * copy_index (counted per CTA from 0) unissued and to give each of its waits wait_ns
  * nanoseconds instead of 2 s. The waits on that copy then expire without any fault: the
  * kernel sets its error bit (tcgen05 GEMM 128 with others of its pipeline, attention 4096,
- * DeltaNet 1024, ring GEMV 16384), waits for the copies it did issue, frees its tensor memory
- * and returns; that launch's results are invalid. The error is reported as any other:
- * ab2_op_error for the op-level calls, AB2_ERR_CUDA from the context's step or ab2_sync.
- * which: 1 the tcgen05 GEMM's weight copy, 2 the tensor-core attention's K/V tile copy, 3 the
- * DeltaNet state copy, 4 a weight stage of the batch-1..8 mma.sync GEMV (counted per warp).
+ * DeltaNet 1024), waits for the copies it did issue, frees its tensor memory and returns; that
+ * launch's results are invalid. The error is reported as any other: ab2_op_error for the
+ * op-level calls, AB2_ERR_CUDA from the context's step or ab2_sync. which: 1 the tcgen05
+ * GEMM's weight copy, 2 the tensor-core attention's K/V tile copy, 3 the DeltaNet state copy.
  * wait_ns = 0 disarms; otherwise at least 1000. Nothing is withheld unless this is called. */
 int ab2_debug_arm_wait_timeout(int which, int copy_index, uint32_t wait_ns);
 /* The packed tensor expanded back to f32 [m][n] (exact). */

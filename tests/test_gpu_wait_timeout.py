@@ -15,7 +15,7 @@ WAIT_NS = 5_000_000  # 5 ms instead of the production 2 s
 def disarm(pkg):
     """An arm that a failing test did not consume must not reach a later test's launch."""
     yield
-    for which in (1, 2, 3, 4):
+    for which in (1, 2, 3):
         pkg.debug_arm_wait_timeout(which, 0, 0)
 
 
@@ -38,32 +38,6 @@ def test_gemm_weight_copy_timeout(pkg, synth, cuda):
     print(f"GEMM error word 0x{code:x}")
     assert code & 128, hex(code)            # the converters' wait for the weight stage
     pkg.q8_gemv(w, x, y1, batch)            # the hook was consumed: a normal launch
-    assert pkg.op_error() == 0
-    assert torch.equal(y1, y0)
-
-
-@pytest.mark.parametrize("batch", [1, 8])
-def test_gemv_ring_stage_timeout(pkg, synth, cuda, batch):
-    # the batch-1..8 mma.sync GEMV streams its weights through per-warp rings of bulk copies;
-    # every warp's third stage is withheld (32768 x 2048: four stages per unit, 3.5 units per
-    # warp). The reduction of its split-K partials is in split order, so normal launches are
-    # bit-identical.
-    torch = cuda
-    m, n = 32768, 2048
-    rng = np.random.default_rng(37)
-    w = pkg.Q8Tensor(synth.random_q8_0(rng, m, n), m, n)
-    x = torch.from_numpy(rng.normal(0, 1, size=(batch, n)).astype(np.float32)).cuda()
-    y0 = torch.empty((batch, m), dtype=torch.float32, device="cuda")
-    y1 = torch.empty_like(y0)
-    assert pkg.op_error() == 0
-    pkg.q8_gemv(w, x, y0, batch)
-    assert pkg.op_error() == 0
-    pkg.debug_arm_wait_timeout(pkg.WAIT_TEST_GEMV, 2, WAIT_NS)
-    pkg.q8_gemv(w, x, y1, batch)
-    code = pkg.op_error()
-    print(f"GEMV error word 0x{code:x}")
-    assert code & 16384, hex(code)
-    pkg.q8_gemv(w, x, y1, batch)
     assert pkg.op_error() == 0
     assert torch.equal(y1, y0)
 
