@@ -27,21 +27,29 @@ def _need_two(cuda):
         pytest.skip("needs two GPUs")
 
 
-def _run(pkg, gguf, device, tp, B, n0, steps, exact, graph=False):
-    """Seeded state at n0 tokens, `steps` greedy steps of slots [0, B) from fixed tokens:
-    the logits of every step, the split info, layer 0's recurrent state and the first
-    attention layer's K cache of slot 0."""
+def _run(pkg, gguf, device, tp, B, n0, steps, exact, graph=False, prompt=0):
+    """Seeded state at n0 tokens (or, with prompt > 0, a prefill of that many tokens into each
+    slot), then `steps` greedy steps of slots [0, B) from fixed tokens: the logits of every
+    step (the prefills' last-token logits first), the split info, layer 0's recurrent state
+    and the first attention layer's K cache of slot 0."""
     from ane_infer_b200 import synth
-    ctx = pkg.DecodeContext(gguf, device=device, max_batch=B, max_ctx=n0 + steps + 8,
+    ctx = pkg.DecodeContext(gguf, device=device, max_batch=B, max_ctx=n0 + prompt + steps + 8,
                             exact_max_batch=B if exact else 0, tp=tp)
     try:
-        ctx.seed_state(seed=5, n_slots=B, n_tokens=n0)
+        out = []
+        if prompt:
+            for b in range(B):
+                lg, _ = ctx.prefill(b, synth.seeded_tokens(prompt, ctx.config["vocab"], seed=60 + b))
+                out.append(lg[None])
+            n0 = prompt
+        else:
+            ctx.seed_state(seed=5, n_slots=B, n_tokens=n0)
         ctx.step_graph(graph)
         toks = synth.seeded_tokens(B, ctx.config["vocab"], seed=9)
-        out = []
         for _ in range(steps):
             lg, toks = ctx.decode_step(toks)
             out.append(lg)
+        out = [np.concatenate(out[:B])] + out[B:] if prompt else out
         attn = ctx.layer_is_deltanet.index(False)
         rec, _ = ctx.get_dn_state(0, 0)
         k, _ = ctx.get_kv(attn, 0, n0 + steps)
@@ -60,8 +68,8 @@ def _worker(rank, world, tp_id, gguf_path, out_path, cases):
     pkg = load_pkg()
     gguf = np.fromfile(gguf_path, dtype=np.uint8)
     res = {}
-    for name, (B, n0, steps, exact, graph) in cases.items():
-        res[name] = _run(pkg, gguf, rank, (rank, world, tp_id[name]), B, n0, steps, exact, graph)
+    for name, case in cases.items():
+        res[name] = _run(pkg, gguf, rank, (rank, world, tp_id[name]), *case)
     with open(f"{out_path}.{rank}", "wb") as f:
         pickle.dump(res, f)
 
@@ -102,6 +110,7 @@ CASES_TINY = {
     "short_graph": (3, 40, 4, True, True),  # the same through the captured step graph
     "long": (1, 3000, 3, True, False),      # split plans differ: merge order only
     "tc": (9, 40, 1, False, False),         # tcgen05 path
+    "prefill": (2, 0, 3, True, False, 100),  # GPU prefill of 100 tokens per slot, then decode
 }
 
 
@@ -113,20 +122,22 @@ def test_split_tiny_matches_one_gpu(pkg, cuda, synth, tiny_gguf, tmp_path):
         s = res["short"]["split"]
         assert (s["rank"], s["world"], s["dn_h0"], s["dn_heads"], s["kv_h0"], s["kv_heads"]) == \
             (r, 2, r * cfg["dn_heads"] // 2, cfg["dn_heads"] // 2, r, 1)
-    for name, (B, n0, steps, exact, graph) in CASES_TINY.items():
-        one = _run(pkg, tiny_gguf, 0, None, B, n0, steps, exact, graph)
+    for name, case in CASES_TINY.items():
+        exact = case[3]
+        one = _run(pkg, tiny_gguf, 0, None, *case)
         r0, r1 = ranks[0][name], ranks[1][name]
         if exact:
             # replicated GEMMs on identical gathered inputs: the ranks agree bit for bit
             assert np.array_equal(r0["logits"], r1["logits"]), name
-        if name.startswith("short"):
+        if name.startswith("short") or name == "prefill":
             assert np.array_equal(r0["logits"], one["logits"]), name
             # each rank holds exactly its heads of the single-GPU state (zeros elsewhere)
             for r, res in enumerate((r0, r1)):
                 h = cfg["dn_heads"] // 2
                 assert np.array_equal(res["rec"][r * h:(r + 1) * h], one["rec"][r * h:(r + 1) * h])
                 assert not res["rec"][(1 - r) * h:(2 - r) * h].any()
-                assert np.array_equal(res["k"][r], one["k"][r])
+                if name.startswith("short"):
+                    assert np.array_equal(res["k"][r], one["k"][r])
         else:
             # the first step (later ones may follow a near-tie greedy pick apart)
             tol = LONG_TOL if name == "long" else TC_TOL
