@@ -145,3 +145,43 @@ def test_prefill_rejects_bad_requests(pkg, synth, tiny_gguf):
         with pytest.raises(pkg.Ab2Error) as ei:
             ctx.prefill(0, [1, 2])
         assert ei.value.code == -3
+
+
+def test_prefill_long_prompt_split_attention(pkg, oracle, synth, tiny_gguf, tiny_model):
+    """A 700-token prompt (11 chunks): from the fourth chunk on, the tokens' attention spans
+    more than one split of the slot's cache, so the per-token split partials and their merge
+    run on the shared slot too."""
+    prompt = synth.seeded_tokens(700, 32000, seed=77)
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=720, kv_bf16=True) as ctx:
+        lg, nx = ctx.prefill(0, prompt)
+        seq, lo = _oracle_run(tiny_model, prompt)
+        err = rel_err(lg, lo)
+        print(f"700-token prefill: last-token logit rel err {err:.2e}")
+        assert err < PREFILL_TOL
+        assert argmax_consistent(nx, lo, lg)
+        _check_states(ctx, seq, 700, ctx.layer_is_deltanet)
+
+
+@pytest.mark.parametrize("exact", [True, False])
+def test_prefill_after_long_seeded_context(pkg, synth, tiny_gguf, exact):
+    """Slots seeded with 2000 tokens of state, then 100 more tokens: prefill in one context
+    against one decode step per token in another context with the same seeded state. The
+    attention of every prompt token reads the long seeded prefix through several splits."""
+    prompt = synth.seeded_tokens(100, 32000, seed=8)
+    kw = dict(max_batch=1 if exact else 16, max_ctx=2112, kv_bf16=True)
+    with pkg.DecodeContext(tiny_gguf, **kw) as a, pkg.DecodeContext(tiny_gguf, **kw) as b:
+        for ctx in (a, b):
+            ctx.seed_state(seed=3, n_slots=1, n_tokens=2000)
+        lg_a, _ = a.prefill(0, prompt)
+        for t in prompt:
+            lg_b, _ = b.decode_step([int(t)])
+        tol = PREFILL_TOL if exact else LOGIT_TOL
+        assert rel_err(lg_a, lg_b[0]) < tol
+        assert a.get_pos(0) == b.get_pos(0) == 2100
+        for l, dn in enumerate(a.layer_is_deltanet):
+            if dn:
+                assert rel_err(a.get_dn_state(l, 0)[0], b.get_dn_state(l, 0)[0]) < tol
+            else:
+                ka, va = a.get_kv(l, 0, 2100)
+                kb, vb = b.get_kv(l, 0, 2100)
+                assert rel_err(ka, kb) < KV_TOL and rel_err(va, vb) < KV_TOL
