@@ -398,6 +398,25 @@ def run_ours(args):
                 "seq_per_gpu": B_weak, "global_batch": world * B_weak, "ms_per_step": round(wms / args.steps, 4),
                 "scaling": "weak"}
 
+    # ---- prefill of one 512-token prompt into slot 0 (after every timed decode phase; the
+    # slot's seeded state is replaced), through the host-buffer API, median of 3 calls
+    prefill = None
+    if args.prefill_tokens > 0 and args.prefill_tokens < cap:
+        n_pf = args.prefill_tokens
+        prompt = synth.seeded_tokens(n_pf, cfg["vocab"], seed=3)
+        pf_times = []
+        for i in range(4):
+            ctx.reset_slot(0)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ctx.prefill(0, prompt, want_logits=True)
+            if i:  # the first call is the warm-up
+                pf_times.append(time.perf_counter() - t0)
+        pf_s = max_over_ranks(statistics.median(pf_times))
+        prefill = {"value": round(world * n_pf / pf_s, 1), "unit": "tok/s", "prompt_tokens": n_pf,
+                   "ms_per_prompt": round(pf_s * 1e3, 3), "sequences": world,
+                   "timing": "host wall clock around the synchronous ab2_prefill call, median of 3, max over ranks"}
+
     # ---- CPU baseline (rank 0, N = 1): the oracle on one sequence of the same workload
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -429,6 +448,7 @@ def run_ours(args):
             "kernel_ms_per_step": {k: round(v["ms"] / args.steps, 4) for k, v in prof.items()},
             "weak_scaling": weak,
             "cpu_baseline": cpu,
+            "prefill": prefill,
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B * world,
                     "d2h_bytes_per_step": 4 * B * world,
                     "steps": n_e2e},
@@ -541,9 +561,9 @@ def run_split(args):
 
 def run_prefill(args):
     """Prefill throughput of one sequence on one GPU: --prefill N prompt tokens through
-    ab2_prefill (64-token chunks), prompt tokens per second from CUDA events on the context's
-    stream around each call (the call is synchronous; its host-to-device copy of the ids and
-    its device-to-host copy of the last logits are inside)."""
+    ab2_prefill (64-token chunks), prompt tokens per second from the host clock around each
+    call (the call is synchronous; its host-to-device copy of the ids and its device-to-host
+    copy of the last logits are inside)."""
     import torch
     pkg = load_pkg()
     from ane_infer_b200 import synth
@@ -744,6 +764,8 @@ def main():
     ap.add_argument("--k", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--prefill", type=int, default=0, help="time the prefill of this many prompt tokens instead")
+    ap.add_argument("--prefill-tokens", type=int, default=512,
+                    help="the decode run also times the prefill of one prompt of this many tokens (0: skip)")
     ap.add_argument("--prefill-batch", type=int, default=64,
                     help="max_batch of the prefill context (> 1: its GEMMs run on tcgen05)")
     ap.add_argument("--split", choices=["sequences", "heads"], default="sequences",
