@@ -201,58 +201,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     return s;
 }
 
-// ----------------------------------------------------------------------------------------
-// RMSNorm of one row into the activation layout of the next GEMM, the fast path of
-// rmsnorm_act_kernel (D a multiple of 8, at most kNormChunks * 2048): thread tid of a
-// 256-thread block holds x and the norm weights of elements (tid + 256 ch) * 8 .. + 7 in
-// xv / wv. Every thread of the block calls it; red is shared scratch of 8 floats.
-constexpr int kNormChunks = 2;
-__device__ __forceinline__ void rmsnorm_act_fast(const float4 (&xv)[kNormChunks][2], const float4 (&wv)[kNormChunks][2],
-                                                 int D, float eps, const ActOut& out, int b, float* red) {
-    const int tid = threadIdx.x;
-    float ss = 0.0f;
-#pragma unroll
-    for (int ch = 0; ch < kNormChunks; ch++) {
-        if ((tid + ch * 256) * 8 < D) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                ss += xv[ch][h].x * xv[ch][h].x;
-                ss += xv[ch][h].y * xv[ch][h].y;
-                ss += xv[ch][h].z * xv[ch][h].z;
-                ss += xv[ch][h].w * xv[ch][h].w;
-            }
-        }
-    }
-    ss = block_sum<256>(ss, red);
-    ss = ss / (float)D;
-    const float inv = 1.0f / sqrtf(ss + eps);
-#pragma unroll
-    for (int ch = 0; ch < kNormChunks; ch++) {
-        const int k0 = (tid + ch * 256) * 8;
-        if (k0 >= D) continue;
-        const float xs[8] = {xv[ch][0].x, xv[ch][0].y, xv[ch][0].z, xv[ch][0].w,
-                             xv[ch][1].x, xv[ch][1].y, xv[ch][1].z, xv[ch][1].w};
-        const float ws[8] = {wv[ch][0].x, wv[ch][0].y, wv[ch][0].z, wv[ch][0].w,
-                             wv[ch][1].x, wv[ch][1].y, wv[ch][1].z, wv[ch][1].w};
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) v[e] = xs[e] * inv * ws[e];
-        if (out.x16) {
-            // 8 consecutive k of one row are one 16-byte chunk of the x16 image
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                __half2 t = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
-                pk[e] = *reinterpret_cast<uint32_t*>(&t);
-            }
-            *reinterpret_cast<uint4*>(out.buf + x16_offset(out.npad, b, k0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; e++) act_store(out, b, k0 + e, v[e]);
-        }
-    }
-}
-
 // f32::total_cmp ordering key (greedy_sample, crates/cli/src/main.rs:1767-1785)
 __device__ __forceinline__ int32_t total_key(float f) {
     int32_t b = __float_as_int(f);

@@ -74,16 +74,6 @@ struct GemmEpi {
     const void* pf = nullptr;  // optional: the next GEMM's weights, prefetched into L2 by this launch
     int64_t pf_bytes = 0;
     WaitTest wt{};             // wait limit and the test hook (tcgen05 path)
-    // mma.sync path, batch 1, RESID mode: the RMSNorm of the updated residual row that the
-    // next GEMM takes (nt_x[0..nt_D) * rms * nt_w into nt_out), run by the launch's last CTA
-    // to finish its outputs (nt_ticket: a counter at zero, re-armed by that CTA); none when
-    // nt_w is null
-    const float* nt_x = nullptr;
-    const float* nt_w = nullptr;
-    int nt_D = 0;
-    float nt_eps = 0.0f;
-    ActOut nt_out{};
-    unsigned* nt_ticket = nullptr;
 };
 
 // the batch above which the tcgen05 path (q8t weights, x16 activations) is used

@@ -4,12 +4,14 @@
 
 namespace ab2 {
 
+// out = x * (1 / sqrt(mean(x^2) + eps)) * w, written as activation fragments for the next
+// GEMM (rmsnorm_vec, crates/cli/src/main.rs:1106-1113). One CTA per batch row.
 // out = x * (1 / sqrt(mean(x^2) + eps)) * w, written in the next GEMM's activation layout
 // (rmsnorm_vec, crates/cli/src/main.rs:1106-1113). One CTA per batch row. Rows of up to
-// kNormChunks * 2048 elements with D a multiple of 8 take the fast path (rmsnorm_act_fast,
-// whose arithmetic the one-sequence mma.sync GEMM's fused tail shares): each thread holds 8
-// consecutive elements per chunk in registers, so x is read once; the norm weights do not
-// depend on the previous kernel and are loaded before the grid dependency wait.
+// kNormChunks * 2048 elements with D a multiple of 8 take the fast path: each thread holds 8 consecutive elements per chunk in
+// registers, so x is read once; the norm weights do not depend on the previous kernel and
+// are loaded before the grid dependency wait.
+constexpr int kNormChunks = 2;
 
 __global__ void __launch_bounds__(256) rmsnorm_act_kernel(const float* __restrict__ x, int ldx,
                                                           const float* __restrict__ w, int D, float eps, ActOut out,
@@ -63,7 +65,47 @@ __global__ void __launch_bounds__(256) rmsnorm_act_kernel(const float* __restric
             for (int i = tid; i < zero_n; i += 256) zr[i] = 0.0f;
         }
     }
-    rmsnorm_act_fast(xv, wv, D, eps, out, b, red);
+    float ss = 0.0f;
+#pragma unroll
+    for (int ch = 0; ch < kNormChunks; ch++) {
+        if ((tid + ch * 256) * 8 < D) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                ss += xv[ch][h].x * xv[ch][h].x;
+                ss += xv[ch][h].y * xv[ch][h].y;
+                ss += xv[ch][h].z * xv[ch][h].z;
+                ss += xv[ch][h].w * xv[ch][h].w;
+            }
+        }
+    }
+    ss = block_sum<256>(ss, red);
+    ss = ss / (float)D;
+    const float inv = 1.0f / sqrtf(ss + eps);
+#pragma unroll
+    for (int ch = 0; ch < kNormChunks; ch++) {
+        const int k0 = (tid + ch * 256) * 8;
+        if (k0 >= D) continue;
+        const float xs[8] = {xv[ch][0].x, xv[ch][0].y, xv[ch][0].z, xv[ch][0].w,
+                             xv[ch][1].x, xv[ch][1].y, xv[ch][1].z, xv[ch][1].w};
+        const float ws[8] = {wv[ch][0].x, wv[ch][0].y, wv[ch][0].z, wv[ch][0].w,
+                             wv[ch][1].x, wv[ch][1].y, wv[ch][1].z, wv[ch][1].w};
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = xs[e] * inv * ws[e];
+        if (out.x16) {
+            // 8 consecutive k of one row are one 16-byte chunk of the x16 image
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                __half2 t = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
+                pk[e] = *reinterpret_cast<uint32_t*>(&t);
+            }
+            *reinterpret_cast<uint4*>(out.buf + x16_offset(out.npad, b, k0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) act_store(out, b, k0 + e, v[e]);
+        }
+    }
 }
 
 // The x16 layout pads K to a multiple of 64; the pad is cleared, because it meets zero

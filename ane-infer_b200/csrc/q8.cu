@@ -145,7 +145,6 @@ __global__ void __launch_bounds__(WARPS * 32) q8_gemm_kernel(const uint4* __rest
                                                              unsigned* __restrict__ tickets, GemmEpi ep) {
     constexpr int NTILE = PACKED ? 1 : 2 * NT;
     constexpr int U = 4;
-    static_assert(WARPS * 32 == 256, "the fused RMSNorm tail runs on 256 threads");
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int mt = blockIdx.x * WARPS + warp;
     const int nsplit = gridDim.y, split = blockIdx.y;
@@ -246,33 +245,8 @@ __global__ void __launch_bounds__(WARPS * 32) q8_gemm_kernel(const uint4* __rest
         }
         if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
     }
-    if (mt < M16) gemm_epilogue<NT, PACKED>(acc, mt, lane, batch, ep);
-    if (ep.nt_w) {
-        // The RMSNorm that feeds the next GEMM, in place of its own launch: every CTA that
-        // wrote outputs (one per row group) counts itself after its writes, and the last one
-        // normalises the whole row with rmsnorm_act_kernel's arithmetic.
-        __shared__ unsigned s_tail;
-        __shared__ float red[8];
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) s_tail = atomicAdd(ep.nt_ticket, 1u) == gridDim.x - 1u ? 1u : 0u;
-        __syncthreads();
-        if (!s_tail) return;
-        __threadfence();
-        float4 xv[kNormChunks][2], wv[kNormChunks][2];
-#pragma unroll
-        for (int ch = 0; ch < kNormChunks; ch++) {
-            const int k0 = (threadIdx.x + ch * 256) * 8;
-            if (k0 < ep.nt_D) {
-                xv[ch][0] = __ldcg(reinterpret_cast<const float4*>(ep.nt_x + k0));
-                xv[ch][1] = __ldcg(reinterpret_cast<const float4*>(ep.nt_x + k0 + 4));
-                wv[ch][0] = *reinterpret_cast<const float4*>(ep.nt_w + k0);
-                wv[ch][1] = *reinterpret_cast<const float4*>(ep.nt_w + k0 + 4);
-            }
-        }
-        rmsnorm_act_fast(xv, wv, ep.nt_D, ep.nt_eps, ep.nt_out, 0, red);
-        if (threadIdx.x == 0) *ep.nt_ticket = 0u;
-    }
+    if (mt >= M16) return;
+    gemm_epilogue<NT, PACKED>(acc, mt, lane, batch, ep);
 }
 
 // ------------------------------------------------------------------------------ launchers

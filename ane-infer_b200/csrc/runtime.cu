@@ -520,7 +520,6 @@ struct ab2_ctx {
     float2* rope = nullptr;     // [cap][rot/2]
     float* tmp_out = nullptr;   // [D] for per-layer entry points
     unsigned* err_d = nullptr;  // tensor-core pipeline error word (0 = ok)
-    unsigned* nrm_tk = nullptr; // counter of the RMSNorm fused into a one-sequence GEMM (0 at rest)
     alignas(64) uint8_t tmap_k[128];  // TMA tensor maps over the bf16 K / V caches ([rows][hd])
     alignas(64) uint8_t tmap_v[128];
     int exact_max = 1;          // steps of at most this many sequences take the exact mma.sync GEMM
@@ -742,7 +741,6 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     RET(x->dalloc(&x->xfa, actb));
     RET(x->dalloc(&x->xfb, actb));
     RET(x->dalloc(&x->err_d, 16));
-    RET(x->dalloc(&x->nrm_tk, 16));
     RET(x->dalloc(&x->logits, (size_t)B * c.vocab * 4));
     RET(x->dalloc(&x->tok_d, (size_t)B * 4));
     RET(x->dalloc(&x->next_d, (size_t)B * 4));
@@ -853,24 +851,6 @@ bool umma_for(const ab2_ctx* x, int B) { return x->use_umma && B > x->exact_max;
 
 ActOut act(const ab2_ctx* x, uint8_t* buf, int K, int B) { return act_out(buf, K, B, umma_for(x, B)); }
 
-// A decode step of one sequence on the mma.sync path folds each RMSNorm into the GEMM that
-// updates the residual before it (the last CTA of that GEMM normalises the row), which takes
-// 48 launches and their dependency hops out of the step for the 2B shape.
-bool norm_fused(const ab2_ctx* x, int B) {
-    const int64_t D = x->c.dim;
-    return B == 1 && !umma_for(x, B) && D % 8 == 0 && D <= kNormChunks * 2048;
-}
-
-// the RMSNorm `w` of the residual row into the activations xfa, in the epilogue of a RESID GEMM
-void fuse_norm(ab2_ctx* x, const float* w, GemmEpi& e) {
-    e.nt_x = x->x;
-    e.nt_w = w;
-    e.nt_D = (int)x->c.dim;
-    e.nt_eps = x->c.eps;
-    e.nt_out = act(x, x->xfa, (int)x->c.dim, 1);
-    e.nt_ticket = x->nrm_tk;
-}
-
 // L2 prefetch hint for a launch that precedes the tcgen05 GEMM on weight `w` (none on the
 // mma.sync path, whose weights are in the other layout); at most `cap` bytes
 void set_prefetch(ab2_ctx* x, int B, const Q8Weight* w, const void** pf, int64_t* pf_bytes,
@@ -932,10 +912,8 @@ int step_attn_chunk(const ab2_ctx* x, int B, int max_len) {
 // the mixer output goes to `out` with epilogue `mode` (RESID into x, or STORE)
 // With pf_p0 >= 0 the B rows are consecutive prompt tokens of sequence s0 at positions
 // pf_p0.. (a prefill chunk): the chunked DeltaNet kernel, and attention over one shared slot.
-// next_norm: with a fused RMSNorm (norm_fused), the norm weights of the row the output
-// projection updates (the FFN's input norm), applied in that GEMM's epilogue
 int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out, int ldo, int mode,
-              cudaStream_t st, int64_t pf_p0 = -1, const float* next_norm = nullptr) {
+              cudaStream_t st, int64_t pf_p0 = -1) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
     RET(gemm(x, L.w_in, x->xfa, B, epi_store(x->proj, x->ldp, L.w_in.M), st));
@@ -1029,14 +1007,13 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
     }
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
     set_prefetch(x, B, &L.gate_up, &e.pf, &e.pf_bytes);
-    if (next_norm) fuse_norm(x, next_norm, e);
     return gemm(x, L.w_out, x->xfb, B, e, st);
 }
 
 // next: the weight of the GEMM that follows this FFN on the stream (prefetched into L2 by the
 // down projection), or null
 int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cudaStream_t st,
-            const Q8Weight* next = nullptr, const float* next_norm = nullptr) {
+            const Q8Weight* next = nullptr) {
     const int D = (int)x->c.dim, F = (int)x->c.ffn;
     GemmEpi e = mode == EPI_RESID ? epi_resid(out, ldo, D) : epi_store(out, ldo, D);
     set_prefetch(x, B, next, &e.pf, &e.pf_bytes, kPrefetchCap);
@@ -1053,7 +1030,6 @@ int run_ffn(ab2_ctx* x, const Layer& L, int B, float* out, int ldo, int mode, cu
         return gemm(x, L.down, nullptr, B, e, st, x->h2, 2 * F);
     }
     RET(gemm(x, L.gate_up, x->xfa, B, epi_swiglu(act(x, x->xfb, F, B), F), st));
-    if (next_norm) fuse_norm(x, next_norm, e);
     return gemm(x, L.down, x->xfb, B, e, st);
 }
 
@@ -1081,41 +1057,33 @@ int enqueue_body(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, int slot,
         if (pf_p0 >= 0) launch_pos_fill(x->pf_pos, (int)pf_p0, B, st);
     }
     const ActOut xa = act(x, x->xfa, D, B);
-    // one-sequence decode on the mma.sync path: every RMSNorm after the first runs in the
-    // epilogue of the GEMM before it (the final norm in the last layer's down projection)
-    const bool fused = pf_p0 < 0 && norm_fused(x, B);
     for (size_t li = 0; li < x->layers.size(); li++) {
         const Layer& L = x->layers[li];
-        const bool last = li + 1 == x->layers.size();
-        const Q8Weight* next = !last ? &x->layers[li + 1].w_in : &x->lm_head;
-        if (!fused || li == 0) {
+        const Q8Weight* next = li + 1 < x->layers.size() ? &x->layers[li + 1].w_in : &x->lm_head;
+        {
             // units of a split pair add into the STORE output: clear those projection rows
             const int64_t z0 = umma_for(x, B) ? umma_plan(L.w_in.MT, L.w_in.KT, L.w_in.M, x->num_sms).zero_row0 : L.w_in.M;
             ProfScope ps(x, PC_OTHER, st);
             launch_rmsnorm_act(x->x, D, L.attn_norm, D, c.eps, B, xa, st, z0 < L.w_in.M ? x->proj + z0 : nullptr,
                                x->ldp, (int)(L.w_in.M - z0));
         }
-        RET(run_mixer(x, L, pf_p0 >= 0 ? slot : 0, B, max_len, x->x, D, EPI_RESID, st, pf_p0,
-                      fused ? L.post_norm : nullptr));
-        if (!fused) {
+        RET(run_mixer(x, L, pf_p0 >= 0 ? slot : 0, B, max_len, x->x, D, EPI_RESID, st, pf_p0));
+        {
             // on the tcgen05 path the gate/up projection adds into h2: clear it
             const int F2 = 2 * (int)c.ffn;
             ProfScope ps(x, PC_OTHER, st);
             launch_rmsnorm_act(x->x, D, L.post_norm, D, c.eps, B, xa, st, umma_for(x, B) ? x->h2 : nullptr, F2, F2);
         }
-        RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next,
-                    fused ? (last ? x->final_norm : x->layers[li + 1].attn_norm) : nullptr));
+        RET(run_ffn(x, L, B, x->x, D, EPI_RESID, st, next));
     }
     return 0;
 }
 
-// final norm of the B residual rows at xrows (unless `normed`: the body's last GEMM did it),
-// lm_head into logits_d [B][vocab], argmax
-int enqueue_head(ab2_ctx* x, const float* xrows, int B, float* logits_d, int32_t* next_d, cudaStream_t st,
-                 bool normed = false) {
+// final norm of the B residual rows at xrows, lm_head into logits_d [B][vocab], argmax
+int enqueue_head(ab2_ctx* x, const float* xrows, int B, float* logits_d, int32_t* next_d, cudaStream_t st) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
-    if (!normed) {
+    {
         // the lm_head's split units (all of them for small vocabularies, the K pieces of its
         // last pairs for large ones) add into the logits: clear those columns first
         const int64_t V = c.vocab;
@@ -1136,7 +1104,7 @@ int enqueue_head(ab2_ctx* x, const float* xrows, int B, float* logits_d, int32_t
 int enqueue_kernels(ab2_ctx* x, const int32_t* tok_d, int B, int max_len, float* logits_d, int32_t* next_d,
                     cudaStream_t st) {
     RET(enqueue_body(x, tok_d, B, max_len, 0, -1, st));
-    RET(enqueue_head(x, x->x, B, logits_d, next_d, st, norm_fused(x, B)));
+    RET(enqueue_head(x, x->x, B, logits_d, next_d, st));
     {
         ProfScope ps(x, PC_OTHER, st);
         launch_pos_advance(x->pos_d, B, st);
@@ -1222,7 +1190,6 @@ int64_t launches_per_step(const ab2_ctx* x, int B) {
     // embed + 7 per layer + final norm + lm_head + 2 argmax passes + position advance
     const int64_t per_layer = 7;
     int64_t n = 1 + (int64_t)x->layers.size() * per_layer + 1 + 1 + 2 + 1;
-    if (norm_fused(x, B)) n -= 2 * (int64_t)x->layers.size();  // the norms after the first run in GEMMs
     if (x->kv_bf16 && x->c.n_attn > 0) {
         // the tensor-core attention adds a merge kernel when the current context is split
         int max_len = 1;
