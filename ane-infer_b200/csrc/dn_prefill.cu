@@ -39,6 +39,7 @@ constexpr int kRows = kT / kPfCluster;    // rows of A and P each CTA computes (
 constexpr int kTg = kPfThreads / kCols;   // thread groups of one column (16)
 constexpr int kLd = DK + 4;               // padded row stride of q and k (conflict-free float4 rows)
 constexpr int kLv = kCols + 1;            // padded row stride of the per-CTA column buffers
+constexpr int kSb = 16;                   // rows per block of the forward substitution
 
 struct PfSmem {
     static constexpr int K = 0;                      // [kT][kLd] normed keys
@@ -110,9 +111,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    // this CTA's columns of the head's state: [DK rows][kCols], 8 float4 per row
-    for (int e = tid; e < DK * kCols / 4; e += kPfThreads)
-        reinterpret_cast<float4*>(S)[e] = reinterpret_cast<const float4*>(Sg + (size_t)(e >> 3) * DK + c0)[e & 7];
+    // this CTA's columns of the head's state: [DK rows][kCols], 8 float4 per row, copied
+    // asynchronously (cp.async: the thread goes on to the conv while they travel; waited
+    // for before the first barrier)
+    for (int e = tid; e < DK * kCols / 4; e += kPfThreads) {
+        const uint32_t dsm = (uint32_t)__cvta_generic_to_shared(reinterpret_cast<float4*>(S) + e);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dsm),
+                     "l"(reinterpret_cast<const float4*>(Sg + (size_t)(e >> 3) * DK + c0) + (e & 7))
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     // the gate values of this thread's outputs (token e / kCols, column e % kCols), loaded now
     float gate[kT * kCols / kPfThreads];
 #pragma unroll
@@ -123,14 +131,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     if (ch >= 0) {
         // conv_shift_and_append + conv_apply + SiLU per token (deltanet_cache.rs:34-54,
         // deltanet.rs:444-450), the window carried in registers; the chunk's inputs are
-        // loaded 16 at a time ahead of the window's serial dependency
+        // loaded 32 at a time ahead of the window's serial dependency
         cs = *reinterpret_cast<const float4*>(p.conv + (size_t)ch * 4);
-        for (int t0 = 0; t0 < T; t0 += 16) {
-            float xin[16];
+        for (int t0 = 0; t0 < T; t0 += 32) {
+            float xin[32];
 #pragma unroll
-            for (int u = 0; u < 16; u++) xin[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
+            for (int u = 0; u < 32; u++) xin[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
 #pragma unroll
-            for (int u = 0; u < 16; u++) {
+            for (int u = 0; u < 32; u++) {
                 if (t0 + u >= T) break;
                 cs = make_float4(cs.y, cs.z, cs.w, xin[u]);
                 float sum = cs.x * cw.x;
@@ -147,6 +155,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         beta[t] = ref_sigmoid(pr[4 * p.D + hg]);
         g[t] = sa * ref_softplus(pr[4 * p.D + H_all + hg] + dtb);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     if (warp == 0) {
         // inclusive prefix sum of the log-decays: lane l holds tokens 2l, 2l + 1
@@ -245,29 +254,41 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         }
     }
     cluster.sync();  // all of A and P has arrived; R is complete
-    // (I + A) Delta = R by forward substitution: a column is 8 lanes of one warp (column
-    // tid / 8, part tid % 8 over s = part, part + 8, ...), so a row needs only the warp
-    if (tid < kCols * 8) {
-        const int col = tid >> 3, part = tid & 7;
-        float* vc = Vb + col;
-        for (int t = 1; t < T; t++) {
-            // the (at most 8) terms s = part + 8m < t: loads issued together, then a tree sum
-            const float* at = A + t * kT;
-            float pr[kT / 8];
+    // (I + A) Delta = R by forward substitution in blocks of kSb rows: warp 0 solves a block
+    // (lane = column, the block's values in registers), then every thread subtracts the
+    // block's contribution from the rows below it
+    for (int jb = 0; jb < T; jb += kSb) {
+        const int nb = min(kSb, T - jb);
+        if (warp == 0) {
+            float dl[kSb];
 #pragma unroll
-            for (int m = 0; m < kT / 8; m++) {
-                const int s = part + 8 * m;
-                pr[m] = s < t ? at[s] * vc[s * kLv] : 0.0f;
+            for (int r = 0; r < kSb; r++) {
+                dl[r] = 0.0f;
+                if (r < nb) {
+                    const float* at = A + (jb + r) * kT + jb;
+                    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+                    for (int s2 = 0; s2 < r; s2++) {
+                        if (s2 & 1) a1 += at[s2] * dl[s2];
+                        else a0 += at[s2] * dl[s2];
+                    }
+                    dl[r] = Vb[(jb + r) * kLv + lane] - (a0 + a1);
+                }
             }
-            float a = ((pr[0] + pr[1]) + (pr[2] + pr[3])) + ((pr[4] + pr[5]) + (pr[6] + pr[7]));
-            a += __shfl_xor_sync(0xffffffffu, a, 1);
-            a += __shfl_xor_sync(0xffffffffu, a, 2);
-            a += __shfl_xor_sync(0xffffffffu, a, 4);
-            if (part == 0) vc[t * kLv] -= a;
-            __syncwarp();
+#pragma unroll
+            for (int r = 0; r < kSb; r++)
+                if (r < nb) Vb[(jb + r) * kLv + lane] = dl[r];
         }
+        __syncthreads();
+        for (int e = tid; e < (T - jb - nb) * kCols; e += kPfThreads) {
+            const int t = jb + nb + e / kCols, col = e % kCols;
+            const float* at = A + t * kT + jb;
+            float a = 0.0f;
+            for (int s2 = 0; s2 < nb; s2++) a += at[s2] * Vb[(jb + s2) * kLv + col];
+            Vb[t * kLv + col] -= a;
+        }
+        __syncthreads();
     }
-    __syncthreads();
     // O += P Delta (column j, tokens tg + kTg u)
 #pragma unroll
     for (int u = 0; u < 4; u++) {
