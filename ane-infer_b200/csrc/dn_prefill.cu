@@ -40,6 +40,8 @@ constexpr int kTg = kPfThreads / kCols;   // thread groups of one column (16)
 constexpr int kLd = DK + 4;               // padded row stride of q and k (conflict-free float4 rows)
 constexpr int kLv = kCols + 1;            // padded row stride of the per-CTA column buffers
 constexpr int kSb = 16;                   // rows per block of the forward substitution
+constexpr int kConvCh = 2 * DK + kCols;   // conv channels of a CTA: q, k and its v columns
+constexpr int kConvTok = 16;              // tokens per conv work item
 
 struct PfSmem {
     static constexpr int K = 0;                      // [kT][kLd] normed keys
@@ -90,23 +92,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     const int c0 = c * kCols;                                  // first value column of this CTA
     float* Sg = p.S + (size_t)h * DK * DK;
 
-    // this thread's conv channel: q and k (every CTA: all 256), v (this CTA's 16 columns)
-    int ch = -1, ch_c = 0;
-    float* dst = nullptr;
-    int ld = 0;
-    if (tid < 2 * DK) {
-        ch_c = tid % DK;
-        ch = (tid / DK) * p.D + hg * DK + ch_c;
-        dst = tid < DK ? Qb : Kb;
-        ld = kLd;
-    } else if (tid < 2 * DK + kCols) {
-        ch_c = tid - 2 * DK;
-        ch = 2 * p.D + hg * DK + c0 + ch_c;
-        dst = Vb;
-        ld = kLv;
-    }
-    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f), cs = cw;
-    if (ch >= 0) cw = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
+    // conv channels of this CTA: q and k (every CTA: all 256), v (its kCols columns); channel
+    // cc of kConvCh maps to the model's channel conv_channel(cc)
+    auto conv_channel = [&](int cc) {
+        return cc < 2 * DK ? (cc / DK) * p.D + hg * DK + cc % DK : 2 * p.D + hg * DK + c0 + (cc - 2 * DK);
+    };
     const float sa = p.ssm_a[hg], dtb = p.dt_bias[hg];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -128,32 +118,51 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         const int e = tid + u * kPfThreads, t = e / kCols;
         gate[u] = t < T ? p.proj[(size_t)t * p.ldp + 3 * p.D + hg * DK + c0 + e % kCols] : 0.0f;
     }
-    if (ch >= 0) {
-        // conv_shift_and_append + conv_apply + SiLU per token (deltanet_cache.rs:34-54,
-        // deltanet.rs:444-450), the window carried in registers; the chunk's inputs are
-        // loaded 32 at a time ahead of the window's serial dependency
-        cs = *reinterpret_cast<const float4*>(p.conv + (size_t)ch * 4);
-        for (int t0 = 0; t0 < T; t0 += 32) {
-            float xin[32];
-#pragma unroll
-            for (int u = 0; u < 32; u++) xin[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
-#pragma unroll
-            for (int u = 0; u < 32; u++) {
-                if (t0 + u >= T) break;
-                cs = make_float4(cs.y, cs.z, cs.w, xin[u]);
-                float sum = cs.x * cw.x;
-                sum += cs.y * cw.y;
-                sum += cs.z * cw.z;
-                sum += cs.w * cw.w;
-                dst[(t0 + u) * ld + ch_c] = ref_silu(sum);
-            }
+    // conv_shift_and_append + conv_apply + SiLU per token (deltanet_cache.rs:34-54,
+    // deltanet.rs:444-450). A token's window is the channel's last 4 inputs, so the work splits
+    // into items of (channel, 16 tokens) with no order between them: an item loads the 3 inputs
+    // before its tokens (from the conv state for the first block) with its own 16 in one round.
+    // The item holding the chunk's last token keeps the final window, the new conv state.
+    const int nblk = (T + kConvTok - 1) / kConvTok, nitems = kConvCh * nblk;
+    float4 fin_cs = make_float4(0.f, 0.f, 0.f, 0.f);
+    int fin_ch = -1;
+#pragma unroll 1
+    for (int e = tid; e < nitems; e += kPfThreads) {
+        const int cc = e % kConvCh, t0 = (e / kConvCh) * kConvTok, ch = conv_channel(cc);
+        const float4 cw = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
+        float4 cs;
+        if (t0 == 0) {
+            cs = *reinterpret_cast<const float4*>(p.conv + (size_t)ch * 4);
+        } else {
+            const float* pr = p.proj + (size_t)(t0 - 3) * p.ldp + ch;
+            cs = make_float4(0.0f, pr[0], pr[p.ldp], pr[2 * (size_t)p.ldp]);
         }
-    } else if (tid >= 3 * DK && tid - 3 * DK < T) {
+        float xin[kConvTok];
+#pragma unroll
+        for (int u = 0; u < kConvTok; u++) xin[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
+        float* dst = cc < DK ? Qb + cc : cc < 2 * DK ? Kb + (cc - DK) : Vb + (cc - 2 * DK);
+        const int ld = cc < 2 * DK ? kLd : kLv;
+#pragma unroll
+        for (int u = 0; u < kConvTok; u++) {
+            if (t0 + u >= T) break;
+            cs = make_float4(cs.y, cs.z, cs.w, xin[u]);
+            float sum = cs.x * cw.x;
+            sum += cs.y * cw.y;
+            sum += cs.z * cw.z;
+            sum += cs.w * cw.w;
+            dst[(t0 + u) * ld] = ref_silu(sum);
+        }
+        if (t0 + kConvTok >= T) {
+            fin_cs = cs;
+            fin_ch = ch;
+            if (cc < 2 * DK && c != 0) fin_ch = -1;  // q and k channels: one CTA of the cluster writes
+        }
+    }
+    if (tid < T) {
         // beta = sigmoid(W_beta x) and log d = ssm_a * softplus(W_alpha x + dt_bias) (deltanet.rs:469-480)
-        const int t = tid - 3 * DK;
-        const float* pr = p.proj + (size_t)t * p.ldp;
-        beta[t] = ref_sigmoid(pr[4 * p.D + hg]);
-        g[t] = sa * ref_softplus(pr[4 * p.D + H_all + hg] + dtb);
+        const float* pr = p.proj + (size_t)tid * p.ldp;
+        beta[tid] = ref_sigmoid(pr[4 * p.D + hg]);
+        g[tid] = sa * ref_softplus(pr[4 * p.D + H_all + hg] + dtb);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
@@ -199,7 +208,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     cluster.sync();
     // the windows after the chunk: the q and k channels' by one CTA of the cluster, the v
     // channels' by the CTA that owns them
-    if (ch >= 0 && (tid >= 2 * DK || c == 0)) *reinterpret_cast<float4*>(p.conv + (size_t)ch * 4) = cs;
+    if (fin_ch >= 0) *reinterpret_cast<float4*>(p.conv + (size_t)fin_ch * 4) = fin_cs;
 
     // rows [kRows c, kRows (c+1)) of A and P, one entry of each per thread, stored into every
     // CTA of the cluster
