@@ -174,13 +174,14 @@ class DecodeContext:
     def __init__(self, gguf, device: int = 0, max_batch: int = 1, max_ctx: int = 4096, kv_bf16: bool = True,
                  rope_dims: int = 0, exact_max_batch: int = 0, tp=None):
         """exact_max_batch: steps of at most this many sequences multiply the Q8_0 weights exactly
-        (mma.sync); larger steps use the tcgen05 path with f16 operands. 0 (default) = 1.
+        (mma.sync); larger steps use the tcgen05 path with f16 operands. 0 (default) = 1; -1:
+        every step on tcgen05, one sequence included.
         tp: (rank, world, id) to join a head-parallel split of `world` GPUs (id from
         tp_unique_id(), the same on every rank); returns once every rank has joined."""
         lib = load_library()
         buf = _host(gguf, np.uint8)
         opt = Ab2Options(int(kv_bf16), int(rope_dims), int(exact_max_batch))
-        self.exact_max_batch = int(exact_max_batch) or 1
+        self.exact_max_batch = 0 if int(exact_max_batch) < 0 else int(exact_max_batch) or 1
         h = C.c_void_p()
         if tp is None:
             _check(lib.ab2_create(_hp(buf), buf.size, device, max_batch, max_ctx, C.byref(opt), C.byref(h)))

@@ -1292,8 +1292,8 @@ static int create_ctx(const uint8_t* gguf, uint64_t len, int device, int max_bat
     *out = nullptr;
     if (max_batch < 1 || max_batch > 64) return seterr(AB2_ERR_ARG, "max_batch must be in [1, 64]");
     if (max_ctx < 1) return seterr(AB2_ERR_ARG, "max_ctx must be positive");
-    if (opt && (opt->exact_max_batch < 0 || opt->exact_max_batch > 64))
-        return seterr(AB2_ERR_ARG, "exact_max_batch must be in [0, 64]");
+    if (opt && (opt->exact_max_batch < -1 || opt->exact_max_batch > 64))
+        return seterr(AB2_ERR_ARG, "exact_max_batch must be -1 or in [0, 64]");
     {
         // the file is checked on the host first, so a bad model fails the same way with or
         // without a GPU
@@ -1317,7 +1317,8 @@ static int create_ctx(const uint8_t* gguf, uint64_t len, int device, int max_bat
     x->cap = max_ctx;
     x->kv_bf16 = opt ? opt->kv_bf16 != 0 : true;
     x->rot = opt ? opt->rope_dims : 0;
-    x->exact_max = opt && opt->exact_max_batch > 0 ? opt->exact_max_batch : 1;
+    // -1: no exact path, every step (one sequence too) on tcgen05; 0 (the default): 1
+    x->exact_max = !opt || opt->exact_max_batch == 0 ? 1 : opt->exact_max_batch < 0 ? 0 : opt->exact_max_batch;
     x->use_umma = max_batch > x->exact_max;
     x->tp_rank = tp_rank;
     x->tp_world = tp_world;

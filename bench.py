@@ -491,9 +491,9 @@ def run_split(args):
     n_e2e = max(2, args.steps // 2)
     cap = args.ctx + args.warmup + 2 * args.steps + n_e2e + 16
     if world > 1:
-        ctx = open_split_context(gguf, local, B, cap)
+        ctx = open_split_context(gguf, local, B, cap, exact_max_batch=args.exact_max_batch)
     else:
-        ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap)
+        ctx = pkg.DecodeContext(gguf, device=local, max_batch=B, max_ctx=cap, exact_max_batch=args.exact_max_batch)
     split = ctx.split()
     cfg = ctx.config
     # every rank seeds its part of one state and feeds the same tokens
@@ -768,6 +768,8 @@ def main():
                     help="the decode run also times the prefill of one prompt of this many tokens (0: skip)")
     ap.add_argument("--prefill-batch", type=int, default=64,
                     help="max_batch of the prefill context (> 1: its GEMMs run on tcgen05)")
+    ap.add_argument("--exact-max-batch", type=int, default=0,
+                    help="--split heads: the contexts' exact_max_batch (-1: one sequence on tcgen05 too)")
     ap.add_argument("--split", choices=["sequences", "heads"], default="sequences",
                     help="heads: time the head-parallel split's decode-step latency (use --batch 1)")
     args = ap.parse_args()

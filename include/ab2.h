@@ -38,7 +38,9 @@ typedef struct ab2_options {
     /* Steps of at most this many sequences multiply the Q8_0 weights exactly (mma.sync, the
      * weights q*d kept exact in f32 sums, activations as an f16 hi/lo pair); larger steps use
      * the tcgen05 path, whose operands are rounded once to f16. 0 (default) = 1: one sequence
-     * exact, every batched step on the tensor-core path. At most 64. */
+     * exact, every batched step on the tensor-core path. -1: no exact path, one sequence on
+     * the tensor-core path too (lower latency, the batched path's declared rounding). At most
+     * 64. */
     int32_t exact_max_batch;
     int32_t reserved[5];
 } ab2_options;

@@ -193,7 +193,7 @@ def test_wait_timeout_hook_arguments(pkg):
 
 def test_create_rejects_bad_exact_max_batch(pkg, tiny_gguf):
     """exact_max_batch is checked before any device work."""
-    for bad in (-1, 65):
+    for bad in (-2, 65):
         with pytest.raises(pkg.Ab2Error) as ei:
             pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=8, exact_max_batch=bad)
         assert ei.value.code == -1 and "exact_max_batch" in str(ei.value)

@@ -268,6 +268,27 @@ def test_exact_max_batch_option(pkg, oracle, tiny_gguf, tiny_model):
     assert errs[4] < 1e-4 and errs[0] < LOGIT_TOL and errs[0] > 10 * errs[4]
 
 
+def test_single_sequence_on_tensor_cores(pkg, oracle, tiny_gguf, tiny_model):
+    """exact_max_batch = -1: one sequence also runs on the tcgen05 path (the batched path's
+    declared f16 operand rounding), within the logit bar for 16 greedy steps."""
+    ctx = pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=40, kv_bf16=True, exact_max_batch=-1)
+    assert ctx.tensor_core_gemm(1)
+    seq = tiny_model.new_seq(kv_bf16=True)
+    tok, worst = 17, 0.0
+    for step in range(16):
+        lg, nx = ctx.decode_step([tok])
+        lo = seq.forward(tok)
+        err = rel_err(lg[0], lo)
+        worst = max(worst, err)
+        assert err < LOGIT_TOL, (step, err)
+        assert argmax_consistent(int(nx[0]), lo, lg[0]), step
+        if int(nx[0]) != oracle.greedy(lo):
+            break  # a near tie: the continuations part
+        tok = int(nx[0])
+    ctx.close()
+    print(f"one sequence on tcgen05: worst logit rel err {worst:.2e}")
+
+
 def test_state_io_and_capacity(pkg, tiny_gguf):
     ctx = pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=8, kv_bf16=True)
     rng = np.random.default_rng(4)
