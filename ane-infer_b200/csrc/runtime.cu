@@ -530,7 +530,7 @@ struct ab2_ctx {
     int dn_h0 = 0, dn_hl = 0, kv_h0 = 0, kv_hl = 0;
     bool dn_split = false, kv_split = false;  // which mixers are split (the others run replicated)
     ncclComm_t nccl = nullptr;  // the communicator of the split
-    bool use_umma = false;      // max_batch > exact_max: q8t weights are packed too
+    bool use_umma = false;      // some step has more rows than exact_max: q8t weights are packed too
     // pinned host staging
     int32_t *tok_h = nullptr, *next_h = nullptr;
     unsigned* err_h = nullptr;
@@ -1319,7 +1319,9 @@ static int create_ctx(const uint8_t* gguf, uint64_t len, int device, int max_bat
     x->rot = opt ? opt->rope_dims : 0;
     // -1: no exact path, every step (one sequence too) on tcgen05; 0 (the default): 1
     x->exact_max = !opt || opt->exact_max_batch == 0 ? 1 : opt->exact_max_batch < 0 ? 0 : opt->exact_max_batch;
-    x->use_umma = max_batch > x->exact_max;
+    // the tcgen05 weights are packed when a decode step or a prefill chunk (kPrefillChunk
+    // rows) can have more rows than exact_max
+    x->use_umma = std::max(max_batch, kPrefillChunk) > x->exact_max;
     x->tp_rank = tp_rank;
     x->tp_world = tp_world;
     cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device);

@@ -570,7 +570,8 @@ def run_prefill(args):
     shape = synth.shape_2b()
     gguf = synth.build_model_gguf(shape, seed=0)
     n = args.prefill
-    ctx = pkg.DecodeContext(gguf, device=0, max_batch=args.prefill_batch, max_ctx=n + 8, kv_bf16=True)
+    ctx = pkg.DecodeContext(gguf, device=0, max_batch=args.prefill_batch, max_ctx=n + 8, kv_bf16=True,
+                            exact_max_batch=args.exact_max_batch)
     cfg = ctx.config
     prompt = synth.seeded_tokens(n, cfg["vocab"], seed=3)
     for _ in range(args.warmup):
@@ -766,10 +767,10 @@ def main():
     ap.add_argument("--prefill", type=int, default=0, help="time the prefill of this many prompt tokens instead")
     ap.add_argument("--prefill-tokens", type=int, default=512,
                     help="the decode run also times the prefill of one prompt of this many tokens (0: skip)")
-    ap.add_argument("--prefill-batch", type=int, default=64,
-                    help="max_batch of the prefill context (> 1: its GEMMs run on tcgen05)")
+    ap.add_argument("--prefill-batch", type=int, default=64, help="max_batch of the prefill context")
     ap.add_argument("--exact-max-batch", type=int, default=0,
-                    help="--split heads: the contexts' exact_max_batch (-1: one sequence on tcgen05 too)")
+                    help="--split heads and --prefill: the contexts' exact_max_batch (-1: one sequence on "
+                         "tcgen05 too; 64: prefill chunks on the exact path)")
     ap.add_argument("--split", choices=["sequences", "heads"], default="sequences",
                     help="heads: time the head-parallel split's decode-step latency (use --batch 1)")
     args = ap.parse_args()

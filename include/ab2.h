@@ -40,7 +40,8 @@ typedef struct ab2_options {
      * the tcgen05 path, whose operands are rounded once to f16. 0 (default) = 1: one sequence
      * exact, every batched step on the tensor-core path. -1: no exact path, one sequence on
      * the tensor-core path too (lower latency, the batched path's declared rounding). At most
-     * 64. */
+     * 64. ab2_prefill runs its prompt in 64-row steps, so a prefill is exact only with 64 here.
+     * Unless it is 64, the context holds the tensor-core copy of the weights too. */
     int32_t exact_max_batch;
     int32_t reserved[5];
 } ab2_options;

@@ -3,10 +3,11 @@ chunkwise form, each token's attention over the slot's cache) against the oracle
 token-by-token qwen35_forward_token, the reference's own prompt loop
 (crates/cli/src/main.rs:358-362).
 
-On the exact-weight path the prefill and the oracle differ only in the order of f32 sums
-(the 64-row GEMM's K order, the chunkwise recurrence), so the last token's logits and every
-state agree to PREFILL_TOL. On the tcgen05 path (a context whose batched steps run on the
-tensor cores) the GEMM operands are rounded to f16 and the decode parity bar applies."""
+A prefill chunk is a 64-row step, so it runs on the exact-weight path only in a context with
+exact_max_batch = 64 (EXACT below). There the prefill and the oracle differ only in the order
+of f32 sums (the 64-row GEMM's K order, the chunkwise recurrence), so the last token's logits
+and every state agree to PREFILL_TOL. In a default context the chunk runs on the tcgen05 path,
+whose GEMM operands are rounded to f16, and the decode parity bar applies."""
 import numpy as np
 import pytest
 
@@ -17,6 +18,7 @@ pytestmark = pytest.mark.gpu
 PREFILL_TOL = 1e-4   # max|d| <= PREFILL_TOL * max|ref|: logits and recurrent / conv state
 KV_TOL = 1e-2        # bf16 cache entries (one bf16 ulp is 2^-8 relative)
 LOGIT_TOL = 1e-2     # tcgen05 path (f16 operands), the decode parity bar
+EXACT = 64           # exact_max_batch that keeps a 64-row prefill chunk on the exact path
 
 
 def _oracle_run(model, tokens, seq=None):
@@ -46,7 +48,7 @@ def test_prefill_tiny_matches_oracle(pkg, oracle, synth, tiny_gguf, tiny_model, 
     and every DeltaNet, conv and KV state equal the oracle's after the same prompt; then 16
     greedy decode steps from the prefilled state follow the oracle's."""
     prompt = synth.seeded_tokens(n, 32000, seed=40 + n)
-    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=n + 24, kv_bf16=True) as ctx:
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=n + 24, kv_bf16=True, exact_max_batch=EXACT) as ctx:
         lg, nx = ctx.prefill(0, prompt)
         seq, lo = _oracle_run(tiny_model, prompt)
         err = rel_err(lg, lo)
@@ -70,7 +72,7 @@ def test_prefill_continues_a_sequence(pkg, oracle, synth, tiny_gguf, tiny_model)
     """Decode 5 tokens, then prefill 70 more from position 5 (a chunk that starts mid-sequence
     and crosses the 64-token boundary), then prefill 3 more."""
     toks = synth.seeded_tokens(78, 32000, seed=7)
-    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=96, kv_bf16=True) as ctx:
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=96, kv_bf16=True, exact_max_batch=EXACT) as ctx:
         for t in toks[:5]:
             ctx.decode_step([int(t)])
         ctx.prefill(0, toks[5:75])
@@ -85,7 +87,7 @@ def test_prefill_matches_stepwise_decode(pkg, synth, tiny_gguf):
     """Prefill of slot 1 against one decode step per token of the same prompt in slot 0 of
     the same context: the same logits to PREFILL_TOL, and slot 1's prefill leaves slot 0 alone."""
     prompt = synth.seeded_tokens(100, 32000, seed=3)
-    with pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=128, kv_bf16=True, exact_max_batch=2) as ctx:
+    with pkg.DecodeContext(tiny_gguf, max_batch=2, max_ctx=128, kv_bf16=True, exact_max_batch=EXACT) as ctx:
         lg1, _ = ctx.prefill(1, prompt)
         assert ctx.get_pos(0) == 0
         assert not ctx.get_dn_state(0, 0)[0].any()
@@ -98,10 +100,10 @@ def test_prefill_matches_stepwise_decode(pkg, synth, tiny_gguf):
 
 
 def test_prefill_tensor_core_path(pkg, oracle, synth, tiny_gguf, tiny_model):
-    """A context whose batched steps run on tcgen05 prefills with that GEMM (64-row chunks):
+    """A default context prefills on the tcgen05 GEMM (64-row chunks, even with max_batch 1):
     within the decode parity bar of the oracle."""
     prompt = synth.seeded_tokens(130, 32000, seed=11)
-    with pkg.DecodeContext(tiny_gguf, max_batch=16, max_ctx=140, kv_bf16=True) as ctx:
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=140, kv_bf16=True) as ctx:
         assert ctx.tensor_core_gemm(64)
         lg, nx = ctx.prefill(0, prompt)
         seq, lo = _oracle_run(tiny_model, prompt)
@@ -115,7 +117,7 @@ def test_prefill_2b_matches_oracle(pkg, oracle, synth):
     """The 2B shape (16 DeltaNet heads, hd-256 attention): 70 prompt tokens (two chunks)."""
     gguf = synth.build_model_gguf(synth.shape_2b(), seed=0)
     prompt = synth.seeded_tokens(70, 151936, seed=5)
-    with pkg.DecodeContext(gguf, max_batch=1, max_ctx=80, kv_bf16=True) as ctx:
+    with pkg.DecodeContext(gguf, max_batch=1, max_ctx=80, kv_bf16=True, exact_max_batch=EXACT) as ctx:
         lg, nx = ctx.prefill(0, prompt)
         model = oracle.Model(gguf, ctx_cap=80)
         seq, lo = _oracle_run(model, prompt)
@@ -152,7 +154,7 @@ def test_prefill_long_prompt_split_attention(pkg, oracle, synth, tiny_gguf, tiny
     more than one split of the slot's cache, so the per-token split partials and their merge
     run on the shared slot too."""
     prompt = synth.seeded_tokens(700, 32000, seed=77)
-    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=720, kv_bf16=True) as ctx:
+    with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=720, kv_bf16=True, exact_max_batch=EXACT) as ctx:
         lg, nx = ctx.prefill(0, prompt)
         seq, lo = _oracle_run(tiny_model, prompt)
         err = rel_err(lg, lo)
@@ -168,7 +170,7 @@ def test_prefill_after_long_seeded_context(pkg, synth, tiny_gguf, exact):
     against one decode step per token in another context with the same seeded state. The
     attention of every prompt token reads the long seeded prefix through several splits."""
     prompt = synth.seeded_tokens(100, 32000, seed=8)
-    kw = dict(max_batch=1 if exact else 16, max_ctx=2112, kv_bf16=True)
+    kw = dict(max_batch=1, max_ctx=2112, kv_bf16=True, exact_max_batch=EXACT if exact else 0)
     with pkg.DecodeContext(tiny_gguf, **kw) as a, pkg.DecodeContext(tiny_gguf, **kw) as b:
         for ctx in (a, b):
             ctx.seed_state(seed=3, n_slots=1, n_tokens=2000)

@@ -34,7 +34,7 @@ def _run(pkg, gguf, device, tp, B, n0, steps, exact, graph=False, prompt=0):
     and the first attention layer's K cache of slot 0."""
     from ane_infer_b200 import synth
     ctx = pkg.DecodeContext(gguf, device=device, max_batch=B, max_ctx=n0 + prompt + steps + 8,
-                            exact_max_batch=B if exact else 0, tp=tp)
+                            exact_max_batch=(64 if prompt else B) if exact else 0, tp=tp)
     try:
         out = []
         if prompt:
