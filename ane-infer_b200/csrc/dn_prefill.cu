@@ -18,8 +18,8 @@
 // holds the chunk's normed q and k, computes kT / kPfCluster rows of A and P and stores them
 // into every CTA's shared memory (distributed shared memory), and owns 128 / kPfCluster of
 // the head's value columns: their slice of the state, of V, Delta and O. The gated RMSNorm's
-// sum of squares over the 128 columns is exchanged the same way. The products run on the
-// CUDA cores in f32, like the reference's.
+// sum of squares over the 128 columns is exchanged the same way. The matrix products run on
+// the tensor cores in 3xTF32 (about f32 accuracy, below); the rest is f32 on the CUDA cores.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -36,9 +36,10 @@ constexpr int kPfThreads = 512;
 constexpr int kPfCluster = 4;             // CTAs per head (16 clusters of 8 do not fit at once)
 constexpr int kCols = DK / kPfCluster;    // value columns per CTA (32)
 constexpr int kRows = kT / kPfCluster;    // rows of A and P each CTA computes (16)
-constexpr int kTg = kPfThreads / kCols;   // thread groups of one column (16)
 constexpr int kLd = DK + 4;               // padded row stride of q and k (conflict-free float4 rows)
-constexpr int kLv = kCols + 1;            // padded row stride of the per-CTA column buffers
+constexpr int kLv = kCols + 8;            // padded row stride of V / Delta and O (conflict-free fragments)
+constexpr int kLs = kCols + 8;            // padded row stride of the state slice
+constexpr int kLp = kT + 4;               // padded row stride of A and P
 constexpr int kSb = 16;                   // rows per block of the forward substitution
 constexpr int kConvCh = 2 * DK + kCols;   // conv channels of a CTA: q, k and its v columns
 constexpr int kConvTok = 16;              // tokens per conv work item
@@ -46,12 +47,12 @@ constexpr int kConvTok = 16;              // tokens per conv work item
 struct PfSmem {
     static constexpr int K = 0;                      // [kT][kLd] normed keys
     static constexpr int Q = K + kT * kLd;           // [kT][kLd] normed, scaled queries
-    static constexpr int S = Q + kT * kLd;           // [DK][kCols] this CTA's columns of the state
-    static constexpr int V = S + DK * kCols;         // [kT][kLv] values; later R, then Delta
+    static constexpr int S = Q + kT * kLd;           // [DK][kLs] this CTA's columns of the state
+    static constexpr int V = S + DK * kLs;           // [kT][kLv] values; later R, then Delta
     static constexpr int O = V + kT * kLv;           // [kT][kLv] outputs
-    static constexpr int A = O + kT * kLv;           // [kT][kT]
-    static constexpr int P = A + kT * kT;            // [kT][kT]
-    static constexpr int G = P + kT * kT;            // [kT] cumulative log-decay
+    static constexpr int A = O + kT * kLv;           // [kT][kLp]
+    static constexpr int P = A + kT * kLp;           // [kT][kLp]
+    static constexpr int G = P + kT * kLp;           // [kT] cumulative log-decay
     static constexpr int BETA = G + kT;              // [kT]
     static constexpr int EG = BETA + kT;             // [kT] e^{g_t}
     static constexpr int W = EG + kT;                // [kT] e^{g_{T-1} - g_t}
@@ -60,14 +61,49 @@ struct PfSmem {
     static constexpr int bytes = floats * 4;
 };
 static_assert(PfSmem::bytes <= 227 * 1024, "prefill shared memory");
-static_assert(kCols == 32 && kTg == 16 && kRows * kT == 2 * kPfThreads, "prefill thread mapping");
+// the warp tilings below: 16 warps; A/P rows are one m16 tile per CTA; 4 x 4 tiles of 16
+// tokens x 8 columns; 8 x 4 tiles of 16 state rows x 8 columns
+static_assert(kPfThreads == 512 && kCols == 32 && kRows == 16 && kT == 64, "prefill warp tiling");
 
-__device__ __forceinline__ float dot4(float4 a, float4 b, float acc) {
-    acc += a.x * b.x;
-    acc += a.y * b.y;
-    acc += a.z * b.z;
-    acc += a.w * b.w;
-    return acc;
+// The chunk's matrix products run on the tensor cores at about f32 accuracy (3xTF32): each
+// f32 operand is split into a tf32 high part and a tf32 remainder, and the three products
+// that matter (lo*hi, hi*lo, hi*hi) are accumulated in f32 by mma.sync m16n8k8. Fragments
+// (g = lane / 4, q = lane % 4): A[16 x 8] a0 (g, q), a1 (g + 8, q), a2 (g, q + 4),
+// a3 (g + 8, q + 4); B[8 x 8] b0 (q, g), b1 (q + 4, g); C[16 x 8] c0 (g, 2q), c1 (g, 2q + 1),
+// c2 (g + 8, 2q), c3 (g + 8, 2q + 1).
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+    hi = to_tf32(x);
+    lo = to_tf32(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+struct SplitB {
+    uint32_t h0, l0, h1, l1;
+};
+__device__ __forceinline__ SplitB split_b(float b0, float b1) {
+    SplitB r;
+    split_tf32(b0, r.h0, r.l0);
+    split_tf32(b1, r.h1, r.l1);
+    return r;
+}
+// c += A B (A as four f32 fragment values, B pre-split)
+__device__ __forceinline__ void mma3(float c[4], const float a[4], const SplitB& b) {
+    uint32_t ah[4], al[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) split_tf32(a[i], ah[i], al[i]);
+    mma_tf32(c, al, b.h0, b.h1);
+    mma_tf32(c, ah, b.l0, b.l1);
+    mma_tf32(c, ah, b.h0, b.h1);
 }
 
 __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, int T) {
@@ -105,7 +141,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     // asynchronously (cp.async: the thread goes on to the conv while they travel; waited
     // for before the first barrier)
     for (int e = tid; e < DK * kCols / 4; e += kPfThreads) {
-        const uint32_t dsm = (uint32_t)__cvta_generic_to_shared(reinterpret_cast<float4*>(S) + e);
+        const uint32_t dsm = (uint32_t)__cvta_generic_to_shared(reinterpret_cast<float4*>(S + (e >> 3) * kLs) + (e & 7));
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dsm),
                      "l"(reinterpret_cast<const float4*>(Sg + (size_t)(e >> 3) * DK + c0) + (e & 7))
                      : "memory");
@@ -166,6 +202,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
+    // rows past the chunk's last token enter the products as zeros (a shorter last chunk)
+    for (int e = tid; e < (kT - T) * kLd; e += kPfThreads) {
+        Kb[T * kLd + e] = 0.0f;
+        Qb[T * kLd + e] = 0.0f;
+    }
+    for (int e = tid; e < (kT - T) * kLv; e += kPfThreads) Vb[T * kLv + e] = 0.0f;
     if (warp == 0) {
         // inclusive prefix sum of the log-decays: lane l holds tokens 2l, 2l + 1
         const float a0 = 2 * lane < T ? g[2 * lane] : 0.0f;
@@ -199,9 +241,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         }
     }
     __syncthreads();
-    if (tid < T) {
-        eg[tid] = expf(g[tid]);
-        w[tid] = expf(g[T - 1] - g[tid]);
+    if (tid < kT) {
+        eg[tid] = tid < T ? expf(g[tid]) : 0.0f;
+        w[tid] = tid < T ? expf(g[T - 1] - g[tid]) : 0.0f;
     }
     // every CTA of the cluster has started (its shared memory may now be written) and has
     // read the conv windows before they are replaced
@@ -210,55 +252,53 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     // channels' by the CTA that owns them
     if (fin_ch >= 0) *reinterpret_cast<float4*>(p.conv + (size_t)fin_ch * 4) = fin_cs;
 
-    // rows [kRows c, kRows (c+1)) of A and P, one entry of each per thread, stored into every
-    // CTA of the cluster
-#pragma unroll 1
-    for (int u = 0; u < 2; u++) {
-        const int e = tid + u * kPfThreads, t = c * kRows + (e >> 6), s = e & (kT - 1);
-        float kk = 0.0f, qk = 0.0f;
-        if (t < T && s <= t) {
-            const float* kt = Kb + t * kLd;
-            const float* qt = Qb + t * kLd;
-            const float* ks = Kb + s * kLd;
-#pragma unroll 8
-            for (int i = 0; i < DK; i += 4) {
-                const float4 k4 = *reinterpret_cast<const float4*>(ks + i);
-                kk = dot4(*reinterpret_cast<const float4*>(kt + i), k4, kk);
-                qk = dot4(*reinterpret_cast<const float4*>(qt + i), k4, qk);
-            }
+    const int gq = lane >> 2, tq = lane & 3;  // fragment row group and column pair
+    // rows [kRows c, kRows (c+1)) of A (warps 0-7, from k) and P (warps 8-15, from q): warp w
+    // computes columns s of tile w % 8, and stores its entries into every CTA of the cluster
+    {
+        const bool is_a = warp < 8;
+        const float* src = (is_a ? Kb : Qb) + c * kRows * kLd;
+        const float* kr = Kb + ((warp & 7) * 8 + gq) * kLd;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int kk = 0; kk < DK; kk += 8) {
+            const float a[4] = {src[gq * kLd + kk + tq], src[(gq + 8) * kLd + kk + tq], src[gq * kLd + kk + tq + 4],
+                                src[(gq + 8) * kLd + kk + tq + 4]};
+            mma3(acc, a, split_b(kr[kk + tq], kr[kk + tq + 4]));
         }
-        const bool in = t < T && s <= t;  // rows and columns past T were never written
-        const float dec = in ? expf(g[t] - g[s]) : 0.0f;
-        const float a_ts = in && s < t ? beta[t] * dec * kk : 0.0f;
-        const float p_ts = in ? dec * qk : 0.0f;
+        float* dstm = is_a ? A : P;
 #pragma unroll
-        for (int r = 0; r < kPfCluster; r++) {
-            cluster.map_shared_rank(A, r)[t * kT + s] = a_ts;
-            cluster.map_shared_rank(P, r)[t * kT + s] = p_ts;
+        for (int i = 0; i < 4; i++) {
+            const int t = c * kRows + gq + 8 * (i >> 1), s = (warp & 7) * 8 + 2 * tq + (i & 1);
+            const bool in = t < T && s <= t;  // the causal part of the chunk
+            const float dec = in ? expf(g[t] - g[s]) : 0.0f;
+            const float v = is_a ? (in && s < t ? beta[t] * dec * acc[i] : 0.0f) : (in ? dec * acc[i] : 0.0f);
+#pragma unroll
+            for (int r = 0; r < kPfCluster; r++) cluster.map_shared_rank(dstm, r)[t * kLp + s] = v;
         }
     }
 
-    // R = beta (V - e^g K S0) and e^g Q S0 for this CTA's columns; thread: column j,
-    // tokens tg + kTg u
-    const int j = tid & (kCols - 1), tg = tid / kCols;
+    // R = beta (V - e^g K S0) into V and e^g Q S0 into O for this CTA's columns: warp w
+    // computes tokens of tile w / 4 and columns of tile w % 4
     {
-        float ks0[4] = {0.f, 0.f, 0.f, 0.f}, qs0[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int i = 0; i < DK; i += 4) {
-            const float4 s4 = make_float4(S[i * kCols + j], S[(i + 1) * kCols + j], S[(i + 2) * kCols + j],
-                                          S[(i + 3) * kCols + j]);
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int t = tg + kTg * u;
-                ks0[u] = dot4(*reinterpret_cast<const float4*>(Kb + t * kLd + i), s4, ks0[u]);
-                qs0[u] = dot4(*reinterpret_cast<const float4*>(Qb + t * kLd + i), s4, qs0[u]);
-            }
+        const int r0 = (warp >> 2) * 16 + gq, n0 = (warp & 3) * 8;
+        float ck[4] = {0.f, 0.f, 0.f, 0.f}, cq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int kk = 0; kk < DK; kk += 8) {
+            const SplitB b = split_b(S[(kk + tq) * kLs + n0 + gq], S[(kk + tq + 4) * kLs + n0 + gq]);
+            const float ak[4] = {Kb[r0 * kLd + kk + tq], Kb[(r0 + 8) * kLd + kk + tq], Kb[r0 * kLd + kk + tq + 4],
+                                 Kb[(r0 + 8) * kLd + kk + tq + 4]};
+            const float aq[4] = {Qb[r0 * kLd + kk + tq], Qb[(r0 + 8) * kLd + kk + tq], Qb[r0 * kLd + kk + tq + 4],
+                                 Qb[(r0 + 8) * kLd + kk + tq + 4]};
+            mma3(ck, ak, b);
+            mma3(cq, aq, b);
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int t = tg + kTg * u;
+        for (int i = 0; i < 4; i++) {
+            const int t = r0 + 8 * (i >> 1), jc = n0 + 2 * tq + (i & 1);
             if (t < T) {
-                Vb[t * kLv + j] = beta[t] * (Vb[t * kLv + j] - eg[t] * ks0[u]);
-                Ob[t * kLv + j] = eg[t] * qs0[u];
+                Vb[t * kLv + jc] = beta[t] * (Vb[t * kLv + jc] - eg[t] * ck[i]);
+                Ob[t * kLv + jc] = eg[t] * cq[i];
             }
         }
     }
@@ -274,7 +314,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
             for (int r = 0; r < kSb; r++) {
                 dl[r] = 0.0f;
                 if (r < nb) {
-                    const float* at = A + (jb + r) * kT + jb;
+                    const float* at = A + (jb + r) * kLp + jb;
                     float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
                     for (int s2 = 0; s2 < r; s2++) {
@@ -291,51 +331,52 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         __syncthreads();
         for (int e = tid; e < (T - jb - nb) * kCols; e += kPfThreads) {
             const int t = jb + nb + e / kCols, col = e % kCols;
-            const float* at = A + t * kT + jb;
+            const float* at = A + t * kLp + jb;
             float a = 0.0f;
             for (int s2 = 0; s2 < nb; s2++) a += at[s2] * Vb[(jb + s2) * kLv + col];
             Vb[t * kLv + col] -= a;
         }
         __syncthreads();
     }
-    // O += P Delta (column j, tokens tg + kTg u)
+    // O += P Delta (P is causal: the k range stops at the tile's last token): warp w, token
+    // tile w / 4, column tile w % 4
+    {
+        const int r0 = (warp >> 2) * 16 + gq, n0 = (warp & 3) * 8;
+        float co[4];
 #pragma unroll
-    for (int u = 0; u < 4; u++) {
-        const int t = tg + kTg * u;
-        if (t < T) {
-            const float* pt = P + t * kT;
-            float o0 = Ob[t * kLv + j], o1 = 0.0f;
-            int s = 0;
-            for (; s + 2 <= t + 1; s += 2) {
-                o0 += pt[s] * Vb[s * kLv + j];
-                o1 += pt[s + 1] * Vb[(s + 1) * kLv + j];
-            }
-            if (s <= t) o0 += pt[s] * Vb[s * kLv + j];
-            Ob[t * kLv + j] = o0 + o1;
+        for (int i = 0; i < 4; i++) co[i] = Ob[(r0 + 8 * (i >> 1)) * kLv + n0 + 2 * tq + (i & 1)];
+        const int kend = min(T, (warp >> 2) * 16 + 16);
+        for (int kk = 0; kk < kend; kk += 8) {
+            const float a[4] = {P[r0 * kLp + kk + tq], P[(r0 + 8) * kLp + kk + tq], P[r0 * kLp + kk + tq + 4],
+                                P[(r0 + 8) * kLp + kk + tq + 4]};
+            mma3(co, a, split_b(Vb[(kk + tq) * kLv + n0 + gq], Vb[(kk + tq + 4) * kLv + n0 + gq]));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int t = r0 + 8 * (i >> 1);
+            if (t < T) Ob[t * kLv + n0 + 2 * tq + (i & 1)] = co[i];
         }
     }
-    // S_T = e^{g_{T-1}} S0 + K^T diag(w) Delta for this CTA's columns (column j, rows
-    // tg * 8 .. tg * 8 + 7), to HBM
+    // S_T = e^{g_{T-1}} S0 + K^T diag(w) Delta for this CTA's columns, to HBM: tiles of 16
+    // state rows x 8 columns, two per warp
     {
         const float eT = eg[T - 1];
-        float acc[8];
+#pragma unroll 1
+        for (int tile = warp; tile < (DK / 16) * (kCols / 8); tile += kPfThreads / 32) {
+            const int i0 = (tile >> 2) * 16 + gq, n0 = (tile & 3) * 8;
+            float cs4[4];
 #pragma unroll
-        for (int r = 0; r < 8; r++) acc[r] = eT * S[(tg * 8 + r) * kCols + j];
-        for (int t = 0; t < T; t++) {
-            const float dw = w[t] * Vb[t * kLv + j];
-            const float4 ka = *reinterpret_cast<const float4*>(Kb + t * kLd + tg * 8);
-            const float4 kb = *reinterpret_cast<const float4*>(Kb + t * kLd + tg * 8 + 4);
-            acc[0] += ka.x * dw;
-            acc[1] += ka.y * dw;
-            acc[2] += ka.z * dw;
-            acc[3] += ka.w * dw;
-            acc[4] += kb.x * dw;
-            acc[5] += kb.y * dw;
-            acc[6] += kb.z * dw;
-            acc[7] += kb.w * dw;
+            for (int i = 0; i < 4; i++) cs4[i] = eT * S[(i0 + 8 * (i >> 1)) * kLs + n0 + 2 * tq + (i & 1)];
+            for (int kk = 0; kk < T; kk += 8) {
+                const float a[4] = {Kb[(kk + tq) * kLd + i0], Kb[(kk + tq) * kLd + i0 + 8], Kb[(kk + tq + 4) * kLd + i0],
+                                    Kb[(kk + tq + 4) * kLd + i0 + 8]};
+                mma3(cs4, a,
+                     split_b(w[kk + tq] * Vb[(kk + tq) * kLv + n0 + gq], w[kk + tq + 4] * Vb[(kk + tq + 4) * kLv + n0 + gq]));
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                Sg[(size_t)(i0 + 8 * (i >> 1)) * DK + c0 + n0 + 2 * tq + (i & 1)] = cs4[i];
         }
-#pragma unroll
-        for (int r = 0; r < 8; r++) Sg[(size_t)(tg * 8 + r) * DK + c0 + j] = acc[r];
     }
     __syncthreads();
     // gated RMSNorm with ssm_norm, times SiLU(gate) (deltanet.rs:514-533): each CTA's sum of
