@@ -15,9 +15,10 @@
 // SiLU(gate) are the decode mixer's, token by token, fused around it.
 //
 // Each head runs on a thread-block cluster of kPfCluster CTAs. Every CTA of the cluster
-// holds the chunk's normed q and k and computes all of A and P, and owns 128 / kPfCluster of
+// holds the chunk's normed q and k, computes kT / kPfCluster rows of A and P and stores them
+// into every CTA's shared memory (distributed shared memory), and owns 128 / kPfCluster of
 // the head's value columns: their slice of the state, of V, Delta and O. The gated RMSNorm's
-// sum of squares over the 128 columns is exchanged through distributed shared memory. The matrix products run on
+// sum of squares over the 128 columns is exchanged the same way. The matrix products run on
 // the tensor cores in 3xTF32 (about f32 accuracy, below); the rest is f32 on the CUDA cores.
 #include <cooperative_groups.h>
 
@@ -34,6 +35,7 @@ constexpr int kT = kPrefillChunk;         // tokens per launch
 constexpr int kPfThreads = 512;
 constexpr int kPfCluster = 4;             // CTAs per head (16 clusters of 8 do not fit at once)
 constexpr int kCols = DK / kPfCluster;    // value columns per CTA (32)
+constexpr int kRows = kT / kPfCluster;    // rows of A and P each CTA computes (16)
 constexpr int kLd = DK + 4;               // padded row stride of q and k (conflict-free float4 rows)
 constexpr int kLv = kCols + 8;            // padded row stride of V / Delta and O (conflict-free fragments)
 constexpr int kLs = kCols + 8;            // padded row stride of the state slice
@@ -59,9 +61,9 @@ struct PfSmem {
     static constexpr int bytes = floats * 4;
 };
 static_assert(PfSmem::bytes <= 227 * 1024, "prefill shared memory");
-// the warp tilings below: 16 warps; the causal 16 x 8 tiles of A and P; 4 x 4 tiles of 16
+// the warp tilings below: 16 warps; A/P rows are one m16 tile per CTA; 4 x 4 tiles of 16
 // tokens x 8 columns; 8 x 4 tiles of 16 state rows x 8 columns
-static_assert(kPfThreads == 512 && kCols == 32 && kT == 64, "prefill warp tiling");
+static_assert(kPfThreads == 512 && kCols == 32 && kRows == 16 && kT == 64, "prefill warp tiling");
 
 // The chunk's matrix products run on the tensor cores at about f32 accuracy (3xTF32): each
 // f32 operand is split into a tf32 high part and a tf32 remainder, and the three products
@@ -251,15 +253,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     if (fin_ch >= 0) *reinterpret_cast<float4*>(p.conv + (size_t)fin_ch * 4) = fin_cs;
 
     const int gq = lane >> 2, tq = lane & 3;  // fragment row group and column pair
-    // A (from k) and P (from q), all 64 rows in every CTA of the cluster (recomputing them is
-    // cheaper than exchanging them): the causal tiles of 16 rows x 8 columns, 20 per matrix
-    // (row tile m has 2m + 2 of them), spread over the warps
-#pragma unroll 1
-    for (int k = warp; k < 40; k += kPfThreads / 32) {
-        const bool is_a = k < 20;
-        const int r = k % 20, mt = r < 2 ? 0 : r < 6 ? 1 : r < 12 ? 2 : 3, nt = r - mt * (mt + 1);
-        const float* src = (is_a ? Kb : Qb) + (mt * 16) * kLd;
-        const float* kr = Kb + (nt * 8 + gq) * kLd;
+    // rows [kRows c, kRows (c+1)) of A (warps 0-7, from k) and P (warps 8-15, from q): warp w
+    // computes columns s of tile w % 8, and stores its entries into every CTA of the cluster
+    {
+        const bool is_a = warp < 8;
+        const float* src = (is_a ? Kb : Qb) + c * kRows * kLd;
+        const float* kr = Kb + ((warp & 7) * 8 + gq) * kLd;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
         for (int kk = 0; kk < DK; kk += 8) {
@@ -270,10 +269,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         float* dstm = is_a ? A : P;
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const int t = mt * 16 + gq + 8 * (i >> 1), s2 = nt * 8 + 2 * tq + (i & 1);
-            const bool in = t < T && s2 <= t;  // the causal part of the chunk
-            const float dec = in ? expf(g[t] - g[s2]) : 0.0f;
-            dstm[t * kLp + s2] = is_a ? (in && s2 < t ? beta[t] * dec * acc[i] : 0.0f) : (in ? dec * acc[i] : 0.0f);
+            const int t = c * kRows + gq + 8 * (i >> 1), s = (warp & 7) * 8 + 2 * tq + (i & 1);
+            const bool in = t < T && s <= t;  // the causal part of the chunk
+            const float dec = in ? expf(g[t] - g[s]) : 0.0f;
+            const float v = is_a ? (in && s < t ? beta[t] * dec * acc[i] : 0.0f) : (in ? dec * acc[i] : 0.0f);
+#pragma unroll
+            for (int r = 0; r < kPfCluster; r++) cluster.map_shared_rank(dstm, r)[t * kLp + s] = v;
         }
     }
 
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
             }
         }
     }
-    __syncthreads();  // A, P and R are complete
+    cluster.sync();  // all of A and P has arrived; R is complete
     // (I + A) Delta = R by forward substitution in blocks of kSb rows: warp 0 solves a block
     // (lane = column, the block's values in registers), then every thread subtracts the
     // block's contribution from the rows below it
