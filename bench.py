@@ -192,7 +192,8 @@ def cpu_reference_tokps(gguf, shape, ctx_len: int, n_tokens: int = 0, seconds: f
     s.forward(tok)          # warm-up token
     t0 = time.perf_counter()
     done = 0
-    while (n_tokens and done < n_tokens) or (not n_tokens and time.perf_counter() - t0 < seconds):
+    limit = n_tokens or 62  # the sample stays inside the oracle's context (ctx_len + 64)
+    while done < limit and (n_tokens or time.perf_counter() - t0 < seconds):
         tok = oracle.greedy(s.forward(tok))
         done += 1
     dt = time.perf_counter() - t0
@@ -594,6 +595,14 @@ def run_prefill(args):
     ctx.profile(False)
     med = statistics.median(times)
     tc = ctx.tensor_core_gemm(64)
+    ctx.close()
+    # the reference's prompt loop runs one qwen35_forward_token per prompt token
+    # (crates/cli/src/main.rs:358-362): the oracle's rate from position 0, about 10 s of tokens
+    cpu = None
+    if not args.no_cpu:
+        v, n_cpu, dt, cores = cpu_reference_tokps(gguf, shape, 0, seconds=min(args.cpu_seconds, 10.0))
+        cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"the first {n_cpu} tokens of one prompt, token by token, in {dt:.1f} s"}
     print(json.dumps({
         "metric": f"prefill tok/s, 2B-shape Q8_0, one sequence, {n}-token prompt",
         "value": round(n / med, 1), "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -606,9 +615,9 @@ def run_prefill(args):
                    "timing": "host wall clock around the synchronous call, median of steps"},
         "kernel_ms": {k: round(v["ms"], 3) for k, v in prof.items()},
         "gpu_launches_per_prefill": sum(v["launches"] for v in prof.values()),
+        "cpu_baseline": cpu,
         "clocks": clocks,
     }), flush=True)
-    ctx.close()
 
 
 # --------------------------------------------------------------------------- op benchmarks
