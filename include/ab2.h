@@ -92,7 +92,9 @@ int ab2_get_config(ab2_ctx* ctx, ab2_config* out);
 /* A fresh id for one split (ncclGetUniqueId); made on one rank and passed to all. */
 int ab2_tp_unique_id(uint8_t* id, uint64_t id_len);
 /* ab2_create for rank tp_rank of tp_world (1..8); returns once all ranks have joined.
- * tp_world = 1 is ab2_create (id may be NULL). */
+ * tp_world = 1 is ab2_create (id may be NULL). A rank that never joins (it failed before
+ * this call) leaves the others waiting in NCCL's bootstrap on the host, with no device work
+ * pending: bound the call with a timeout of the caller's own. */
 int ab2_create_tp(const uint8_t* gguf, uint64_t len, int device, int max_batch, int max_ctx,
                   const ab2_options* opt, int tp_rank, int tp_world, const uint8_t* tp_id,
                   uint64_t id_len, ab2_ctx** out);
