@@ -274,8 +274,9 @@ class DecodeContext:
         return logits, nxt
 
     def prefill(self, slot: int, tokens, want_logits: bool = True):
-        """Run a prompt through slot `slot` from its position on (chunks of 64 tokens on the
-        GPU); returns (logits of the last token [vocab] or None, its argmax)."""
+        """Run a prompt through slot `slot` from its position on (steps of 128 tokens on the
+        GPU, 64 with exact_max_batch 64); returns (logits of the last token [vocab] or None,
+        its argmax)."""
         t = _host(tokens, np.int32).reshape(-1)
         nxt = np.zeros(1, dtype=np.int32)
         logits = np.empty(self.config["vocab"], dtype=np.float32) if want_logits else None

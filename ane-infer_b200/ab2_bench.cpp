@@ -256,7 +256,7 @@ void run_device(const Args& a, const std::vector<uint8_t>& gguf, const ab2_confi
         gate->wait();
         out->pp0 = Clock::now();
         if (a.prefill && a.kv_bf16) {
-            // prompt: each sequence's tokens through one prefill call (chunks of 64 on the GPU)
+            // prompt: each sequence's tokens through one prefill call (steps of 128 on the GPU)
             std::vector<int32_t> ids((size_t)a.pp);
             for (int b = 0; b < B && a.pp > 0 && !out->rc; b++) {
                 for (long i = 0; i < a.pp; i++) ids[(size_t)i] = prompt_id(b, i);

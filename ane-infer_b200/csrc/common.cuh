@@ -91,9 +91,10 @@ __device__ __forceinline__ void xfrag_store(uint8_t* xf, const XfragShape& s, in
 // Activation layout of the tcgen05 GEMM ("x16"): the B operand in f16, stored exactly as the
 // shared-memory image of K-major 128-byte-swizzled tiles, so one bulk copy per 64-wide K tile
 // lands it ready for tcgen05.mma: [K/64][npad rows][128 B], where the 16-byte chunk j of row n
-// is stored at chunk position j ^ (n % 8). npad = batch rounded up to 16, 32 or 64.
-// the tcgen05 GEMM takes the activations as its M = 64 operand: always 64 rows (batch <= 64)
-__host__ __device__ inline int x16_npad(int batch) { return (void)batch, 64; }
+// is stored at chunk position j ^ (n % 8).
+// the tcgen05 GEMM takes the activations as its N operand: 64 rows for a batch of up to 64,
+// 128 rows for 65..128 (a prefill step)
+__host__ __device__ inline int x16_npad(int batch) { return batch > 64 ? 128 : 64; }
 __host__ __device__ inline size_t x16_bytes(int K, int batch) {
     return (size_t)((K + 63) / 64) * x16_npad(batch) * 128;
 }

@@ -400,8 +400,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
         const float gt = gate[u];
         float nv = Ob[t * kLv + col] * rms * p.ssm_norm[hc];
         nv *= gt / (1.0f + expf(-gt));
-        act_store(p.out, t, hg * DK + hc, nv);
-        if (p.o_out) p.o_out[(size_t)t * p.D + hg * DK + hc] = nv;
+        act_store(p.out, p.row0 + t, hg * DK + hc, nv);
+        if (p.o_out) p.o_out[(size_t)(p.row0 + t) * p.D + hg * DK + hc] = nv;
     }
 }
 

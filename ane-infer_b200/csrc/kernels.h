@@ -107,8 +107,9 @@ UmmaPlan umma_plan(int MT, int KT, int64_t M, int num_sms);
 int umma_nsplit(int MT, int KT, int mode, int num_sms);
 void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, int64_t base, int64_t grp,
                        int64_t stride, cudaStream_t st);
-// h2 (optional): the activations are silu(g) * u of this f32 gate/up scratch ([batch][h2_ld],
-// gate and up interleaved per 64 columns) instead of the x16 image
+// batch <= 128 (x16 holds x16_npad(batch) rows). h2 (optional): the activations are
+// silu(g) * u of this f32 gate/up scratch ([batch][h2_ld], gate and up interleaved per 64
+// columns) instead of the x16 image
 int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
                    cudaStream_t st, const float* h2 = nullptr, int h2_ld = 0);
 
@@ -149,6 +150,7 @@ struct DnParams {
     int H_all = 0;       // heads of the model (0: = H); the projection holds all of them
     ActOut out;          // activations of the ssm_out GEMM (K = D)
     float* o_out;        // optional f32 copy of the gated output [B][D]
+    int row0 = 0;        // prefill: the first output row (of out and o_out) of this launch
     unsigned* err = nullptr;  // bit 1024 set when a state copy did not arrive in time
     const void* pf = nullptr;  // optional: weights of the following GEMM, prefetched into L2
     int64_t pf_bytes = 0;
@@ -156,9 +158,13 @@ struct DnParams {
 };
 void launch_deltanet(const DnParams& p, int batch, cudaStream_t st);
 // dn_prefill.cu: the DeltaNet mixer of `tokens` (<= kPrefillChunk) consecutive tokens of one
-// sequence (proj and out rows are tokens; S and conv point at that sequence's state); chunked
-// form of the recurrence. Returns 0, or -1 for an unsupported shape, -2 for a launch failure.
+// sequence (proj rows are tokens, out rows are row0 + token; S and conv point at that
+// sequence's state); chunked form of the recurrence. Returns 0, or -1 for an unsupported
+// shape, -2 for a launch failure.
 constexpr int kPrefillChunk = 64;
+// tokens per prefill step (the rows of its GEMMs): kPrefillChunk on the exact mma.sync path,
+// kPrefillRowsTc on the tcgen05 path (N = 128), whose DeltaNet mixer runs as two launches
+constexpr int kPrefillRowsTc = 128;
 int launch_dn_prefill(const DnParams& p, int tokens, cudaStream_t st);
 // recurrence core only (op API): q,k,v bf16 [B][H][128], beta/decay f32 [B][H], o f32 [B][H][128]
 void launch_gated_delta(float* S, const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* beta,

@@ -1,9 +1,9 @@
 // q8_umma.cu -- batched Q8_0 dequant-GEMM on the 5th-generation tensor cores (tcgen05).
 //
-// Y[b][m] = sum_k X[b][k] W[m][k] for a batch of up to 64 sequences. The weights are the
-// A side of every MMA, taken from tensor memory, and the activations the N = 64 side, taken
-// from shared memory: D[128 x 64] (+)= W[128 x 16] X[64 x 16]^T, two 128-row weight tiles
-// per stage. Keeping the converted f16 weights out of shared memory halves its traffic per
+// Y[b][m] = sum_k X[b][k] W[m][k] for a batch of up to 64 sequences (or the up to 128 tokens
+// of a prefill step). The weights are the A side of every MMA, taken from tensor memory, and
+// the activations the N = 64 (or 128) side, taken from shared memory: D[128 x N] (+)=
+// W[128 x 16] X[N x 16]^T, two 128-row weight tiles per stage. Keeping the converted f16 weights out of shared memory halves its traffic per
 // stage (17 KB raw weights in and out, 16 KB of activation reads), which is what bounded
 // the shared-memory-operand form of this kernel.
 // W is stored in 128-row x 64-column Q8_0 tiles (the "q8u" layout, 8.5 KB each) grouped in
@@ -44,14 +44,27 @@ namespace ab2 {
 constexpr int kRows = kUTileRows;                 // 128 weight rows per tile (the MMA's M)
 constexpr int kPairRows = 2 * kRows;              // 256 weight rows per unit
 constexpr int kTileK = 64;
-constexpr int kBatchRows = 64;                    // the MMA's N: activation rows (batch padded to 64)
+constexpr int kMaxBatchRows = 128;                // the MMA's N: activation rows (a step's batch padded to 64, a
+                                                  // prefill step's tokens to 128)
 constexpr int kStageTiles = 2;                    // weight tiles per pipeline stage: one K tile of a pair
 constexpr int kWStageBytes = kStageTiles * kUTileBytes;
 constexpr int kWStages = 8;                       // raw weight ring (136 KB)
-constexpr int kAGroup = 4;                        // activation K tiles per copy
-constexpr int kXStages = 2;                       // activation ring (64 KB)
-constexpr int kXSlots = kXStages * kAGroup;       // the same ring as one-tile slots (SwiGLU source)
-constexpr int kXTileBytes = kBatchRows * kTileK * 2;  // 8 KB
+constexpr int kXStages = 2;                       // activation ring: two stages of 32 KB
+constexpr int kXRingBytes = 64 * 1024;
+constexpr int kXSlotsMax = 8;                     // barrier slots of the ring as one-tile slots (SwiGLU source)
+// The activation side for NB = 64 or 128 rows: a K tile of the image is NB rows of 128 bytes,
+// a copy brings a 32 KB group of them, and the TMEM accumulators of a unit (two weight tiles
+// x NB f32 columns) are double-buffered at NB = 64; at NB = 128 one accumulator fills the 256
+// columns beside the operand ring, so a unit's MMAs wait for the previous unit's epilogue.
+template <int NB>
+struct XShape {
+    static_assert(NB == 64 || NB == 128, "64 or 128 activation rows");
+    static constexpr int kTileBytes = NB * kTileK * 2;  // 8 or 16 KB
+    static constexpr int kGroup = kXRingBytes / kXStages / kTileBytes;  // K tiles per copy: 4 or 2
+    static constexpr int kSlots = kXStages * kGroup;
+    static constexpr int kAccBufs = NB == 64 ? 2 : 1;
+    static constexpr int kAccCols = 2 * NB;  // one accumulator: kStageTiles tiles of NB columns
+};
 constexpr int kOpStages = 4;                      // f16 weight operand ring in TMEM
 // TMEM columns: the operand ring in [0, 256) (stage s, tile t at s*64 + t*32: 32 columns hold
 // a row's 64 f16 of K), the two accumulators in [256, 512) (unit buffer j at 256 + j*128,
@@ -66,7 +79,9 @@ constexpr int kEpiBar = 1;                        // named barrier of the epilog
 constexpr int kStageLd = kPairRows + 4;           // floats per staged accumulator row (16-byte pad)
 constexpr int kMinKTilesPerSplit = 4;
 static_assert(kConvWarps * 32 == kStageTiles * kRows, "one converter thread per weight row of a stage");
-static_assert(kOpStages * kStageTiles * 32 <= (int)kAccCol0 && kAccCol0 + 2 * kPairRows / 2 <= kTmemCols,
+static_assert(kOpStages * kStageTiles * 32 <= (int)kAccCol0 &&
+                  kAccCol0 + XShape<64>::kAccBufs * XShape<64>::kAccCols <= kTmemCols &&
+                  kAccCol0 + XShape<128>::kAccBufs * XShape<128>::kAccCols <= kTmemCols,
               "TMEM column budget");
 
 // ------------------------------------------------------------------------------ repack
@@ -104,16 +119,19 @@ void launch_q8t_repack(const uint8_t* src, int64_t rows, int KB, Q8Weight& w, in
 struct UmmaSmem {  // offsets from the 1024-aligned dynamic shared-memory base
     static constexpr int w_off(int s) { return s * kWStageBytes; }
     static constexpr int x_base() { return (kWStages * kWStageBytes + 1023) / 1024 * 1024; }
-    // activation stage s of xg K tiles (xg = kAGroup for copied images, 1 for the SwiGLU source)
-    static constexpr int x_off(int s, int xg) { return x_base() + s * xg * kXTileBytes; }
-    static constexpr int bar_off() { return x_base() + kXSlots * kXTileBytes; }
-    // w_full/w_free[W], op_full/op_free[Op], x_full/x_free[kXSlots], acc_full/acc_free[2], mma_done, tmem slot
-    static constexpr int n_bars() { return 2 * kWStages + 2 * kOpStages + 2 * kXSlots + 4 + 1; }
+    // activation stage s of xg K tiles of tb bytes (xg = the copy group for copied images, 1 for
+    // the SwiGLU source)
+    static constexpr int x_off(int s, int xg, int tb) { return x_base() + s * xg * tb; }
+    static constexpr int bar_off() { return x_base() + kXRingBytes; }
+    // w_full/w_free[W], op_full/op_free[Op], x_full/x_free[kXSlotsMax], acc_full/acc_free[2], mma_done, tmem slot
+    static constexpr int n_bars() { return 2 * kWStages + 2 * kOpStages + 2 * kXSlotsMax + 4 + 1; }
     static constexpr int bytes() { return bar_off() + n_bars() * 8 + 16; }
 };
-static_assert(kXTileBytes % 1024 == 0 && UmmaSmem::x_base() % 1024 == 0, "operand tiles must stay 1024-aligned");
+static_assert(XShape<64>::kTileBytes % 1024 == 0 && UmmaSmem::x_base() % 1024 == 0 &&
+                  XShape<64>::kSlots <= kXSlotsMax && XShape<128>::kSlots <= kXSlotsMax,
+              "operand tiles must stay 1024-aligned");
 // the last unit's accumulator is staged over the raw weight ring, idle by then
-static_assert(kBatchRows * kStageLd * 4 <= UmmaSmem::x_base(), "the staged accumulator fits in the weight ring");
+static_assert(kMaxBatchRows * kStageLd * 4 <= UmmaSmem::x_base(), "the staged accumulator fits in the weight ring");
 
 // Unit u covers the len K tiles from k0 of row-tile pair mt: a main unit (pair u / ks, K split
 // u % ks) or, from main_units on, a K piece of one of the tail pairs. A CTA takes units
@@ -236,6 +254,7 @@ __device__ __forceinline__ void glu_store(uint8_t* tile, int n, int j, const Glu
     }
 }
 
+template <int NB>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
     q8_umma_gemm_kernel(const uint8_t* __restrict__ wt, UnitPlan P, const uint8_t* __restrict__ x16,
                         const float* __restrict__ h2, int h2_ld, int batch, unsigned* __restrict__ err, GemmEpi ep) {
@@ -246,13 +265,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     uint64_t* op_full = w_free + kWStages;
     uint64_t* op_free = op_full + kOpStages;
     uint64_t* x_full = op_free + kOpStages;
-    uint64_t* x_free = x_full + kXSlots;
-    uint64_t* acc_full = x_free + kXSlots;
+    uint64_t* x_free = x_full + kXSlotsMax;
+    uint64_t* acc_full = x_free + kXSlotsMax;
     uint64_t* acc_free = acc_full + 2;
     uint64_t* mma_done = acc_free + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
     __shared__ int s_abort;
 
+    using X = XShape<NB>;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, U = P.units, KT = P.KT;
     const uint32_t WL = ep.wt.wait_ns;  // the limit of every wait below
@@ -267,12 +287,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             mbar_init(&op_full[s], kConvWarps * 32);
             mbar_init(&op_free[s], 1);
         }
-        for (int s = 0; s < kXSlots; s++) {
+        for (int s = 0; s < X::kSlots; s++) {
             // a copied stage completes on its bytes; a SwiGLU tile on all epilogue threads' stores
             mbar_init(&x_full[s], h2 ? kEpiWarps * 32 : 1);
             mbar_init(&x_free[s], 1);
         }
-        for (int j = 0; j < 2; j++) {
+        for (int j = 0; j < X::kAccBufs; j++) {
             mbar_init(&acc_full[j], 1);
             mbar_init(&acc_free[j], kEpiWarps * 32);
         }
@@ -328,7 +348,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                 int mt, k0, len;
                 bool split;
                 unit_range(u, P, mt, k0, len, split);
-                for (int q = 0; q < len; q += kAGroup, g++) {
+                for (int q = 0; q < len; q += X::kGroup, g++) {
                     const int s = g % kXStages;
                     if (g >= kXStages && !mbar_wait(&x_free[s], ((g / kXStages) - 1) & 1, WL)) {
                         atomicOr(err, 4u);
@@ -336,10 +356,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                         ok = false;
                         break;
                     }
-                    const uint32_t bytes = (uint32_t)min(kAGroup, len - q) * kXTileBytes;
+                    const uint32_t bytes = (uint32_t)min(X::kGroup, len - q) * X::kTileBytes;
                     mbar_arrive_expect_tx(&x_full[s], bytes);
-                    bulk_g2s(smem + UmmaSmem::x_off(s, kAGroup), x16 + (size_t)(k0 + q) * kXTileBytes, bytes,
-                             &x_full[s]);
+                    bulk_g2s(smem + UmmaSmem::x_off(s, X::kGroup, X::kTileBytes),
+                             x16 + (size_t)(k0 + q) * X::kTileBytes, bytes, &x_full[s]);
                 }
             }
             for (int j = max(0, g - kXStages); j < g; j++)
@@ -348,23 +368,23 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
     } else if (warp == kWarpMma) {
         // ---------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_f16(kRows, kBatchRows);
-            const int xg = h2 ? 1 : kAGroup, xs = h2 ? kXSlots : kXStages;  // tiles per stage, stages
+            constexpr uint32_t idesc = umma_idesc_f16(kRows, NB);
+            const int xg = h2 ? 1 : X::kGroup, xs = h2 ? X::kSlots : kXStages;  // tiles per stage, stages
             int st = 0, sx = 0, xph = 0, j = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < U && ok; u += G, j++) {
                 int mt, k0, len;
                 bool split;
                 unit_range(u, P, mt, k0, len, split);
-                if (j >= 2) {
-                    if (!mbar_wait(&acc_free[j & 1], ((j >> 1) - 1) & 1, WL)) {
+                if (j >= X::kAccBufs) {
+                    if (!mbar_wait(&acc_free[j % X::kAccBufs], ((j / X::kAccBufs) - 1) & 1, WL)) {
                         atomicOr(err, 16u);
                         ok = false;
                         break;
                     }
                     tc_fence_after();  // the epilogue's TMEM loads of this accumulator are done
                 }
-                const uint32_t d = tmem + kAccCol0 + (uint32_t)((j & 1) * kPairRows / 2);
+                const uint32_t d = tmem + kAccCol0 + (uint32_t)((j % X::kAccBufs) * X::kAccCols);
                 int ux = 0;  // K tile within the activation stage sx
                 for (int q = 0; q < len; q++, st++) {
                     const int so = st % kOpStages;
@@ -377,14 +397,15 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     tc_fence_after();  // the converters' TMEM stores of this stage are complete
                     // one descriptor per stage: a K16 step advances its start address by 32 bytes,
                     // i.e. 2 in the descriptor's 16-byte units
-                    const uint64_t xd = umma_desc_sw128(smem_u32(smem + UmmaSmem::x_off(sx, xg) + ux * kXTileBytes));
+                    const uint64_t xd =
+                        umma_desc_sw128(smem_u32(smem + UmmaSmem::x_off(sx, xg, X::kTileBytes) + ux * X::kTileBytes));
                     const uint32_t a0 = tmem + kOpCol0 + (uint32_t)(so * kStageTiles * 32);
                     const uint32_t acc0 = q > 0 ? 1u : 0u;
 #pragma unroll
                     for (int k = 0; k < kTileK / 16; k++)
 #pragma unroll
                         for (int t = 0; t < kStageTiles; t++)
-                            umma_ts_f16(d + t * kBatchRows, a0 + t * 32 + k * 8, xd + (uint64_t)(2 * k), idesc,
+                            umma_ts_f16(d + t * NB, a0 + t * 32 + k * 8, xd + (uint64_t)(2 * k), idesc,
                                         k > 0 ? 1u : acc0);
                     if (++ux == xg || q == len - 1) {
                         umma_commit(&x_free[sx]);
@@ -396,7 +417,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     }
                     umma_commit(&op_free[so]);
                 }
-                umma_commit(&acc_full[j & 1]);
+                umma_commit(&acc_full[j % X::kAccBufs]);
             }
             if (!ok) s_abort = 1;
             umma_commit(mma_done);  // every MMA issued above has completed before TMEM is freed
@@ -473,29 +494,37 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             const int how = (split || ep.mode == EPI_ADD) ? 2 : (ep.mode == EPI_RESID ? 1 : 0);
             if (h2) {
                 // this unit's activation tiles from the gate/up sums: thread et takes the
-                // 16-byte chunk jn = et % 8 (8 K) of rows et / 8 + 16 i, i = 0..3, as two loads
-                // of two rows, each issued half a tile ahead of its use
+                // 16-byte chunk jn = et % 8 (8 K) of rows et / 8 + 16 i, i = 0 .. NB / 16 - 1,
+                // as loads of two rows (64 rows per pass), each issued half a pass ahead of its use
                 const int jn = et & 7, n0 = et >> 3;
                 GluLoad ra, rb;
                 glu_load(h2, h2_ld, batch, k0, n0, jn, ra);
                 for (int kq = 0; kq < len && !fail; kq++, gx++) {
-                    const int s = gx % kXSlots;
-                    glu_load(h2, h2_ld, batch, k0 + kq, n0 + 32, jn, rb);
-                    if (gx >= kXSlots && !mbar_wait(&x_free[s], ((gx / kXSlots) - 1) & 1, WL)) {
-                        atomicOr(err, 2048u);
-                        s_abort = 1;
-                        fail = true;
-                        break;
+                    const int s = gx % X::kSlots;
+                    uint8_t* tile = smem + UmmaSmem::x_off(s, 1, X::kTileBytes);
+#pragma unroll
+                    for (int ps = 0; ps < NB / 64; ps++) {
+                        const int nb = n0 + 64 * ps;
+                        glu_load(h2, h2_ld, batch, k0 + kq, nb + 32, jn, rb);
+                        if (ps == 0 && gx >= X::kSlots && !mbar_wait(&x_free[s], ((gx / X::kSlots) - 1) & 1, WL)) {
+                            atomicOr(err, 2048u);
+                            s_abort = 1;
+                            fail = true;
+                            break;
+                        }
+                        glu_store(tile, nb, jn, ra);
+                        if (ps + 1 < NB / 64)
+                            glu_load(h2, h2_ld, batch, k0 + kq, nb + 64, jn, ra);
+                        else if (kq + 1 < len)
+                            glu_load(h2, h2_ld, batch, k0 + kq + 1, n0, jn, ra);
+                        glu_store(tile, nb + 32, jn, rb);
                     }
-                    uint8_t* tile = smem + UmmaSmem::x_off(s, 1);
-                    glu_store(tile, n0, jn, ra);
-                    if (kq + 1 < len) glu_load(h2, h2_ld, batch, k0 + kq + 1, n0, jn, ra);
-                    glu_store(tile, n0 + 32, jn, rb);
+                    if (fail) break;
                     fence_proxy_async_smem();  // the MMAs read the tile through the async proxy
                     mbar_arrive(&x_full[s]);
                 }
             }
-            if (!fail && !mbar_wait(&acc_full[j & 1], (j >> 1) & 1, WL)) {
+            if (!fail && !mbar_wait(&acc_full[j % X::kAccBufs], (j / X::kAccBufs) & 1, WL)) {
                 fail = true;
                 atomicOr(err, 512u);
                 s_abort = 1;
@@ -503,20 +532,23 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             // one outcome for all epilogue threads, which meet at a named barrier below
             if (epi_bar_or(fail || *(volatile int*)&s_abort)) break;
             tc_fence_after();
-            const uint32_t dq = tmem + ((uint32_t)(q * 32) << 16) + kAccCol0 + (uint32_t)((j & 1) * kPairRows / 2);
+            const uint32_t dq =
+                tmem + ((uint32_t)(q * 32) << 16) + kAccCol0 + (uint32_t)((j % X::kAccBufs) * X::kAccCols);
             const int pr = mt;  // row-tile pair: rows pr*256 .. pr*256+255
             if (u + G < U) {
                 // more units follow: write straight from TMEM, lanes on consecutive rows m
 #pragma unroll 1
-                for (int t = 0; t < kStageTiles; t++) {
+                for (int tb = 0; tb < kStageTiles * NB / 64; tb++) {
+                    // 64 batch rows b0 .. b0 + 63 of weight tile t
+                    const int t = tb / (NB / 64), b0 = (tb % (NB / 64)) * 64;
                     float v[64];
-                    tmem_ld64(dq + t * kBatchRows, v);
+                    tmem_ld64(dq + t * NB + b0, v);
                     const int m = pr * kPairRows + t * kRows + q * 32 + lane;
                     if (m < ep.m_out) {
 #pragma unroll
-                        for (int b = 0; b < kBatchRows; b++) {
-                            if (b >= batch) break;
-                            float* yp = ep.y + (size_t)b * ep.ldy + m;
+                        for (int b = 0; b < 64; b++) {
+                            if (b0 + b >= batch) break;
+                            float* yp = ep.y + (size_t)(b0 + b) * ep.ldy + m;
                             if (how == 2)
                                 atomicAdd(yp, v[b]);  // result unused: compiles to a reduction
                             else
@@ -525,11 +557,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&acc_free[j & 1]);  // this thread's TMEM loads are done
+                mbar_arrive(&acc_free[j % X::kAccBufs]);  // this thread's TMEM loads are done
                 continue;
             }
             // The last unit: the raw weight ring is idle (every stage was converted before the
-            // last MMA), so the accumulator is staged over it as [64 batch rows][kStageLd
+            // last MMA), so the accumulator is staged over it as [NB batch rows][kStageLd
             // floats], each lane writing its weight row's column of it (consecutive lanes,
             // consecutive words). Each batch row's outputs then leave in one bulk operation: a
             // bulk store, or a bulk f32 add at L2 when the output accumulates (K splits,
@@ -537,12 +569,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1)
             // rate when all CTAs reached their epilogue together.
             float* stage = reinterpret_cast<float*>(smem);
 #pragma unroll 1
-            for (int t = 0; t < kStageTiles; t++) {
+            for (int tb = 0; tb < kStageTiles * NB / 64; tb++) {
+                const int t = tb / (NB / 64), b0 = (tb % (NB / 64)) * 64;
                 float v[64];
-                tmem_ld64(dq + t * kBatchRows, v);
+                tmem_ld64(dq + t * NB + b0, v);
                 const int ml = t * kRows + q * 32 + lane;
 #pragma unroll
-                for (int b = 0; b < kBatchRows; b++) stage[b * kStageLd + ml] = v[b];
+                for (int b = 0; b < 64; b++) stage[(b0 + b) * kStageLd + ml] = v[b];
             }
             fence_proxy_async_smem();  // the bulk operations read the staged rows through the async proxy
             tc_fence_before();
@@ -629,19 +662,19 @@ UmmaPlan umma_plan(int MT, int KT, int64_t M, int num_sms) {
     return p;
 }
 
-int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
-                   cudaStream_t st, const float* h2, int h2_ld) {
+template <int NB>
+static int launch_umma_t(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep,
+                         int num_sms, cudaStream_t st, const float* h2, int h2_ld) {
     const int smem = UmmaSmem::bytes() + 1024;
     static bool attr_set[64] = {};  // per device, before the first launch
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_set[dev & 63]) {
-        if (cudaFuncSetAttribute(q8_umma_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        if (cudaFuncSetAttribute(q8_umma_gemm_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return -1;
         attr_set[dev & 63] = true;
     }
-    if (ep.mode == EPI_SWIGLU) return -3;  // SwiGLU: EPI_ADD into h2, then a launch with the h2 source
     const UmmaPlan pl = umma_plan(w.MT, w.KT, w.M, num_sms);
     UnitPlan P;
     P.KT = w.KT;
@@ -653,14 +686,24 @@ int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* e
     P.kper_tail = pl.kper_tail;
     P.units = pl.units;
     const int G = std::min(pl.units, num_sms);
-    // the SwiGLU source reads whole 64-column gate/up groups of h2 (K = ffn a multiple of 64)
-    if (h2 && (w.KB % 2 != 0 || h2_ld < 2 * 32 * w.KB || (h2_ld & 3) != 0)) return -1;
     GemmEpi e = ep;
     e.wt = take_wait_test(kWaitTestGemm, st);
-    if (launch_pdl(q8_umma_gemm_kernel, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, P, x16, h2, h2_ld, batch, err,
-                   e) != cudaSuccess)
+    if (launch_pdl(q8_umma_gemm_kernel<NB>, dim3(G), dim3(kUmmaThreads), smem, st, w.qt, P, x16, h2, h2_ld, batch,
+                   err, e) != cudaSuccess)
         return -2;
     return 0;
+}
+
+// batch <= 64 runs the N = 64 form (the activation image x16 holds 64 rows), 65..128 the
+// N = 128 form (128 rows: a prefill step)
+int launch_q8_umma(const Q8Weight& w, const uint8_t* x16, int batch, unsigned* err, const GemmEpi& ep, int num_sms,
+                   cudaStream_t st, const float* h2, int h2_ld) {
+    if (batch < 1 || batch > kMaxBatchRows) return -1;
+    if (ep.mode == EPI_SWIGLU) return -3;  // SwiGLU: EPI_ADD into h2, then a launch with the h2 source
+    // the SwiGLU source reads whole 64-column gate/up groups of h2 (K = ffn a multiple of 64)
+    if (h2 && (w.KB % 2 != 0 || h2_ld < 2 * 32 * w.KB || (h2_ld & 3) != 0)) return -1;
+    return batch > 64 ? launch_umma_t<128>(w, x16, batch, err, ep, num_sms, st, h2, h2_ld)
+                      : launch_umma_t<64>(w, x16, batch, err, ep, num_sms, st, h2, h2_ld);
 }
 
 }  // namespace ab2

@@ -497,11 +497,12 @@ struct ab2_ctx {
     void* vc = nullptr;
     int32_t* pos_d = nullptr;   // [max_batch]
     std::vector<int64_t> pos_h;
-    int32_t* pf_pos = nullptr;  // [kPrefillChunk] positions of a prefill chunk's tokens
-    int32_t* pf_tok = nullptr;  // [kPrefillChunk] token ids of a prefill chunk
+    int pf_rows = kPrefillChunk;  // tokens per prefill step (kPrefillRowsTc on the tcgen05 path)
+    int32_t* pf_pos = nullptr;  // [pf_rows] positions of a prefill step's tokens
+    int32_t* pf_tok = nullptr;  // [pf_rows] token ids of a prefill step
     int64_t s_stride = 0, conv_stride = 0, kv_slot = 0;
-    // scratch, for `rows` = max(max_batch, kPrefillChunk) rows (sequences of a step, or
-    // tokens of a prefill chunk)
+    // scratch, for `rows` = max(max_batch, pf_rows) rows (sequences of a step, or tokens of
+    // a prefill step)
     int rows = 0;
     float* x = nullptr;         // residual stream [rows][D]
     float* proj = nullptr;      // [max_batch][ldp]
@@ -726,10 +727,10 @@ int build_context(ab2_ctx* x, const uint8_t* data, uint64_t len) {
     x->pos_h.assign(B, 0);
 
     // ---- scratch (rows: the sequences of a step or the tokens of a prefill chunk)
-    const int R = std::max(B, kPrefillChunk);
+    const int R = std::max(B, x->pf_rows);
     x->rows = R;
-    RET(x->dalloc(&x->pf_pos, (size_t)kPrefillChunk * 4));
-    RET(x->dalloc(&x->pf_tok, (size_t)kPrefillChunk * 4));
+    RET(x->dalloc(&x->pf_pos, (size_t)x->pf_rows * 4));
+    RET(x->dalloc(&x->pf_tok, (size_t)x->pf_rows * 4));
     int64_t mproj = 0, maxk = D;
     for (auto& L : x->layers) mproj = std::max<int64_t>(mproj, L.w_in.M);
     maxk = std::max<int64_t>(maxk, F);
@@ -940,8 +941,19 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.err = x->err_d;
         set_prefetch(x, B, &L.w_out, &p.pf, &p.pf_bytes);
         ProfScope ps(x, PC_DN, st);
-        if (pf_p0 < 0) launch_deltanet(p, B, st);
-        else if (launch_dn_prefill(p, B, st)) return seterr(AB2_ERR_SHAPE, "DeltaNet prefill: unsupported shape");
+        if (pf_p0 < 0) {
+            launch_deltanet(p, B, st);
+        } else {
+            // the chunked kernel takes kPrefillChunk tokens per launch: a wider prefill step
+            // runs as consecutive launches, each continuing from the state the last one left
+            for (int r0 = 0; r0 < B; r0 += kPrefillChunk) {
+                DnParams q = p;
+                q.proj = p.proj + (size_t)r0 * p.ldp;
+                q.row0 = r0;
+                if (launch_dn_prefill(q, std::min(kPrefillChunk, B - r0), st))
+                    return seterr(AB2_ERR_SHAPE, "DeltaNet prefill: unsupported shape");
+            }
+        }
     } else {
         const size_t kvel = x->kv_bf16 ? 2 : 4;
         AttnParams p;
@@ -1319,9 +1331,11 @@ static int create_ctx(const uint8_t* gguf, uint64_t len, int device, int max_bat
     x->rot = opt ? opt->rope_dims : 0;
     // -1: no exact path, every step (one sequence too) on tcgen05; 0 (the default): 1
     x->exact_max = !opt || opt->exact_max_batch == 0 ? 1 : opt->exact_max_batch < 0 ? 0 : opt->exact_max_batch;
-    // the tcgen05 weights are packed when a decode step or a prefill chunk (kPrefillChunk
-    // rows) can have more rows than exact_max
+    // the tcgen05 weights are packed when a decode step or a prefill step (kPrefillChunk
+    // rows on the exact path) can have more rows than exact_max; a prefill step then takes
+    // kPrefillRowsTc tokens, the tcgen05 GEMM's widest N
     x->use_umma = std::max(max_batch, kPrefillChunk) > x->exact_max;
+    x->pf_rows = x->use_umma ? kPrefillRowsTc : kPrefillChunk;
     x->tp_rank = tp_rank;
     x->tp_world = tp_world;
     cudaDeviceGetAttribute(&x->num_sms, cudaDevAttrMultiProcessorCount, device);
@@ -1662,10 +1676,10 @@ AB2_API int ab2_prefill(ab2_ctx* x, int slot, const int32_t* tokens, int64_t n, 
             return seterr(AB2_ERR_ARG, "prompt token %lld (id %d) is outside [0, %lld)", (long long)i, tokens[i],
                           (long long)c.vocab);
     cudaStream_t st = x->stream;
-    // chunks of up to kPrefillChunk tokens, in stream order (each chunk's id copy follows the
-    // previous chunk's kernels on the stream)
-    for (int64_t t0 = 0; t0 < n; t0 += kPrefillChunk) {
-        const int T = (int)std::min<int64_t>(kPrefillChunk, n - t0);
+    // steps of up to pf_rows tokens, in stream order (each step's id copy follows the
+    // previous step's kernels on the stream)
+    for (int64_t t0 = 0; t0 < n; t0 += x->pf_rows) {
+        const int T = (int)std::min<int64_t>(x->pf_rows, n - t0);
         CK(cudaMemcpyAsync(x->pf_tok, tokens + t0, (size_t)T * 4, cudaMemcpyHostToDevice, st));
         RET(enqueue_body(x, x->pf_tok, T, (int)(p0 + t0 + T), slot, p0 + t0, st));
         if (t0 + T == n) RET(enqueue_head(x, x->x + (size_t)(T - 1) * c.dim, 1, x->logits, x->next_d, st));
@@ -1835,7 +1849,7 @@ AB2_API void ab2_q8_destroy(ab2_q8* w) {
 
 AB2_API int ab2_q8_gemv(ab2_q8* w, const float* xin, int batch, float* y, void* stream) {
     if (!w || !xin || !y) return seterr(AB2_ERR_ARG, "null argument");
-    if (batch < 1 || batch > 64) return seterr(AB2_ERR_CAPACITY, "batch must be in [1, 64]");
+    if (batch < 1 || batch > 128) return seterr(AB2_ERR_CAPACITY, "batch must be in [1, 128]");
     DeviceGuard dev_guard(w->device);
     CK(dev_guard.err);
     OpCache& oc = g_ops[w->device & 63];

@@ -562,7 +562,8 @@ def run_split(args):
 
 def run_prefill(args):
     """Prefill throughput of one sequence on one GPU: --prefill N prompt tokens through
-    ab2_prefill (64-token chunks), prompt tokens per second from the host clock around each
+    ab2_prefill (128-token steps; 64 with --exact-max-batch 64), prompt tokens per second
+    from the host clock around each
     call (the call is synchronous; its host-to-device copy of the ids and its device-to-host
     copy of the last logits are inside)."""
     import torch
@@ -610,7 +611,7 @@ def run_prefill(args):
         "dtype": "f16 MMA operands (q*d rounded once), f32 accumulate, bf16 KV" if tc else
                  "exact Q8_0 weights x f16 hi/lo activations, f32 accumulate, bf16 KV",
         "data": "synthetic (seeded random Q8_0 weights and prompt ids)",
-        "config": {"workload": f"2B-shape Qwen3.5 hybrid prefill of {n} tokens in 64-token chunks",
+        "config": {"workload": f"2B-shape Qwen3.5 hybrid prefill of {n} tokens in {64 if not tc else 128}-token steps",
                    "model": "qwen35-hybrid-2B-shape (random init)", "max_batch": args.prefill_batch,
                    "timing": "host wall clock around the synchronous call, median of steps"},
         "kernel_ms": {k: round(v["ms"], 3) for k, v in prof.items()},
@@ -779,7 +780,7 @@ def main():
     ap.add_argument("--prefill-batch", type=int, default=64, help="max_batch of the prefill context")
     ap.add_argument("--exact-max-batch", type=int, default=0,
                     help="--split heads and --prefill: the contexts' exact_max_batch (-1: one sequence on "
-                         "tcgen05 too; 64: prefill chunks on the exact path)")
+                         "tcgen05 too; 64: 64-token prefill steps on the exact path)")
     ap.add_argument("--split", choices=["sequences", "heads"], default="sequences",
                     help="heads: time the head-parallel split's decode-step latency (use --batch 1)")
     args = ap.parse_args()

@@ -141,10 +141,11 @@ int ab2_decode_step(ab2_ctx* ctx, const int32_t* tokens, int batch, float* logit
  * token's logits [vocab] and argmax come back (either pointer may be NULL). Host buffers;
  * synchronous. Replaces the reference's prompt loop over qwen35_forward_token
  * (crates/cli/src/main.rs:358-362) and ane_prefill_tokens (main.rs:1168). The tokens go
- * through in chunks of 64: every projection as a 64-row GEMM, the DeltaNet recurrence in its
- * chunkwise form (the plan of HANDOVER.md:67-72), each token's attention over the slot's
- * cache. Needs the bf16 KV cache and conv kernel 4. Ids outside [0, vocab) and prompts that
- * do not fit in max_ctx are rejected before any work is queued. */
+ * through in steps of 128 (of 64 when exact_max_batch is 64): every projection as one GEMM
+ * over the step's rows, the DeltaNet recurrence in its chunkwise form over 64 tokens at a
+ * time (the plan of HANDOVER.md:67-72), each token's attention over the slot's cache. Needs
+ * the bf16 KV cache and conv kernel 4. Ids outside [0, vocab) and prompts that do not fit in
+ * max_ctx are rejected before any work is queued. */
 int ab2_prefill(ab2_ctx* ctx, int slot, const int32_t* tokens, int64_t n, float* logits, int32_t* next_token);
 /* Same with device buffers, enqueued on `stream` (a cudaStream_t; NULL = the context's own
  * stream) without synchronising. tokens_dev may alias next_dev of the previous step. The
@@ -190,8 +191,8 @@ void ab2_q8_destroy(ab2_q8* w);
  * Replaces q8_gemv (crates/engine/src/q8_gemv.rs:130) and encode_gemv_prealloc
  * (crates/engine/src/gpu_full_decode.rs:1048). stream may be NULL (legacy default). */
 int ab2_q8_gemv(ab2_q8* w, const float* x, int batch, float* y, void* stream);
-/* Batches of 9 or more run on the tcgen05 path, whose f16 weights are q*d rounded once
- * (relative error <= 2^-11 per weight); smaller batches keep the weights exact. */
+/* batch is 1..128. Batches of 9 or more run on the tcgen05 path, whose f16 weights are q*d
+ * rounded once (relative error <= 2^-11 per weight); smaller batches keep the weights exact. */
 /* ab2_q8_gemv for batch 1..8 that allocates nothing: no reference counterpart. For callers
  * that cannot call cudaMalloc (device memory already carved up by their own pool, or a
  * thread where cudaMalloc's implicit synchronisation would stall other streams). Its

@@ -1,13 +1,13 @@
-"""GPU: prefill of a prompt (ab2_prefill: chunks of 64 tokens, the DeltaNet recurrence in its
-chunkwise form, each token's attention over the slot's cache) against the oracle's
-token-by-token qwen35_forward_token, the reference's own prompt loop
+"""GPU: prefill of a prompt (ab2_prefill: steps of up to 128 tokens, the DeltaNet recurrence in
+its chunkwise form over 64 tokens at a time, each token's attention over the slot's cache)
+against the oracle's token-by-token qwen35_forward_token, the reference's own prompt loop
 (crates/cli/src/main.rs:358-362).
 
-A prefill chunk is a 64-row step, so it runs on the exact-weight path only in a context with
-exact_max_batch = 64 (EXACT below). There the prefill and the oracle differ only in the order
-of f32 sums (the 64-row GEMM's K order, the chunkwise recurrence), so the last token's logits
-and every state agree to PREFILL_TOL. In a default context the chunk runs on the tcgen05 path,
-whose GEMM operands are rounded to f16, and the decode parity bar applies."""
+In a context with exact_max_batch = 64 (EXACT below) a prefill step is 64 rows on the
+exact-weight path. There the prefill and the oracle differ only in the order of f32 sums
+(the 64-row GEMM's K order, the chunkwise recurrence), so the last token's logits and every
+state agree to PREFILL_TOL. In a default context a step is 128 rows on the tcgen05 path (its
+N = 128 form), whose GEMM operands are rounded to f16, and the decode parity bar applies."""
 import numpy as np
 import pytest
 
@@ -100,7 +100,8 @@ def test_prefill_matches_stepwise_decode(pkg, synth, tiny_gguf):
 
 
 def test_prefill_tensor_core_path(pkg, oracle, synth, tiny_gguf, tiny_model):
-    """A default context prefills on the tcgen05 GEMM (64-row chunks, even with max_batch 1):
+    """A default context prefills on the tcgen05 GEMM, even with max_batch 1: a 128-row step
+    (the GEMM's N = 128 form, the DeltaNet mixer as two 64-token launches) and a 2-row step,
     within the decode parity bar of the oracle."""
     prompt = synth.seeded_tokens(130, 32000, seed=11)
     with pkg.DecodeContext(tiny_gguf, max_batch=1, max_ctx=140, kv_bf16=True) as ctx:
@@ -126,6 +127,29 @@ def test_prefill_2b_matches_oracle(pkg, oracle, synth):
         assert err < PREFILL_TOL
         assert argmax_consistent(nx, lo, lg)
         _check_states(ctx, seq, 70, ctx.layer_is_deltanet)
+
+
+def test_prefill_2b_tensor_core_path(pkg, oracle, synth):
+    """The 2B shape in a default context: 70 prompt tokens as one 70-row step of the N = 128
+    tcgen05 GEMM (rows 70..127 of its operand are padding), then 8 greedy decode steps, all
+    within the decode parity bar of the oracle's token-by-token forward."""
+    gguf = synth.build_model_gguf(synth.shape_2b(), seed=0)
+    prompt = synth.seeded_tokens(70, 151936, seed=6)
+    with pkg.DecodeContext(gguf, max_batch=1, max_ctx=90, kv_bf16=True) as ctx:
+        lg, nx = ctx.prefill(0, prompt)
+        model = oracle.Model(gguf, ctx_cap=90)
+        seq, lo = _oracle_run(model, prompt)
+        err = rel_err(lg, lo)
+        print(f"2B tcgen05 prefill: last-token logit rel err {err:.2e}")
+        assert err < LOGIT_TOL
+        assert argmax_consistent(nx, lo, lg)
+        _check_states(ctx, seq, 70, ctx.layer_is_deltanet, tol=LOGIT_TOL)
+        t = nx
+        for i in range(8):
+            lgd, nxd = ctx.decode_step([t])
+            lod = seq.forward(t)  # the GPU's token on both sides: a near tie cannot part them
+            assert rel_err(lgd[0], lod) < LOGIT_TOL, (i, rel_err(lgd[0], lod))
+            t = int(nxd[0])
 
 
 def test_prefill_rejects_bad_requests(pkg, synth, tiny_gguf):

@@ -102,7 +102,7 @@ TC_DECLARED_TOL = 2e-5
 
 
 @pytest.mark.parametrize("m,n", SHAPES)
-@pytest.mark.parametrize("batch", [9, 32, 64])
+@pytest.mark.parametrize("batch", [9, 32, 64, 65, 128])  # 65 and 128: the N = 128 form
 def test_tc_gemm_matches_declared_rounding(pkg, oracle, synth, cuda, m, n, batch):
     torch = cuda
     rng = np.random.default_rng(m * 3 + n + batch)
@@ -172,8 +172,8 @@ def test_gemv_rejects_bad_batch(pkg, synth, cuda):
     torch = cuda
     rng = np.random.default_rng(0)
     w = pkg.Q8Tensor(synth.random_q8_0(rng, 32, 64), 32, 64)
-    x = torch.zeros((65, 64), device="cuda")
-    y = torch.zeros((65, 32), device="cuda")
+    x = torch.zeros((129, 64), device="cuda")
+    y = torch.zeros((129, 32), device="cuda")
     with pytest.raises(pkg.Ab2Error) as ei:
-        pkg.q8_gemv(w, x, y, 65)
+        pkg.q8_gemv(w, x, y, 129)
     assert ei.value.code == -6
