@@ -21,57 +21,17 @@
 #include <algorithm>
 #include <cstdint>
 
+#include "attn_tiles.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "umma.cuh"
 
 namespace ab2 {
 
-constexpr int kT = 64;  // tokens per tile
 constexpr int kAttnStages = 3;
 constexpr int kCompWarps = 4;
 constexpr int kAttnMmaThreads = (kCompWarps + 1) * 32;  // + one TMA producer warp
-constexpr int kGQ = 4;
 constexpr int kPStride = kT + 8;  // bf16 elements per P row (padding avoids ldmatrix bank conflicts)
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-}
-// f32 -> (hi, lo) bf16 parts with x = hi + lo to about 2^-17 relative
-__device__ __forceinline__ void split_bf16(float x, float& hi, float& lo) {
-    hi = __bfloat162float(__float2bfloat16_rn(x));
-    lo = x - hi;
-}
-
-constexpr int kMaxSplits = 64;  // splits per (sequence, kv head)
 
 template <int HD>
 struct AttnSmem {
@@ -650,6 +610,18 @@ static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, i
     if (core_end) cudaEventRecord(core_end, st);
     if (splits > 1) launch_pdl(attn_merge_kernel<HD>, dim3(p.Hkv, batch), dim3(256), 0, st, p);
     return 0;
+}
+
+// the query/K/V prologue and the split merge alone, for the prefill kernel (attn_prefill.cu)
+int launch_attn_prep(const AttnParams& p, int batch, int hd, cudaStream_t st) {
+    if (hd == 256) return launch_pdl(attn_prep_kernel<256>, dim3(p.Hkv, batch), dim3(128), 0, st, p) == cudaSuccess ? 0 : -2;
+    if (hd == 128) return launch_pdl(attn_prep_kernel<128>, dim3(p.Hkv, batch), dim3(128), 0, st, p) == cudaSuccess ? 0 : -2;
+    return -1;
+}
+int launch_attn_merge(const AttnParams& p, int batch, int hd, cudaStream_t st) {
+    if (hd == 256) return launch_pdl(attn_merge_kernel<256>, dim3(p.Hkv, batch), dim3(256), 0, st, p) == cudaSuccess ? 0 : -2;
+    if (hd == 128) return launch_pdl(attn_merge_kernel<128>, dim3(p.Hkv, batch), dim3(256), 0, st, p) == cudaSuccess ? 0 : -2;
+    return -1;
 }
 
 int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int batch, int hd,

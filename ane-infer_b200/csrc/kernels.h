@@ -222,6 +222,17 @@ int launch_attention_mma(const void* tmk, const void* tmv, const AttnParams& p, 
                          int max_len, int num_sms, cudaStream_t st, cudaEvent_t core_begin = nullptr,
                          cudaEvent_t core_end = nullptr);
 int attn_nsplit(int max_len, int chunk);
+// attn_prefill.cu: causal attention of a prefill step's B rows (consecutive positions of one
+// sequence, all reading one cache slot: p.seq_rows = 0) on the tensor cores, in query blocks
+// of 8 tokens x the kv head's query heads; enqueues the query prep, the kernel and, when the
+// plan cuts the prefix into several splits, the merge. p.chunk from attn_prefill_chunk.
+int attn_prefill_chunk(int rows, int hkv, int max_len, int num_sms);
+int launch_attention_prefill(const void* tmk, const void* tmv, const AttnParams& p, int64_t row_base, int rows,
+                             int hd, int max_len, int num_sms, cudaStream_t st, cudaEvent_t core_begin = nullptr,
+                             cudaEvent_t core_end = nullptr);
+// attn_mma.cu: the query/K/V prologue and the split merge of the tensor-core attention alone
+int launch_attn_prep(const AttnParams& p, int batch, int hd, cudaStream_t st);
+int launch_attn_merge(const AttnParams& p, int batch, int hd, cudaStream_t st);
 int attn_chunk(int batch, int hkv, int max_len, int num_sms);
 int attn_nsplit_bound(int batch, int hkv, int cap, int num_sms);
 size_t attn_ws_floats(int batch, int hkv, int nsplit, int hd, int gq);

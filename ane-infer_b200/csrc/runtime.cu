@@ -978,7 +978,9 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
         p.Hkv = x->kv_hl;
         p.kvh0 = x->kv_h0;
         p.Hkv_all = (int)c.n_kv;
-        p.chunk = step_attn_chunk(x, B, max_len);
+        // a prefill step on the bf16 cache runs the query-block kernel, which plans its own splits
+        const bool pf_tc = pf_p0 >= 0 && x->kv_bf16;
+        p.chunk = pf_tc ? attn_prefill_chunk(B, x->kv_hl, max_len, x->num_sms) : step_attn_chunk(x, B, max_len);
         // a replayed step graph keeps this plan while the longest context stays within its
         // split count, so every position up to the plan's last covered token is valid
         p.max_pos = std::min(x->cap - 1, attn_nsplit(max_len, p.chunk) * p.chunk - 1);
@@ -997,9 +999,11 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
             // small launches of their own).
             const int64_t row_base = ((int64_t)L.local * x->max_batch + s0) * x->kv_hl * x->cap;
             const auto ev = prof_pair(x, PC_ATTN);
-            if (launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len, x->num_sms, st,
-                                     ev.first, ev.second))
-                return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
+            const int rc = pf_tc ? launch_attention_prefill(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len,
+                                                            x->num_sms, st, ev.first, ev.second)
+                                 : launch_attention_mma(x->tmap_k, x->tmap_v, p, row_base, B, (int)c.hd, max_len,
+                                                        x->num_sms, st, ev.first, ev.second);
+            if (rc) return seterr(AB2_ERR_SHAPE, "attention: unsupported head configuration");
         } else {
             ProfScope ps(x, PC_ATTN, st);
             if (launch_attention(p, B, (int)c.hd, x->kv_bf16, max_len, st))
