@@ -162,26 +162,38 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
     const int nblk = (T + kConvTok - 1) / kConvTok, nitems = kConvCh * nblk;
     float4 fin_cs = make_float4(0.f, 0.f, 0.f, 0.f);
     int fin_ch = -1;
-#pragma unroll 1
-    for (int e = tid; e < nitems; e += kPfThreads) {
+    // the inputs of item e: conv weights, the window before its tokens, its tokens' inputs
+    struct ConvIn {
+        float4 cw, cs;
+        float x[kConvTok];
+    };
+    auto conv_load = [&](int e, ConvIn& in) {
         const int cc = e % kConvCh, t0 = (e / kConvCh) * kConvTok, ch = conv_channel(cc);
-        const float4 cw = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
-        float4 cs;
+        in.cw = *reinterpret_cast<const float4*>(p.conv_w + (size_t)ch * 4);
         if (t0 == 0) {
-            cs = *reinterpret_cast<const float4*>(p.conv + (size_t)ch * 4);
+            in.cs = *reinterpret_cast<const float4*>(p.conv + (size_t)ch * 4);
         } else {
             const float* pr = p.proj + (size_t)(t0 - 3) * p.ldp + ch;
-            cs = make_float4(0.0f, pr[0], pr[p.ldp], pr[2 * (size_t)p.ldp]);
+            in.cs = make_float4(0.0f, pr[0], pr[p.ldp], pr[2 * (size_t)p.ldp]);
         }
-        float xin[kConvTok];
 #pragma unroll
-        for (int u = 0; u < kConvTok; u++) xin[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
+        for (int u = 0; u < kConvTok; u++) in.x[u] = t0 + u < T ? p.proj[(size_t)(t0 + u) * p.ldp + ch] : 0.0f;
+    };
+    // software-pipelined: the next item's loads are in flight while this item is computed
+    ConvIn cur, nxt;
+    if (tid < nitems) conv_load(tid, cur);
+#pragma unroll 1
+    for (int e = tid; e < nitems; e += kPfThreads) {
+        if (e + kPfThreads < nitems) conv_load(e + kPfThreads, nxt);
+        const int cc = e % kConvCh, t0 = (e / kConvCh) * kConvTok, ch = conv_channel(cc);
+        float4 cs = cur.cs;
+        const float4 cw = cur.cw;
         float* dst = cc < DK ? Qb + cc : cc < 2 * DK ? Kb + (cc - DK) : Vb + (cc - 2 * DK);
         const int ld = cc < 2 * DK ? kLd : kLv;
 #pragma unroll
         for (int u = 0; u < kConvTok; u++) {
             if (t0 + u >= T) break;
-            cs = make_float4(cs.y, cs.z, cs.w, xin[u]);
+            cs = make_float4(cs.y, cs.z, cs.w, cur.x[u]);
             float sum = cs.x * cw.x;
             sum += cs.y * cw.y;
             sum += cs.z * cw.z;
@@ -193,6 +205,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) dn_prefill_kernel(DnParams p, i
             fin_ch = ch;
             if (cc < 2 * DK && c != 0) fin_ch = -1;  // q and k channels: one CTA of the cluster writes
         }
+        cur = nxt;
     }
     if (tid < T) {
         // beta = sigmoid(W_beta x) and log d = ssm_a * softplus(W_alpha x + dt_bias) (deltanet.rs:469-480)
