@@ -10,8 +10,9 @@
 //     4-7 lo of the M=16 operand), K and V are exact bf16, so scores and outputs keep ~f32
 //     accuracy;
 //   * the online softmax runs per 64-token tile across the warps through shared memory;
-//   * the CTA holding the new position first writes the new (normed, rotated) key and value
-//     into the cache and fences them to the async proxy before TMA reads that tile;
+//   * attn_prep_kernel, launched before it, norms and rotates the queries into a prepared
+//     buffer and appends the new (normed, rotated) key and value to the cache; the attention
+//     kernel's producer waits for it (griddepcontrol.wait) before its first copy;
 //   * the kernel is persistent: CTA c takes the work items (split, sequence, kv head) c,
 //     c + grid, ..., and the producer streams their tiles through one ring without draining
 //     between items; split partials are merged in split order by attn_merge_kernel.
