@@ -418,6 +418,23 @@ def run_ours(args):
                    "ms_per_prompt": round(pf_s * 1e3, 3), "sequences": world,
                    "timing": "host wall clock around the synchronous ab2_prefill call, median of 3, max over ranks"}
 
+    # ---- the config-3 attention op at its largest cell (B=64, ctx 32K), rank 0 at N = 1, after
+    # the timed region: the tensor-core flash-decode alone against the HBM copy peak
+    attn32k = None
+    if rank == 0 and world == 1 and not args.no_attn_op:
+        peak, peak_kind = measured_peaks()
+        fn, nbytes = attn_op_inputs(64, 32768, 16)
+        ms_a = time_flushed(fn, 5, 3)
+        if pkg.op_error():
+            raise RuntimeError("tensor-core pipeline timeout in the attention op")
+        gbs = nbytes / (ms_a / 1e3) / 1e9
+        attn32k = {"op": "gqa flash-decode B=64 ctx=32768 Hq=8 Hkv=2 hd=256 (attn_mma_kernel, query prep, merge)",
+                   "us_per_launch": round(ms_a * 1e3, 2), "algorithmic_bytes": nbytes,
+                   "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "peak_kind": peak_kind,
+                   "frac": round(gbs / peak, 4), "iters": 5, "l2": "flushed before each launch"}
+        del fn
+        torch.cuda.empty_cache()
+
     # ---- CPU baseline (rank 0, N = 1): the oracle on one sequence of the same workload
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -450,6 +467,7 @@ def run_ours(args):
             "weak_scaling": weak,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "attention_op_b64_ctx32k": attn32k,
             "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B * world,
                     "d2h_bytes_per_step": 4 * B * world,
                     "steps": n_e2e},
@@ -673,6 +691,51 @@ def cpu_op_baseline(op: str, B: int, M: int = 0, K: int = 0, ctx: int = 0, secon
             "kind": "port", "sample": f"{what}; {n} calls in {dt * n:.1f} s, scaled to batch {B}"}
 
 
+def attn_op_inputs(B, ctx, extra):
+    """Config-3 attention inputs (Hq 8, Hkv 2, hd 256, RoPE on 64 dims): projections, N(0,1)
+    bf16 caches of ctx tokens (+ extra rows), positions ctx - 1; the call and its K/V bytes."""
+    import torch
+    pkg = load_pkg()
+    Hq, Hkv, hd = 8, 2, 256
+    cap = ctx + extra
+    proj = torch.randn(B, Hq * 2 * hd + 2 * Hkv * hd, device="cuda")
+    kc = torch.randn(B, Hkv, cap, hd, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(B, Hkv, cap, hd, device="cuda").to(torch.bfloat16)
+    pos = torch.full((B,), ctx - 1, dtype=torch.int32, device="cuda")
+    out = torch.empty(B, Hq * hd, device="cuda")
+    st = torch.cuda.current_stream()
+    fn = lambda: pkg.attn_decode(proj, kc, vc, cap, pos, B, Hq, Hkv, hd, True, None, None, 1e7, 64, ctx - 1, out, st)
+    return fn, B * Hkv * ctx * hd * 2 * 2
+
+
+def time_flushed(fn, iters, warmup):
+    """Mean CUDA-event time in ms of fn() on the current stream, L2 flushed before each launch:
+    one 256 MB buffer written and another read, so inputs that fit in L2 come from HBM and
+    the write-back of the flush's own dirty lines is not charged to the timed launch."""
+    import torch
+    st = torch.cuda.current_stream()
+    flush_w = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    flush_r = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def flush_l2():
+        flush_w.fill_(1.0)
+        torch.sum(flush_r, dim=0, out=sink)
+
+    for _ in range(warmup):
+        flush_l2()
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for e0, e1 in ev:
+        flush_l2()
+        e0.record(st)
+        fn()
+        e1.record(st)
+    torch.cuda.synchronize()
+    return sum(e0.elapsed_time(e1) for e0, e1 in ev) / iters
+
+
 def run_op(args):
     """One op of BASELINE configs 2-4 on cuda:0, timed with CUDA events; one JSON line."""
     import numpy as np
@@ -707,42 +770,11 @@ def run_op(args):
         nbytes = B * H * (2 * 128 * 128 * 4 + 3 * 128 * 2 + 128 * 4)
         label = f"gated delta rule B={B} H=16 dk=dv=128"
     else:
-        Hq, Hkv, hd, ctx = 8, 2, 256, args.ctx
-        cap = ctx + args.iters + args.warmup + 8
-        proj = torch.randn(B, Hq * 2 * hd + 2 * Hkv * hd, device="cuda")
-        kc = torch.randn(B, Hkv, cap, hd, device="cuda").to(torch.bfloat16)
-        vc = torch.randn(B, Hkv, cap, hd, device="cuda").to(torch.bfloat16)
-        pos = torch.full((B,), ctx - 1, dtype=torch.int32, device="cuda")
-        out = torch.empty(B, Hq * hd, device="cuda")
-        fn = lambda: pkg.attn_decode(proj, kc, vc, cap, pos, B, Hq, Hkv, hd, True, None, None, 1e7, 64, ctx - 1,
-                                     out, st)
-        nbytes = B * Hkv * ctx * hd * 2 * 2
-        label = f"gqa flash-decode B={B} ctx={ctx} Hq=8 Hkv=2 hd=256"
-    # L2 (126 MB) is flushed before every timed launch by writing one 256 MB buffer and then
-    # reading another, so inputs that fit in L2 (small batches) are read from HBM and the
-    # write-back of the flush's own dirty lines is not charged to the timed launch
-    flush_w = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
-    flush_r = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
-    sink = torch.empty((), dtype=torch.float32, device="cuda")
-
-    def flush_l2():
-        flush_w.fill_(1.0)
-        torch.sum(flush_r, dim=0, out=sink)
-
-    for _ in range(args.warmup):
-        flush_l2()
-        fn()
-    torch.cuda.synchronize()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.iters)]
-    for e0, e1 in ev:
-        flush_l2()
-        e0.record(st)
-        fn()
-        e1.record(st)
-    torch.cuda.synchronize()
+        fn, nbytes = attn_op_inputs(B, args.ctx, args.iters + args.warmup + 8)
+        label = f"gqa flash-decode B={B} ctx={args.ctx} Hq=8 Hkv=2 hd=256"
+    ms = time_flushed(fn, args.iters, args.warmup)
     if pkg.op_error():
         raise RuntimeError("tensor-core pipeline timeout")
-    ms = sum(e0.elapsed_time(e1) for e0, e1 in ev) / args.iters
     gbs = nbytes / (ms / 1e3) / 1e9
     cpu = None
     if not args.no_cpu:
@@ -767,6 +799,8 @@ def main():
     ap.add_argument("--weak", action="store_true", help="run --batch sequences on every GPU (weak scaling)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-attn-op", action="store_true",
+                    help="skip the B=64 ctx-32K attention op figure of the decode line")
     ap.add_argument("--graph", type=int, choices=[0, 1], default=1,
                     help="1: replay each decode step from a captured CUDA graph; 0: stream launches")
     ap.add_argument("--op", choices=["gemm", "recurrence", "attention"], default=None,
