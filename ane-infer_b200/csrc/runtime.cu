@@ -867,6 +867,10 @@ void set_prefetch(ab2_ctx* x, int B, const Q8Weight* w, const void** pf, int64_t
 // lm_head (330 MB for the 2B shape) streams from HBM anyway after its first stages
 constexpr int64_t kPrefetchCap = 32ll << 20;
 
+// rounds of DeltaNet items (one per CTA per round) whose states a batched step's DeltaNet
+// input projection prefetches into L2
+constexpr int kDnLeadRounds = 1;
+
 // h2 (tcgen05 path only): take the activations as silu(g) * u of the gate/up scratch
 int gemm(ab2_ctx* x, const Q8Weight& w, const uint8_t* xf, int B, const GemmEpi& ep, cudaStream_t st,
          const float* h2 = nullptr, int h2_ld = 0) {
@@ -917,7 +921,17 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
               cudaStream_t st, int64_t pf_p0 = -1) {
     const Cfg& c = x->c;
     const int D = (int)c.dim;
-    RET(gemm(x, L.w_in, x->xfa, B, epi_store(x->proj, x->ldp, L.w_in.M), st));
+    GemmEpi e_in = epi_store(x->proj, x->ldp, L.w_in.M);
+    if (L.dn && pf_p0 < 0 && umma_for(x, B)) {
+        // a batched decode step: the input projection pulls into L2 the recurrent states that
+        // the DeltaNet kernel's CTAs load first (item i = slot i / H, head i % H is 64 KiB at
+        // offset i * 64 KiB; each CTA starts with kDnLeadRounds items), so its pipeline fills
+        // from L2 instead of waiting on HBM after the GEMM's CTAs leave the SMs
+        const int64_t total = (int64_t)B * x->s_stride * (int64_t)sizeof(float);
+        e_in.pf = x->dn_S + ((size_t)L.local * x->max_batch + s0) * x->s_stride;
+        e_in.pf_bytes = std::min<int64_t>(total, (int64_t)kDnLeadRounds * x->num_sms * 128 * 128 * sizeof(float));
+    }
+    RET(gemm(x, L.w_in, x->xfa, B, e_in, st));
     if (L.dn) {
         DnParams p;
         p.proj = x->proj;
