@@ -70,6 +70,142 @@ __device__ __forceinline__ bool attn_item(const AttnParams& p, int item, int pai
     return true;
 }
 
+// ---- balanced partition (p.sk_grid > 0). Pair q = b * Hkv + kvh holds n_b = ceil((pos[b] + 1)
+// / kT) tiles (none for a skipped sequence); the pairs' tiles are laid end to end (pair q starts
+// at tile P(q)), and CTA c takes tiles [c * per, (c + 1) * per). Split s of a pair is its piece
+// in the s-th CTA that holds part of it, so split order is token order, as the merge needs.
+__device__ __forceinline__ int sk_tiles(const AttnParams& p, int b) {
+    const int pos = p.pos[b];
+    return attn_pos_ok(p, pos) ? pos / kT + 1 : 0;
+}
+// tiles per CTA: an equal share, at least kSkMinTiles, and enough that no pair of nmax tiles
+// spans more than kMaxSplits CTAs (a run of n tiles meets at most ceil(n / per) + 1 of them)
+constexpr int kSkMinTiles = 4;
+__host__ __device__ inline int sk_per(int64_t total, int nmax, int grid) {
+    int64_t per = (total + grid - 1) / grid;
+    const int64_t by_splits = (nmax + kMaxSplits - 2) / (kMaxSplits - 1);
+    if (per < by_splits) per = by_splits;
+    return (int)(per < kSkMinTiles ? kSkMinTiles : per);
+}
+// warp-wide: total tiles, the longest pair, and the first tile of sequence `bq`'s pairs
+// (every lane gets all three)
+__device__ __forceinline__ void sk_scan(const AttnParams& p, int B, int bq, int lane, int64_t& total, int& nmax,
+                                        int64_t& before) {
+    int64_t t = 0, pre = 0;
+    int m = 0;
+    for (int b = lane; b < B; b += 32) {
+        const int n = sk_tiles(p, b);
+        t += n;
+        if (b < bq) pre += n;
+        m = max(m, n);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        t += __shfl_xor_sync(0xffffffffu, t, o);
+        pre += __shfl_xor_sync(0xffffffffu, pre, o);
+        m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    }
+    total = t * p.Hkv;
+    before = pre * p.Hkv;
+    nmax = m;
+}
+
+// where CTA c's run starts, found once per CTA by warp 0
+struct SkStart {
+    int64_t lo, hi;  // the CTA's tiles [lo, hi)
+    int64_t P;       // first tile of pair (b, kvh)
+    int b, kvh, per;
+};
+__device__ __forceinline__ void sk_find_start(const AttnParams& p, int B, int c, int lane, SkStart& s) {
+    int64_t total, before;
+    int nmax;
+    sk_scan(p, B, 0, lane, total, nmax, before);
+    const int per = sk_per(total, nmax, p.sk_grid);
+    const int64_t lo = (int64_t)c * per, hi = min(lo + per, total);
+    // the sequence whose pairs hold tile lo: an inclusive prefix over the sequences, 32 at a time
+    int64_t run = 0;  // tiles of the sequences before this group of 32
+    int bs = B, ns = 0;
+    int64_t ps = 0;
+    for (int b0 = 0; b0 < B && lo < total; b0 += 32) {
+        const int b = b0 + lane;
+        const int n = b < B ? sk_tiles(p, b) : 0;
+        int64_t v = (int64_t)n * p.Hkv;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int64_t y = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += y;
+        }
+        const bool hit = b < B && n > 0 && run + v > lo;
+        const unsigned m = __ballot_sync(0xffffffffu, hit);
+        if (m) {
+            const int src = __ffs(m) - 1;
+            bs = b0 + src;
+            ns = __shfl_sync(0xffffffffu, n, src);
+            ps = run + __shfl_sync(0xffffffffu, v, src) - (int64_t)ns * p.Hkv;  // first tile of sequence bs
+            break;
+        }
+        run += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) {
+        s.lo = lo;
+        s.hi = hi;
+        s.per = per;
+        if (bs < B) {
+            const int kvh = (int)((lo - ps) / ns);
+            s.b = bs;
+            s.kvh = kvh;
+            s.P = ps + (int64_t)kvh * ns;
+        } else {
+            s.b = B;  // no tiles for this CTA
+            s.kvh = 0;
+            s.P = total;
+        }
+    }
+}
+
+// Walks this CTA's items in order: splits of `chunk` tokens (item c, c + grid, ...) or, with
+// the balanced partition, the pieces of the pairs that meet the CTA's run of tiles.
+struct ItemIter {
+    int item, n_items, pairs, B;
+    int64_t lo = 0, hi = 0, P = 0;
+    int b = 0, kvh = 0, per = 1;
+    __device__ ItemIter(const AttnParams& p, const SkStart& s, int pairs_, int n_items_)
+        : item(blockIdx.x), n_items(n_items_), pairs(pairs_), B(pairs_ / p.Hkv) {
+        if (p.sk_grid > 0) {
+            lo = s.lo, hi = s.hi, P = s.P, b = s.b, kvh = s.kvh, per = s.per;
+        }
+    }
+    __device__ __forceinline__ bool next(const AttnParams& p, AttnItem& it) {
+        if (p.sk_grid <= 0) {
+            while (item < n_items) {
+                const int cur = item;
+                item += gridDim.x;
+                if (attn_item(p, cur, pairs, it)) return true;
+            }
+            return false;
+        }
+        while (b < B && P < hi) {
+            const int n = sk_tiles(p, b);
+            const int64_t P0 = P;
+            const int bb = b, kv = kvh;
+            P += n;
+            if (++kvh == p.Hkv) kvh = 0, b++;
+            if (n == 0 || P0 + n <= lo) continue;
+            const int s0 = (int)(max(lo, P0) - P0), s1 = (int)(min(hi, P0 + n) - P0);
+            it.b = bb;
+            it.kvh = kv;
+            it.split = (int)((int64_t)blockIdx.x - P0 / per);
+            it.nsplit_b = (int)((P0 + n - 1) / per - P0 / per + 1);
+            it.t0 = s0 * kT;
+            it.t1 = min(p.pos[bb] + 1, s1 * kT);
+            it.ntiles = s1 - s0;
+            it.has_new = s1 == n;
+            return true;
+        }
+        return false;
+    }
+};
+
 // the number of kernels launch_attention_mma enqueues: the query/K/V prologue, the attention
 // kernel, and the merge when any split is cut
 int attn_mma_launches(int max_len, int chunk) { return (max_len + chunk - 1) / chunk > 1 ? 3 : 2; }
@@ -228,6 +364,12 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
     }
     // rows 8-15 of the P operand stay zero; rows 0-7 are rewritten for every tile
     for (int i = threadIdx.x; i < 16 * kPStride; i += kAttnMmaThreads) P_s[i] = __float2bfloat16_rn(0.0f);
+    __shared__ SkStart sk_s;
+    if (p.sk_grid > 0) {
+        // the balanced partition reads the positions: after the predecessor, like every role below
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (warp == 0) sk_find_start(p, pairs / p.Hkv, blockIdx.x, lane, sk_s);
+    }
     __syncthreads();
 
     if (warp == kCompWarps) {
@@ -236,9 +378,9 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
             asm volatile("griddepcontrol.wait;" ::: "memory");  // prepared queries and appended K/V
             int i = 0, k = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-                AttnItem it;
-                if (!attn_item(p, item, pairs, it)) continue;
+            ItemIter items(p, sk_s, pairs, n_items);
+            AttnItem it;
+            while (ok && items.next(p, it)) {
                 const int pair = it.b * p.Hkv + it.kvh;
                 const int qs = k & 1;
                 if (k >= 2 && !mbar_wait(&q_free[qs], ((k >> 1) - 1) & 1, WL)) {
@@ -288,9 +430,9 @@ __global__ void __launch_bounds__(kAttnMmaThreads, 1)
     constexpr int NPV = HD / 32;  // 8-dim n-tiles of this warp's HD/4 output dims
     asm volatile("griddepcontrol.wait;" ::: "memory");  // outputs may be read by earlier kernels
     int i = 0, k = 0;  // tile and item counters, in step with the producer
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        AttnItem it;
-        if (!attn_item(p, item, pairs, it)) continue;
+    ItemIter items(p, sk_s, pairs, n_items);
+    AttnItem it;
+    while (items.next(p, it)) {
         const int b = it.b, kvh = it.kvh;
         const float* proj = p.proj + (size_t)b * p.ldp;
 
@@ -470,7 +612,17 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (!attn_pos_ok(p, p.pos[b])) return;
     const int L = p.pos[b] + 1;
-    const int nsplit = (L + p.chunk - 1) / p.chunk;
+    int nsplit = (L + p.chunk - 1) / p.chunk;
+    if (p.sk_grid > 0) {
+        // the balanced partition: the CTAs that held a piece of this pair (every warp computes it)
+        int64_t total, before;
+        int nmax;
+        sk_scan(p, gridDim.y, b, lane, total, nmax, before);
+        const int per = sk_per(total, nmax, p.sk_grid);
+        const int n = sk_tiles(p, b);
+        const int64_t P = before + (int64_t)kvh * n;
+        nsplit = (int)((P + n - 1) / per - P / per + 1);
+    }
     if (nsplit <= 1) return;
     static_assert(kGQ * HD % 4 == 0 && kGQ * HD <= 4 * 256 && kMaxSplits <= 64, "merge tiling: a float4 of outputs per thread");
     const size_t part_floats = (size_t)kGQ * 2 + (size_t)kGQ * HD;
@@ -599,17 +751,33 @@ static int launch_mma_t(const void* tmk, const void* tmv, const AttnParams& p, i
     const int splits = attn_nsplit(max_len, p.chunk);
     if (splits > kMaxSplits || !p.qprep) return -1;
     const int n_items = pairs * splits;
-    const int grid = std::min(n_items, num_sms);
+    int grid = std::min(n_items, num_sms);
+    AttnParams pm = p;
+    pm.sk_grid = 0;
+    if (splits > 1) {
+        // the balanced partition when it beats the chunk plan: per CTA, the chunk plan costs its
+        // items' tiles plus one tile of fixed work per item; the balanced one an equal share of
+        // the tiles plus at most ceil(share / tiles per pair) + 1 items
+        const int max_tiles = (max_len + kT - 1) / kT;
+        const int64_t chunk_cost = (int64_t)((n_items + grid - 1) / grid) * (p.chunk / kT + 1);
+        const int per = sk_per((int64_t)pairs * max_tiles, max_tiles, num_sms);
+        const int64_t sk_cost = per + (per + max_tiles - 1) / max_tiles + 1;
+        if (sk_cost < chunk_cost) {
+            pm.sk_grid = num_sms;
+            grid = num_sms;
+        }
+    }
     if (launch_pdl(attn_prep_kernel<HD>, dim3(p.Hkv, batch), dim3(128), 0, st, p) != cudaSuccess) return -2;
     if (core_begin) cudaEventRecord(core_begin, st);
-    AttnParams pm = p;
     pm.wt = take_wait_test(kWaitTestAttention, st);
     if (launch_pdl(attn_mma_kernel<HD>, dim3(grid), dim3(kAttnMmaThreads), smem, st,
                    *reinterpret_cast<const CUtensorMap*>(tmk), *reinterpret_cast<const CUtensorMap*>(tmv), pm,
                    row_base, pairs, n_items) != cudaSuccess)
         return -2;
     if (core_end) cudaEventRecord(core_end, st);
-    if (splits > 1) launch_pdl(attn_merge_kernel<HD>, dim3(p.Hkv, batch), dim3(256), 0, st, p);
+    AttnParams mp = p;
+    mp.sk_grid = pm.sk_grid;
+    if (splits > 1) launch_pdl(attn_merge_kernel<HD>, dim3(p.Hkv, batch), dim3(256), 0, st, mp);
     return 0;
 }
 

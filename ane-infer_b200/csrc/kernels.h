@@ -191,6 +191,11 @@ struct AttnParams {
     int64_t seq_rows = -1;
     int Hkv_all = 0;     // kv heads of the model (0: = Hkv); the caches hold only this launch's Hkv
     int chunk;           // tokens per split
+    // tensor-core decode kernel and its merge: > 0 = the balanced partition over this many CTAs
+    // (every (sequence, kv head) pair's 64-token tiles laid end to end, CTA c taking an equal
+    // run of them, so a pair cut by CTA boundaries becomes consecutive splits); 0 = splits of
+    // `chunk` tokens dealt to the CTAs round-robin
+    int sk_grid = 0;
     float* ws;           // split partials
     float* qprep = nullptr;  // tensor-core kernel: normed, rotated queries [B][Hkv][Hq/Hkv][HD]
     unsigned* tickets;   // [B*Hkv]
