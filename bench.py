@@ -45,10 +45,10 @@ SHAPE_KEYS = dict(n_layers=24, dim=2048, vocab=151936, ffn=6144, dn_heads=16, dn
 # dram__bytes_read.sum + dram__bytes_write.sum per decode step of each kernel family, from one
 # ncu capture of this benchmark's own step (2B shape, B=64, ctx ~8.2K: the launch list with
 # gpu__time_duration and the DRAM bytes, one pass per launch, ten steps averaged). The GEMM
-# family's figure includes the L2 prefetch of each following GEMM's weights and write-backs
-# of DeltaNet state evicted while the GEMMs run; DeltaNet's leaves part of its state writes
-# to later kernels.
-NCU_TRAFFIC_PER_STEP = {"q8_gemm": 3_275_100_000, "attention": 6_571_800_000, "deltanet": 1_639_700_000}
+# family's figure includes the L2 prefetch of each following GEMM's weights (and of the first
+# DeltaNet states) and write-backs of DeltaNet state evicted while the GEMMs run; DeltaNet's
+# leaves part of its state writes to later kernels.
+NCU_TRAFFIC_PER_STEP = {"q8_gemm": 3_431_700_000, "attention": 6_510_200_000, "deltanet": 1_640_300_000}
 
 
 def load_pkg():
@@ -74,13 +74,32 @@ def measured_peaks():
 
 # --------------------------------------------------------------------------- clocks sampler
 class ClockSampler:
+    """SM clock and clock-event reasons of one GPU while the timed region runs. NVML is polled
+    every 2 ms from a thread, since a timed region lasts only tens of milliseconds; the
+    nvidia-smi loop (200 ms) is the fallback where NVML cannot be loaded. `begin()` drops what
+    was sampled before the region starts; `stop()` ends sampling and summarises it."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_id: str):
-        self.samples = []
+        self.samples = []  # (sm MHz, max sm MHz, set of reason names)
         self.proc = None
+        self.nvml = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(gpu_id)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -90,27 +109,45 @@ class ClockSampler:
         self.t = threading.Thread(target=self._read, daemon=True)
         self.t.start()
 
+    def _poll(self):
+        nv = self.nvml
+        reasons_of = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                bits = int(reasons_of(self.handle))
+            except Exception:
+                break
+            self.samples.append((sm, self.max_mhz, {n for n, b in self.REASONS if bits & b}))
+            time.sleep(0.002)
+
     def _read(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append(parts)
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit() and parts[2].replace(".", "").isdigit():
+                names = {self.REASONS[i][0] for i in range(4) if parts[5 + i].lower() == "active"}
+                self.samples.append((float(parts[1]), float(parts[2]), names))
+
+    def begin(self):
+        self.samples = []
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
+        if self.nvml is None and self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML and nvidia-smi unavailable"]}
+        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         self.t.join(timeout=2)
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.samples)}
+        got = list(self.samples)
+        return {"sm_mhz": statistics.median(s[0] for s in got) if got else None,
+                "sm_max_mhz": max(s[1] for s in got) if got else None,
+                "reasons": sorted(set().union(*(s[2] for s in got))) if got else [],
+                "samples": len(got), "source": "nvml, 2 ms" if self.nvml else "nvidia-smi, 200 ms"}
 
 
 def gpu_id_for(torch, dev: int) -> str:
@@ -308,6 +345,7 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     pos0 = ctx.get_pos(0)
+    clock.begin()
     e0.record(stream)
     dev_steps(args.steps, args.warmup)
     e1.record(stream)
@@ -534,6 +572,7 @@ def run_split(args):
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+    clock.begin()
     e0.record(stream)
     dev_steps(args.steps, args.warmup)
     e1.record(stream)
@@ -599,6 +638,7 @@ def run_prefill(args):
         ctx.prefill(0, prompt, want_logits=False)
     clock = ClockSampler(gpu_id_for(torch, 0))
     time.sleep(0.3)
+    clock.begin()
     times = []
     for _ in range(args.steps):
         ctx.reset_slot(0)

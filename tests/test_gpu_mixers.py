@@ -132,6 +132,78 @@ def test_attn_decode_op_config3(pkg, oracle, cuda, B, ctx):
         assert e < TOL, b
 
 
+def _attn_mma_plan(B, Hkv, max_len, sms):
+    """The tensor-core launcher's choice between chunk splits and the balanced partition
+    (attn_mma_chunk, sk_per and the cost comparison in attn_mma.cu's launch_mma_t)."""
+    kT, kmax = 64, 64
+    pairs = B * Hkv
+    best = None
+    c = (max(4 * kT, -(-max_len // kmax)) + kT - 1) // kT * kT
+    while True:
+        s = -(-max_len // c)
+        cost = -(-(pairs * s) // sms) * (c // kT + 1)
+        if best is None or cost < best[0]:
+            best = (cost, c)
+        if s == 1:
+            break
+        c += kT
+    chunk = best[1]
+    splits = -(-max_len // chunk)
+    if splits <= 1:
+        return "chunk"
+    items = pairs * splits
+    grid = min(items, sms)
+    mt = -(-max_len // kT)
+    per = max(-(-(pairs * mt) // sms), (mt + kmax - 2) // (kmax - 1), 4)
+    chunk_cost = -(-items // grid) * (chunk // kT + 1)
+    return "balanced" if per + -(-per // mt) + 1 < chunk_cost else "chunk"
+
+
+def test_attn_decode_balanced_partition_ragged(pkg, oracle, cuda):
+    """The balanced partition of the tensor-core flash-decode (every pair's tiles laid end to
+    end, an equal run per CTA) on a widely ragged batch of 40 sequences (positions 0, 63, 64,
+    127, max_pos and seeded values between), with one sequence beyond max_pos that must be
+    skipped: a CTA's run then holds many short pairs, long pairs are cut across several
+    CTAs, and the device-side plan has to skip the rejected sequence's tiles. Every computed
+    sequence is checked against the oracle."""
+    torch = cuda
+    B, Hq, Hkv, hd, rot, max_pos = 40, 8, 2, 256, 64, 5999
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert _attn_mma_plan(B, Hkv, max_pos + 1, sms) == "balanced"
+    cap = max_pos + 80
+    rng = np.random.default_rng(4040)
+    pos_h = rng.integers(0, max_pos + 1, size=B).astype(np.int32)
+    pos_h[:6] = [0, 63, 64, 127, max_pos, 1]
+    skipped = 17
+    pos_h[skipped] = max_pos + 40  # inside the cache, beyond max_pos
+    g = torch.Generator(device="cuda").manual_seed(4041)
+    proj = torch.randn(B, Hq * 2 * hd + 2 * Hkv * hd, device="cuda", generator=g)
+    kd = torch.randn(B, Hkv, cap, hd, device="cuda", generator=g).to(torch.bfloat16)
+    vd = torch.randn(B, Hkv, cap, hd, device="cuda", generator=g).to(torch.bfloat16)
+    pre = (kd.float().cpu().numpy(), vd.float().cpu().numpy())
+    pos = torch.from_numpy(pos_h).cuda()
+    out = torch.zeros((B, Hq * hd), dtype=torch.float32, device="cuda")
+    assert pkg.op_error() == 0
+    pkg.attn_decode(proj, kd, vd, cap, pos, B, Hq, Hkv, hd, True, None, None, 1e7, rot, max_pos, out)
+    torch.cuda.synchronize()
+    assert pkg.op_error() & 8192
+    og, pj = out.cpu().numpy(), proj.cpu().numpy()
+    assert float(np.abs(og[skipped]).max()) == 0.0
+    worst = 0.0
+    for b in range(B):
+        if b == skipped:
+            continue
+        qf = pj[b, :Hq * 2 * hd].reshape(Hq, 2 * hd)
+        kn_ = pj[b, Hq * 2 * hd: Hq * 2 * hd + Hkv * hd].reshape(Hkv, hd)
+        vn_ = pj[b, Hq * 2 * hd + Hkv * hd:].reshape(Hkv, hd)
+        ref, _, _ = oracle.attn_op(qf[:, :hd], qf[:, hd:], kn_, vn_, pre[0][b], pre[1][b], int(pos_h[b]), 1e7, rot,
+                                   kv_bf16=True)
+        e = rel_err(og[b].reshape(Hq, hd), ref)
+        worst = max(worst, e)
+        assert e < TOL, (b, int(pos_h[b]), e)
+    print(f"balanced partition, 39 ragged sequences: worst rel err {worst:.2e}")
+
+
 @pytest.mark.parametrize("kv_bf16", [True, False])
 def test_attn_decode_rejects_position_above_max_pos(pkg, oracle, synth, cuda, kv_bf16):
     """ab2_attn_decode's device-side position check: a sequence whose pos[b] is above the
