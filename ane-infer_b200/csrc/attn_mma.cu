@@ -13,9 +13,12 @@
 //   * attn_prep_kernel, launched before it, norms and rotates the queries into a prepared
 //     buffer and appends the new (normed, rotated) key and value to the cache; the attention
 //     kernel's producer waits for it (griddepcontrol.wait) before its first copy;
-//   * the kernel is persistent: CTA c takes the work items (split, sequence, kv head) c,
-//     c + grid, ..., and the producer streams their tiles through one ring without draining
-//     between items; split partials are merged in split order by attn_merge_kernel.
+//   * the kernel is persistent, and the producer streams the tiles of all of a CTA's work
+//     items through one ring without draining between items. The items are either splits of
+//     a fixed chunk dealt round-robin (CTA c takes items c, c + grid, ...) or, when the
+//     launcher's cost model prefers it, the balanced partition: every (sequence, kv head)
+//     pair's tiles laid end to end and an equal run of them per CTA, computed on the device
+//     from the positions. Split partials are merged in split order by attn_merge_kernel.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

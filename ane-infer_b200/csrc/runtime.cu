@@ -925,8 +925,9 @@ int run_mixer(ab2_ctx* x, const Layer& L, int s0, int B, int max_len, float* out
     if (L.dn && pf_p0 < 0 && umma_for(x, B)) {
         // a batched decode step: the input projection pulls into L2 the recurrent states that
         // the DeltaNet kernel's CTAs load first (item i = slot i / H, head i % H is 64 KiB at
-        // offset i * 64 KiB; each CTA starts with kDnLeadRounds items), so its pipeline fills
-        // from L2 instead of waiting on HBM after the GEMM's CTAs leave the SMs
+        // offset i * 64 KiB, and CTA c takes items c, c + grid, ...: the first kDnLeadRounds
+        // items of every CTA are one contiguous range), so its pipeline fills from L2 instead
+        // of waiting on HBM after the GEMM's CTAs leave the SMs
         const int64_t total = (int64_t)B * x->s_stride * (int64_t)sizeof(float);
         e_in.pf = x->dn_S + ((size_t)L.local * x->max_batch + s0) * x->s_stride;
         e_in.pf_bytes = std::min<int64_t>(total, (int64_t)kDnLeadRounds * x->num_sms * 128 * 128 * sizeof(float));
