@@ -81,3 +81,30 @@ def rel_err(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def attn_mma_plan(B, Hkv, max_len, sms):
+    """The tensor-core launcher's choice between chunk splits and the balanced partition
+    (attn_mma_chunk, sk_per and the cost comparison in attn_mma.cu's launch_mma_t)."""
+    kT, kmax = 64, 64
+    pairs = B * Hkv
+    best = None
+    c = (max(4 * kT, -(-max_len // kmax)) + kT - 1) // kT * kT
+    while True:
+        s = -(-max_len // c)
+        cost = -(-(pairs * s) // sms) * (c // kT + 1)
+        if best is None or cost < best[0]:
+            best = (cost, c)
+        if s == 1:
+            break
+        c += kT
+    chunk = best[1]
+    splits = -(-max_len // chunk)
+    if splits <= 1:
+        return "chunk"
+    items = pairs * splits
+    grid = min(items, sms)
+    mt = -(-max_len // kT)
+    per = max(-(-(pairs * mt) // sms), (mt + kmax - 2) // (kmax - 1), 4)
+    chunk_cost = -(-items // grid) * (chunk // kT + 1)
+    return "balanced" if per + -(-per // mt) + 1 < chunk_cost else "chunk"

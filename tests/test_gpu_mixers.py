@@ -3,7 +3,7 @@ recurrence op (config 2), the flash-decode op (config 3) and the per-layer mixer
 import numpy as np
 import pytest
 
-from conftest import rel_err
+from conftest import attn_mma_plan, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -132,33 +132,6 @@ def test_attn_decode_op_config3(pkg, oracle, cuda, B, ctx):
         assert e < TOL, b
 
 
-def _attn_mma_plan(B, Hkv, max_len, sms):
-    """The tensor-core launcher's choice between chunk splits and the balanced partition
-    (attn_mma_chunk, sk_per and the cost comparison in attn_mma.cu's launch_mma_t)."""
-    kT, kmax = 64, 64
-    pairs = B * Hkv
-    best = None
-    c = (max(4 * kT, -(-max_len // kmax)) + kT - 1) // kT * kT
-    while True:
-        s = -(-max_len // c)
-        cost = -(-(pairs * s) // sms) * (c // kT + 1)
-        if best is None or cost < best[0]:
-            best = (cost, c)
-        if s == 1:
-            break
-        c += kT
-    chunk = best[1]
-    splits = -(-max_len // chunk)
-    if splits <= 1:
-        return "chunk"
-    items = pairs * splits
-    grid = min(items, sms)
-    mt = -(-max_len // kT)
-    per = max(-(-(pairs * mt) // sms), (mt + kmax - 2) // (kmax - 1), 4)
-    chunk_cost = -(-items // grid) * (chunk // kT + 1)
-    return "balanced" if per + -(-per // mt) + 1 < chunk_cost else "chunk"
-
-
 def test_attn_decode_balanced_partition_ragged(pkg, oracle, cuda):
     """The balanced partition of the tensor-core flash-decode (every pair's tiles laid end to
     end, an equal run per CTA) on a widely ragged batch of 40 sequences (positions 0, 63, 64,
@@ -169,7 +142,7 @@ def test_attn_decode_balanced_partition_ragged(pkg, oracle, cuda):
     torch = cuda
     B, Hq, Hkv, hd, rot, max_pos = 40, 8, 2, 256, 64, 5999
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert _attn_mma_plan(B, Hkv, max_pos + 1, sms) == "balanced"
+    assert attn_mma_plan(B, Hkv, max_pos + 1, sms) == "balanced"
     cap = max_pos + 80
     rng = np.random.default_rng(4040)
     pos_h = rng.integers(0, max_pos + 1, size=B).astype(np.int32)

@@ -4,7 +4,7 @@ state I/O and capacity errors."""
 import numpy as np
 import pytest
 
-from conftest import argmax_consistent, rel_err
+from conftest import argmax_consistent, attn_mma_plan, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -404,3 +404,47 @@ def test_2b_headline_b64_ctx8k(pkg, oracle, synth, gguf_2b, cuda):
     assert pkg.op_error() == 0
     ctx.close()
     print(f"2B B=64 ctx 8192: {same} of {total} greedy picks identical; worst logit rel err {worst:.2e}")
+
+
+def test_2b_ragged_balanced_attention_step(pkg, oracle, synth, gguf_2b, cuda):
+    """The decode step with the balanced attention partition on a ragged batch: 2B shape,
+    32 sequences whose positions run from 37 to 6000 tokens, tcgen05 GEMM, bf16 KV, step graph.
+    Slots 0 (the longest), 1 (the shortest) and 20 are read back into the oracle, and 4
+    steps run with the device's tokens fed to both sides; logits within the bar every step."""
+    torch = cuda
+    B, n_ctx, steps = 32, 6000, 4
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rng = np.random.default_rng(32)
+    pos = rng.integers(37, n_ctx, size=B)
+    pos[0], pos[1], pos[20] = n_ctx, 37, 2999
+    for step in range(steps):
+        assert attn_mma_plan(B, 2, int(pos.max()) + 1 + step, sms) == "balanced"
+    ctx = pkg.DecodeContext(gguf_2b, max_batch=B, max_ctx=n_ctx + steps + 8, kv_bf16=True)
+    ctx.seed_state(seed=3, n_slots=B, n_tokens=n_ctx, dn_std=0.1, conv_std=1.0, kv_std=1.0)
+    for b in range(B):
+        ctx.set_pos(b, int(pos[b]))
+    ctx.step_graph(True)
+    om = oracle.Model(gguf_2b, ctx_cap=n_ctx + steps + 8)
+    seqs = []
+    for b in (0, 1, 20):
+        s = om.new_seq(kv_bf16=True)
+        for l, dn in enumerate(ctx.layer_is_deltanet):
+            if dn:
+                s.set_dn(l, *ctx.get_dn_state(l, b))
+            else:
+                s.set_kv(l, *ctx.get_kv(l, b, int(pos[b])))
+        s.pos = int(pos[b])
+        seqs.append((b, s))
+    toks = synth.seeded_tokens(B, 151936, seed=4)
+    worst = 0.0
+    for step in range(steps):
+        lg, nx = ctx.decode_step(toks)
+        for b, s in seqs:
+            lo = s.forward(int(toks[b]))
+            e = rel_err(lg[b], lo)
+            worst = max(worst, e)
+            assert e < LOGIT_TOL, (step, b, e)
+        toks = nx
+    assert pkg.op_error() == 0
+    ctx.close()
+    print(f"2B B=32 ragged 37..6000: worst logit rel err {worst:.2e}")
