@@ -1,6 +1,7 @@
 """bench.py on the host (no GPU): the per-op CPU baseline of the op benchmarks (BASELINE
-configs 2-4) returns a well-formed cpu_baseline record for each op, and the algorithmic byte
-counts behind `step_hbm` and `roofline` match the published per-unit formulas."""
+configs 2-4) returns a well-formed cpu_baseline record for each op, the algorithmic byte
+counts behind `step_hbm` and `roofline` match the published per-unit formulas, and the
+clock record's sampler summarises a fake NVML's clocks and reasons."""
 import importlib.util
 import os
 
@@ -65,3 +66,62 @@ def test_kernel_family_accounting(bench, synth):
     per_seq = bench.dn_launch_bytes(cfg, 1)
     assert per_seq == 2 * 16 * 128 * 128 * 4 + 2 * 3 * 2048 * 4 * 4 + (4 * 2048 + 32) * 4 + 2048 * 2
     assert round(per_seq / 1e6, 2) == 2.33
+
+
+class _FakeNvml:
+    """Stands in for pynvml: a GPU whose SM clock and clock-event reasons follow a script."""
+    NVML_CLOCK_SM = 1
+    nvmlClocksEventReasonGpuIdle = 0x1
+
+    def __init__(self, script):
+        self.script = list(script)   # (sm MHz, reason bits) per poll; the last one repeats
+        self.i = 0
+
+    def nvmlInit(self):
+        pass
+
+    def nvmlDeviceGetHandleByPciBusId(self, bus_id):
+        assert bus_id == "00000000:1B:00.0"
+        return "handle"
+
+    def nvmlDeviceGetMaxClockInfo(self, handle, kind):
+        return 1965
+
+    def nvmlDeviceGetClockInfo(self, handle, kind):
+        return self.script[min(self.i, len(self.script) - 1)][0]
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, handle):
+        bits = self.script[min(self.i, len(self.script) - 1)][1]
+        self.i += 1
+        return bits
+
+
+def test_clock_sampler_reads_nvml_during_the_region(bench, monkeypatch):
+    """The clock record polls NVML from a thread: begin() drops the samples taken before the
+    timed region; the summary holds the median SM clock, the maximum and the throttle reasons
+    seen (hw_slowdown 0x8, sw_thermal_slowdown 0x20, hw_thermal_slowdown 0x40, sw_power_cap
+    0x4), and ignores the idle bit."""
+    import sys
+    import time
+    fake = _FakeNvml([(345, 0x1)] * 3 + [(1965, 0x0), (1965, 0x4), (1950, 0x0), (1965, 0x1)])
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    c = bench.ClockSampler("00000000:1B:00.0")
+    deadline = time.time() + 2.0
+    while fake.i < 3 and time.time() < deadline:   # the idle samples before the region
+        time.sleep(0.001)
+    c.begin()
+    while fake.i < 12 and time.time() < deadline:
+        time.sleep(0.001)
+    rec = c.stop()
+    assert rec["source"] == "nvml, 2 ms" and rec["samples"] >= 1
+    assert rec["sm_max_mhz"] == 1965
+    assert rec["sm_mhz"] >= 1950                      # the 345 MHz idle samples were dropped
+    assert set(rec["reasons"]) <= {"sw_power_cap"}
+
+
+def test_clock_sampler_without_nvml_or_nvidia_smi(bench, monkeypatch):
+    import sys
+    monkeypatch.setitem(sys.modules, "pynvml", None)   # import fails
+    monkeypatch.setattr(bench.subprocess, "Popen", lambda *a, **k: (_ for _ in ()).throw(OSError("absent")))
+    rec = bench.ClockSampler("0").stop()
+    assert rec["sm_mhz"] is None and rec["reasons"]
